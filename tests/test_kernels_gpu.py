@@ -1,0 +1,262 @@
+"""Parity of the tcgen05 GEMM family, Adam and frame conversion against the
+numpy oracle, called through the C ABI (ctypes) on a B200.
+
+Tolerances (relative Frobenius error against a float64 oracle):
+  split-TF32 contractions  <= 1e-4   (measured ~1e-6; budget in the spec 1e-3)
+  single-pass TF32         <= 5e-3   (informational mode, not the default)
+  fp32 elementwise (Adam)  <= 1e-6   relative per element, max over elements
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import layers as ol  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL_X3 = 1e-4
+TOL_TF32 = 5e-3
+
+
+def _ctx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from ttrl_b200.device import context
+    return context(0)
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize("m,k,n,relu,bias", [
+    (32, 3136, 512, 1, 1), (32, 512, 6, 0, 1), (256, 512, 6, 0, 1), (256, 3136, 512, 1, 1),
+    (7, 11, 5, 1, 1), (130, 64, 200, 0, 0), (256, 14, 256, 1, 1),
+])
+def test_linear_fwd(m, k, n, relu, bias):
+    ctx = _ctx()
+    rng = np.random.default_rng(m * 7 + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    ref = ol.linear(x.astype(np.float64), w.astype(np.float64), b if bias else None)
+    if relu:
+        ref = np.maximum(ref, 0)
+    y = torch.empty((m, n), device="cuda")
+    ctx.linear_fwd(dev(x), dev(w), dev(b) if bias else None, y, relu=bool(relu))
+    got = host(y)
+    ctx.check_status()
+    assert rel(got, ref) <= TOL_X3
+
+
+@pytest.mark.parametrize("m,k,n", [(32, 3136, 512), (32, 512, 6), (256, 512, 6), (5, 13, 7),
+                                   (256, 3136, 512)])
+def test_linear_dgrad_masked(m, k, n):
+    ctx = _ctx()
+    rng = np.random.default_rng(m + k + n)
+    g = rng.standard_normal((m, n)).astype(np.float32)
+    w = rng.standard_normal((k, n)).astype(np.float32)
+    mask = rng.standard_normal((m, k)).astype(np.float32)
+    ref = (g.astype(np.float64) @ w.astype(np.float64).T) * (mask > 0)
+    dx = torch.empty((m, k), device="cuda")
+    ctx.linear_dgrad(dev(g), dev(w), dev(mask), dx, accumulate=False)
+    assert rel(host(dx), ref) <= TOL_X3
+    # accumulate into the previous result
+    ctx.linear_dgrad(dev(g), dev(w), None, dx, accumulate=True)
+    ref2 = ref + g.astype(np.float64) @ w.astype(np.float64).T
+    assert rel(host(dx), ref2) <= TOL_X3
+
+
+@pytest.mark.parametrize("m,k,n", [(32, 3136, 512), (32, 512, 6), (256, 14, 256), (5, 13, 7),
+                                   (256, 3136, 512)])
+def test_linear_wgrad_with_bias_grad(m, k, n):
+    ctx = _ctx()
+    rng = np.random.default_rng(3 * m + k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    g = rng.standard_normal((m, n)).astype(np.float32)
+    dw = torch.empty((k, n), device="cuda")
+    db = torch.empty((n,), device="cuda")
+    ctx.linear_wgrad(dev(x), dev(g), dw, db, accumulate=False, accumulate_db=False)
+    ref_w = x.astype(np.float64).T @ g.astype(np.float64)
+    ref_b = g.astype(np.float64).sum(0)
+    assert rel(host(dw), ref_w) <= TOL_X3
+    assert rel(host(db), ref_b) <= TOL_X3
+    ctx.linear_wgrad(dev(x), dev(g), dw, db, accumulate=True, accumulate_db=True)
+    assert rel(host(dw), 2 * ref_w) <= TOL_X3
+    assert rel(host(db), 2 * ref_b) <= TOL_X3
+
+
+CONV_CASES = [
+    # n, h, w, c, cout, k, stride, pad
+    (2, 84, 84, 4, 32, 8, 4, 0),     # Nature conv1
+    (2, 20, 20, 32, 64, 4, 2, 0),    # Nature conv2
+    (2, 9, 9, 64, 64, 3, 1, 0),      # Nature conv3
+    (2, 10, 10, 8, 16, 3, 1, 1),     # padded
+    (3, 9, 9, 3, 5, 3, 2, 1),        # odd channels: scalar gather path
+]
+
+
+def _conv_inputs(case, seed):
+    n, h, w, c, cout, k, s, p = case
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    wt = (rng.standard_normal((cout, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    return x, wt, b
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv_fprop(case):
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    n, h, w, c, cout, k, s, p = case
+    x, wt, b = _conv_inputs(case, 1)
+    alpha = 0.5
+    ref = ol.conv2d_nhwc(x.astype(np.float64), wt.astype(np.float64), b, stride=s, padding=p,
+                         input_scale=alpha, apply_relu=True)
+    geom = conv_geom(n, h, w, c, cout, k, k, s, p)
+    y = torch.empty((n * geom.oh * geom.ow, cout), device="cuda")
+    ctx.conv_fprop(dev(x.reshape(-1, c)), dev(ol.oihw_to_krsc(wt)), dev(b), y, geom, alpha, True)
+    assert rel(host(y).reshape(ref.shape), ref) <= TOL_X3
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv_dgrad_masked(case):
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    n, h, w, c, cout, k, s, p = case
+    x, wt, _ = _conv_inputs(case, 2)
+    geom = conv_geom(n, h, w, c, cout, k, k, s, p)
+    rng = np.random.default_rng(5)
+    dy = rng.standard_normal((n, geom.oh, geom.ow, cout)).astype(np.float32)
+    mask = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    ref = ol.conv2d_dgrad(dy.astype(np.float64), wt.astype(np.float64), (n, h, w, c), stride=s,
+                          padding=p) * (mask > 0)
+    dx = torch.empty((n * h * w, c), device="cuda")
+    ctx.conv_dgrad(dev(dy.reshape(-1, cout)), dev(ol.oihw_to_krsc(wt)),
+                   dev(mask.reshape(-1, c)), dx, geom, accumulate=False)
+    assert rel(host(dx).reshape(ref.shape), ref) <= TOL_X3
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv_wgrad_with_bias_grad(case):
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    n, h, w, c, cout, k, s, p = case
+    x, _, _ = _conv_inputs(case, 3)
+    geom = conv_geom(n, h, w, c, cout, k, k, s, p)
+    rng = np.random.default_rng(6)
+    dy = rng.standard_normal((n, geom.oh, geom.ow, cout)).astype(np.float32)
+    alpha = 1.0 / 255.0
+    ref_w = ol.conv2d_wgrad(x.astype(np.float64), dy.astype(np.float64), k, stride=s,
+                            padding=p, input_scale=alpha)
+    ref_b = dy.astype(np.float64).reshape(-1, cout).sum(0)
+    dw = torch.empty((cout, k, k, c), device="cuda")
+    db = torch.empty((cout,), device="cuda")
+    ctx.conv_wgrad(dev(x.reshape(-1, c)), dev(dy.reshape(-1, cout)), dw, db, geom, alpha,
+                   accumulate=False, accumulate_db=False)
+    assert rel(ol.krsc_to_oihw(host(dw)), ref_w) <= TOL_X3
+    assert rel(host(db), ref_b) <= TOL_X3
+
+
+def test_conv_wgrad_split_k_is_deterministic():
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    geom = conv_geom(32, 84, 84, 4, 32, 8, 8, 4, 0)
+    rng = np.random.default_rng(9)
+    x = dev(rng.integers(0, 256, (32 * 84 * 84, 4)).astype(np.float32))
+    dy = dev(rng.standard_normal((32 * 400, 32)).astype(np.float32))
+    outs = []
+    for _ in range(3):
+        dw = torch.empty((32, 8, 8, 4), device="cuda")
+        db = torch.empty((32,), device="cuda")
+        ctx.conv_wgrad(x, dy, dw, db, geom, 1 / 255, False, False)
+        outs.append((host(dw), host(db)))
+    for dw, db in outs[1:]:
+        assert np.array_equal(dw, outs[0][0]) and np.array_equal(db, outs[0][1])
+
+
+def test_tf32_single_pass_mode_is_looser_but_close():
+    from ttrl_b200 import _lib
+    ctx = _ctx()
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((64, 512)).astype(np.float32)
+    w = rng.standard_normal((512, 128)).astype(np.float32)
+    ref = x.astype(np.float64) @ w.astype(np.float64)
+    y = torch.empty((64, 128), device="cuda")
+    ctx.linear_fwd(dev(x), dev(w), None, y, relu=False, precision=_lib.PREC_TF32)
+    e1 = rel(host(y), ref)
+    ctx.linear_fwd(dev(x), dev(w), None, y, relu=False, precision=_lib.PREC_TF32X3)
+    e3 = rel(host(y), ref)
+    assert e1 <= TOL_TF32
+    assert e3 <= TOL_X3
+    assert e3 < e1
+
+
+def test_u8_frames_to_nhwc_with_gather():
+    ctx = _ctx()
+    rng = np.random.default_rng(12)
+    frames = rng.integers(0, 256, (6, 4, 84, 84), dtype=np.uint8)
+    index = np.array([5, 0, 3], dtype=np.int32)
+    out = torch.empty((3 * 84 * 84, 4), device="cuda")
+    ctx.u8_to_f32(torch.from_numpy(frames).cuda(), torch.from_numpy(index).cuda(), out, 1.0)
+    ref = frames[index].transpose(0, 2, 3, 1).reshape(-1, 4).astype(np.float32)
+    assert np.array_equal(host(out), ref)
+
+
+def test_adam_matches_reference_sv_form():
+    ctx = _ctx()
+    rng = np.random.default_rng(13)
+    shapes = [(3136, 512), (512,), (32, 8, 8, 4), (6,), (1,)]
+    ps = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+    Ss = [np.zeros(s, np.float32) for s in shapes]
+    Vs = [np.zeros(s, np.float32) for s in shapes]
+    dps = [dev(p) for p in ps]
+    dS = [dev(s) for s in Ss]
+    dV = [dev(v) for v in Vs]
+    steps = torch.zeros(len(shapes), dtype=torch.int32, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hp = dict(lr=1e-4, b1=0.9, b2=0.999, eps=1.5e-4)
+    for t in range(1, 4):
+        gs = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+        dgs = [dev(g) for g in gs]
+        ctx.adam_step([(dps[i], dgs[i], dS[i], dV[i], i) for i in range(len(shapes))], steps,
+                      ticket, None, hp["lr"], hp["b1"], hp["b2"], hp["eps"], 0.0)
+        for i in range(len(shapes)):
+            ps[i], Ss[i], Vs[i] = ol.adam_step_sv(ps[i], gs[i], Ss[i], Vs[i], t, **hp)
+    for i in range(len(shapes)):
+        for got, want in ((host(dps[i]), ps[i]), (host(dS[i]), Ss[i]), (host(dV[i]), Vs[i])):
+            # normwise (max-abs over max-abs) relative error; elementwise
+            # relative error is ill-conditioned where S = g + b1*S cancels.
+            err = np.max(np.abs(got.astype(np.float64) - want)) / np.max(np.abs(want))
+            assert err <= 1e-6
+    assert host(steps).tolist() == [3] * len(shapes)
+    assert int(host(ticket)[0]) == 0
+
+
+def test_grad_sqnorm_and_clip_factor():
+    ctx = _ctx()
+    rng = np.random.default_rng(14)
+    gs = [rng.standard_normal(s).astype(np.float32) for s in [(100000,), (513,), (7, 3)]]
+    ref = sum(float(np.sum(g.astype(np.float64) ** 2)) for g in gs)
+    out = torch.zeros(2, device="cuda")
+    ws = torch.zeros(ctx.sqnorm_workspace_bytes([g.size for g in gs]), dtype=torch.uint8,
+                     device="cuda")
+    ctx.grad_sqnorm([dev(g) for g in gs], out, 0.5, ws)
+    got = host(out)
+    assert abs(got[0] - ref) / ref <= 1e-6
+    want_scale = 0.5 / (np.sqrt(ref) + 1e-6)
+    assert abs(got[1] - want_scale) / want_scale <= 1e-6

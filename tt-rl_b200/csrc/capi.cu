@@ -1,0 +1,148 @@
+// extern "C" entry points of libttrl_b200.so and the per-thread error text.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "internal.h"
+
+namespace ttrl {
+
+static thread_local char g_last_error[512] = "no error";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int set_cuda_error(const char* what, cudaError_t e) {
+  return set_error(TTRL_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Defined in the kernel translation units.
+int linear_fwd(const float*, const float*, const float*, float*, int, int, int, int, int, float*,
+               size_t, int*, cudaStream_t);
+int linear_dgrad(const float*, const float*, const float*, float*, int, int, int, int, int,
+                 float*, size_t, int*, cudaStream_t);
+int linear_wgrad(const float*, const float*, float*, float*, int, int, int, int, int, int, float*,
+                 size_t, int*, cudaStream_t);
+int conv_fprop(const float*, const float*, const float*, float*, const ttrl_conv_geom*, float, int,
+               int, float*, size_t, int*, cudaStream_t);
+int conv_dgrad(const float*, const float*, const float*, float*, const ttrl_conv_geom*, int, int,
+               float*, size_t, int*, cudaStream_t);
+size_t conv_dgrad_ws(const ttrl_conv_geom*);
+int conv_wgrad(const float*, const float*, float*, float*, const ttrl_conv_geom*, float, int, int,
+               int, float*, size_t, int*, cudaStream_t);
+size_t conv_wgrad_ws(const ttrl_conv_geom*);
+int u8_to_f32(const uint8_t*, const int32_t*, float*, int, int, int, int, float, cudaStream_t);
+int adam_step(const ttrl_adam_tensor*, int, int32_t*, int32_t*, const float*, double, double,
+              double, double, double, cudaStream_t);
+int grad_sqnorm(const float* const*, const int64_t*, int, float*, float, void*, size_t,
+                cudaStream_t);
+size_t sqnorm_ws_bytes(const int64_t*, int);
+
+}  // namespace ttrl
+
+using namespace ttrl;
+
+#define TTRL_STREAM(s) static_cast<cudaStream_t>(s)
+
+extern "C" {
+
+const char* ttrl_last_error(void) { return g_last_error; }
+
+int ttrl_version(void) { return 1; }
+
+int ttrl_init(int device) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return set_cuda_error("cudaSetDevice", e);
+  return gemm_init_device();
+}
+
+size_t ttrl_gemm_workspace_bytes(const ttrl_gemm_desc* d) {
+  return d ? gemm_workspace_bytes(*d) : 0;
+}
+
+int ttrl_gemm(const ttrl_gemm_desc* d, float* workspace, size_t workspace_bytes, int* status,
+              ttrl_stream_t stream) {
+  if (d == nullptr) return set_error(TTRL_EINVAL, "ttrl_gemm: null descriptor");
+  return gemm_run(*d, 0, no_extra(), workspace, workspace_bytes, status, TTRL_STREAM(stream));
+}
+
+int ttrl_linear_fwd(const float* x, const float* w, const float* b, float* y, int m, int k, int n,
+                    int relu, int precision, float* workspace, size_t workspace_bytes,
+                    int* status, ttrl_stream_t stream) {
+  return linear_fwd(x, w, b, y, m, k, n, relu, precision, workspace, workspace_bytes, status,
+                    TTRL_STREAM(stream));
+}
+
+int ttrl_linear_dgrad(const float* g, const float* w, const float* mask, float* dx, int m, int k,
+                      int n, int accumulate, int precision, float* workspace,
+                      size_t workspace_bytes, int* status, ttrl_stream_t stream) {
+  return linear_dgrad(g, w, mask, dx, m, k, n, accumulate, precision, workspace, workspace_bytes,
+                      status, TTRL_STREAM(stream));
+}
+
+int ttrl_linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, int k, int n,
+                      int accumulate, int accumulate_db, int precision, float* workspace,
+                      size_t workspace_bytes, int* status, ttrl_stream_t stream) {
+  return linear_wgrad(x, g, dw, db, m, k, n, accumulate, accumulate_db, precision, workspace,
+                      workspace_bytes, status, TTRL_STREAM(stream));
+}
+
+int ttrl_conv_fprop(const float* x, const float* w, const float* b, float* y,
+                    const ttrl_conv_geom* g, float alpha, int relu, int precision,
+                    float* workspace, size_t workspace_bytes, int* status, ttrl_stream_t stream) {
+  return conv_fprop(x, w, b, y, g, alpha, relu, precision, workspace, workspace_bytes, status,
+                    TTRL_STREAM(stream));
+}
+
+int ttrl_conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
+                    const ttrl_conv_geom* g, int accumulate, int precision, float* workspace,
+                    size_t workspace_bytes, int* status, ttrl_stream_t stream) {
+  return conv_dgrad(dy, w, mask, dx, g, accumulate, precision, workspace, workspace_bytes, status,
+                    TTRL_STREAM(stream));
+}
+
+size_t ttrl_conv_dgrad_workspace_bytes(const ttrl_conv_geom* g) {
+  return g ? conv_dgrad_ws(g) : 0;
+}
+
+int ttrl_conv_wgrad(const float* x, const float* dy, float* dw, float* db,
+                    const ttrl_conv_geom* g, float alpha, int accumulate, int accumulate_db,
+                    int precision, float* workspace, size_t workspace_bytes, int* status,
+                    ttrl_stream_t stream) {
+  return conv_wgrad(x, dy, dw, db, g, alpha, accumulate, accumulate_db, precision, workspace,
+                    workspace_bytes, status, TTRL_STREAM(stream));
+}
+
+size_t ttrl_conv_wgrad_workspace_bytes(const ttrl_conv_geom* g) {
+  return g ? conv_wgrad_ws(g) : 0;
+}
+
+int ttrl_u8_nchw_to_f32_nhwc(const uint8_t* in, const int32_t* index, float* out, int n, int c,
+                             int h, int w, float scale, ttrl_stream_t stream) {
+  return u8_to_f32(in, index, out, n, c, h, w, scale, TTRL_STREAM(stream));
+}
+
+int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
+                   const float* grad_scale, double lr, double b1, double b2, double eps,
+                   double weight_decay, ttrl_stream_t stream) {
+  return adam_step(tensors, count, steps, ticket, grad_scale, lr, b1, b2, eps, weight_decay,
+                   TTRL_STREAM(stream));
+}
+
+int ttrl_grad_sqnorm(const float* const* grads, const int64_t* numels, int count, float* out,
+                     float max_norm, void* workspace, size_t workspace_bytes,
+                     ttrl_stream_t stream) {
+  return grad_sqnorm(grads, numels, count, out, max_norm, workspace, workspace_bytes,
+                     TTRL_STREAM(stream));
+}
+
+size_t ttrl_grad_sqnorm_workspace_bytes(const int64_t* numels, int count) {
+  return numels ? sqnorm_ws_bytes(numels, count) : 0;
+}
+
+}  // extern "C"

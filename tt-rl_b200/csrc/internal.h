@@ -1,0 +1,68 @@
+// Host/device structures shared between the kernels and the C-ABI layer.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/ttrl_b200.h"
+
+namespace ttrl {
+
+// Operand gather modes (chosen on the host from strides and alignment).
+enum : int32_t {
+  kModeKVec = 0,     // 16-byte chunks along k; K-major shared tile
+  kModeMNVec = 1,    // 16-byte chunks along rows; MN-major shared tile
+  kModeScalarK = 2,  // 4-byte gathers, k fastest across threads; K-major tile
+  kModeScalarR = 3   // 4-byte gathers, rows fastest across threads; K-major tile
+};
+
+struct DevOperand {
+  const float* ptr;
+  int32_t kind;
+  int32_t mode;
+  int32_t rows, kdim;
+  int64_t rs, ks;
+  int32_t n, h, w, c, kh, kw, stride, pad, oh, ow;
+  int32_t ones_row;  // row `rows` reads as 1.0 for every valid k
+  int32_t pad0;
+};
+
+// Where the synthetic ones row of operand A lands (the bias gradient).
+struct EpiExtra {
+  int32_t row2;  // tile row holding the column sums, or -1
+  int32_t accumulate2;
+  float* out2;   // out2[c * cs2]
+  int64_t cs2;
+};
+
+struct GemmArgs {
+  DevOperand a, b;
+  ttrl_epilogue ep;
+  EpiExtra ex;
+  int32_t m, n, k;
+  int32_t kblocks;
+  int32_t kb_per_split;
+  int32_t pad0;
+  float* ws;
+  int* status;
+};
+
+int set_error(int code, const char* fmt, ...);
+int set_cuda_error(const char* what, cudaError_t e);
+
+int gemm_init_device();
+size_t gemm_workspace_bytes(const ttrl_gemm_desc& d);
+int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, float* ws,
+             size_t ws_bytes, int* status, cudaStream_t stream);
+
+inline EpiExtra no_extra() {
+  EpiExtra e;
+  e.row2 = -1;
+  e.accumulate2 = 0;
+  e.out2 = nullptr;
+  e.cs2 = 0;
+  return e;
+}
+
+}  // namespace ttrl

@@ -1,0 +1,326 @@
+// Linear and Conv2d forward/backward expressed as tcgen05 GEMMs with fused
+// epilogues, plus the two non-GEMM pieces they need: the col2im gather
+// that finishes the convolution input gradient, and the uint8 frame
+// normalisation that feeds the first convolution.
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace ttrl {
+
+static ttrl_operand dense(const float* p, int rows, int kdim, long long rs, long long ks) {
+  ttrl_operand o;
+  std::memset(&o, 0, sizeof(o));
+  o.ptr = p;
+  o.kind = TTRL_OPND_DENSE;
+  o.rows = rows;
+  o.kdim = kdim;
+  o.rs = rs;
+  o.ks = ks;
+  return o;
+}
+
+static ttrl_operand conv_operand(const float* p, int kind, const ttrl_conv_geom& g) {
+  ttrl_operand o;
+  std::memset(&o, 0, sizeof(o));
+  o.ptr = p;
+  o.kind = kind;
+  const int m = g.n * g.oh * g.ow;
+  const int kk = g.kh * g.kw * g.c;
+  o.rows = kind == TTRL_OPND_CONV_FPROP ? m : kk;
+  o.kdim = kind == TTRL_OPND_CONV_FPROP ? kk : m;
+  o.n = g.n;
+  o.h = g.h;
+  o.w = g.w;
+  o.c = g.c;
+  o.kh = g.kh;
+  o.kw = g.kw;
+  o.stride = g.stride;
+  o.pad = g.pad;
+  o.oh = g.oh;
+  o.ow = g.ow;
+  return o;
+}
+
+static ttrl_epilogue epi(float* out, long long ors, long long ocs) {
+  ttrl_epilogue e;
+  std::memset(&e, 0, sizeof(e));
+  e.out = out;
+  e.ors = ors;
+  e.ocs = ocs;
+  e.alpha = 1.f;
+  return e;
+}
+
+static ttrl_gemm_desc make_desc(int m, int n, int k, int precision) {
+  ttrl_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.m = m;
+  d.n = n;
+  d.k = k;
+  d.precision = precision;
+  return d;
+}
+
+static int check_conv(const ttrl_conv_geom* g) {
+  if (g == nullptr) return set_error(TTRL_EINVAL, "conv: null geometry");
+  if (g->n <= 0 || g->h <= 0 || g->w <= 0 || g->c <= 0 || g->cout <= 0 || g->kh <= 0 ||
+      g->kw <= 0 || g->stride <= 0 || g->pad < 0)
+    return set_error(TTRL_EINVAL, "conv: non-positive extent in geometry");
+  const int sh = g->h + 2 * g->pad - g->kh, sw = g->w + 2 * g->pad - g->kw;
+  if (sh < 0 || sw < 0 || sh % g->stride || sw % g->stride)
+    return set_error(TTRL_EINVAL,
+                     "conv: ragged or empty geometry (h=%d w=%d k=%dx%d s=%d p=%d); the input "
+                     "gradient is only the exact adjoint for exactly divisible strides",
+                     g->h, g->w, g->kh, g->kw, g->stride, g->pad);
+  if (g->oh != sh / g->stride + 1 || g->ow != sw / g->stride + 1)
+    return set_error(TTRL_EINVAL, "conv: oh/ow (%d,%d) disagree with the geometry (%d,%d)", g->oh,
+                     g->ow, sh / g->stride + 1, sw / g->stride + 1);
+  return TTRL_OK;
+}
+
+// ---------------------------------------------------------------- Linear
+
+int linear_fwd(const float* x, const float* w, const float* b, float* y, int m, int k, int n,
+               int relu, int precision, float* ws, size_t wsb, int* status, cudaStream_t st) {
+  if (m <= 0 || n <= 0 || k <= 0) return set_error(TTRL_EINVAL, "linear_fwd: bad extents");
+  ttrl_gemm_desc d;
+  if (m < 128 && n > m) {
+    // Rows of the tile are output features, columns are batch rows.
+    d = make_desc(n, m, k, precision);
+    d.a = dense(w, n, k, 1, n);
+    d.b = dense(x, m, k, k, 1);
+    d.ep = epi(y, 1, n);
+    if (b) {
+      d.ep.bias = b;
+      d.ep.bias_mode = TTRL_BIAS_ROW;
+    }
+  } else {
+    d = make_desc(m, n, k, precision);
+    d.a = dense(x, m, k, k, 1);
+    d.b = dense(w, n, k, 1, n);
+    d.ep = epi(y, n, 1);
+    if (b) {
+      d.ep.bias = b;
+      d.ep.bias_mode = TTRL_BIAS_COL;
+    }
+  }
+  d.ep.relu = relu;
+  return gemm_run(d, 0, no_extra(), ws, wsb, status, st);
+}
+
+int linear_dgrad(const float* g, const float* w, const float* mask, float* dx, int m, int k,
+                 int n, int accumulate, int precision, float* ws, size_t wsb, int* status,
+                 cudaStream_t st) {
+  if (m <= 0 || n <= 0 || k <= 0) return set_error(TTRL_EINVAL, "linear_dgrad: bad extents");
+  ttrl_gemm_desc d;
+  if (m < 128 && k > m) {
+    d = make_desc(k, m, n, precision);
+    d.a = dense(w, k, n, n, 1);
+    d.b = dense(g, m, n, n, 1);
+    d.ep = epi(dx, 1, k);
+    if (mask) {
+      d.ep.mask = mask;
+      d.ep.mrs = 1;
+      d.ep.mcs = k;
+    }
+  } else {
+    d = make_desc(m, k, n, precision);
+    d.a = dense(g, m, n, n, 1);
+    d.b = dense(w, k, n, n, 1);
+    d.ep = epi(dx, k, 1);
+    if (mask) {
+      d.ep.mask = mask;
+      d.ep.mrs = k;
+      d.ep.mcs = 1;
+    }
+  }
+  d.ep.accumulate = accumulate;
+  return gemm_run(d, 0, no_extra(), ws, wsb, status, st);
+}
+
+int linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, int k, int n,
+                 int accumulate, int accumulate_db, int precision, float* ws, size_t wsb,
+                 int* status, cudaStream_t st) {
+  if (m <= 0 || n <= 0 || k <= 0) return set_error(TTRL_EINVAL, "linear_wgrad: bad extents");
+  ttrl_gemm_desc d = make_desc(k + (db ? 1 : 0), n, m, precision);
+  d.a = dense(x, k, m, 1, k);
+  d.b = dense(g, n, m, 1, n);
+  d.ep = epi(dw, n, 1);
+  d.ep.accumulate = accumulate;
+  EpiExtra ex = no_extra();
+  if (db) {
+    ex.row2 = k;
+    ex.out2 = db;
+    ex.cs2 = 1;
+    ex.accumulate2 = accumulate_db;
+  }
+  return gemm_run(d, db ? 1 : 0, ex, ws, wsb, status, st);
+}
+
+// ------------------------------------------------------------------ Conv
+
+int conv_fprop(const float* x, const float* w, const float* b, float* y, const ttrl_conv_geom* g,
+               float alpha, int relu, int precision, float* ws, size_t wsb, int* status,
+               cudaStream_t st) {
+  int rc = check_conv(g);
+  if (rc) return rc;
+  const int m = g->n * g->oh * g->ow;
+  const int kk = g->kh * g->kw * g->c;
+  ttrl_gemm_desc d = make_desc(m, g->cout, kk, precision);
+  d.a = conv_operand(x, TTRL_OPND_CONV_FPROP, *g);
+  d.b = dense(w, g->cout, kk, kk, 1);
+  d.ep = epi(y, g->cout, 1);
+  d.ep.alpha = alpha;
+  if (b) {
+    d.ep.bias = b;
+    d.ep.bias_mode = TTRL_BIAS_COL;
+  }
+  d.ep.relu = relu;
+  return gemm_run(d, 0, no_extra(), ws, wsb, status, st);
+}
+
+// dx[n,iy,ix,c] = sum over the kernel taps that saw (iy,ix) of dxcol, in a
+// fixed (ky, kx) order, then the relu mask of the layer below.
+__global__ void col2im_kernel(const float* __restrict__ dxcol, const float* __restrict__ mask,
+                              float* __restrict__ dx, ttrl_conv_geom g, int accumulate) {
+  const long long total = static_cast<long long>(g.n) * g.h * g.w * g.c;
+  const int kk = g.kh * g.kw * g.c;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % g.c);
+    long long t = idx / g.c;
+    const int ix = static_cast<int>(t % g.w);
+    t /= g.w;
+    const int iy = static_cast<int>(t % g.h);
+    const int img = static_cast<int>(t / g.h);
+    float s = 0.f;
+    for (int ky = 0; ky < g.kh; ++ky) {
+      const int ty = iy + g.pad - ky;
+      if (ty < 0 || ty % g.stride) continue;
+      const int oy = ty / g.stride;
+      if (oy >= g.oh) continue;
+      for (int kx = 0; kx < g.kw; ++kx) {
+        const int tx = ix + g.pad - kx;
+        if (tx < 0 || tx % g.stride) continue;
+        const int ox = tx / g.stride;
+        if (ox >= g.ow) continue;
+        const long long row = (static_cast<long long>(img) * g.oh + oy) * g.ow + ox;
+        s += dxcol[row * kk + (ky * g.kw + kx) * g.c + c];
+      }
+    }
+    if (mask != nullptr && !(mask[idx] > 0.f)) s = 0.f;
+    if (accumulate) s += dx[idx];
+    dx[idx] = s;
+  }
+}
+
+size_t conv_dgrad_ws(const ttrl_conv_geom* g) {
+  const size_t m = static_cast<size_t>(g->n) * g->oh * g->ow;
+  const size_t kk = static_cast<size_t>(g->kh) * g->kw * g->c;
+  ttrl_gemm_desc d = make_desc(static_cast<int>(m), static_cast<int>(kk), g->cout,
+                               TTRL_PREC_TF32X3);
+  return m * kk * sizeof(float) + gemm_workspace_bytes(d);
+}
+
+int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
+               const ttrl_conv_geom* g, int accumulate, int precision, float* ws, size_t wsb,
+               int* status, cudaStream_t st) {
+  int rc = check_conv(g);
+  if (rc) return rc;
+  const int m = g->n * g->oh * g->ow;
+  const int kk = g->kh * g->kw * g->c;
+  const size_t col_bytes = static_cast<size_t>(m) * kk * sizeof(float);
+  if (ws == nullptr || wsb < col_bytes)
+    return set_error(TTRL_EWORKSPACE, "conv_dgrad: needs %zu bytes of workspace, got %zu",
+                     conv_dgrad_ws(g), wsb);
+  float* dxcol = ws;
+  ttrl_gemm_desc d = make_desc(m, kk, g->cout, precision);
+  d.a = dense(dy, m, g->cout, g->cout, 1);
+  d.b = dense(w, kk, g->cout, 1, kk);
+  d.ep = epi(dxcol, kk, 1);
+  // The GEMM's own split-K workspace sits after the column buffer (16-byte
+  // aligned since col_bytes is a multiple of 16 for kk % 4 == 0).
+  const size_t off = (col_bytes + 255) & ~static_cast<size_t>(255);
+  float* ws2 = wsb > off ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + off) : nullptr;
+  rc = gemm_run(d, 0, no_extra(), ws2, wsb > off ? wsb - off : 0, status, st);
+  if (rc) return rc;
+  const long long total = static_cast<long long>(g->n) * g->h * g->w * g->c;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  col2im_kernel<<<blocks, 256, 0, st>>>(dxcol, mask, dx, *g, accumulate);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("col2im launch", e);
+}
+
+size_t conv_wgrad_ws(const ttrl_conv_geom* g) {
+  const int m = g->n * g->oh * g->ow;
+  const int kk = g->kh * g->kw * g->c;
+  ttrl_gemm_desc d = make_desc(kk + 1, g->cout, m, TTRL_PREC_TF32X3);
+  return gemm_workspace_bytes(d);
+}
+
+int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl_conv_geom* g,
+               float alpha, int accumulate, int accumulate_db, int precision, float* ws,
+               size_t wsb, int* status, cudaStream_t st) {
+  int rc = check_conv(g);
+  if (rc) return rc;
+  const int m = g->n * g->oh * g->ow;
+  const int kk = g->kh * g->kw * g->c;
+  ttrl_gemm_desc d = make_desc(kk + (db ? 1 : 0), g->cout, m, precision);
+  d.a = conv_operand(x, TTRL_OPND_CONV_WGRAD, *g);
+  d.b = dense(dy, g->cout, m, 1, g->cout);
+  d.ep = epi(dw, 1, kk);
+  d.ep.alpha = alpha;
+  d.ep.accumulate = accumulate;
+  EpiExtra ex = no_extra();
+  if (db) {
+    ex.row2 = kk;
+    ex.out2 = db;
+    ex.cs2 = 1;
+    ex.accumulate2 = accumulate_db;
+  }
+  return gemm_run(d, db ? 1 : 0, ex, ws, wsb, status, st);
+}
+
+// ------------------------------------------------------- frame conversion
+
+__global__ void u8_nchw_to_f32_nhwc_kernel(const uint8_t* __restrict__ in,
+                                           const int32_t* __restrict__ index,
+                                           float* __restrict__ out, int n, int c, int h, int w,
+                                           float scale) {
+  const long long pixels = static_cast<long long>(n) * h * w;
+  const int hw = h * w;
+  for (long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; p < pixels;
+       p += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int img = static_cast<int>(p / hw);
+    const int pix = static_cast<int>(p - static_cast<long long>(img) * hw);
+    const int src = index ? index[img] : img;
+    const uint8_t* base = in + static_cast<long long>(src) * c * hw + pix;
+    float* o = out + p * c;
+    if (c == 4) {
+      float4 v = make_float4(base[0] * scale, base[hw] * scale, base[2 * hw] * scale,
+                             base[3 * hw] * scale);
+      *reinterpret_cast<float4*>(o) = v;
+    } else {
+      for (int ch = 0; ch < c; ++ch) o[ch] = base[static_cast<long long>(ch) * hw] * scale;
+    }
+  }
+}
+
+int u8_to_f32(const uint8_t* in, const int32_t* index, float* out, int n, int c, int h, int w,
+              float scale, cudaStream_t st) {
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return set_error(TTRL_EINVAL, "u8_to_f32: bad extents");
+  if (in == nullptr || out == nullptr) return set_error(TTRL_EINVAL, "u8_to_f32: null pointer");
+  if (c == 4 && (reinterpret_cast<uintptr_t>(out) & 15u))
+    return set_error(TTRL_EINVAL, "u8_to_f32: output must be 16-byte aligned");
+  const long long pixels = static_cast<long long>(n) * h * w;
+  int blocks = static_cast<int>((pixels + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  u8_nchw_to_f32_nhwc_kernel<<<blocks, 256, 0, st>>>(in, index, out, n, c, h, w, scale);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("u8_to_f32 launch", e);
+}
+
+}  // namespace ttrl

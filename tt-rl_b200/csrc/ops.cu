@@ -1,0 +1,263 @@
+// Elementwise, reduction and strided-copy kernels behind the generic tape
+// ops (ttrl/engine/ops/{elementwise,unary,select,reduce,shape}.py). Each op
+// is one launch; reductions are sequential per output element (or a fixed
+// tree inside one block), so results are deterministic.
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace ttrl {
+
+struct EwArgs {
+  int op;
+  int ndim;
+  float scalar;
+  int pad0;
+  const float* a;
+  const float* b;
+  float* out;
+  int64_t n;
+  int64_t shape[4];
+  int64_t as[4];
+  int64_t bs[4];
+};
+
+__device__ __forceinline__ float ew_apply(int op, float x, float y, float s) {
+  switch (op) {
+    case TTRL_EW_ADD: return x + y;
+    case TTRL_EW_SUB: return x - y;
+    case TTRL_EW_MUL: return x * y;
+    case TTRL_EW_DIV: return x / y;
+    case TTRL_EW_ADD_S: return x + s;
+    case TTRL_EW_SUB_S: return x - s;
+    case TTRL_EW_RSUB_S: return s - x;
+    case TTRL_EW_MUL_S: return x * s;
+    case TTRL_EW_DIV_S: return x / s;
+    case TTRL_EW_RELU: return x > 0.f ? x : 0.f;
+    case TTRL_EW_RELU_BW: return y > 0.f ? x : 0.f;  // x = grad, y = forward input
+    case TTRL_EW_ABS: return fabsf(x);
+    case TTRL_EW_SIGN: return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
+    case TTRL_EW_NEG: return -x;
+    case TTRL_EW_EXP: return expf(x);
+    case TTRL_EW_LOG: return logf(x);
+    case TTRL_EW_TANH: return tanhf(x);
+    case TTRL_EW_SIGMOID: return 1.f / (1.f + expf(-x));
+    case TTRL_EW_SQRT: return sqrtf(x);
+    case TTRL_EW_SQUARE: return x * x;
+    case TTRL_EW_EQZ: return x == 0.f ? 1.f : 0.f;
+    case TTRL_EW_FILL: return s;
+    case TTRL_EW_COPY: return x;
+    case TTRL_EW_GT_S: return x > s ? 1.f : 0.f;
+    default: return 0.f;
+  }
+}
+
+__global__ void ew_kernel(const __grid_constant__ EwArgs a) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < a.n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t rem = i, ao = 0, bo = 0;
+#pragma unroll
+    for (int d = 3; d >= 0; --d) {
+      if (d < a.ndim) {
+        const int64_t idx = rem % a.shape[d];
+        rem /= a.shape[d];
+        ao += idx * a.as[d];
+        bo += idx * a.bs[d];
+      }
+    }
+    const float x = a.a ? a.a[ao] : 0.f;
+    const float y = a.b ? a.b[bo] : 0.f;
+    a.out[i] = ew_apply(a.op, x, y, a.scalar);
+  }
+}
+
+int ew(int op, const float* x, const int64_t* xs, const float* y, const int64_t* ys, float* out,
+       const int64_t* shape, int ndim, float scalar, cudaStream_t st) {
+  if (ndim < 1 || ndim > 4) return set_error(TTRL_EINVAL, "ew: rank %d outside [1, 4]", ndim);
+  if (out == nullptr) return set_error(TTRL_EINVAL, "ew: null output");
+  EwArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.op = op;
+  a.ndim = ndim;
+  a.scalar = scalar;
+  a.a = x;
+  a.b = y;
+  a.out = out;
+  int64_t n = 1;
+  for (int d = 0; d < ndim; ++d) {
+    if (shape[d] < 0) return set_error(TTRL_EINVAL, "ew: negative extent");
+    a.shape[d] = shape[d];
+    a.as[d] = xs ? xs[d] : 0;
+    a.bs[d] = ys ? ys[d] : 0;
+    n *= shape[d];
+  }
+  a.n = n;
+  if (n == 0) return TTRL_OK;
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  ew_kernel<<<blocks, 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("ew launch", e);
+}
+
+// ------------------------------------------------------------ reductions
+
+// in viewed as [outer][n][inner]; out [outer][inner].
+__global__ void reduce_thread_kernel(int op, const float* __restrict__ in, float* __restrict__ out,
+                                     int64_t outer, int64_t n, int64_t inner) {
+  const int64_t total = outer * inner;
+  for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < total;
+       o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i0 = o / inner, j = o - i0 * inner;
+    const float* p = in + i0 * n * inner + j;
+    if (op == TTRL_RED_SUM) {
+      float s = 0.f;
+      for (int64_t k = 0; k < n; ++k) s += p[k * inner];
+      out[o] = s;
+    } else {
+      float best = p[0];
+      int64_t arg = 0;
+      for (int64_t k = 1; k < n; ++k) {
+        const float v = p[k * inner];
+        if (v > best) {
+          best = v;
+          arg = k;
+        }
+      }
+      out[o] = op == TTRL_RED_MAX ? best : static_cast<float>(arg);
+    }
+  }
+}
+
+// One block per output element, fixed-shape tree: for long reductions.
+__global__ void reduce_block_kernel(int op, const float* __restrict__ in, float* __restrict__ out,
+                                    int64_t n, int64_t inner) {
+  __shared__ float vals[256];
+  __shared__ int64_t args[256];
+  const int64_t o = blockIdx.x;
+  const int64_t i0 = o / inner, j = o - i0 * inner;
+  const float* p = in + i0 * n * inner + j;
+  float acc = op == TTRL_RED_SUM ? 0.f : -INFINITY;
+  int64_t arg = n;  // argmax: smallest index among maxima
+  for (int64_t k = threadIdx.x; k < n; k += blockDim.x) {
+    const float v = p[k * inner];
+    if (op == TTRL_RED_SUM) {
+      acc += v;
+    } else if (v > acc || arg == n) {
+      if (!(v <= acc) || arg == n) {
+        acc = v;
+        arg = k;
+      }
+    }
+  }
+  vals[threadIdx.x] = acc;
+  args[threadIdx.x] = arg;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      const float a = vals[threadIdx.x], b = vals[threadIdx.x + w];
+      if (op == TTRL_RED_SUM) {
+        vals[threadIdx.x] = a + b;
+      } else {
+        const int64_t ia = args[threadIdx.x], ib = args[threadIdx.x + w];
+        const bool take_b = (ib != n) && (ia == n || b > a || (b == a && ib < ia));
+        if (take_b) {
+          vals[threadIdx.x] = b;
+          args[threadIdx.x] = ib;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0)
+    out[o] = op == TTRL_RED_ARGMAX ? static_cast<float>(args[0]) : vals[0];
+}
+
+int reduce(int op, const float* in, float* out, int64_t outer, int64_t n, int64_t inner,
+           cudaStream_t st) {
+  if (in == nullptr || out == nullptr) return set_error(TTRL_EINVAL, "reduce: null pointer");
+  if (outer <= 0 || n <= 0 || inner <= 0) return set_error(TTRL_EINVAL, "reduce: empty extent");
+  const int64_t total = outer * inner;
+  if (total < 512 && n >= 1024) {
+    reduce_block_kernel<<<static_cast<unsigned>(total), 256, 0, st>>>(op, in, out, n, inner);
+  } else {
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    reduce_thread_kernel<<<blocks, 256, 0, st>>>(op, in, out, outer, n, inner);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("reduce launch", e);
+}
+
+// ---------------------------------------------------------- strided copy
+
+__global__ void copy_strided_kernel(const __grid_constant__ EwArgs a) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < a.n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t rem = i, so = 0, dof = 0;
+#pragma unroll
+    for (int d = 3; d >= 0; --d) {
+      if (d < a.ndim) {
+        const int64_t idx = rem % a.shape[d];
+        rem /= a.shape[d];
+        so += idx * a.as[d];
+        dof += idx * a.bs[d];
+      }
+    }
+    float v = a.a[so];
+    if (a.op) v += a.out[dof];
+    a.out[dof] = v;
+  }
+}
+
+int copy_strided(float* dst, const int64_t* ds, const float* src, const int64_t* ss,
+                 const int64_t* shape, int ndim, int accumulate, cudaStream_t st) {
+  if (ndim < 1 || ndim > 4) return set_error(TTRL_EINVAL, "copy: rank %d outside [1, 4]", ndim);
+  if (dst == nullptr || src == nullptr) return set_error(TTRL_EINVAL, "copy: null pointer");
+  EwArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.op = accumulate;
+  a.ndim = ndim;
+  a.a = src;
+  a.out = dst;
+  int64_t n = 1;
+  for (int d = 0; d < ndim; ++d) {
+    a.shape[d] = shape[d];
+    a.as[d] = ss[d];
+    a.bs[d] = ds[d];
+    n *= shape[d];
+  }
+  a.n = n;
+  if (n == 0) return TTRL_OK;
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  copy_strided_kernel<<<blocks, 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("copy launch", e);
+}
+
+// ------------------------------------------------------ Polyak / average
+
+__global__ void axpby_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n,
+                             float keep, float take) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    // Order of ttrl/algos/sac/targets.py:55-61: add(mul(dst, 1-tau), mul(src, tau)).
+    const float a = dst[i] * keep;
+    const float b = src[i] * take;
+    dst[i] = a + b;
+  }
+}
+
+int polyak(float* dst, const float* src, int64_t n, float tau, cudaStream_t st) {
+  if (n <= 0) return TTRL_OK;
+  if (dst == nullptr || src == nullptr) return set_error(TTRL_EINVAL, "polyak: null pointer");
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  axpby_kernel<<<blocks, 256, 0, st>>>(dst, src, n, 1.0f - tau, tau);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("polyak launch", e);
+}
+
+}  // namespace ttrl

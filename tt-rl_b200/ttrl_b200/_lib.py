@@ -1,0 +1,146 @@
+"""ctypes binding of ``libttrl_b200.so``, the C ABI declared in
+``include/ttrl_b200.h``.
+
+This is the binding a maintainer of the reference would add: the reference
+is pure Python over ``ttnn``, so its natural FFI for a native backend is
+ctypes over plain pointers. Loading fails loudly when the library is missing;
+there is no CPU fallback anywhere in this package.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+__all__ = [
+    "LIB_PATH", "TtrlError", "lib", "Operand", "Epilogue", "GemmDesc", "ConvGeom",
+    "AdamTensor", "PREC_TF32X3", "PREC_TF32", "OPND_DENSE", "OPND_CONV_FPROP",
+    "OPND_CONV_WGRAD", "BIAS_NONE", "BIAS_ROW", "BIAS_COL", "EXPORTED_SYMBOLS",
+]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libttrl_b200.so")
+
+PREC_TF32X3 = 0
+PREC_TF32 = 1
+OPND_DENSE = 0
+OPND_CONV_FPROP = 1
+OPND_CONV_WGRAD = 2
+BIAS_NONE = 0
+BIAS_ROW = 1
+BIAS_COL = 2
+
+_c_int = ctypes.c_int
+_c_float = ctypes.c_float
+_c_double = ctypes.c_double
+_c_size = ctypes.c_size_t
+_vp = ctypes.c_void_p
+
+
+class TtrlError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, code: int, what: str, message: str):
+        super().__init__(f"{what} failed with code {code}: {message}")
+        self.code = code
+
+
+class Operand(ctypes.Structure):
+    _fields_ = [
+        ("ptr", _vp), ("kind", ctypes.c_int32), ("rows", ctypes.c_int32),
+        ("kdim", ctypes.c_int32), ("pad0", ctypes.c_int32),
+        ("rs", ctypes.c_int64), ("ks", ctypes.c_int64),
+        ("n", ctypes.c_int32), ("h", ctypes.c_int32), ("w", ctypes.c_int32),
+        ("c", ctypes.c_int32), ("kh", ctypes.c_int32), ("kw", ctypes.c_int32),
+        ("stride", ctypes.c_int32), ("pad", ctypes.c_int32),
+        ("oh", ctypes.c_int32), ("ow", ctypes.c_int32),
+    ]
+
+
+class Epilogue(ctypes.Structure):
+    _fields_ = [
+        ("out", _vp), ("ors", ctypes.c_int64), ("ocs", ctypes.c_int64),
+        ("alpha", _c_float), ("bias_mode", ctypes.c_int32), ("bias", _vp),
+        ("mask", _vp), ("mrs", ctypes.c_int64), ("mcs", ctypes.c_int64),
+        ("relu", ctypes.c_int32), ("accumulate", ctypes.c_int32),
+    ]
+
+
+class GemmDesc(ctypes.Structure):
+    _fields_ = [
+        ("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+        ("precision", ctypes.c_int32), ("splits", ctypes.c_int32), ("pad0", ctypes.c_int32),
+        ("a", Operand), ("b", Operand), ("ep", Epilogue),
+    ]
+
+
+class ConvGeom(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in
+                ("n", "h", "w", "c", "cout", "kh", "kw", "stride", "pad", "oh", "ow")]
+
+
+class AdamTensor(ctypes.Structure):
+    _fields_ = [
+        ("param", _vp), ("grad", _vp), ("s", _vp), ("v", _vp),
+        ("numel", ctypes.c_int64), ("step_index", ctypes.c_int32), ("pad0", ctypes.c_int32),
+    ]
+
+
+# name -> (restype, argtypes). Every symbol include/ttrl_b200.h declares.
+_SIGNATURES = {
+    "ttrl_last_error": (ctypes.c_char_p, []),
+    "ttrl_version": (_c_int, []),
+    "ttrl_init": (_c_int, [_c_int]),
+    "ttrl_gemm_workspace_bytes": (_c_size, [ctypes.POINTER(GemmDesc)]),
+    "ttrl_gemm": (_c_int, [ctypes.POINTER(GemmDesc), _vp, _c_size, _vp, _vp]),
+    "ttrl_linear_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                 _vp, _c_size, _vp, _vp]),
+    "ttrl_linear_dgrad": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                   _vp, _c_size, _vp, _vp]),
+    "ttrl_linear_wgrad": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                   _c_int, _vp, _c_size, _vp, _vp]),
+    "ttrl_conv_fprop": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ConvGeom), _c_float, _c_int,
+                                 _c_int, _vp, _c_size, _vp, _vp]),
+    "ttrl_conv_dgrad": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ConvGeom), _c_int, _c_int,
+                                 _vp, _c_size, _vp, _vp]),
+    "ttrl_conv_dgrad_workspace_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),
+    "ttrl_conv_wgrad": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ConvGeom), _c_float, _c_int,
+                                 _c_int, _c_int, _vp, _c_size, _vp, _vp]),
+    "ttrl_conv_wgrad_workspace_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),
+    "ttrl_u8_nchw_to_f32_nhwc": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                          _c_float, _vp]),
+    "ttrl_adam_step": (_c_int, [ctypes.POINTER(AdamTensor), _c_int, _vp, _vp, _vp, _c_double,
+                                _c_double, _c_double, _c_double, _c_double, _vp]),
+    "ttrl_grad_sqnorm": (_c_int, [ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int64), _c_int,
+                                  _vp, _c_float, _vp, _c_size, _vp]),
+    "ttrl_grad_sqnorm_workspace_bytes": (_c_size, [ctypes.POINTER(ctypes.c_int64), _c_int]),
+}
+
+EXPORTED_SYMBOLS = tuple(sorted(_SIGNATURES))
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library, with every signature bound. Raises if absent."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: the sm_100a kernels have not been built. "
+                "Run `make -C tt-rl_b200/csrc` (or __graft_entry__.build()). There is "
+                "no CPU fallback."
+            )
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (restype, argtypes) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _LIB = handle
+    return _LIB
+
+
+def check(code: int, what: str) -> None:
+    """Raise TtrlError for a non-zero return code."""
+    if code != 0:
+        msg = lib().ttrl_last_error().decode(errors="replace")
+        raise TtrlError(code, what, msg)
