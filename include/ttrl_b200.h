@@ -220,11 +220,14 @@ typedef struct {
  * kernel leaves it zero). `grad_scale` (device float, may be NULL)
  * multiplies every gradient first (the clip factor of
  * ttrl/algos/grads.py:29-43); weight_decay adds wd*p to g next
- * (adam.py:110-113). Up to TTRL_ADAM_MAX_TENSORS tensors per call. */
+ * (adam.py:110-113). `lr_device` (device double, may be NULL) overrides
+ * `lr` at execution time, so a replayed graph follows a learning-rate
+ * schedule (ttrl/algos/ppo/learn.py:54-56). Up to TTRL_ADAM_MAX_TENSORS
+ * tensors per call. */
 #define TTRL_ADAM_MAX_TENSORS 64
 int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
-                   const float* grad_scale, double lr, double b1, double b2, double eps,
-                   double weight_decay, ttrl_stream_t stream);
+                   const float* grad_scale, const double* lr_device, double lr, double b1,
+                   double b2, double eps, double weight_decay, ttrl_stream_t stream);
 
 /* out[0] = sum over tensors of sum(g^2), accumulated in double and reduced
  * in a fixed order (ttrl/algos/grads.py:13-26 grad_norm's float64 sum,
@@ -238,6 +241,83 @@ int ttrl_grad_sqnorm(const float* const* grads, const int64_t* numels, int count
                      float max_norm, void* workspace, size_t workspace_bytes,
                      ttrl_stream_t stream);
 size_t ttrl_grad_sqnorm_workspace_bytes(const int64_t* numels, int count);
+
+/* ------------------------------------------------------- tape primitives */
+
+/* Elementwise op codes of ttrl_ew. Binary ops read a and b; *_S ops combine
+ * a with `scalar`; unary ops read a only. */
+enum {
+  TTRL_EW_ADD = 0, TTRL_EW_SUB = 1, TTRL_EW_MUL = 2, TTRL_EW_DIV = 3,
+  TTRL_EW_ADD_S = 4, TTRL_EW_SUB_S = 5, TTRL_EW_RSUB_S = 6, TTRL_EW_MUL_S = 7,
+  TTRL_EW_DIV_S = 8, TTRL_EW_RELU = 9, TTRL_EW_RELU_BW = 10, TTRL_EW_ABS = 11,
+  TTRL_EW_SIGN = 12, TTRL_EW_NEG = 13, TTRL_EW_EXP = 14, TTRL_EW_LOG = 15,
+  TTRL_EW_TANH = 16, TTRL_EW_SIGMOID = 17, TTRL_EW_SQRT = 18, TTRL_EW_SQUARE = 19,
+  TTRL_EW_EQZ = 20, TTRL_EW_FILL = 21, TTRL_EW_COPY = 22, TTRL_EW_GT_S = 23,
+  TTRL_EW_EQ = 24
+};
+
+/* out[i] = op(a[i], b[i], scalar) over a contiguous output of rank <= 4;
+ * a and b are read through their own element strides (0 = broadcast).
+ * One launch per tape op of ttrl/engine/ops/{elementwise,unary}.py
+ * (add/sub/mul/div, relu/relu_bw, abs, sign, exp, log, tanh, sigmoid,
+ * sqrt, square, eqz, full_like). */
+int ttrl_ew(int op, const float* a, const int64_t* a_strides, const float* b,
+            const int64_t* b_strides, float* out, const int64_t* shape, int ndim, float scalar,
+            ttrl_stream_t stream);
+
+enum { TTRL_RED_SUM = 0, TTRL_RED_MAX = 1, TTRL_RED_ARGMAX = 2 };
+
+/* Reduce the middle axis of in viewed as [outer][n][inner] into
+ * out[outer][inner] (argmax as an fp32 index, first maximum wins).
+ * Sequential or fixed-tree order: deterministic. Replaces ttnn.sum /
+ * ttnn.max / ttnn.argmax of ttrl/engine/ops/reduce.py:11-99. */
+int ttrl_reduce(int op, const float* in, float* out, int64_t outer, int64_t n, int64_t inner,
+                ttrl_stream_t stream);
+
+/* dst (=|+=) src over a rank <= 4 box, both read through element strides.
+ * Backs concat / split / slice (ttrl/engine/ops/shape.py). */
+int ttrl_copy_strided(float* dst, const int64_t* dst_strides, const float* src,
+                      const int64_t* src_strides, const int64_t* shape, int ndim, int accumulate,
+                      ttrl_stream_t stream);
+
+/* dst = (1 - tau) * dst + tau * src, elementwise, in that operation order
+ * (ttrl/algos/sac/targets.py:55-61, the Polyak blend). */
+int ttrl_polyak(float* dst, const float* src, int64_t n, float tau, ttrl_stream_t stream);
+
+/* dst[i][:] = src[idx[i]][:] for n rows of `row` 4-byte words (fp32 or
+ * int32 payloads): the minibatch gather of
+ * ttrl/buffers/rollout.py:271-282, done on the device. */
+int ttrl_gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row,
+                     ttrl_stream_t stream);
+
+/* ------------------------------------------------------------------ losses */
+
+/* One DQN update's loss head, fused: the online Q(s,a) gather, the
+ * (double-)DQN bootstrap target (argmax of `q_sel` with the optional
+ * action-mask penalty, value read from `q_tgt`, done mask, per-sample
+ * discount), the Huber loss (optionally importance-weighted), its mean,
+ * mean Q, optional |TD|, and dq = d loss / d q.
+ * ttrl/algos/dqn/losses.py:77-140 with ttrl/engine/ops/functional.py:56-69,
+ * ttrl/algos/mask.py:113-121. Vectors are [batch]; matrices [batch][actions]. */
+int ttrl_dqn_loss(const float* q, const float* q_sel, const float* q_tgt, const float* onehot,
+                  const float* rewards, const float* dones, const float* discounts,
+                  const float* next_mask, const float* is_weights, float* loss, float* mean_q,
+                  float* td_abs, float* dq, int batch, int actions, float delta, int accumulate,
+                  ttrl_stream_t stream);
+
+/* PPO's objective and its gradient, fused: log-softmax, new log-prob of the
+ * taken actions, clipped surrogate, clipped value loss (x0.5), entropy
+ * bonus, reduced by the mean (valid == NULL) or the masked mean over
+ * `valid`; metrics[4] = {loss, policy_loss, value_loss, entropy};
+ * dlogits = d loss / d logits, dvalue = d loss / d value.
+ * ttrl/algos/ppo/loss.py:27-83 with ttrl/algos/ppo/policy.py:64-76 and
+ * ttrl/engine/ops/functional.py:160-178. */
+int ttrl_ppo_loss(const float* logits, const float* value, const int32_t* actions,
+                  const float* old_logp, const float* adv, const float* returns,
+                  const float* old_values, const float* valid, float* metrics, float* new_logp,
+                  float* dlogits, float* dvalue, int batch, int actions_n, float clip_eps,
+                  float value_clip_eps, float value_coef, float entropy_coef,
+                  ttrl_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,119 @@
+"""PPO Nature-CNN learner (BASELINE configs[1] shapes, smaller rollout) on
+the B200 against the oracle: the graph-replayed rollout update reproduces a
+sequence of oracle minibatch steps (forward, PPO objective, backward,
+grad-norm clip 0.5, Adam) on the same permutations.
+
+Tolerances: gradients 1e-4 relative Frobenius; per-step metrics 1e-4
+relative; post-update parameters 1e-3 relative Frobenius (the spec's budget
+for TF32 GEMM paths: with eps = 1e-8 Adam moves every element by about
++-lr whatever its gradient's size, so elements whose gradient is near zero
+dominate this measure).
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import learner as ref  # noqa: E402
+from tests.helpers import nature_state_dict, nchw_to_nhwc, rel  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _rollout(rng, n):
+    obs = rng.integers(0, 256, (n, 4, 84, 84), dtype=np.uint8)
+    actions = rng.integers(0, 6, n)
+    adv = rng.standard_normal(n).astype(np.float32)
+    returns = rng.standard_normal(n).astype(np.float32)
+    return obs, actions, adv, returns
+
+
+@pytest.mark.parametrize("epochs", [1, 2])
+def test_ppo_rollout_update_matches_oracle(epochs):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from ttrl_b200.algos.ppo import PPOConfig, PPOLearner, initial_old_logp
+    from ttrl_b200.nets import build_actor_critic
+
+    rng = np.random.default_rng(11)
+    p = ref.nature_params(rng, heads=(("pi", 6), ("v", 1)))
+    net = build_actor_critic((4, 84, 84), 6, "cuda", batch=256)
+    net.load_state_dict(nature_state_dict(p, heads=("pi", "v")))
+    n = 512
+    obs, actions, adv, returns = _rollout(rng, n)
+    old_logp, values = initial_old_logp(net, obs, actions, "cuda")
+    cfg = PPOConfig(epochs=epochs, minibatch_size=256)
+    learner = PPOLearner(net, n, (4, 84, 84), "cuda", cfg=cfg, seed=7)
+    learner.load_rollout(obs, actions, old_logp, values, returns, adv)
+    learner.draw_permutations()
+    perms = learner.perm_host.numpy().copy()
+    learner.replay()
+    got = learner.read_metrics()
+    torch.cuda.synchronize()
+
+    # oracle: same minibatches, same order, float64
+    adv_n = (adv - adv.mean()) / (adv.std() + 1e-8)
+    params = {k: v.astype(np.float64) for k, v in p.items()}
+    state = {}
+    x_all = nchw_to_nhwc(obs).astype(np.float64)
+    losses = []
+    for t, idx in enumerate(perms, start=1):
+        m, _, params, state, _ = ref.ppo_minibatch_step(
+            params, state, t, x_all[idx], actions[idx], old_logp[idx].astype(np.float64),
+            adv_n[idx].astype(np.float64), returns[idx].astype(np.float64),
+            values[idx].astype(np.float64), lr=cfg.lr, eps=cfg.eps,
+            max_grad_norm=cfg.max_grad_norm)
+        losses.append(m["loss"])
+    assert rel(got["loss"], np.mean(losses)) <= 1e-4
+    sd = net.state_dict()
+    want = nature_state_dict(params, heads=("pi", "v"))
+    for name in sd:
+        assert rel(sd[name], want[name]) <= 1e-3, name
+    assert learner.optimizer.steps == [len(perms)] * len(learner.params)
+    learner.close()
+
+
+def test_ppo_minibatch_gradients_match_oracle():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from ttrl_b200.algos.ppo import PPOConfig, objective
+    from ttrl_b200.engine.autograd import Tensor
+    from ttrl_b200.nets import build_actor_critic
+    from tests.helpers import TOL_GRAD
+
+    rng = np.random.default_rng(21)
+    p = ref.nature_params(rng, heads=(("pi", 6), ("v", 1)))
+    net = build_actor_critic((4, 84, 84), 6, "cuda", batch=256)
+    net.load_state_dict(nature_state_dict(p, heads=("pi", "v")))
+    obs, actions, adv, returns = _rollout(rng, 256)
+    old_logp = (np.log(1 / 6) + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    values = rng.standard_normal(256).astype(np.float32)
+    x = nchw_to_nhwc(obs).astype(np.float32)
+    rows = Tensor(torch.from_numpy(x.reshape(1, 1, -1, 4)).cuda())
+    logits, value = net(rows)
+    batch = {"actions": torch.from_numpy(actions.astype(np.int32)).cuda(),
+             "old_logp": torch.from_numpy(old_logp).cuda(),
+             "advantages": torch.from_numpy(adv).cuda(),
+             "returns": torch.from_numpy(returns).cuda(),
+             "values": torch.from_numpy(values).cuda()}
+    loss, parts, new_logp = objective(logits, value, batch, PPOConfig())
+    loss.backward()
+    f64 = {k: v.astype(np.float64) for k, v in p.items()}
+    outs, cache = ref.nature_forward(f64, x.astype(np.float64), heads=("pi", "v"))
+    rl, rparts, rlogp, dl, dv = ref.ppo_objective_and_grads(
+        outs["pi"], outs["v"], actions, old_logp.astype(np.float64), adv.astype(np.float64),
+        returns.astype(np.float64), values.astype(np.float64))
+    from tests.helpers import device_gates
+    gates = device_gates(net, rows)
+    grads = ref.nature_backward(f64, cache, {"pi": dl, "v": dv}, gates=gates)
+    assert rel(loss.numpy(), rl) <= 1e-5
+    for k in ("policy_loss", "value_loss", "entropy"):
+        assert rel(parts[k].numpy(), rparts[k]) <= 1e-5, k
+    assert rel(new_logp.numpy().reshape(-1), rlogp) <= 1e-5
+    named = nature_state_dict(grads, heads=("pi", "v"))
+    for name, prm in net.named_parameters():
+        g = prm.grad.detach().cpu().numpy()
+        if name.endswith("weight") and g.ndim == 4:
+            g = g.transpose(0, 3, 1, 2)
+        assert rel(g.reshape(named[name].shape), named[name]) <= TOL_GRAD, name

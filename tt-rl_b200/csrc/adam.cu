@@ -24,6 +24,7 @@ struct AdamArgs {
   int32_t* steps;
   int32_t* ticket;
   const float* grad_scale;
+  const double* lr_device;
   double lr, b1, b2, eps, wd;
 };
 
@@ -40,7 +41,8 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
   const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
   const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
   const double c = sqrt((1.0 - a.b2) / bc2);
-  const float alpha_t = static_cast<float>(a.lr * (1.0 - a.b1) / bc1 / c);
+  const double lr = a.lr_device ? *a.lr_device : a.lr;
+  const float alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
   const float eps_t = static_cast<float>(a.eps / c);
   const float b1 = static_cast<float>(a.b1), b2 = static_cast<float>(a.b2);
   const float wd = static_cast<float>(a.wd);
@@ -86,8 +88,8 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
 }
 
 int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
-              const float* grad_scale, double lr, double b1, double b2, double eps, double wd,
-              cudaStream_t st) {
+              const float* grad_scale, const double* lr_device, double lr, double b1, double b2,
+              double eps, double wd, cudaStream_t st) {
   if (count <= 0) return TTRL_OK;
   if (count > TTRL_ADAM_MAX_TENSORS)
     return set_error(TTRL_EINVAL, "adam: %d tensors exceeds the per-call limit %d", count,
@@ -110,6 +112,7 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
   a.steps = steps;
   a.ticket = ticket;
   a.grad_scale = grad_scale;
+  a.lr_device = lr_device;
   a.lr = lr;
   a.b1 = b1;
   a.b2 = b2;

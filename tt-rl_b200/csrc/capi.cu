@@ -37,11 +37,20 @@ int conv_wgrad(const float*, const float*, float*, float*, const ttrl_conv_geom*
                int, float*, size_t, int*, cudaStream_t);
 size_t conv_wgrad_ws(const ttrl_conv_geom*);
 int u8_to_f32(const uint8_t*, const int32_t*, float*, int, int, int, int, float, cudaStream_t);
-int adam_step(const ttrl_adam_tensor*, int, int32_t*, int32_t*, const float*, double, double,
-              double, double, double, cudaStream_t);
+int adam_step(const ttrl_adam_tensor*, int, int32_t*, int32_t*, const float*, const double*,
+              double, double, double, double, double, cudaStream_t);
 int grad_sqnorm(const float* const*, const int64_t*, int, float*, float, void*, size_t,
                 cudaStream_t);
 size_t sqnorm_ws_bytes(const int64_t*, int);
+int ew(int, const float*, const int64_t*, const float*, const int64_t*, float*, const int64_t*,
+       int, float, cudaStream_t);
+int reduce(int, const float*, float*, int64_t, int64_t, int64_t, cudaStream_t);
+int copy_strided(float*, const int64_t*, const float*, const int64_t*, const int64_t*, int, int,
+                 cudaStream_t);
+int polyak(float*, const float*, int64_t, float, cudaStream_t);
+int gather_rows(const void*, const int32_t*, void*, int, int, cudaStream_t);
+
+
 
 }  // namespace ttrl
 
@@ -128,10 +137,10 @@ int ttrl_u8_nchw_to_f32_nhwc(const uint8_t* in, const int32_t* index, float* out
 }
 
 int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
-                   const float* grad_scale, double lr, double b1, double b2, double eps,
-                   double weight_decay, ttrl_stream_t stream) {
-  return adam_step(tensors, count, steps, ticket, grad_scale, lr, b1, b2, eps, weight_decay,
-                   TTRL_STREAM(stream));
+                   const float* grad_scale, const double* lr_device, double lr, double b1,
+                   double b2, double eps, double weight_decay, ttrl_stream_t stream) {
+  return adam_step(tensors, count, steps, ticket, grad_scale, lr_device, lr, b1, b2, eps,
+                   weight_decay, TTRL_STREAM(stream));
 }
 
 int ttrl_grad_sqnorm(const float* const* grads, const int64_t* numels, int count, float* out,
@@ -143,6 +152,55 @@ int ttrl_grad_sqnorm(const float* const* grads, const int64_t* numels, int count
 
 size_t ttrl_grad_sqnorm_workspace_bytes(const int64_t* numels, int count) {
   return numels ? sqnorm_ws_bytes(numels, count) : 0;
+}
+
+int ttrl_ew(int op, const float* a, const int64_t* a_strides, const float* b,
+            const int64_t* b_strides, float* out, const int64_t* shape, int ndim, float scalar,
+            ttrl_stream_t stream) {
+  return ew(op, a, a_strides, b, b_strides, out, shape, ndim, scalar, TTRL_STREAM(stream));
+}
+
+int ttrl_reduce(int op, const float* in, float* out, int64_t outer, int64_t n, int64_t inner,
+                ttrl_stream_t stream) {
+  return reduce(op, in, out, outer, n, inner, TTRL_STREAM(stream));
+}
+
+int ttrl_copy_strided(float* dst, const int64_t* dst_strides, const float* src,
+                      const int64_t* src_strides, const int64_t* shape, int ndim, int accumulate,
+                      ttrl_stream_t stream) {
+  return copy_strided(dst, dst_strides, src, src_strides, shape, ndim, accumulate,
+                      TTRL_STREAM(stream));
+}
+
+int ttrl_polyak(float* dst, const float* src, int64_t n, float tau, ttrl_stream_t stream) {
+  return polyak(dst, src, n, tau, TTRL_STREAM(stream));
+}
+
+int ttrl_gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row,
+                     ttrl_stream_t stream) {
+  return gather_rows(src, idx, dst, n, row, TTRL_STREAM(stream));
+}
+
+int ttrl_dqn_loss(const float* q, const float* q_sel, const float* q_tgt, const float* onehot,
+                  const float* rewards, const float* dones, const float* discounts,
+                  const float* next_mask, const float* is_weights, float* loss, float* mean_q,
+                  float* td_abs, float* dq, int batch, int actions, float delta, int accumulate,
+                  ttrl_stream_t stream) {
+  DqnArgs a{q, q_sel, q_tgt, onehot, rewards, dones, discounts, next_mask, is_weights,
+            loss, mean_q, td_abs, dq, batch, actions, delta, accumulate};
+  return dqn_loss(a, TTRL_STREAM(stream));
+}
+
+int ttrl_ppo_loss(const float* logits, const float* value, const int32_t* actions,
+                  const float* old_logp, const float* adv, const float* returns,
+                  const float* old_values, const float* valid, float* metrics, float* new_logp,
+                  float* dlogits, float* dvalue, int batch, int actions_n, float clip_eps,
+                  float value_clip_eps, float value_coef, float entropy_coef,
+                  ttrl_stream_t stream) {
+  PpoArgs a{logits, value, actions, old_logp, adv, returns, old_values, valid, metrics,
+            new_logp, dlogits, dvalue, batch, actions_n, clip_eps, value_clip_eps, value_coef,
+            entropy_coef};
+  return ppo_loss(a, TTRL_STREAM(stream));
 }
 
 }  // extern "C"

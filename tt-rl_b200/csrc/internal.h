@@ -56,6 +56,47 @@ size_t gemm_workspace_bytes(const ttrl_gemm_desc& d);
 int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, float* ws,
              size_t ws_bytes, int* status, cudaStream_t stream);
 
+// Fused DQN loss head (ttrl/algos/dqn/losses.py:77-140).
+struct DqnArgs {
+  const float* q;          // [B, A] online(s), requires grad
+  const float* q_sel;      // [B, A] selector: online(s') (double) or target(s')
+  const float* q_tgt;      // [B, A] target(s')
+  const float* onehot;     // [B, A] taken actions
+  const float* rewards;    // [B]
+  const float* dones;      // [B]
+  const float* discounts;  // [B]
+  const float* next_mask;  // [B, A] or null
+  const float* is_weights; // [B] or null
+  float* loss;             // [1]
+  float* mean_q;           // [1]
+  float* td_abs;           // [B] or null
+  float* dq;               // [B, A]
+  int batch, actions;
+  float delta;
+  int accumulate;          // dq += instead of =
+};
+
+// Fused PPO objective (ttrl/algos/ppo/loss.py:42-83).
+struct PpoArgs {
+  const float* logits;     // [B, A]
+  const float* value;      // [B]
+  const int32_t* actions;  // [B]
+  const float* old_logp;   // [B]
+  const float* adv;        // [B]
+  const float* returns;    // [B]
+  const float* old_values; // [B]
+  const float* valid;      // [B] or null: masked mean (recurrent path)
+  float* metrics;          // [4]: loss, policy_loss, value_loss, entropy
+  float* new_logp;         // [B] or null
+  float* dlogits;          // [B, A]
+  float* dvalue;           // [B]
+  int batch, num_actions;
+  float clip, vclip, vcoef, entcoef;
+};
+
+int dqn_loss(const DqnArgs& args, cudaStream_t st);
+int ppo_loss(const PpoArgs& args, cudaStream_t st);
+
 inline EpiExtra no_extra() {
   EpiExtra e;
   e.row2 = -1;

@@ -49,6 +49,7 @@ __device__ __forceinline__ float ew_apply(int op, float x, float y, float s) {
     case TTRL_EW_FILL: return s;
     case TTRL_EW_COPY: return x;
     case TTRL_EW_GT_S: return x > s ? 1.f : 0.f;
+    case TTRL_EW_EQ: return x == y ? 1.f : 0.f;
     default: return 0.f;
   }
 }

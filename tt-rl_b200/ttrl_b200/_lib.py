@@ -108,12 +108,32 @@ _SIGNATURES = {
     "ttrl_conv_wgrad_workspace_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),
     "ttrl_u8_nchw_to_f32_nhwc": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                           _c_float, _vp]),
-    "ttrl_adam_step": (_c_int, [ctypes.POINTER(AdamTensor), _c_int, _vp, _vp, _vp, _c_double,
-                                _c_double, _c_double, _c_double, _c_double, _vp]),
+    "ttrl_adam_step": (_c_int, [ctypes.POINTER(AdamTensor), _c_int, _vp, _vp, _vp, _vp,
+                                _c_double, _c_double, _c_double, _c_double, _c_double, _vp]),
     "ttrl_grad_sqnorm": (_c_int, [ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int64), _c_int,
                                   _vp, _c_float, _vp, _c_size, _vp]),
     "ttrl_grad_sqnorm_workspace_bytes": (_c_size, [ctypes.POINTER(ctypes.c_int64), _c_int]),
+    "ttrl_ew": (_c_int, [_c_int, _vp, ctypes.POINTER(ctypes.c_int64), _vp,
+                         ctypes.POINTER(ctypes.c_int64), _vp, ctypes.POINTER(ctypes.c_int64),
+                         _c_int, _c_float, _vp]),
+    "ttrl_reduce": (_c_int, [_c_int, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                             _vp]),
+    "ttrl_copy_strided": (_c_int, [_vp, ctypes.POINTER(ctypes.c_int64), _vp,
+                                   ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+                                   _c_int, _c_int, _vp]),
+    "ttrl_polyak": (_c_int, [_vp, _vp, ctypes.c_int64, _c_float, _vp]),
+    "ttrl_gather_rows": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),
+    "ttrl_dqn_loss": (_c_int, [_vp] * 13 + [_c_int, _c_int, _c_float, _c_int, _vp]),
+    "ttrl_ppo_loss": (_c_int, [_vp] * 12 + [_c_int, _c_int, _c_float, _c_float, _c_float,
+                                             _c_float, _vp]),
 }
+
+# Elementwise / reduction op codes (include/ttrl_b200.h).
+EW = {name: i for i, name in enumerate((
+    "add", "sub", "mul", "div", "add_s", "sub_s", "rsub_s", "mul_s", "div_s", "relu", "relu_bw",
+    "abs", "sign", "neg", "exp", "log", "tanh", "sigmoid", "sqrt", "square", "eqz", "fill",
+    "copy", "gt_s", "eq"))}
+RED_SUM, RED_MAX, RED_ARGMAX = 0, 1, 2
 
 EXPORTED_SYMBOLS = tuple(sorted(_SIGNATURES))
 

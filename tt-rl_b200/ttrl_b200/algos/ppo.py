@@ -1,0 +1,238 @@
+"""PPO's learning half on the B200 kernels (ttrl/algos/ppo/{loss,learn}.py).
+
+`objective` has the reference's signature and semantics (clipped surrogate,
+PPO2 value clipping with the 0.5, entropy bonus; mean or masked-mean
+reduction) and runs as one fused kernel that also produces d loss / d
+(logits, value).
+
+`PPOLearner` is the graph-replayed learner: the rollout lives in HBM (uint8
+frames plus the per-sample fields), each minibatch is gathered on the device
+by index, and one CUDA graph holds every gradient step of a rollout update
+-- `epochs x minibatches` of forward, loss, backward, device-side grad-norm
+clip and fused Adam. The minibatch permutations are drawn on the host from
+the learner's numpy generator exactly as ttrl/buffers/rollout.py:241-283
+draws them, and uploaded (a few KB) before each replay.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ttrl_b200.algos.grads import clip_grad_norm_device
+from ttrl_b200.device import context
+from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
+from ttrl_b200.engine.ops import ppo_objective
+from ttrl_b200.engine.optim import Adam
+from ttrl_b200.engine.trace import capture
+
+__all__ = ["PPOConfig", "PPOLearner", "objective", "normalize_advantages"]
+
+
+@dataclass(frozen=True)
+class PPOConfig:
+    """The learner fields of ttrl/algos/ppo/config.py:22-211 this path reads."""
+    clip_eps: float = 0.1
+    value_clip_eps: float = 0.1
+    value_coef: float = 0.5
+    entropy_coef: float = 0.01
+    lr: float = 2.5e-4
+    eps: float = 1e-8
+    max_grad_norm: float = 0.5
+    epochs: int = 4
+    minibatch_size: int = 256
+    normalize_adv: bool = True
+
+
+def normalize_advantages(adv: np.ndarray) -> np.ndarray:
+    """(adv - mean) / (std + 1e-8) over the whole rollout
+    (ttrl/buffers/rollout.py:269-270)."""
+    adv = np.asarray(adv)
+    return (adv - adv.mean()) / (adv.std() + 1e-8)
+
+
+def objective(logits: Tensor, value: Tensor, batch: dict, cfg: PPOConfig, *, valid=None):
+    """-> (loss, parts, new_logp) for one minibatch; `batch` holds device
+    tensors actions (int32), old_logp, advantages, returns, values."""
+    return ppo_objective(
+        logits, value, batch["actions"], batch["old_logp"], batch["advantages"],
+        batch["returns"], batch["values"], clip_eps=cfg.clip_eps,
+        value_clip_eps=cfg.value_clip_eps, value_coef=cfg.value_coef,
+        entropy_coef=cfg.entropy_coef, valid=valid)
+
+
+class PPOLearner:
+    """Graph-replayed PPO learner over a device-resident rollout."""
+
+    METRICS = ("loss", "policy_loss", "value_loss", "entropy", "grad_sq")
+
+    def __init__(self, net, rollout_size: int, obs_shape, device=None, *,
+                 cfg: PPOConfig = PPOConfig(), seed: int = 0):
+        self.net = net
+        self.cfg = cfg
+        self.device = as_device(device)
+        self.ctx = context(self.device)
+        self.rollout_size = int(rollout_size)
+        self.obs_shape = tuple(int(v) for v in obs_shape)
+        mb = cfg.minibatch_size
+        self.minibatches = self.rollout_size // mb
+        if self.minibatches == 0:
+            raise ValueError(f"rollout of {rollout_size} holds no minibatch of {mb}")
+        self.steps_per_update = cfg.epochs * self.minibatches
+        self.params = list(net.parameters())
+        self.optimizer = Adam(self.params, lr=cfg.lr, eps=cfg.eps)
+        self.rng = np.random.default_rng(seed)
+        dev = self.device
+        c, h, w = self.obs_shape
+        R = self.rollout_size
+        # Device-resident rollout (address-stable: written in place).
+        self.obs = torch.zeros((R, c, h, w), dtype=torch.uint8, device=dev)
+        self.actions = torch.zeros(R, dtype=torch.int32, device=dev)
+        self.old_logp = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.values = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.returns = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.advantages = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.perm = torch.zeros((self.steps_per_update, mb), dtype=torch.int32, device=dev)
+        self.perm_host = torch.zeros((self.steps_per_update, mb), dtype=torch.int32,
+                                     pin_memory=True)
+        # Minibatch staging (gathered per step on the device).
+        self.mb_rows = torch.empty((1, 1, mb * h * w, c), dtype=torch.float32, device=dev)
+        self.mb_actions = torch.empty(mb, dtype=torch.int32, device=dev)
+        self.mb_fields = {k: torch.empty(mb, dtype=torch.float32, device=dev)
+                          for k in ("old_logp", "values", "returns", "advantages")}
+        self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
+                                      dtype=torch.float32, device=dev)
+        self._graph = None
+
+    # -- rollout -----------------------------------------------------------
+
+    def load_rollout(self, obs_u8, actions, old_logp, values, returns, advantages) -> None:
+        """Upload one rollout (host arrays). Advantages are normalised over
+        the rollout here when cfg.normalize_adv, as the reference does."""
+        adv = normalize_advantages(advantages) if self.cfg.normalize_adv else advantages
+        self.obs.copy_(torch.from_numpy(np.ascontiguousarray(obs_u8, np.uint8)))
+        self.actions.copy_(torch.from_numpy(np.asarray(actions, np.int32)))
+        self.old_logp.copy_(torch.from_numpy(np.asarray(old_logp, np.float32)))
+        self.values.copy_(torch.from_numpy(np.asarray(values, np.float32)))
+        self.returns.copy_(torch.from_numpy(np.asarray(returns, np.float32)))
+        self.advantages.copy_(torch.from_numpy(np.asarray(adv, np.float32)))
+
+    def draw_permutations(self) -> None:
+        """One permutation of the rollout per epoch, cut into minibatches."""
+        mb = self.cfg.minibatch_size
+        rows = []
+        for _ in range(self.cfg.epochs):
+            perm = self.rng.permutation(self.rollout_size)
+            for start in range(0, self.minibatches * mb, mb):
+                rows.append(perm[start:start + mb])
+        self.perm_host.numpy()[:] = np.stack(rows).astype(np.int32)
+        self.perm.copy_(self.perm_host, non_blocking=True)
+
+    # -- one gradient step ---------------------------------------------------
+
+    def _minibatch_step(self, k: int) -> None:
+        cfg = self.cfg
+        ctx = self.ctx
+        idx = self.perm[k]
+        c = self.obs_shape[0]
+        ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c), 1.0)
+        ctx.gather_rows(self.actions, idx, self.mb_actions)
+        for name, src in (("old_logp", self.old_logp), ("values", self.values),
+                          ("returns", self.returns), ("advantages", self.advantages)):
+            ctx.gather_rows(src, idx, self.mb_fields[name])
+        self.optimizer.zero_grad()
+        logits, value = self.net(Tensor(self.mb_rows))
+        loss, parts, _ = ppo_objective(
+            logits, value, self.mb_actions, self.mb_fields["old_logp"],
+            self.mb_fields["advantages"], self.mb_fields["returns"], self.mb_fields["values"],
+            clip_eps=cfg.clip_eps, value_clip_eps=cfg.value_clip_eps,
+            value_coef=cfg.value_coef, entropy_coef=cfg.entropy_coef)
+        loss.backward()
+        norm = clip_grad_norm_device(self.params, cfg.max_grad_norm, self.optimizer)
+        self.optimizer.step()
+        row = self.metric_buf[k]
+        ctx.copy_strided(row[0:1], loss.data.reshape(1))
+        for j, key in enumerate(("policy_loss", "value_loss", "entropy")):
+            ctx.copy_strided(row[j + 1:j + 2], parts[key].data.reshape(1))
+        ctx.copy_strided(row[4:5], norm[0:1])
+
+    def _update_body(self) -> None:
+        for k in range(self.steps_per_update):
+            self._minibatch_step(k)
+
+    def update_eager(self) -> None:
+        """One rollout update, op by op (no graph)."""
+        self._update_body()
+        self.optimizer.captured_indices = None
+
+    def capture(self) -> None:
+        """Warm up (kernel loading, workspace and gradient buffers), then
+        capture one whole rollout update into a CUDA graph."""
+        # Warm-up on scratch copies of the parameters would change nothing
+        # observable except the first update; run one real minibatch step
+        # and roll the optimizer state back so replays start from step 0.
+        saved = [p.data.clone() for p in self.params]
+        m_saved = [m.clone() for m in self.optimizer.m]
+        v_saved = [v.clone() for v in self.optimizer.v]
+        steps_saved = self.optimizer._dev_steps.clone()
+        host_steps = (self.optimizer.t, list(self.optimizer.steps))
+        self._minibatch_step(0)
+        torch.cuda.synchronize(self.device)
+        for p, s in zip(self.params, saved):
+            p.data.copy_(s)
+        for m, s in zip(self.optimizer.m, m_saved):
+            m.copy_(s)
+        for v, s in zip(self.optimizer.v, v_saved):
+            v.copy_(s)
+        self.optimizer._dev_steps.copy_(steps_saved)
+        self.optimizer.t, self.optimizer.steps = host_steps[0], host_steps[1]
+        self._graph, _ = capture(self.device, self._update_body)
+
+    def replay(self) -> None:
+        """One rollout update (epochs x minibatches gradient steps)."""
+        if self._graph is None:
+            self.capture()
+        self._graph.replay()
+        opt = self.optimizer
+        for _ in range(self.steps_per_update):
+            opt.advance(range(len(self.params)))
+
+    def read_metrics(self) -> dict:
+        """Mean over the rollout update's steps, like ttrl/algos/ppo/learn.py:69-73."""
+        host = self.metric_buf.detach().to("cpu").numpy().astype(np.float64)
+        out = {k: float(host[:, j].mean()) for j, k in enumerate(self.METRICS)}
+        out["grad_norm"] = float(np.sqrt(host[:, 4]).mean())
+        out["minibatches"] = float(self.steps_per_update)
+        return out
+
+    def close(self) -> None:
+        if self._graph is not None:
+            self._graph.close()
+            self._graph = None
+
+
+def initial_old_logp(net, obs_u8: np.ndarray, actions: np.ndarray, device, chunk: int = 256):
+    """log pi_0(a|s) and V_0(s) of the initial policy over a rollout, by the
+    device forward (setup only; not part of a timed update)."""
+    dev = as_device(device)
+    ctx = context(dev)
+    n, c, h, w = obs_u8.shape
+    logp = np.zeros(n, np.float32)
+    vals = np.zeros(n, np.float32)
+    frames = torch.from_numpy(np.ascontiguousarray(obs_u8)).to(dev)
+    rows = torch.empty((1, 1, chunk * h * w, c), dtype=torch.float32, device=dev)
+    with no_grad():
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            if e - s != chunk:
+                raise ValueError("rollout size must be a multiple of the chunk")
+            ctx.u8_to_f32(frames[s:e], None, rows.reshape(-1, c), 1.0)
+            logits, value = net(Tensor(rows))
+            lg = logits.numpy().astype(np.float64)
+            mx = lg.max(axis=1, keepdims=True)
+            lsm = lg - mx - np.log(np.exp(lg - mx).sum(axis=1, keepdims=True))
+            logp[s:e] = lsm[np.arange(e - s), actions[s:e]]
+            vals[s:e] = value.numpy().reshape(-1)
+    return logp, vals

@@ -213,7 +213,8 @@ class DeviceContext:
 
     # -- optimizer -------------------------------------------------------
 
-    def adam_step(self, tensors, steps, ticket, grad_scale, lr, b1, b2, eps, wd) -> None:
+    def adam_step(self, tensors, steps, ticket, grad_scale, lr, b1, b2, eps, wd,
+                  lr_device=None) -> None:
         """`tensors`: list of (param, grad, S, V, step_index)."""
         for start in range(0, len(tensors), 64):
             chunk = tensors[start:start + 64]
@@ -223,8 +224,9 @@ class DeviceContext:
                                          _ptr(_f32(s, "S")), _ptr(_f32(v, "V")), p.numel(),
                                          int(idx), 0)
             check(lib().ttrl_adam_step(arr, len(chunk), _ptr(steps), _ptr(ticket),
-                                       _ptr(grad_scale), float(lr), float(b1), float(b2),
-                                       float(eps), float(wd), self.stream), "ttrl_adam_step")
+                                       _ptr(grad_scale), _ptr(lr_device), float(lr), float(b1),
+                                       float(b2), float(eps), float(wd), self.stream),
+                  "ttrl_adam_step")
 
     def grad_sqnorm(self, grads, out, max_norm: float, workspace) -> None:
         if len(grads) > 64:
@@ -242,6 +244,82 @@ class DeviceContext:
     def sqnorm_workspace_bytes(numels) -> int:
         arr = (ctypes.c_int64 * len(numels))(*numels)
         return int(lib().ttrl_grad_sqnorm_workspace_bytes(arr, len(numels)))
+
+    # -- tape primitives ---------------------------------------------------
+
+    def ew(self, op: str, a, b, out, scalar: float = 0.0) -> None:
+        """out = op(a, b, scalar); a/b broadcast to out's shape (rank <= 4)."""
+        shape = tuple(out.shape) or (1,)
+        nd = len(shape)
+        if nd > 4:
+            raise ValueError(f"elementwise ops support rank <= 4, got {shape}")
+
+        def strides(t):
+            if t is None:
+                return None, None
+            if t.dtype != torch.float32:
+                raise ValueError(f"elementwise operand must be float32, got {t.dtype}")
+            ex = t.expand(shape) if t.dim() else t.reshape((1,) * nd).expand(shape)
+            return t.data_ptr(), (ctypes.c_int64 * nd)(*ex.stride())
+
+        ap, ast = strides(a)
+        bp, bst = strides(b)
+        if not out.is_contiguous():
+            raise ValueError("elementwise output must be contiguous")
+        sh = (ctypes.c_int64 * nd)(*shape)
+        check(lib().ttrl_ew(_lib.EW[op], ap, ast, bp, bst, out.data_ptr(), sh, nd,
+                            float(scalar), self.stream), f"ttrl_ew({op})")
+
+    def reduce(self, op: int, inp, out, outer: int, n: int, inner: int) -> None:
+        check(lib().ttrl_reduce(op, _ptr(_f32(inp, "in")), _ptr(_f32(out, "out")), int(outer),
+                                int(n), int(inner), self.stream), "ttrl_reduce")
+
+    def copy_strided(self, dst, src, accumulate: bool = False) -> None:
+        """dst (=|+=) src elementwise for two same-shape (possibly strided) views."""
+        shape = tuple(dst.shape) or (1,)
+        nd = len(shape)
+        if tuple(src.shape) != tuple(dst.shape):
+            raise ValueError(f"copy shape mismatch {tuple(src.shape)} vs {tuple(dst.shape)}")
+        sh = (ctypes.c_int64 * nd)(*shape)
+        ds = (ctypes.c_int64 * nd)(*(dst.stride() if dst.dim() else (1,)))
+        ss = (ctypes.c_int64 * nd)(*(src.stride() if src.dim() else (1,)))
+        check(lib().ttrl_copy_strided(dst.data_ptr(), ds, src.data_ptr(), ss, sh, nd,
+                                      int(accumulate), self.stream), "ttrl_copy_strided")
+
+    def polyak(self, dst, src, tau: float) -> None:
+        check(lib().ttrl_polyak(_ptr(_f32(dst, "dst")), _ptr(_f32(src, "src")), dst.numel(),
+                                float(tau), self.stream), "ttrl_polyak")
+
+    def gather_rows(self, src, idx, dst) -> None:
+        """dst[i] = src[idx[i]] over the leading axis (4-byte elements)."""
+        if src.element_size() != 4 or dst.element_size() != 4 or idx.dtype != torch.int32:
+            raise ValueError("gather_rows moves 4-byte rows by int32 index")
+        row = 1
+        for d in src.shape[1:]:
+            row *= int(d)
+        check(lib().ttrl_gather_rows(src.data_ptr(), idx.data_ptr(), dst.data_ptr(),
+                                     int(idx.numel()), row, self.stream), "ttrl_gather_rows")
+
+    def dqn_loss(self, q, q_sel, q_tgt, onehot, rewards, dones, discounts, next_mask,
+                 is_weights, loss, mean_q, td_abs, dq, delta: float,
+                 accumulate: bool = False) -> None:
+        b, a = q.shape[0], q.shape[1]
+        check(lib().ttrl_dqn_loss(_ptr(q), _ptr(q_sel), _ptr(q_tgt), _ptr(onehot),
+                                  _ptr(rewards), _ptr(dones), _ptr(discounts), _ptr(next_mask),
+                                  _ptr(is_weights), _ptr(loss), _ptr(mean_q), _ptr(td_abs),
+                                  _ptr(dq), b, a, float(delta), int(accumulate), self.stream),
+              "ttrl_dqn_loss")
+
+    def ppo_loss(self, logits, value, actions, old_logp, adv, returns, old_values, valid,
+                 metrics, new_logp, dlogits, dvalue, clip, vclip, vcoef, entcoef) -> None:
+        b, a = logits.shape[0], logits.shape[1]
+        if actions.dtype != torch.int32:
+            raise ValueError("ppo_loss: actions must be int32")
+        check(lib().ttrl_ppo_loss(_ptr(logits), _ptr(value), _ptr(actions), _ptr(old_logp),
+                                  _ptr(adv), _ptr(returns), _ptr(old_values), _ptr(valid),
+                                  _ptr(metrics), _ptr(new_logp), _ptr(dlogits), _ptr(dvalue), b,
+                                  a, float(clip), float(vclip), float(vcoef), float(entcoef),
+                                  self.stream), "ttrl_ppo_loss")
 
 
 def context(device=None) -> DeviceContext:

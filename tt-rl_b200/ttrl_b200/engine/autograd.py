@@ -1,0 +1,312 @@
+"""Reverse-mode autograd tape over CUDA tensors.
+
+Same contract as the reference tape (ttrl/engine/autograd.py:56-235):
+`Tensor(data, requires_grad, _parents, _op)`, fp32 gradient accumulation,
+post-order DFS over an explicit stack, a scalar seed of 1.0, no
+retain_graph (the tape is torn down in a `finally`), and `no_grad`.
+
+Two additions serve the fused kernels:
+
+* A tensor produced by a fused Linear/Conv2d + ReLU node carries
+  `_premask = True`: every gradient it holds is already multiplied by its
+  ReLU mask (y > 0). Fused consumers write their input gradient with the
+  mask applied in the GEMM epilogue and pass `premasked=True`; any other
+  contribution is masked on the way in by `_accumulate`. The fused node's
+  backward therefore reads `out.grad` as the gradient of the pre-activation.
+* A parameter owns one persistent gradient buffer (`_grad_buf`). Fused
+  weight-gradient kernels write into it (or accumulate into it), so a
+  captured CUDA graph always finds the gradient at the same address.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ttrl_b200.device import context
+
+__all__ = ["Tensor", "backward", "no_grad", "is_grad_enabled", "DEFAULT_DTYPE"]
+
+DEFAULT_DTYPE = torch.float32
+GRAD_ACCUM_DTYPE = torch.float32
+
+_GRAD_ENABLED = True
+
+#: The tensor whose backward() is running. A fused loss node that is the root
+#: receives the unit seed and can skip scaling its precomputed gradient.
+_BACKWARD_ROOT = None
+
+
+def backward_root():
+    return _BACKWARD_ROOT
+
+
+def is_grad_enabled() -> bool:
+    return _GRAD_ENABLED
+
+
+class no_grad:
+    """Ops built inside record no tape (ttrl/engine/autograd.py:30-44)."""
+
+    def __enter__(self):
+        global _GRAD_ENABLED
+        self._prev = _GRAD_ENABLED
+        _GRAD_ENABLED = False
+        return self
+
+    def __exit__(self, *exc):
+        global _GRAD_ENABLED
+        _GRAD_ENABLED = self._prev
+        return False
+
+
+def _no_backward(grad):
+    return None
+
+
+def _default_device():
+    if not torch.cuda.is_available():
+        raise RuntimeError("ttrl_b200 needs a CUDA device; there is no CPU fallback")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def as_device(device) -> torch.device:
+    """Normalise the reference's `device` argument to a torch CUDA device."""
+    if device is None:
+        return _default_device()
+    if hasattr(device, "torch_device"):
+        return device.torch_device
+    d = torch.device(device) if not isinstance(device, torch.device) else device
+    if d.type != "cuda":
+        raise ValueError(f"ttrl_b200 runs on CUDA devices only, got {device!r}")
+    if d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    return d
+
+
+class Tensor:
+    """A node in the autograd graph, backed by a CUDA tensor."""
+
+    __slots__ = ("data", "requires_grad", "grad", "_backward", "_parents", "_op",
+                 "_backward_done", "_premask", "_grad_buf", "_grad_owned", "__weakref__")
+
+    def __init__(self, data, requires_grad: bool = False, _parents=(), _op: str = ""):
+        self.data = data
+        self.requires_grad = requires_grad
+        self.grad = None
+        self._backward = _no_backward
+        self._parents = tuple(_parents)
+        self._op = _op
+        self._backward_done = False
+        self._premask = False
+        self._grad_buf = None
+        self._grad_owned = False
+
+    # -- construction ------------------------------------------------------
+
+    @staticmethod
+    def from_numpy(array, device=None, *, requires_grad=False, dtype=DEFAULT_DTYPE,
+                   layout=None) -> "Tensor":
+        dev = as_device(device)
+        arr = np.ascontiguousarray(np.asarray(array))
+        if dtype in (torch.float32, None, np.float32):
+            arr = arr.astype(np.float32, copy=False)
+            t = torch.from_numpy(arr).to(dev)
+        else:
+            t = torch.from_numpy(arr).to(dev, dtype=dtype)
+        return Tensor(t, requires_grad)
+
+    def numpy(self) -> np.ndarray:
+        out = self.data.detach().to("cpu").numpy()
+        return out.astype(np.float32) if out.dtype != np.float32 and out.dtype.kind == "f" else out
+
+    # -- introspection -----------------------------------------------------
+
+    @property
+    def shape(self):
+        return tuple(self.data.shape)
+
+    @property
+    def device(self):
+        return self.data.device
+
+    @property
+    def dtype(self):
+        return self.data.dtype
+
+    def __repr__(self):
+        return f"Tensor(shape={self.shape}, op={self._op or 'leaf'}, grad={self.requires_grad})"
+
+    # -- gradient plumbing -------------------------------------------------
+
+    def _accumulate(self, grad, premasked: bool = False):
+        """Add one gradient contribution (a torch tensor shaped like data)."""
+        if grad.dtype != GRAD_ACCUM_DTYPE:
+            grad = grad.to(GRAD_ACCUM_DTYPE)
+        if tuple(grad.shape) != tuple(self.data.shape):
+            grad = grad.reshape(self.data.shape)
+        ctx = context(self.data.device)
+        if self._premask and not premasked:
+            masked = torch.empty_like(grad)
+            ctx.ew("relu_bw", grad, self.data, masked)
+            grad = masked
+        if self.grad is None:
+            self.grad = grad
+            self._grad_owned = False
+        elif self._grad_owned:
+            ctx.ew("add", self.grad, grad, self.grad)
+        else:
+            total = torch.empty_like(self.grad)
+            ctx.ew("add", self.grad, grad, total)
+            self.grad = total
+            self._grad_owned = True
+
+    def _grad_slot(self):
+        """(buffer, accumulate) for a fused kernel about to write this tensor's
+        gradient. Parameters write into their persistent `_grad_buf`."""
+        if self.grad is None:
+            if self._op == "" and self.requires_grad:
+                if self._grad_buf is None or self._grad_buf.shape != self.data.shape:
+                    self._grad_buf = torch.empty_like(self.data)
+                return self._grad_buf, False
+            return torch.empty_like(self.data), False
+        if self._grad_owned and self.grad.is_contiguous():
+            return self.grad, True
+        # A gradient we do not own (bound from another op): copy it into a
+        # buffer of our own, then accumulate into that.
+        if self._op == "" and self.requires_grad:
+            if self._grad_buf is None or self._grad_buf.shape != self.data.shape:
+                self._grad_buf = torch.empty_like(self.data)
+            buf = self._grad_buf
+        else:
+            buf = torch.empty_like(self.data)
+        if buf.data_ptr() != self.grad.data_ptr():
+            context(self.data.device).copy_strided(buf, self.grad.reshape(buf.shape))
+        return buf, True
+
+    def _set_grad(self, buf):
+        """Record that a fused kernel wrote (or accumulated) `buf`."""
+        self.grad = buf
+        self._grad_owned = True
+
+    def zero_grad(self):
+        self.grad = None
+        self._grad_owned = False
+
+    def detach(self) -> "Tensor":
+        return Tensor(self.data, requires_grad=False)
+
+    def backward(self):
+        if not self.requires_grad:
+            raise RuntimeError(
+                "backward() called on a Tensor that requires no gradient; it "
+                "carries no tape (a leaf, a detached node, or built inside "
+                "no_grad()), so this call would silently produce no parameter "
+                "gradients at all."
+            )
+        if self._backward_done:
+            raise RuntimeError(
+                "backward() called a second time on the same graph; this tape "
+                "does not keep saved activations alive for a second pass "
+                "(no retain_graph). Build a fresh forward pass instead."
+            )
+        topo: list[Tensor] = []
+        seen: set[int] = set()
+        stack: list[tuple[Tensor, bool]] = [(self, False)]
+        while stack:
+            node, expanded = stack.pop()
+            if expanded:
+                topo.append(node)
+                continue
+            if id(node) in seen:
+                continue
+            seen.add(id(node))
+            stack.append((node, True))
+            for parent in node._parents:
+                if id(parent) not in seen:
+                    stack.append((parent, False))
+
+        numel = 1
+        for dim in self.shape:
+            numel *= dim
+        if numel != 1:
+            raise RuntimeError(
+                f"backward() called on a non-scalar Tensor with shape {self.shape} "
+                f"(numel={numel}); there is no `gradient=` kwarg to seed a "
+                "non-scalar backward pass, so reduce to a scalar first."
+            )
+        seed = torch.empty_like(self.data, dtype=GRAD_ACCUM_DTYPE)
+        context(self.data.device).ew("fill", None, None, seed, 1.0)
+        self.grad = seed
+        self._grad_owned = True
+        global _BACKWARD_ROOT
+        prev_root, _BACKWARD_ROOT = _BACKWARD_ROOT, self
+        try:
+            for node in reversed(topo):
+                grad = node.grad
+                if grad is not None:
+                    if node._backward_done and node is not self:
+                        raise RuntimeError(
+                            "backward() reached a node whose tape was already "
+                            "consumed by a previous backward() call on a graph "
+                            "sharing this subgraph; reusing a consumed subgraph "
+                            "is not supported (no retain_graph)."
+                        )
+                    node._backward(grad)
+        finally:
+            _BACKWARD_ROOT = prev_root
+            for node in topo:
+                if node._op:
+                    node._backward_done = True
+                node._backward = _no_backward
+                node._parents = ()
+
+    # -- operators ---------------------------------------------------------
+
+    def __add__(self, other):
+        from ttrl_b200.engine.ops import add
+        return add(self, other)
+
+    __radd__ = __add__
+
+    def __mul__(self, other):
+        from ttrl_b200.engine.ops import mul
+        return mul(self, other)
+
+    __rmul__ = __mul__
+
+    def __sub__(self, other):
+        from ttrl_b200.engine.ops import sub
+        return sub(self, other)
+
+    def __rsub__(self, other):
+        from ttrl_b200.engine.ops import sub
+        return sub(other, self)
+
+    def __neg__(self):
+        from ttrl_b200.engine.ops import mul
+        return mul(self, -1.0)
+
+    def __truediv__(self, other):
+        from ttrl_b200.engine.ops import div
+        return div(self, other)
+
+
+def backward(tensor: Tensor) -> None:
+    tensor.backward()
+
+
+# --------------------------------------------------------------------------
+# shared op-building helpers (ttrl/engine/autograd.py:205-235)
+# --------------------------------------------------------------------------
+
+def _is_scalar(x) -> bool:
+    return not isinstance(x, Tensor) and not hasattr(x, "shape")
+
+
+def _needs(*tensors) -> bool:
+    return _GRAD_ENABLED and any(t.requires_grad for t in tensors)
+
+
+def _detached(data) -> Tensor:
+    return Tensor(data, requires_grad=False)

@@ -1,0 +1,242 @@
+"""`Conv2d` over flattened-NHWC activations (ttrl/engine/conv/module.py).
+
+The weight is held on the device as [Cout][KH][KW][Cin] ("KRSC"), the order
+the implicit GEMM walks one output row in; `weight_numpy`,
+`weight_grad_numpy`, `load_weight_numpy` and the state_dict use the logical
+OIHW form, as the reference's do, so checkpoints are interchangeable.
+
+Geometry rules follow ttrl/engine/conv/geometry.py: output sizes, and a
+refusal of ragged strides (the input gradient is only the exact adjoint for
+exactly divisible strides). A space-to-depth `fold` is accepted and checked
+like the reference's, and computes the identical convolution (the fold is a
+re-indexing the reference needs for its hardware; the GEMM here gathers the
+unfolded window directly).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+from ttrl_b200.device import conv_geom
+from ttrl_b200.engine.autograd import Tensor, as_device
+from ttrl_b200.engine.nn import Module
+from ttrl_b200.engine.ops import conv2d_nhwc
+from ttrl_b200.engine.tensor import restore_in_place
+
+__all__ = ["Conv2d", "ConvGeometry", "ConvDoesNotFit", "conv_out_size"]
+
+
+class ConvDoesNotFit(ValueError):
+    """Kept for interface compatibility (ttrl/engine/conv/geometry.py:127-133).
+    A B200 has no per-core L1 ceiling on these layers, so nothing raises it."""
+
+
+def conv_out_size(size: int, kernel: int, stride: int, padding: int, *, axis: str = "h") -> int:
+    """(size + 2*padding - kernel) // stride + 1, with the geometry checked
+    (ttrl/engine/conv/geometry.py:94-124)."""
+    if kernel <= 0 or stride <= 0 or padding < 0:
+        raise ValueError(
+            f"conv2d: kernel and stride must be > 0 and padding >= 0, got "
+            f"kernel={kernel}, stride={stride}, padding={padding}"
+        )
+    span = size + 2 * padding - kernel
+    if span < 0:
+        raise ValueError(
+            f"conv2d: input {axis}={size} with padding={padding} is smaller than "
+            f"kernel={kernel}; output would be empty"
+        )
+    if span % stride != 0:
+        raise ValueError(
+            f"conv2d: ragged geometry on {axis}: (size + 2*padding - kernel) = "
+            f"{span} is not a multiple of stride={stride} (size={size}, "
+            f"kernel={kernel}, padding={padding}). The input gradient is only "
+            f"the true adjoint for exactly divisible strides."
+        )
+    return span // stride + 1
+
+
+@dataclass(frozen=True)
+class ConvGeometry:
+    batch: int
+    in_channels: int
+    in_h: int
+    in_w: int
+    out_channels: int
+    kernel: int
+    stride: int = 1
+    padding: int = 0
+    fold: int = 1
+
+    def __post_init__(self) -> None:
+        if min(self.batch, self.in_channels, self.in_h, self.in_w, self.out_channels) <= 0:
+            raise ValueError(f"conv2d: batch, channels and input extent must be > 0, got {self}")
+        if self.fold < 1:
+            raise ValueError(f"conv2d: fold must be >= 1, got {self.fold}")
+        if self.fold > 1:
+            if self.stride != self.fold or self.padding != 0:
+                raise ValueError(
+                    f"conv2d: space-to-depth needs stride == fold and padding == 0, got "
+                    f"stride={self.stride} fold={self.fold} padding={self.padding}"
+                )
+            for name, size in (("kernel", self.kernel), ("in_h", self.in_h), ("in_w", self.in_w)):
+                if size % self.fold:
+                    raise ValueError(f"conv2d: fold={self.fold} must divide {name}={size}")
+        _ = (self.out_h, self.out_w)
+
+    @property
+    def out_h(self) -> int:
+        return conv_out_size(self.in_h, self.kernel, self.stride, self.padding, axis="h")
+
+    @property
+    def out_w(self) -> int:
+        return conv_out_size(self.in_w, self.kernel, self.stride, self.padding, axis="w")
+
+    @property
+    def out_shape(self) -> tuple[int, int, int]:
+        return (self.out_channels, self.out_h, self.out_w)
+
+    @property
+    def in_numel(self) -> int:
+        return self.batch * self.in_channels * self.in_h * self.in_w
+
+    def kernel_geom(self):
+        return conv_geom(self.batch, self.in_h, self.in_w, self.in_channels, self.out_channels,
+                         self.kernel, self.kernel, self.stride, self.padding)
+
+
+class Conv2d(Module):
+    """A convolution holding its own weight (KRSC on device) and bias."""
+
+    def __init__(self, in_shape, out_channels: int, kernel: int, device=None, *, batch: int,
+                 stride: int = 1, padding: int = 0, bias: bool = True, fold: int = 1,
+                 input_scale: float = 1.0, weight=None, needs_input_grad: bool = True,
+                 profile=None):
+        if len(tuple(in_shape)) != 3:
+            raise ValueError(
+                f"Conv2d: in_shape must be (channels, height, width), got {tuple(in_shape)}"
+            )
+        in_channels, in_h, in_w = (int(v) for v in in_shape)
+        self.geom = ConvGeometry(
+            batch=int(batch), in_channels=in_channels, in_h=in_h, in_w=in_w,
+            out_channels=int(out_channels), kernel=int(kernel), stride=int(stride),
+            padding=int(padding), fold=int(fold),
+        )
+        self.device = as_device(device)
+        self.input_scale = float(input_scale)
+        self.needs_input_grad = bool(needs_input_grad)
+        if weight is None:
+            bound = 1.0 / math.sqrt(in_channels * kernel * kernel)
+            weight = np.random.uniform(
+                -bound, bound, (out_channels, in_channels, kernel, kernel)
+            ).astype(np.float32)
+        else:
+            weight = np.asarray(weight, np.float32)
+            want = (out_channels, in_channels, kernel, kernel)
+            if weight.shape != want:
+                raise ValueError(f"Conv2d: weight must have shape {want}, got {weight.shape}")
+        self._oihw_shape = weight.shape
+        self.weight = Tensor.from_numpy(np.ascontiguousarray(weight.transpose(0, 2, 3, 1)),
+                                        self.device, requires_grad=True)
+        if bias:
+            bound = 1.0 / math.sqrt(in_channels * kernel * kernel)
+            b = np.random.uniform(-bound, bound, (1, 1, 1, out_channels)).astype(np.float32)
+            self.bias = Tensor.from_numpy(b, self.device, requires_grad=True)
+        else:
+            self.bias = None
+        self._kgeom = self.geom.kernel_geom()
+
+    @property
+    def out_shape(self) -> tuple[int, int, int]:
+        return self.geom.out_shape
+
+    @property
+    def out_numel(self) -> int:
+        return self.geom.batch * int(np.prod(self.geom.out_shape))
+
+    def __repr__(self) -> str:
+        g = self.geom
+        return (f"Conv2d({g.in_channels}x{g.in_h}x{g.in_w} -> {self.out_shape}, k{g.kernel}, "
+                f"s{g.stride}, p{g.padding}, fold={g.fold})")
+
+    # -- parameters ------------------------------------------------------
+
+    def weight_numpy(self) -> np.ndarray:
+        return np.ascontiguousarray(self.weight.numpy().transpose(0, 3, 1, 2))
+
+    def weight_grad_numpy(self) -> np.ndarray:
+        if self.weight.grad is None:
+            raise ValueError("Conv2d.weight_grad_numpy: no gradient has been accumulated")
+        g = self.weight.grad.detach().to("cpu").numpy()
+        return np.ascontiguousarray(g.transpose(0, 3, 1, 2))
+
+    def load_weight_numpy(self, w_oihw) -> None:
+        w = np.asarray(w_oihw, np.float32)
+        if w.shape != self._oihw_shape:
+            raise ValueError(
+                f"Conv2d.load_weight_numpy: expected shape {self._oihw_shape}, got {w.shape}"
+            )
+        restore_in_place(self.weight.data, w.transpose(0, 2, 3, 1))
+
+    def state_dict(self) -> dict:
+        state = {"weight": self.weight_numpy()}
+        if self.bias is not None:
+            state["bias"] = self.bias.numpy()
+        return state
+
+    def load_state_dict(self, state: dict, device=None) -> None:
+        reference = self.state_dict()
+        got, expected = set(state.keys()), set(reference)
+        if got != expected:
+            raise ValueError(
+                "load_state_dict: checkpoint keys do not match module "
+                f"parameters (missing={sorted(expected - got)}, "
+                f"extra={sorted(got - expected)})"
+            )
+        for name, want in reference.items():
+            shape = tuple(int(d) for d in np.asarray(state[name]).shape)
+            if shape != want.shape:
+                raise ValueError(
+                    f"load_state_dict: shape mismatch for {name!r}: "
+                    f"checkpoint has {shape}, parameter expects {want.shape}"
+                )
+        self.load_weight_numpy(state["weight"])
+        if self.bias is not None:
+            restore_in_place(self.bias.data, state["bias"])
+
+    def at_batch(self, batch: int) -> "Conv2d":
+        """This layer at another activation batch, sharing weight and bias."""
+        view = object.__new__(Conv2d)
+        view.__dict__.update(self.__dict__)
+        g = self.geom
+        view.geom = ConvGeometry(batch=int(batch), in_channels=g.in_channels, in_h=g.in_h,
+                                 in_w=g.in_w, out_channels=g.out_channels, kernel=g.kernel,
+                                 stride=g.stride, padding=g.padding, fold=g.fold)
+        view._kgeom = view.geom.kernel_geom()
+        view.needs_input_grad = False
+        return view
+
+    # -- call ------------------------------------------------------------
+
+    def _check_input(self, x: Tensor) -> None:
+        numel = 1
+        for d in x.shape:
+            numel *= int(d)
+        if numel != self.geom.in_numel:
+            raise ValueError(
+                f"conv2d: activation has {numel} elements but this layer's geometry "
+                f"{self.geom} requires {self.geom.in_numel}; the layer was built for a "
+                "different input."
+            )
+
+    def forward(self, x: Tensor) -> Tensor:
+        self._check_input(x)
+        return conv2d_nhwc(x, self.weight, self.bias, self._kgeom, input_scale=self.input_scale,
+                           relu=False, needs_input_grad=self.needs_input_grad)
+
+    def forward_relu(self, x: Tensor) -> Tensor:
+        self._check_input(x)
+        return conv2d_nhwc(x, self.weight, self.bias, self._kgeom, input_scale=self.input_scale,
+                           relu=True, needs_input_grad=self.needs_input_grad)

@@ -1,0 +1,193 @@
+"""Optimizers: `Optimizer`, `Adam`, `adam_fused_scalars`
+(ttrl/engine/optim/{base,adam,scalars,checkpoint}.py).
+
+Adam keeps the reference's stored S = m/(1-b1), V = v/(1-b2) moments and
+its per-parameter step counts, and runs as ONE multi-tensor CUDA kernel per
+step. The step counts live on the device (the kernel reads and advances
+them), so the whole update -- Adam included -- can be captured into a CUDA
+graph and replayed with the correct bias correction every time. A host
+mirror of the counts backs `state_dict`.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from ttrl_b200.device import context
+from ttrl_b200.engine.tensor import MASTER_DTYPE, restore_in_place, to_host
+
+__all__ = ["Optimizer", "Adam", "adam_fused_scalars"]
+
+
+def adam_fused_scalars(lr: float, b1: float, b2: float, eps: float, t: int) -> tuple[float, float]:
+    """(alpha_t, eps_t) folding the bias correction (ttrl/engine/optim/scalars.py:13-27)."""
+    if t < 1:
+        raise ValueError(f"adam_fused_scalars: t must be >= 1, got {t}")
+    bc1 = 1 - b1 ** t
+    bc2 = 1 - b2 ** t
+    c = math.sqrt((1 - b2) / bc2)
+    return lr * (1 - b1) / bc1 / c, eps / c
+
+
+class Optimizer:
+    def __init__(self, params):
+        self.params = list(params)
+
+    def zero_grad(self) -> None:
+        for p in self.params:
+            p.zero_grad()
+
+    def step(self) -> None:
+        raise NotImplementedError
+
+
+class Adam(Optimizer):
+    """Adam over fp32 parameters, updated in place by one fused kernel."""
+
+    def __init__(self, params, lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0):
+        super().__init__(params)
+        if not self.params:
+            raise ValueError("Adam: params is empty, so there is nothing to optimize")
+        if lr <= 0:
+            raise ValueError(f"Adam: lr must be > 0, got {lr}")
+        b1, b2 = betas
+        if not (0.0 <= b1 < 1.0 and 0.0 <= b2 < 1.0):
+            raise ValueError(f"Adam: betas must be in [0, 1), got {betas}")
+        if eps <= 0:
+            raise ValueError(f"Adam: eps must be > 0, got {eps}")
+        if weight_decay < 0:
+            raise ValueError(f"Adam: weight_decay must be >= 0, got {weight_decay}")
+        wrong = [i for i, p in enumerate(self.params) if p.data.dtype != MASTER_DTYPE]
+        if wrong:
+            raise ValueError(f"Adam: parameters must be {MASTER_DTYPE}; parameters {wrong} are not")
+        self.b1, self.b2 = b1, b2
+        self.eps = eps
+        self.weight_decay = weight_decay
+        self.t = 0
+        self.steps = [0] * len(self.params)
+        dev = self.params[0].data.device
+        self._device = dev
+        self.m = [torch.zeros_like(p.data) for p in self.params]   # S
+        self.v = [torch.zeros_like(p.data) for p in self.params]   # V
+        self._dev_steps = torch.zeros(len(self.params), dtype=torch.int32, device=dev)
+        self._ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._lr_dev = torch.zeros(1, dtype=torch.float64, device=dev)
+        self._lr = float(lr)
+        self._lr_dev.copy_(torch.tensor([self._lr], dtype=torch.float64))
+        # Set by a device-side gradient clip for the next step() (see
+        # ttrl_b200.algos.grads.clip_grad_norm_device).
+        self.grad_scale = None
+        # Indices stepped by the launch recorded inside a graph capture.
+        self.captured_indices: list[int] | None = None
+
+    # The learning rate lives on the device too, so a replayed graph reads
+    # the current value (PPO's annealing, ttrl/algos/ppo/learn.py:54-56).
+    @property
+    def lr(self) -> float:
+        return self._lr
+
+    @lr.setter
+    def lr(self, value: float) -> None:
+        self._lr = float(value)
+        self._lr_dev.copy_(torch.tensor([self._lr], dtype=torch.float64))
+
+    @property
+    def _m_scale(self) -> float:
+        return 1 - self.b1
+
+    @property
+    def _v_scale(self) -> float:
+        return 1 - self.b2
+
+    def step(self) -> None:
+        """One update of every parameter that holds a gradient."""
+        tensors = []
+        stepped = []
+        for i, p in enumerate(self.params):
+            if p.grad is None:
+                continue
+            g = p.grad if p.grad.is_contiguous() else p.grad.contiguous()
+            tensors.append((p.data, g.reshape(p.data.shape), self.m[i], self.v[i], i))
+            stepped.append(i)
+        if tensors:
+            context(self._device).adam_step(
+                tensors, self._dev_steps, self._ticket, self.grad_scale, self._lr, self.b1,
+                self.b2, self.eps, self.weight_decay, lr_device=self._lr_dev)
+        self.grad_scale = None
+        if torch.cuda.is_current_stream_capturing():
+            # Recorded, not run: TrainStep advances the host mirror per replay.
+            self.captured_indices = stepped
+            return
+        self.advance(stepped)
+
+    def advance(self, stepped) -> None:
+        """Advance the host mirror of the device step counters."""
+        self.t += 1
+        for i in stepped:
+            self.steps[i] += 1
+
+    def _step_scalars(self, t: int) -> tuple[float, float]:
+        return adam_fused_scalars(self._lr, self.b1, self.b2, self.eps, t)
+
+    # -- checkpoint (ttrl/engine/optim/checkpoint.py) ---------------------
+
+    def state_dict(self) -> dict:
+        return {
+            "t": self.t,
+            "steps": list(self.steps),
+            "lr": self._lr,
+            "betas": (self.b1, self.b2),
+            "eps": self.eps,
+            "weight_decay": self.weight_decay,
+            "m": [to_host(m) * self._m_scale for m in self.m],
+            "v": [to_host(v) * self._v_scale for v in self.v],
+        }
+
+    def load_state_dict(self, state: dict, device=None) -> None:
+        if len(state["m"]) != len(self.m) or len(state["v"]) != len(self.v):
+            raise ValueError(
+                f"Adam.load_state_dict: checkpoint has {len(state['m'])} m and "
+                f"{len(state['v'])} v buffers, expected {len(self.m)} of each."
+            )
+        for key, buffers in (("m", self.m), ("v", self.v)):
+            for i, (arr, buf) in enumerate(zip(state[key], buffers)):
+                got = tuple(np.asarray(arr).shape)
+                if got != tuple(buf.shape):
+                    raise ValueError(
+                        f"Adam.load_state_dict: {key}[{i}] has shape {got}, which does "
+                        f"not match its parameter's shape {tuple(buf.shape)}."
+                    )
+        t = int(state["t"])
+        steps = [int(s) for s in state.get("steps", [t] * len(self.params))]
+        lr = state.get("lr", self._lr)
+        b1, b2 = state.get("betas", (self.b1, self.b2))
+        eps = state.get("eps", self.eps)
+        weight_decay = state.get("weight_decay", self.weight_decay)
+        if len(steps) != len(self.params):
+            raise ValueError(f"Adam.load_state_dict: checkpoint has {len(steps)} step counters, "
+                             f"expected {len(self.params)}.")
+        if t < 0 or any(s < 0 for s in steps):
+            raise ValueError(f"Adam.load_state_dict: step counts must be >= 0, got t={t}.")
+        if not lr > 0:
+            raise ValueError(f"Adam.load_state_dict: lr must be > 0, got {lr}.")
+        if not (0.0 <= b1 < 1.0 and 0.0 <= b2 < 1.0):
+            raise ValueError(f"Adam.load_state_dict: betas must be in [0, 1), got {(b1, b2)}.")
+        if not eps > 0:
+            raise ValueError(f"Adam.load_state_dict: eps must be > 0, got {eps}.")
+        if weight_decay < 0:
+            raise ValueError(f"Adam.load_state_dict: weight_decay must be >= 0, got {weight_decay}.")
+        self.t = t
+        self.steps = steps
+        self.lr = lr
+        self.b1, self.b2 = b1, b2
+        self.eps = eps
+        self.weight_decay = weight_decay
+        ms, vs = self._m_scale, self._v_scale
+        for i, arr in enumerate(state["m"]):
+            restore_in_place(self.m[i], np.asarray(arr) / ms)
+        for i, arr in enumerate(state["v"]):
+            restore_in_place(self.v[i], np.asarray(arr) / vs)
+        self._dev_steps.copy_(torch.tensor(steps, dtype=torch.int32))

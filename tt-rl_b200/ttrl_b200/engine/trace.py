@@ -1,0 +1,97 @@
+"""CUDA-graph capture and replay with the reference's trace interface
+(ttrl/engine/trace.py): `capture(device, record) -> (CapturedTrace, result)`.
+
+Capture is a callback, as in the reference, so no caller can leave a stream
+in capture mode: every exit path out of `record()` ends the capture inside
+this module. A host read inside the recorded region (an `.item()`, a
+`.numpy()`) is refused by CUDA during capture and surfaces as
+`TraceCaptureError`, as the reference's ttnn error does.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, TypeVar
+
+import torch
+
+from ttrl_b200.engine.autograd import as_device
+from ttrl_b200.engine.config import DEFAULT, EngineConfig
+
+__all__ = ["CapturedTrace", "TraceCaptureError", "capture", "HOST_READ_DURING_CAPTURE"]
+
+HOST_READ_DURING_CAPTURE = "operation not permitted when stream is capturing"
+
+R = TypeVar("R")
+
+
+class TraceCaptureError(RuntimeError):
+    """Graph capture failed. There is no eager fallback."""
+
+
+class CapturedTrace:
+    """One captured CUDA graph, replayable until closed."""
+
+    __slots__ = ("device", "_graph")
+
+    def __init__(self, device, graph):
+        self.device = device
+        self._graph = graph
+
+    @property
+    def live(self) -> bool:
+        return self._graph is not None
+
+    def replay(self, *, cfg: EngineConfig = DEFAULT, blocking: bool | None = None) -> None:
+        """Launch the graph on the device's current stream (non-blocking by
+        default: a later host read on the same stream is the barrier)."""
+        if self._graph is None:
+            raise RuntimeError("replay() on a closed CapturedTrace")
+        self._graph.replay()
+        wait = cfg.trace_blocking if blocking is None else blocking
+        if wait:
+            torch.cuda.current_stream(self.device).synchronize()
+
+    def close(self) -> None:
+        if self._graph is None:
+            return
+        graph, self._graph = self._graph, None
+        graph.reset()
+
+    def __enter__(self) -> "CapturedTrace":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+
+def capture(device, record: Callable[[], R], *, pool=None) -> tuple[CapturedTrace, R]:
+    """Record `record()`'s device work into a CUDA graph.
+
+    `record` must launch device work only. Run the same work once eagerly
+    beforehand (kernel loading, workspace sizing). Nothing has executed when
+    this returns; replay once before reading outputs.
+    """
+    dev = as_device(device)
+    graph = torch.cuda.CUDAGraph()
+    result = None
+    try:
+        with torch.cuda.device(dev):
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(graph, pool=pool, capture_error_mode="thread_local"):
+                result = record()
+    except BaseException as e:
+        try:
+            graph.reset()
+        except Exception:
+            pass
+        if isinstance(e, (KeyboardInterrupt, SystemExit)):
+            raise
+        if HOST_READ_DURING_CAPTURE in str(e) or "capturing" in str(e):
+            raise TraceCaptureError(
+                "graph capture failed because the captured work reads a tensor back "
+                "to host (.numpy(), .item(), .cpu()) or allocates with the CUDA "
+                "runtime, which CUDA does not allow during capture. Move every host "
+                "read after the replay, or run this step eagerly. Error: " + str(e)
+            ) from e
+        raise TraceCaptureError(f"graph capture failed: {e}") from e
+    return CapturedTrace(dev, graph), result
