@@ -1,0 +1,470 @@
+"""Learner throughput of the B200 backend on BASELINE.json's workload.
+
+Headline (configs[1] at N=1, configs[4] at N>1): PPO Nature-CNN learner
+samples/sec. One bench "step" is one PPO rollout update: a rollout of
+8 envs x 128 steps (1024 uint8 [4,84,84] frames plus per-sample fields)
+resident in HBM, 4 epochs x 4 minibatches of 256, each minibatch step = the
+Nature-CNN actor-critic forward, the PPO objective, backward, device-side
+grad-norm clip 0.5 and Adam (lr 2.5e-4) -- all 16 gradient steps replayed
+from ONE CUDA graph. samples/sec = 256 x minibatch steps / s, summed over
+ranks. At N>1 every rank runs its own seed stream and the online
+parameters are averaged by an NCCL all-reduce (ReduceOp.AVG) every 50
+rollout updates (the reference's sync_every unit).
+
+Also reported: the Nature-DQN batch-32 update (configs[0] shapes; forward x3,
+double-DQN Huber loss, backward, Adam) as updates/sec from one graph replay
+each, end-to-end numbers through host buffers, the live per-kernel roofline,
+the CPU baseline, and the clocks seen during the timed region.
+
+`--impl reference` times the reference's arithmetic on the host CPU (the
+numpy oracle restating it; the reference itself needs ttnn and a
+Tenstorrent chip) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "tt-rl_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+MB = 256
+ROLLOUT = 8 * 128
+EPOCHS = 4
+STEPS_PER_UPDATE = EPOCHS * (ROLLOUT // MB)
+SAMPLES_PER_UPDATE = STEPS_PER_UPDATE * MB
+SYNC_EVERY = 50
+PPO_FLOP_PER_SAMPLE = 2 * 24_762_880      # 3F' - conv1 dX, 2 per MAC
+DQN_FLOP_PER_UPDATE = 2 * 43_453_440 * 32
+
+METRIC = "PPO learner samples/sec (Nature-CNN actor-critic, minibatch 256, fwd+bwd+clip+Adam, graph-replayed)"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-dqn", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        try:
+            rows = open(self.path).read().strip().splitlines()
+        except OSError:
+            rows = []
+        for row in rows:
+            f = [x.strip() for x in row.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if self.path:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------ helpers
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+def _rollout(rng):
+    obs = rng.integers(0, 256, (ROLLOUT, 4, 84, 84), dtype=np.uint8)
+    actions = rng.integers(0, 6, ROLLOUT)
+    adv = rng.standard_normal(ROLLOUT).astype(np.float32)
+    returns = rng.standard_normal(ROLLOUT).astype(np.float32)
+    return obs, actions, adv, returns
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------- CPU arms
+
+def cpu_ppo_steps(n_steps: int, seed: int = 0):
+    """The reference's arithmetic on the host (numpy fp32, all BLAS threads):
+    PPO minibatch steps of 256. Returns seconds per step."""
+    from oracle import learner as ref
+    rng = np.random.default_rng(seed)
+    p = ref.nature_params(rng, heads=(("pi", 6), ("v", 1)))
+    x = rng.integers(0, 256, (MB, 84, 84, 4)).astype(np.float32)
+    acts = rng.integers(0, 6, MB)
+    f = lambda: rng.standard_normal(MB).astype(np.float32)  # noqa: E731
+    old, adv, ret, val = f() * 0.1 + np.log(1 / 6), f(), f(), f()
+    state = {}
+    times = []
+    for t in range(1, n_steps + 1):
+        t0 = time.perf_counter()
+        _, _, p, state, _ = ref.ppo_minibatch_step(p, state, t, x, acts, old, adv, ret, val,
+                                                   lr=2.5e-4, eps=1e-8, max_grad_norm=0.5)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    warm = min(args.warmup, 1)
+    steps = max(1, min(args.steps, 3))
+    cpu_ppo_steps(warm)
+    times = cpu_ppo_steps(steps, seed=1)
+    total = sum(times)
+    value = MB * steps / total
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s",
+        "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": 1000 * total / steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded uint8 frames, N(0,1) advantages/returns)",
+        "config": {"workload": "ppo_nature_cnn_minibatch256", "minibatch": MB,
+                   "note": "each reference step is one PPO minibatch step of 256 samples"},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} PPO minibatch steps of 256 (numpy fp32 restatement "
+                                   "of the reference's tape, objective, clip and Adam)"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------- GPU arm
+
+def build_ppo(device, seed):
+    import torch
+    from ttrl_b200.algos.ppo import PPOConfig, PPOLearner, initial_old_logp
+    from ttrl_b200.nets import build_actor_critic
+    np.random.seed(seed)
+    net = build_actor_critic((4, 84, 84), 6, device, batch=MB)
+    learner = PPOLearner(net, ROLLOUT, (4, 84, 84), device,
+                         cfg=PPOConfig(epochs=EPOCHS, minibatch_size=MB), seed=seed)
+    rng = np.random.default_rng(seed)
+    obs, actions, adv, returns = _rollout(rng)
+    old_logp, values = initial_old_logp(net, obs, actions, device)
+    learner.load_rollout(obs, actions, old_logp, values, returns, adv)
+    learner.draw_permutations()
+    torch.cuda.synchronize(device)
+    host = {"obs": obs, "actions": actions.astype(np.int32), "old_logp": old_logp,
+            "values": values, "returns": returns, "adv": adv}
+    return learner, host
+
+
+def kernel_profile(learner, device):
+    """One eager minibatch step with CUDA events around every kernel-family
+    call (on the launching stream): per-call duration and algorithmic FLOPs."""
+    import torch
+    from ttrl_b200.device import context
+    ctx = context(device)
+    records = []
+    ctx.profile = records
+    try:
+        learner._minibatch_step(0)
+        torch.cuda.synchronize(device)
+    finally:
+        ctx.profile = None
+    # roll back the optimizer step this profiling pass took
+    return [(name, flops, s.elapsed_time(e) * 1e-3) for name, flops, s, e in records]
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = _dist()
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        sys.exit(1)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+        group = dist.group.WORLD
+    from ttrl_b200.device import context
+    from ttrl_b200.engine.mesh import ParamSync
+
+    ctx = context(device)
+    seed = 1234 + rank * 1_000_003
+    learner, host = build_ppo(device, seed)
+    sync = ParamSync([learner.net], sync_every=SYNC_EVERY, group=group)
+    # L2 flush buffer (> 126 MB), written by our fill kernel between steps.
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
+
+    def do_flush():
+        ctx.ew("fill", None, None, flush, 0.0)
+
+    # capture + warm-up
+    learner.capture()
+    launches_per_step = learner.launches_per_replay
+    for _ in range(max(args.warmup, 3)):
+        learner.replay()
+    if group is not None:
+        sync.average()
+    torch.cuda.synchronize(device)
+
+    # timed region: K rollout updates, each bracketed by its own events
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    sync_ms = 0.0
+    syncs = 0
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        for k in range(K):
+            do_flush()
+            starts[k].record()
+            learner.replay()
+            if group is not None and (k + 1) % SYNC_EVERY == 0:
+                sync.average()
+                syncs += 1
+            ends[k].record()
+        torch.cuda.synchronize(device)
+    clock = clocks.summary()
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(per_step)
+    if group is not None:
+        import torch.distributed as dist
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    value = SAMPLES_PER_UPDATE * K * world / (total_ms * 1e-3)
+
+    # end to end through host buffers: per step the rollout (pinned host ->
+    # device), fresh permutations, the graph, and the metric read-back.
+    pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory()
+              for k, v in host.items()}
+    E = max(3, min(K, 20))
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values()) + \
+        learner.perm_host.numel() * 4
+    d2h = learner.metric_buf.numel() * 4
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(E):
+        learner.obs.copy_(pinned["obs"], non_blocking=True)
+        learner.actions.copy_(pinned["actions"], non_blocking=True)
+        learner.old_logp.copy_(pinned["old_logp"], non_blocking=True)
+        learner.values.copy_(pinned["values"], non_blocking=True)
+        learner.returns.copy_(pinned["returns"], non_blocking=True)
+        learner.advantages.copy_(pinned["adv"], non_blocking=True)
+        learner.draw_permutations()
+        learner.replay()
+        learner.read_metrics()  # device -> host, synchronises
+    e2e_s = time.perf_counter() - t0
+    if group is not None:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = SAMPLES_PER_UPDATE * E * world / e2e_s
+
+    out = None
+    if rank == 0:
+        peaks = _peaks()
+        # live per-kernel roofline (dominant contraction of one minibatch step)
+        prof = kernel_profile(learner, device)
+        gemms = [r for r in prof if r[1] > 0]
+        dom = max(gemms, key=lambda r: r[2])
+        achieved = dom[1] / dom[2] / 1e12
+        step_tflops = PPO_FLOP_PER_SAMPLE * SAMPLES_PER_UPDATE * K * world / (total_ms * 1e-3) / 1e12
+        out = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": K,
+            "warmup": max(args.warmup, 3), "ms_per_step": total_ms / K,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded uint8 frames U{0..255}, actions U[0,6), advantages and "
+                    "returns N(0,1), old log-probs and values from the initial policy)",
+            "config": {"workload": "ppo_nature_cnn_rollout8x128_mb256_epochs4",
+                       "global_batch": MB * world, "minibatch": MB, "rollout": ROLLOUT,
+                       "epochs": EPOCHS, "grad_steps_per_step": STEPS_PER_UPDATE,
+                       "parallelism": f"dp{world}", "sync_every_updates": SYNC_EVERY,
+                       "syncs_in_timed_region": syncs,
+                       "precision": "split-TF32 tensor cores (tcgen05 kind::tf32 x3), fp32 "
+                                    "accumulate and fp32 elementwise",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "steps": E},
+            "gpu_launches": launches_per_step * K,
+            "gpu_launches_per_step": launches_per_step,
+            "roofline": {
+                "bound": "tensor", "kernel": dom[0], "achieved": achieved,
+                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "peak_source": f"{peaks['source']} dense bf16 (TF32 dense is half; split-TF32 "
+                               "issues 3 MMAs per product)",
+                "whole_step_tflops": step_tflops,
+            },
+            "kernel_times_us": {f"{n}#{i}": round(t * 1e6, 2) for i, (n, _, t) in enumerate(prof)},
+            "clocks": clock,
+        }
+        if world == 1 and not args.no_dqn:
+            out["dqn"] = bench_dqn(device, args)
+        if world == 1 and not args.no_cpu_baseline:
+            times = cpu_ppo_steps(2, seed=2)
+            t = statistics.median(times)
+            out["cpu_baseline"] = {
+                "value": MB / t, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": "2 PPO minibatch steps of 256 (numpy fp32 restatement of the "
+                          "reference's forward, objective, backward, clip and Adam), median"}
+    learner.close()
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+def bench_dqn(device, args):
+    """Nature-DQN batch-32 update (forward x3, double-DQN Huber, backward,
+    grad_sq, Adam) as one graph replay; updates/sec, device time."""
+    import torch
+    from ttrl_b200.algos import dqn
+    from ttrl_b200.device import context
+    from ttrl_b200.engine.optim import Adam
+    from ttrl_b200.engine.step import TrainStep
+    from ttrl_b200.nets import build_q_net
+    np.random.seed(7)
+    online = build_q_net((4, 84, 84), 6, device, batch=32)
+    target = build_q_net((4, 84, 84), 6, device, batch=32)
+    target.copy_from(online)
+    opt = Adam(list(online.parameters()), lr=1e-4, eps=1.5e-4)
+    inputs = dqn.step_inputs((4, 84, 84), device, batch=32, num_actions=6)
+    step = TrainStep(lambda i: dqn.update_loss(online, target, i, num_actions=6, double=True),
+                     inputs, device, optimizer=opt, mode="traced_fwd_bwd")
+    rng = np.random.default_rng(3)
+    obs = rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8)
+    nxt = rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8)
+    act = rng.integers(0, 6, 32)
+    arrays = {"obs": obs, "next_obs": nxt, "actions_onehot": np.eye(6, dtype=np.float32)[act],
+              "rewards": rng.choice([-1.0, 0.0, 1.0], (32, 1)).astype(np.float32),
+              "dones": (rng.random((32, 1)) < 0.01).astype(np.float32),
+              "discounts": np.full((32, 1), 0.99, np.float32)}
+    for k, v in arrays.items():
+        step.load_input(k, v)
+    step.run()
+    launches = step.launches_per_replay
+    for _ in range(10):
+        step.launch()
+    ctx = context(device)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
+    K = max(50, args.steps * 5)
+    s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize(device)
+    for k in range(K):
+        ctx.ew("fill", None, None, flush, 0.0)
+        s[k].record()
+        step.launch()
+        e[k].record()
+    torch.cuda.synchronize(device)
+    ms = sum(a.elapsed_time(b) for a, b in zip(s, e)) / K
+    # end to end: host arrays -> pinned staging -> device, replay, metric read
+    E = 50
+    t0 = time.perf_counter()
+    for _ in range(E):
+        for k, v in arrays.items():
+            step.load_input(k, v)
+        step.run()
+    e2e_ms = (time.perf_counter() - t0) * 1000 / E
+    h2d = sum(v.nbytes for v in arrays.values())
+    step.close()
+    return {"metric": "Nature-DQN batch-32 learner updates/sec (fwd x3 + bwd + Adam, one graph "
+                      "replay per update)",
+            "value": 1000.0 / ms, "unit": "updates/s", "ms_per_update": ms,
+            "e2e": {"value": 1000.0 / e2e_ms, "unit": "updates/s", "ms_per_update": e2e_ms,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 3 * 4},
+            "gpu_launches_per_update": launches,
+            "achieved_tflops": DQN_FLOP_PER_UPDATE / (ms * 1e-3) / 1e12,
+            "target": ">= 5000 updates/s"}
+
+
+def main():
+    args = _args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -59,6 +59,10 @@ const char* ttrl_last_error(void);
 /* ABI version of this library. */
 int ttrl_version(void);
 
+/* Number of kernels this library has enqueued in this process (launches
+ * recorded into a CUDA graph count once, at capture). */
+unsigned long long ttrl_launch_count(void);
+
 /* One-time per-device set-up (kernel attributes, driver entry points).
  * Call once per device, outside any stream capture, before other calls. */
 int ttrl_init(int device);
@@ -74,12 +78,16 @@ enum {
   TTRL_OPND_CONV_WGRAD = 2  /* transposed im2col: r=(ky,kx,c), k=(n,oy,ox) */
 };
 
+/* Operand flag: every value is exactly representable in tf32 (e.g. raw
+ * 0..255 pixel values), so the split-TF32 path needs no low part for it. */
+#define TTRL_OPND_EXACT_TF32 1
+
 typedef struct {
   const void* ptr;
   int32_t kind;
   int32_t rows;   /* extent along the tile-row dimension */
   int32_t kdim;   /* extent along the reduction dimension */
-  int32_t pad0;
+  int32_t flags;  /* TTRL_OPND_* flags */
   int64_t rs, ks; /* DENSE: element strides */
   /* conv geometry (CONV_* kinds): input [n][h][w][c], kernel kh x kw,
    * stride, symmetric zero padding, output oh x ow */
@@ -152,11 +160,16 @@ int ttrl_linear_wgrad(const float* x, const float* g, float* dw, float* db, int 
 
 /* ------------------------------------------------------------------ Conv */
 
+/* Conv flag: the input activation holds values exactly representable in
+ * tf32 (the raw 0..255 frames a first layer reads; its 1/255 is `alpha`). */
+#define TTRL_CONV_INPUT_EXACT 1
+
 typedef struct {
   int32_t n, h, w, c;      /* input, NHWC */
   int32_t cout, kh, kw;    /* kernel */
   int32_t stride, pad;
   int32_t oh, ow;          /* output extent (validated) */
+  int32_t flags;           /* TTRL_CONV_* flags */
 } ttrl_conv_geom;
 
 /* y[N*OH*OW, Cout] = alpha * conv(x, W) (+ b) (then ReLU if relu).

@@ -119,6 +119,7 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
   a.eps = eps;
   a.wd = wd;
   adam_kernel<<<static_cast<unsigned>(chunks), kAdamThreads, 0, st>>>(a);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("adam launch", e);
 }
@@ -214,6 +215,7 @@ int grad_sqnorm(const float* const* grads, const int64_t* numels, int count, flo
   a.out = out;
   a.max_norm = max_norm;
   sqnorm_kernel<<<static_cast<unsigned>(chunks), kSqThreads, 0, st>>>(a);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("grad_sqnorm launch", e);
 }

@@ -1,6 +1,7 @@
 // extern "C" entry points of libttrl_b200.so and the per-thread error text.
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 
 #include "internal.h"
@@ -8,6 +9,9 @@
 namespace ttrl {
 
 static thread_local char g_last_error[512] = "no error";
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -64,6 +68,10 @@ const char* ttrl_last_error(void) { return g_last_error; }
 
 int ttrl_version(void) { return 1; }
 
+unsigned long long ttrl_launch_count(void) {
+  return g_launches.load(std::memory_order_relaxed);
+}
+
 int ttrl_init(int device) {
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return set_cuda_error("cudaSetDevice", e);
@@ -77,7 +85,7 @@ size_t ttrl_gemm_workspace_bytes(const ttrl_gemm_desc* d) {
 int ttrl_gemm(const ttrl_gemm_desc* d, float* workspace, size_t workspace_bytes, int* status,
               ttrl_stream_t stream) {
   if (d == nullptr) return set_error(TTRL_EINVAL, "ttrl_gemm: null descriptor");
-  return gemm_run(*d, 0, no_extra(), workspace, workspace_bytes, status, TTRL_STREAM(stream));
+  return gemm_run_ws(*d, 0, no_extra(), workspace, workspace_bytes, status, TTRL_STREAM(stream));
 }
 
 int ttrl_linear_fwd(const float* x, const float* w, const float* b, float* y, int m, int k, int n,

@@ -56,6 +56,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   return false;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
@@ -224,7 +228,7 @@ __device__ __forceinline__ uint32_t mnmajor_off(int row, int k) {
 // cleared) and the exact fp32 remainder.
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-  lo = isfinite(x) ? x - hi : 0.0f;  // inf/nan travel in the high part only
+  lo = x - hi;
 }
 
 }  // namespace ttrl

@@ -17,6 +17,12 @@ enum : int32_t {
   kModeScalarR = 3   // 4-byte gathers, rows fastest across threads; K-major tile
 };
 
+// n / d by multiply-high and shift, for 0 <= n < 2^31 (Granlund-Montgomery).
+struct FastDiv {
+  uint32_t d, mul, shr, pad0;
+};
+FastDiv make_fastdiv(int d);
+
 struct DevOperand {
   const float* ptr;
   int32_t kind;
@@ -25,8 +31,14 @@ struct DevOperand {
   int64_t rs, ks;
   int32_t n, h, w, c, kh, kw, stride, pad, oh, ow;
   int32_t ones_row;  // row `rows` reads as 1.0 for every valid k
-  int32_t pad0;
+  int32_t exact;     // values exactly representable in tf32: no low part
+  FastDiv f_ohw, f_ow, f_c, f_kw;  // conv index decomposition
 };
+
+// Split-K tile counters live in the first kCounterBytes of every workspace
+// handed to the library; they must be zero before first use and every
+// kernel leaves them zero.
+constexpr size_t kCounterBytes = 64 * 1024;
 
 // Where the synthetic ones row of operand A lands (the bias gradient).
 struct EpiExtra {
@@ -43,18 +55,35 @@ struct GemmArgs {
   int32_t m, n, k;
   int32_t kblocks;
   int32_t kb_per_split;
-  int32_t pad0;
-  float* ws;
+  int32_t reduce_in_kernel;  // last split CTA sums the partials (else a second kernel)
+  float* ws;      // split-K partials [splits][m][n], or null
+  int* counters;  // split-K arrival counter per output tile
   int* status;
 };
 
 int set_error(int code, const char* fmt, ...);
+
+// Host-side count of kernels this library has enqueued (graph captures
+// included), for launch accounting.
+void note_launch();
 int set_cuda_error(const char* what, cudaError_t e);
 
 int gemm_init_device();
 size_t gemm_workspace_bytes(const ttrl_gemm_desc& d);
-int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, float* ws,
-             size_t ws_bytes, int* status, cudaStream_t stream);
+// Launch one GEMM. `counters` (kCounterBytes, zeroed) and `partials` back
+// a split-K schedule; both may be null when K is not split.
+int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* counters,
+             float* partials, size_t partial_bytes, int* status, cudaStream_t stream);
+
+// gemm_run over one caller workspace laid out as [counters | partials].
+inline int gemm_run_ws(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, float* ws,
+                       size_t ws_bytes, int* status, cudaStream_t stream) {
+  const bool ok = ws != nullptr && ws_bytes >= kCounterBytes;
+  return gemm_run(d, a_ones_row, ex, ok ? reinterpret_cast<int*>(ws) : nullptr,
+                  ok ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes)
+                     : nullptr,
+                  ok ? ws_bytes - kCounterBytes : 0, status, stream);
+}
 
 // Fused DQN loss head (ttrl/algos/dqn/losses.py:77-140).
 struct DqnArgs {

@@ -40,6 +40,7 @@ static ttrl_operand conv_operand(const float* p, int kind, const ttrl_conv_geom&
   o.pad = g.pad;
   o.oh = g.oh;
   o.ow = g.ow;
+  if (g.flags & TTRL_CONV_INPUT_EXACT) o.flags |= TTRL_OPND_EXACT_TF32;
   return o;
 }
 
@@ -107,7 +108,7 @@ int linear_fwd(const float* x, const float* w, const float* b, float* y, int m, 
     }
   }
   d.ep.relu = relu;
-  return gemm_run(d, 0, no_extra(), ws, wsb, status, st);
+  return gemm_run_ws(d, 0, no_extra(), ws, wsb, status, st);
 }
 
 int linear_dgrad(const float* g, const float* w, const float* mask, float* dx, int m, int k,
@@ -137,7 +138,7 @@ int linear_dgrad(const float* g, const float* w, const float* mask, float* dx, i
     }
   }
   d.ep.accumulate = accumulate;
-  return gemm_run(d, 0, no_extra(), ws, wsb, status, st);
+  return gemm_run_ws(d, 0, no_extra(), ws, wsb, status, st);
 }
 
 int linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, int k, int n,
@@ -156,7 +157,7 @@ int linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, in
     ex.cs2 = 1;
     ex.accumulate2 = accumulate_db;
   }
-  return gemm_run(d, db ? 1 : 0, ex, ws, wsb, status, st);
+  return gemm_run_ws(d, db ? 1 : 0, ex, ws, wsb, status, st);
 }
 
 // ------------------------------------------------------------------ Conv
@@ -178,7 +179,7 @@ int conv_fprop(const float* x, const float* w, const float* b, float* y, const t
     d.ep.bias_mode = TTRL_BIAS_COL;
   }
   d.ep.relu = relu;
-  return gemm_run(d, 0, no_extra(), ws, wsb, status, st);
+  return gemm_run_ws(d, 0, no_extra(), ws, wsb, status, st);
 }
 
 // dx[n,iy,ix,c] = sum over the kernel taps that saw (iy,ix) of dxcol, in a
@@ -221,7 +222,8 @@ size_t conv_dgrad_ws(const ttrl_conv_geom* g) {
   const size_t kk = static_cast<size_t>(g->kh) * g->kw * g->c;
   ttrl_gemm_desc d = make_desc(static_cast<int>(m), static_cast<int>(kk), g->cout,
                                TTRL_PREC_TF32X3);
-  return m * kk * sizeof(float) + gemm_workspace_bytes(d);
+  // [counters | column buffer | the GEMM's split-K partials]
+  return gemm_workspace_bytes(d) + ((m * kk * sizeof(float) + 255) & ~static_cast<size_t>(255));
 }
 
 int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
@@ -231,25 +233,26 @@ int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
   if (rc) return rc;
   const int m = g->n * g->oh * g->ow;
   const int kk = g->kh * g->kw * g->c;
-  const size_t col_bytes = static_cast<size_t>(m) * kk * sizeof(float);
-  if (ws == nullptr || wsb < col_bytes)
-    return set_error(TTRL_EWORKSPACE, "conv_dgrad: needs %zu bytes of workspace, got %zu",
-                     conv_dgrad_ws(g), wsb);
-  float* dxcol = ws;
+  const size_t need = conv_dgrad_ws(g);
+  if (ws == nullptr || wsb < need)
+    return set_error(TTRL_EWORKSPACE, "conv_dgrad: needs %zu bytes of workspace, got %zu", need,
+                     wsb);
+  const size_t col_bytes =
+      (static_cast<size_t>(m) * kk * sizeof(float) + 255) & ~static_cast<size_t>(255);
+  float* dxcol = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
   ttrl_gemm_desc d = make_desc(m, kk, g->cout, precision);
   d.a = dense(dy, m, g->cout, g->cout, 1);
   d.b = dense(w, kk, g->cout, 1, kk);
   d.ep = epi(dxcol, kk, 1);
-  // The GEMM's own split-K workspace sits after the column buffer (16-byte
-  // aligned since col_bytes is a multiple of 16 for kk % 4 == 0).
-  const size_t off = (col_bytes + 255) & ~static_cast<size_t>(255);
-  float* ws2 = wsb > off ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + off) : nullptr;
-  rc = gemm_run(d, 0, no_extra(), ws2, wsb > off ? wsb - off : 0, status, st);
+  rc = gemm_run(d, 0, no_extra(), reinterpret_cast<int*>(ws),
+                reinterpret_cast<float*>(reinterpret_cast<char*>(dxcol) + col_bytes),
+                wsb - kCounterBytes - col_bytes, status, st);
   if (rc) return rc;
   const long long total = static_cast<long long>(g->n) * g->h * g->w * g->c;
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
   col2im_kernel<<<blocks, 256, 0, st>>>(dxcol, mask, dx, *g, accumulate);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("col2im launch", e);
 }
@@ -281,7 +284,7 @@ int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl
     ex.cs2 = 1;
     ex.accumulate2 = accumulate_db;
   }
-  return gemm_run(d, db ? 1 : 0, ex, ws, wsb, status, st);
+  return gemm_run_ws(d, db ? 1 : 0, ex, ws, wsb, status, st);
 }
 
 // ------------------------------------------------------- frame conversion
@@ -319,6 +322,7 @@ int u8_to_f32(const uint8_t* in, const int32_t* index, float* out, int n, int c,
   int blocks = static_cast<int>((pixels + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
   u8_nchw_to_f32_nhwc_kernel<<<blocks, 256, 0, st>>>(in, index, out, n, c, h, w, scale);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("u8_to_f32 launch", e);
 }

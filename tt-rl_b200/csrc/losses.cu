@@ -117,6 +117,7 @@ int dqn_loss(const DqnArgs& args, cudaStream_t st) {
       !args.discounts || !args.loss || !args.mean_q || !args.dq)
     return set_error(TTRL_EINVAL, "dqn_loss: null pointer");
   dqn_loss_kernel<<<1, kLossThreads, 0, st>>>(args);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("dqn_loss launch", e);
 }
@@ -227,6 +228,7 @@ int ppo_loss(const PpoArgs& args, cudaStream_t st) {
       !args.returns || !args.old_values || !args.metrics || !args.dlogits || !args.dvalue)
     return set_error(TTRL_EINVAL, "ppo_loss: null pointer");
   ppo_loss_kernel<<<1, kLossThreads, 0, st>>>(args);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("ppo_loss launch", e);
 }
@@ -251,6 +253,7 @@ int gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row, 
   if (blocks > 148 * 8) blocks = 148 * 8;
   gather_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint32_t*>(src), idx,
                                             static_cast<uint32_t*>(dst), n, row);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("gather_rows launch", e);
 }

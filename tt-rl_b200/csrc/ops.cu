@@ -98,6 +98,7 @@ int ew(int op, const float* x, const int64_t* xs, const float* y, const int64_t*
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
   ew_kernel<<<blocks, 256, 0, st>>>(a);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("ew launch", e);
 }
@@ -182,10 +183,12 @@ int reduce(int op, const float* in, float* out, int64_t outer, int64_t n, int64_
   const int64_t total = outer * inner;
   if (total < 512 && n >= 1024) {
     reduce_block_kernel<<<static_cast<unsigned>(total), 256, 0, st>>>(op, in, out, n, inner);
+    note_launch();
   } else {
     int blocks = static_cast<int>((total + 255) / 256);
     if (blocks > 148 * 8) blocks = 148 * 8;
     reduce_thread_kernel<<<blocks, 256, 0, st>>>(op, in, out, outer, n, inner);
+    note_launch();
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("reduce launch", e);
@@ -234,6 +237,7 @@ int copy_strided(float* dst, const int64_t* ds, const float* src, const int64_t*
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
   copy_strided_kernel<<<blocks, 256, 0, st>>>(a);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("copy launch", e);
 }
@@ -257,6 +261,7 @@ int polyak(float* dst, const float* src, int64_t n, float tau, cudaStream_t st) 
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
   axpby_kernel<<<blocks, 256, 0, st>>>(dst, src, n, 1.0f - tau, tau);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("polyak launch", e);
 }

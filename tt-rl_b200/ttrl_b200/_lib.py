@@ -47,7 +47,7 @@ class TtrlError(RuntimeError):
 class Operand(ctypes.Structure):
     _fields_ = [
         ("ptr", _vp), ("kind", ctypes.c_int32), ("rows", ctypes.c_int32),
-        ("kdim", ctypes.c_int32), ("pad0", ctypes.c_int32),
+        ("kdim", ctypes.c_int32), ("flags", ctypes.c_int32),
         ("rs", ctypes.c_int64), ("ks", ctypes.c_int64),
         ("n", ctypes.c_int32), ("h", ctypes.c_int32), ("w", ctypes.c_int32),
         ("c", ctypes.c_int32), ("kh", ctypes.c_int32), ("kw", ctypes.c_int32),
@@ -75,7 +75,10 @@ class GemmDesc(ctypes.Structure):
 
 class ConvGeom(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in
-                ("n", "h", "w", "c", "cout", "kh", "kw", "stride", "pad", "oh", "ow")]
+                ("n", "h", "w", "c", "cout", "kh", "kw", "stride", "pad", "oh", "ow", "flags")]
+
+
+CONV_INPUT_EXACT = 1
 
 
 class AdamTensor(ctypes.Structure):
@@ -89,6 +92,7 @@ class AdamTensor(ctypes.Structure):
 _SIGNATURES = {
     "ttrl_last_error": (ctypes.c_char_p, []),
     "ttrl_version": (_c_int, []),
+    "ttrl_launch_count": (ctypes.c_ulonglong, []),
     "ttrl_init": (_c_int, [_c_int]),
     "ttrl_gemm_workspace_bytes": (_c_size, [ctypes.POINTER(GemmDesc)]),
     "ttrl_gemm": (_c_int, [ctypes.POINTER(GemmDesc), _vp, _c_size, _vp, _vp]),

@@ -62,7 +62,9 @@ def obs_to_rows(obs: Tensor) -> Tensor:
     b, c, h, w = obs.shape
     out = torch.empty((1, 1, b * h * w, c), dtype=torch.float32, device=obs.data.device)
     context(obs.data.device).u8_to_f32(obs.data, None, out.reshape(-1, c), 1.0)
-    return Tensor(out, requires_grad=False)
+    rows = Tensor(out, requires_grad=False)
+    rows._exact = True  # raw 0..255 values
+    return rows
 
 
 def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool = True,

@@ -105,6 +105,7 @@ class PPOLearner:
         self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
                                       dtype=torch.float32, device=dev)
         self._graph = None
+        self.launches_per_replay = 0
 
     # -- rollout -----------------------------------------------------------
 
@@ -143,7 +144,9 @@ class PPOLearner:
                           ("returns", self.returns), ("advantages", self.advantages)):
             ctx.gather_rows(src, idx, self.mb_fields[name])
         self.optimizer.zero_grad()
-        logits, value = self.net(Tensor(self.mb_rows))
+        rows = Tensor(self.mb_rows)
+        rows._exact = True  # raw 0..255 frame values
+        logits, value = self.net(rows)
         loss, parts, _ = ppo_objective(
             logits, value, self.mb_actions, self.mb_fields["old_logp"],
             self.mb_fields["advantages"], self.mb_fields["returns"], self.mb_fields["values"],
@@ -188,7 +191,10 @@ class PPOLearner:
             v.copy_(s)
         self.optimizer._dev_steps.copy_(steps_saved)
         self.optimizer.t, self.optimizer.steps = host_steps[0], host_steps[1]
+        from ttrl_b200._lib import lib
+        before = lib().ttrl_launch_count()
         self._graph, _ = capture(self.device, self._update_body)
+        self.launches_per_replay = int(lib().ttrl_launch_count() - before)
 
     def replay(self) -> None:
         """One rollout update (epochs x minibatches gradient steps)."""
@@ -229,7 +235,9 @@ def initial_old_logp(net, obs_u8: np.ndarray, actions: np.ndarray, device, chunk
             if e - s != chunk:
                 raise ValueError("rollout size must be a multiple of the chunk")
             ctx.u8_to_f32(frames[s:e], None, rows.reshape(-1, c), 1.0)
-            logits, value = net(Tensor(rows))
+            x = Tensor(rows)
+            x._exact = True
+            logits, value = net(x)
             lg = logits.numpy().astype(np.float64)
             mx = lg.max(axis=1, keepdims=True)
             lsm = lg - mx - np.log(np.exp(lg - mx).sum(axis=1, keepdims=True))

@@ -32,6 +32,35 @@ PRECISION = _lib.PREC_TF32X3
 _CONTEXTS: dict[int, "DeviceContext"] = {}
 
 
+class _NoProfile:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_PROFILE = _NoProfile()
+
+
+class _Profile:
+    """CUDA events around one library call on the launching stream."""
+
+    def __init__(self, ctx, name, flops):
+        self.ctx, self.name, self.flops = ctx, name, flops
+
+    def __enter__(self):
+        self.start = torch.cuda.Event(enable_timing=True)
+        self.end = torch.cuda.Event(enable_timing=True)
+        self.start.record(torch.cuda.current_stream(self.ctx.device))
+        return self
+
+    def __exit__(self, *exc):
+        self.end.record(torch.cuda.current_stream(self.ctx.device))
+        self.ctx.profile.append((self.name, self.flops, self.start, self.end))
+        return False
+
+
 def _ptr(t) -> int | None:
     if t is None:
         return None
@@ -58,6 +87,7 @@ class Geom:
     kw: int
     stride: int
     pad: int
+    input_exact: bool = False  # input values exactly representable in tf32
 
     @property
     def oh(self) -> int:
@@ -69,7 +99,16 @@ class Geom:
 
     def c_struct(self) -> _lib.ConvGeom:
         return _lib.ConvGeom(self.n, self.h, self.w, self.c, self.cout, self.kh, self.kw,
-                             self.stride, self.pad, self.oh, self.ow)
+                             self.stride, self.pad, self.oh, self.ow,
+                             _lib.CONV_INPUT_EXACT if self.input_exact else 0)
+
+    def with_exact_input(self, exact: bool) -> "Geom":
+        from dataclasses import replace
+        return replace(self, input_exact=bool(exact))
+
+
+def _conv_flops(g: "Geom") -> int:
+    return 2 * g.n * g.oh * g.ow * g.cout * g.kh * g.kw * g.c
 
 
 def conv_geom(n, h, w, c, cout, kh, kw=None, stride=1, pad=0) -> Geom:
@@ -89,7 +128,14 @@ class DeviceContext:
         self._ws = None
         self._ws_bytes = 0
         self._retired: list = []
+        # When a list, every GEMM-family call appends (name, flops, start, end).
+        self.profile = None
         self.reserve(64 << 20)
+
+    def _timed(self, name: str, flops: int = 0):
+        if self.profile is None or torch.cuda.is_current_stream_capturing():
+            return _NO_PROFILE
+        return _Profile(self, name, flops)
 
     # -- workspace -------------------------------------------------------
 
@@ -107,7 +153,9 @@ class DeviceContext:
             )
         size = max(nbytes, 2 * self._ws_bytes)
         size = (size + (1 << 20) - 1) & ~((1 << 20) - 1)
-        buf = torch.empty(size, dtype=torch.uint8, device=self.device)
+        # zeroed: its first 64 KB hold split-K tile counters the kernels
+        # expect at zero (and always leave at zero)
+        buf = torch.zeros(size, dtype=torch.uint8, device=self.device)
         if self._ws is not None:
             self._retired.append(self._ws)
         self._ws = buf
@@ -138,20 +186,22 @@ class DeviceContext:
         m, k = x.shape[-2], x.shape[-1]
         n = w.shape[1]
         ws, wsb = self.workspace()
-        check(lib().ttrl_linear_fwd(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")),
-                                    _ptr(_f32(b, "b")), _ptr(_f32(y, "y")), m, k, n,
-                                    int(relu), precision, ws, wsb, self.status_ptr(),
-                                    self.stream), "ttrl_linear_fwd")
+        with self._timed(f"linear_fwd[{m}x{k}x{n}]", 2 * m * k * n):
+            check(lib().ttrl_linear_fwd(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")),
+                                        _ptr(_f32(b, "b")), _ptr(_f32(y, "y")), m, k, n,
+                                        int(relu), precision, ws, wsb, self.status_ptr(),
+                                        self.stream), "ttrl_linear_fwd")
 
     def linear_dgrad(self, g, w, mask, dx, accumulate: bool,
                      precision: int = PRECISION) -> None:
         m, n = g.shape[-2], g.shape[-1]
         k = w.shape[0]
         ws, wsb = self.workspace()
-        check(lib().ttrl_linear_dgrad(_ptr(_f32(g, "g")), _ptr(_f32(w, "w")),
-                                      _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")), m, k, n,
-                                      int(accumulate), precision, ws, wsb, self.status_ptr(),
-                                      self.stream), "ttrl_linear_dgrad")
+        with self._timed(f"linear_dgrad[{m}x{k}x{n}]", 2 * m * k * n):
+            check(lib().ttrl_linear_dgrad(_ptr(_f32(g, "g")), _ptr(_f32(w, "w")),
+                                          _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")), m, k, n,
+                                          int(accumulate), precision, ws, wsb, self.status_ptr(),
+                                          self.stream), "ttrl_linear_dgrad")
 
     def linear_wgrad(self, x, g, dw, db, accumulate: bool, accumulate_db: bool,
                      precision: int = PRECISION) -> None:
@@ -161,10 +211,11 @@ class DeviceContext:
         desc.m, desc.n, desc.k, desc.precision = k + (1 if db is not None else 0), n, m, precision
         need = lib().ttrl_gemm_workspace_bytes(ctypes.byref(desc))
         ws, wsb = self.workspace(need)
-        check(lib().ttrl_linear_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(g, "g")),
-                                      _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), m, k, n,
-                                      int(accumulate), int(accumulate_db), precision, ws, wsb,
-                                      self.status_ptr(), self.stream), "ttrl_linear_wgrad")
+        with self._timed(f"linear_wgrad[{m}x{k}x{n}]", 2 * m * k * n):
+            check(lib().ttrl_linear_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(g, "g")),
+                                          _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), m, k, n,
+                                          int(accumulate), int(accumulate_db), precision, ws, wsb,
+                                          self.status_ptr(), self.stream), "ttrl_linear_wgrad")
 
     # -- conv ------------------------------------------------------------
 
@@ -172,31 +223,37 @@ class DeviceContext:
                    precision: int = PRECISION) -> None:
         g = geom.c_struct()
         ws, wsb = self.workspace()
-        check(lib().ttrl_conv_fprop(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")), _ptr(_f32(b, "b")),
-                                    _ptr(_f32(y, "y")), ctypes.byref(g), float(alpha),
-                                    int(relu), precision, ws, wsb, self.status_ptr(),
-                                    self.stream), "ttrl_conv_fprop")
+        with self._timed(f"conv_fprop[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom)):
+            check(lib().ttrl_conv_fprop(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")), _ptr(_f32(b, "b")),
+                                        _ptr(_f32(y, "y")), ctypes.byref(g), float(alpha),
+                                        int(relu), precision, ws, wsb, self.status_ptr(),
+                                        self.stream), "ttrl_conv_fprop")
 
     def conv_dgrad(self, dy, w, mask, dx, geom: Geom, accumulate: bool,
                    precision: int = PRECISION) -> None:
         g = geom.c_struct()
         need = lib().ttrl_conv_dgrad_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
-        check(lib().ttrl_conv_dgrad(_ptr(_f32(dy, "dy")), _ptr(_f32(w, "w")),
-                                    _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
-                                    ctypes.byref(g), int(accumulate), precision, ws, wsb,
-                                    self.status_ptr(), self.stream), "ttrl_conv_dgrad")
+        with self._timed(f"conv_dgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom)):
+            check(lib().ttrl_conv_dgrad(_ptr(_f32(dy, "dy")), _ptr(_f32(w, "w")),
+                                        _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
+                                        ctypes.byref(g), int(accumulate), precision, ws, wsb,
+                                        self.status_ptr(), self.stream), "ttrl_conv_dgrad")
 
     def conv_wgrad(self, x, dy, dw, db, geom: Geom, alpha: float, accumulate: bool,
                    accumulate_db: bool, precision: int = PRECISION) -> None:
         g = geom.c_struct()
         need = lib().ttrl_conv_wgrad_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
-        check(lib().ttrl_conv_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(dy, "dy")),
-                                    _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), ctypes.byref(g),
-                                    float(alpha), int(accumulate), int(accumulate_db),
-                                    precision, ws, wsb, self.status_ptr(), self.stream),
-              "ttrl_conv_wgrad")
+        with self._timed(f"conv_wgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom)):
+            check(lib().ttrl_conv_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(dy, "dy")),
+                                        _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), ctypes.byref(g),
+                                        float(alpha), int(accumulate), int(accumulate_db),
+                                        precision, ws, wsb, self.status_ptr(), self.stream),
+                  "ttrl_conv_wgrad")
 
     def u8_to_f32(self, frames, index, out, scale: float = 1.0) -> None:
         if frames.dtype != torch.uint8 or frames.dim() != 4:

@@ -88,7 +88,8 @@ class Tensor:
     """A node in the autograd graph, backed by a CUDA tensor."""
 
     __slots__ = ("data", "requires_grad", "grad", "_backward", "_parents", "_op",
-                 "_backward_done", "_premask", "_grad_buf", "_grad_owned", "__weakref__")
+                 "_backward_done", "_premask", "_grad_buf", "_grad_owned", "_exact",
+                 "__weakref__")
 
     def __init__(self, data, requires_grad: bool = False, _parents=(), _op: str = ""):
         self.data = data
@@ -101,6 +102,9 @@ class Tensor:
         self._premask = False
         self._grad_buf = None
         self._grad_owned = False
+        # Every value is exactly representable in tf32 (raw 0..255 pixels):
+        # a convolution reading it skips the split-TF32 low part.
+        self._exact = False
 
     # -- construction ------------------------------------------------------
 

@@ -476,6 +476,8 @@ def conv2d_nhwc(x: Tensor, w: Tensor, b: Tensor | None, geom, *, input_scale: fl
     xd = x.data.reshape(-1, geom.c)
     if not xd.is_contiguous():
         xd = xd.contiguous()
+    if x._exact:
+        geom = geom.with_exact_input(True)
     rows = geom.n * geom.oh * geom.ow
     y = _new((1, 1, rows, geom.cout), xd)
     ctx = _ctx(xd)

@@ -150,6 +150,7 @@ class TrainStep:
         self._trace = None
         self._pack: MetricPack | None = None
         self._captured_grads: list = []
+        self.launches_per_replay = 0
 
     def load_input(self, name: str, array) -> None:
         self._binder.load(name, array)
@@ -199,7 +200,10 @@ class TrainStep:
         self.step_fn(self.inputs)
         if self.optimizer is not None:
             self.optimizer.zero_grad()
+        from ttrl_b200._lib import lib
+        before = lib().ttrl_launch_count()
         self._trace, self._pack = capture(self.device, self._record)
+        self.launches_per_replay = int(lib().ttrl_launch_count() - before)
         if self.optimizer is not None:
             self._captured_grads = [(p, p.grad) for p in self.optimizer.params]
         # Capture only records: run it once so this first call is a real step.

@@ -1,0 +1,93 @@
+"""Small, self-contained kernel cases for profiling (`ncu -k ... python -m
+ttrl_b200.profile_case <case>`): each case builds seeded inputs of the
+Nature-CNN shapes and launches one kernel family a few times.
+
+    python -m ttrl_b200.profile_case conv1_fprop --batch 256 --reps 3
+    python -m ttrl_b200.profile_case dqn_update --reps 3
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import numpy as np
+import torch
+
+from ttrl_b200.device import context, conv_geom
+
+CONV = {"conv1": (84, 4, 32, 8, 4), "conv2": (20, 32, 64, 4, 2), "conv3": (9, 64, 64, 3, 1)}
+
+
+def _conv_case(layer: str, kind: str, batch: int, reps: int) -> None:
+    hw, c, co, k, s = CONV[layer]
+    g = conv_geom(batch, hw, hw, c, co, k, k, s, 0)
+    rng = np.random.default_rng(0)
+    dev = torch.device("cuda", 0)
+    x = torch.from_numpy(rng.standard_normal((batch * hw * hw, c)).astype(np.float32)).to(dev)
+    w = torch.from_numpy(rng.standard_normal((co, k, k, c)).astype(np.float32)).to(dev)
+    b = torch.zeros(co, device=dev)
+    y = torch.empty((batch * g.oh * g.ow, co), device=dev)
+    ctx = context(dev)
+    for _ in range(reps):
+        if kind == "fprop":
+            ctx.conv_fprop(x, w, b, y, g, 1.0, True)
+        elif kind == "dgrad":
+            ctx.conv_dgrad(y, w, x, torch.empty_like(x), g, False)
+        else:
+            ctx.conv_wgrad(x, y, torch.empty_like(w), b, g, 1.0, False, False)
+    torch.cuda.synchronize()
+
+
+def _linear_case(reps: int, batch: int) -> None:
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy(rng.standard_normal((batch, 3136)).astype(np.float32)).to(dev)
+    w = torch.from_numpy(rng.standard_normal((3136, 512)).astype(np.float32)).to(dev)
+    b = torch.zeros(512, device=dev)
+    y = torch.empty((batch, 512), device=dev)
+    ctx = context(dev)
+    for _ in range(reps):
+        ctx.linear_fwd(x, w, b, y, True)
+    torch.cuda.synchronize()
+
+
+def _dqn_case(reps: int) -> None:
+    from ttrl_b200.algos import dqn
+    from ttrl_b200.engine.optim import Adam
+    from ttrl_b200.engine.step import TrainStep
+    from ttrl_b200.nets import build_q_net
+    np.random.seed(0)
+    online = build_q_net((4, 84, 84), 6, "cuda", batch=32)
+    target = build_q_net((4, 84, 84), 6, "cuda", batch=32)
+    opt = Adam(list(online.parameters()), lr=1e-4, eps=1.5e-4)
+    inputs = dqn.step_inputs((4, 84, 84), "cuda", batch=32, num_actions=6)
+    step = TrainStep(lambda i: dqn.update_loss(online, target, i, num_actions=6), inputs,
+                     "cuda", optimizer=opt, mode="traced_fwd_bwd")
+    rng = np.random.default_rng(1)
+    step.load_input("obs", rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8))
+    step.load_input("next_obs", rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8))
+    step.load_input("actions_onehot", np.eye(6, dtype=np.float32)[rng.integers(0, 6, 32)])
+    for _ in range(reps):
+        step.launch()
+    torch.cuda.synchronize()
+    step.close()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    if a.case == "dqn_update":
+        _dqn_case(a.reps)
+        return
+    if a.case == "fc1_fwd":
+        _linear_case(a.reps, a.batch)
+        return
+    layer, kind = a.case.split("_")
+    _conv_case(layer, kind, a.batch, a.reps)
+
+
+if __name__ == "__main__":
+    main()
