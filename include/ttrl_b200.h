@@ -142,6 +142,25 @@ int ttrl_linear_fwd(const float* x, const float* w, const float* b, float* y, in
                     int n, int relu, int precision, float* workspace, size_t workspace_bytes,
                     int* status, ttrl_stream_t stream);
 
+/* Fixed scratch size of ttrl_linear_fwd_noalloc: 64 KB of split-K counters
+ * plus partial sums. */
+#define TTRL_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* ttrl_linear_fwd without a workspace argument, for callers that cannot
+ * allocate device memory (a C host that owns no memory pool, or a loop that
+ * must not let cudaMalloc synchronise the device). It has no counterpart in
+ * the reference. Its split-K scratch is a fixed array of
+ * TTRL_NOALLOC_SCRATCH_BYTES inside this library, one per device, and it
+ * calls no allocating routine. Shapes whose split-K scratch exceeds that
+ * size are refused with TTRL_EWORKSPACE before anything is enqueued. The
+ * array is shared by every call on the device: calls issued to one stream
+ * are safe, calls whose GPU work overlaps race and may give wrong results.
+ * Output is bit-identical to ttrl_linear_fwd on the same inputs. Uses the
+ * current device. */
+int ttrl_linear_fwd_noalloc(const float* x, const float* w, const float* b, float* y, int m,
+                            int k, int n, int relu, int precision, int* status,
+                            ttrl_stream_t stream);
+
 /* dx[M,K] (=|+=) (g[M,N] @ W[K,N]^T) masked by (mask > 0) when mask != NULL.
  * Replaces matmul's dA = g @ b^T (ttrl/engine/ops/matmul.py:79-81) and the
  * relu_bw of the layer below it. */

@@ -98,6 +98,8 @@ _SIGNATURES = {
     "ttrl_gemm": (_c_int, [ctypes.POINTER(GemmDesc), _vp, _c_size, _vp, _vp]),
     "ttrl_linear_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                  _vp, _c_size, _vp, _vp]),
+    "ttrl_linear_fwd_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                         _c_int, _vp, _vp]),
     "ttrl_linear_dgrad": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                    _vp, _c_size, _vp, _vp]),
     "ttrl_linear_wgrad": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
