@@ -13,7 +13,7 @@ import numpy as np
 
 __all__ = [
     "conv_out", "conv2d_nhwc", "conv2d_dgrad", "conv2d_wgrad", "oihw_to_krsc", "krsc_to_oihw",
-    "linear", "adam_fused_scalars", "adam_step_sv", "relu",
+    "linear", "linear_backward", "adam_fused_scalars", "adam_step_sv", "relu",
 ]
 
 
@@ -126,6 +126,14 @@ def linear(x, w, b=None):
     if b is not None:
         y = y + np.asarray(b).reshape(1, -1)
     return y
+
+
+def linear_backward(x, w, dy):
+    """(dx, dW, db) of y = x @ W + b: dx = dy W^T, dW = x^T dy, db = sum
+    over rows (ttrl/engine/ops/matmul.py:72-84, broadcast.py:11-30)."""
+    x = np.asarray(x)
+    dy = np.asarray(dy)
+    return dy @ np.asarray(w).T, x.T @ dy, dy.sum(axis=0, keepdims=True)
 
 
 def adam_fused_scalars(lr, b1, b2, eps, t):

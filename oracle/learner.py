@@ -27,7 +27,7 @@ from oracle.layers import (adam_step_sv, conv2d_dgrad, conv2d_nhwc, conv2d_wgrad
 
 __all__ = ["NATURE", "nature_params", "nature_forward", "nature_backward", "huber_grad",
            "dqn_loss_head", "dqn_update", "ppo_objective_and_grads", "ppo_minibatch_step",
-           "log_softmax"]
+           "log_softmax", "clip_grad_norm_scale", "sigmoid", "gru_cell_forward", "gru_cell_backward"]
 
 #: (out_channels, kernel, stride) of ttrl/nets/towers.py:40.
 NATURE = ((32, 8, 4), (64, 4, 2), (64, 3, 1))
@@ -154,6 +154,13 @@ def dqn_update(online, target, obs, next_obs, actions, rewards, dones, discounts
     return metrics, grads, new_params, new_state
 
 
+def clip_grad_norm_scale(grads, max_norm):
+    """(norm, scale) of ttrl/algos/grads.py:13-43: the f64 global L2 norm,
+    and max_norm / (norm + 1e-6) when norm > max_norm, else None."""
+    norm = float(np.sqrt(sum(float(np.sum(np.asarray(g, np.float64) ** 2)) for g in grads)))
+    return norm, (max_norm / (norm + 1e-6) if norm > max_norm else None)
+
+
 def log_softmax(x):
     m = x.max(axis=1, keepdims=True)
     sh = x - m
@@ -161,9 +168,17 @@ def log_softmax(x):
 
 
 def ppo_objective_and_grads(logits, value, actions, old_logp, adv, returns, old_values, *,
-                            clip=0.1, vclip=0.1, vcoef=0.5, entcoef=0.01):
-    """PPO's loss terms and d loss / d (logits, value), mean reduction."""
+                            clip=0.1, vclip=0.1, vcoef=0.5, entcoef=0.01, valid=None):
+    """PPO's loss terms and d loss / d (logits, value)
+    (ttrl/algos/ppo/loss.py:42-83). The reduction is the mean, or with
+    `valid` the masked mean sum(x * valid) / sum(valid) of
+    ttrl/algos/ppo/loss.py:27-39."""
     b = logits.shape[0]
+    if valid is None:
+        w = np.full(b, 1.0 / b)
+    else:
+        valid = np.asarray(valid, np.float64).reshape(-1)
+        w = valid / valid.sum()
     lsm = log_softmax(logits)
     p = np.exp(lsm)
     new_logp = lsm[np.arange(b), actions]
@@ -173,26 +188,26 @@ def ppo_objective_and_grads(logits, value, actions, old_logp, adv, returns, old_
     cl = np.clip(ratio, 1 - clip, 1 + clip)
     s2 = cl * adv
     surr = np.minimum(s1, s2)
-    policy_loss = -surr.mean()
+    policy_loss = -(surr * w).sum()
     v = value.reshape(-1)
     vcl = old_values + np.clip(v - old_values, -vclip, vclip)
     ue, ce = v - returns, vcl - returns
     vmax = np.maximum(ue * ue, ce * ce)
-    value_loss = 0.5 * vmax.mean()
-    entropy = ent.mean()
+    value_loss = 0.5 * (vmax * w).sum()
+    entropy = (ent * w).sum()
     loss = policy_loss + vcoef * value_loss - entcoef * entropy
     # gradients; min/max/clamp follow the relu identities: ties go to the
     # first operand, clamp passes strictly inside the band.
-    g_s = -1.0 / b
+    g_s = -w
     take2 = (s1 - s2) > 0
     pass_c = (ratio > 1 - clip) & (ratio < 1 + clip)
     dratio = np.where(take2, 0.0, g_s * adv) + np.where(take2, g_s * adv * pass_c, 0.0)
     dnl = dratio * ratio
-    gv = vcoef * 0.5 / b
+    gv = vcoef * 0.5 * w
     takeb = (ce * ce - ue * ue) > 0
     vpass = (v - old_values > -vclip) & (v - old_values < vclip)
     dv = np.where(takeb, 0.0, 2 * gv * ue) + np.where(takeb, 2 * gv * ce * vpass, 0.0)
-    ge = -entcoef / b
+    ge = (-entcoef * w)[:, None]
     onehot = np.zeros_like(logits)
     onehot[np.arange(b), actions] = 1.0
     dlogits = dnl[:, None] * (onehot - p) + ge * (-p * (lsm + ent[:, None]))
@@ -218,3 +233,44 @@ def ppo_minibatch_step(params, adam_state, t, x_nhwc, actions, old_logp, adv, re
         new_state[k] = (S, V)
     metrics = dict(parts, loss=loss, grad_norm=norm)
     return metrics, grads, new_params, new_state, new_logp
+
+
+def sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def gru_cell_forward(x, h, w_ih, w_hh, b_ih, b_hh):
+    """One GRU step, gates in (reset, update, candidate) order with W stored
+    (in, 3H) (ttrl/engine/recurrent.py:86-94):
+        r = sig(x Wr + br + h Ur + cr), z = sig(x Wz + bz + h Uz + cz),
+        n = tanh(x Wn + bn + r * (h Un + cn)), h' = (1 - z) n + z h.
+    Returns (h', cache)."""
+    H = h.shape[1]
+    gi = x @ w_ih + b_ih.reshape(1, -1)
+    gh = h @ w_hh + b_hh.reshape(1, -1)
+    r = sigmoid(gi[:, :H] + gh[:, :H])
+    z = sigmoid(gi[:, H:2 * H] + gh[:, H:2 * H])
+    n = np.tanh(gi[:, 2 * H:] + r * gh[:, 2 * H:])
+    h1 = (1.0 - z) * n + z * h
+    return h1, {"x": x, "h": h, "r": r, "z": z, "n": n, "ghn": gh[:, 2 * H:]}
+
+
+def gru_cell_backward(dh1, cache, w_ih, w_hh):
+    """Gradients of one GRU step given d h'. Returns a dict with dx, dh and
+    the four parameter gradients (biases as (1, 3H))."""
+    x, h, r, z, n, ghn = (cache[k] for k in ("x", "h", "r", "z", "n", "ghn"))
+    dn = dh1 * (1.0 - z)
+    dz = dh1 * (h - n)
+    dh = dh1 * z
+    dan = dn * (1.0 - n * n)          # d pre-tanh
+    dr = dan * ghn
+    dghn = dan * r
+    dar = dr * r * (1.0 - r)
+    daz = dz * z * (1.0 - z)
+    dgi = np.concatenate([dar, daz, dan], axis=1)
+    dgh = np.concatenate([dar, daz, dghn], axis=1)
+    return {
+        "dx": dgi @ w_ih.T, "dh": dh + dgh @ w_hh.T,
+        "weight_ih": x.T @ dgi, "weight_hh": h.T @ dgh,
+        "bias_ih": dgi.sum(0, keepdims=True), "bias_hh": dgh.sum(0, keepdims=True),
+    }

@@ -1,0 +1,397 @@
+"""Generate the golden vectors under tests/golden/ from the reference itself.
+
+Run in a container that has the reference checkout (its path is the first
+argument, or TTRL_REFERENCE):
+
+    python tests/golden/make_golden.py /path/to/tt-rl
+
+The reference's device code imports `ttnn` at module scope; this script
+installs `ttnn_numpy` (a float32 numpy stand-in) under that name first, so
+the reference's OWN autograd tape (ttrl/engine/autograd.py), ops
+(ttrl/engine/ops/*), Adam (ttrl/engine/optim/adam.py), Linear
+(ttrl/engine/layers.py), GRU (ttrl/engine/recurrent.py), gradient clipping
+(ttrl/algos/grads.py), DQN update body (ttrl/algos/dqn/losses.py:77-140), PPO
+objective (ttrl/algos/ppo/loss.py:42-83) and ParamSync
+(ttrl/engine/mesh/sync.py) run unchanged. Modules that are pure numpy/Python
+run as they are: adam_fused_scalars (ttrl/engine/optim/scalars.py:13-27), the
+deploy conv tower (ttrl/deploy/conv.py:31-50) and conv geometry
+(ttrl/engine/conv/geometry.py).
+
+Outputs (all seeded, small): one .npz per case family plus index.json. The
+tests never import the reference; they read these files.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from types import SimpleNamespace
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _install(reference: str):
+    sys.path.insert(0, HERE)
+    import ttnn_numpy
+    sys.modules["ttnn"] = ttnn_numpy
+    sys.path.insert(0, reference)
+    return ttnn_numpy
+
+
+def _save(name: str, arrays: dict, index: dict, note: str) -> None:
+    path = os.path.join(HERE, f"{name}.npz")
+    np.savez_compressed(path, **{k: np.asarray(v) for k, v in arrays.items()})
+    index[name] = {"note": note, "keys": sorted(arrays)}
+
+
+def adam_scalars(index):
+    from ttrl.engine.optim.scalars import adam_fused_scalars
+    rows = []
+    for lr, b1, b2, eps in [(1e-4, 0.9, 0.999, 1.5e-4), (2.5e-4, 0.9, 0.999, 1e-8),
+                            (3e-4, 0.9, 0.999, 1e-8), (1e-3, 0.5, 0.9, 1e-5)]:
+        for t in (1, 2, 3, 10, 100, 1000, 8000, 100000):
+            a, e = adam_fused_scalars(lr, b1, b2, eps, t)
+            rows.append([lr, b1, b2, eps, t, a, e])
+    _save("adam_scalars", {"rows": np.array(rows, np.float64)}, index,
+          "ttrl/engine/optim/scalars.py:13-27: (lr,b1,b2,eps,t) -> (alpha_t, eps_t)")
+
+
+def adam_steps(index):
+    from ttrl.engine.autograd import Tensor
+    from ttrl.engine.optim.adam import Adam
+    import ttnn
+    out = {}
+    for case, (lr, eps, wd) in enumerate([(1e-4, 1.5e-4, 0.0), (2.5e-4, 1e-8, 0.0),
+                                          (1e-3, 1e-8, 0.01)]):
+        rng = np.random.default_rng(100 + case)
+        shapes = [(37,), (5, 7), (64, 3)]
+        init = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+        params = [Tensor.from_numpy(a, ttnn.DEVICE, requires_grad=True) for a in init]
+        opt = Adam(params, lr=lr, eps=eps, weight_decay=wd)
+        grads = []
+        for step in range(6):
+            g_step = [rng.standard_normal(s).astype(np.float32) * (0.1 + step) for s in shapes]
+            for i, p in enumerate(params):
+                # Parameter 1 gets no gradient on step 2: its own step count lags.
+                p.grad = None if (i == 1 and step == 2) else ttnn.Tensor(g_step[i])
+            grads.append(g_step)
+            opt.step()
+        pre = f"c{case}_"
+        out[pre + "hyper"] = np.array([lr, eps, wd], np.float64)
+        for i in range(len(shapes)):
+            out[pre + f"p{i}_init"] = init[i]
+            out[pre + f"p{i}_grads"] = np.stack([g[i] for g in grads])
+            out[pre + f"p{i}_final"] = params[i].numpy()
+            out[pre + f"p{i}_S"] = opt.m[i].to_numpy()
+            out[pre + f"p{i}_V"] = opt.v[i].to_numpy()
+        out[pre + "steps"] = np.array(opt.steps, np.int64)
+    _save("adam_steps", out, index,
+          "ttrl/engine/optim/adam.py:93-134 over 6 steps; param 1 has no grad on step 2")
+
+
+class _FakeQNet:
+    """Stands in for a Q network: returns preset Q tensors in call order
+    (online(obs), target(next_obs), online(next_obs)) and exposes the
+    online(obs) leaf as its only parameter."""
+
+    def __init__(self, outputs):
+        self.outputs = list(outputs)
+        self.calls = 0
+
+    def __call__(self, obs):
+        q = self.outputs[self.calls]
+        self.calls += 1
+        return q
+
+    def parameters(self):
+        return [self.outputs[0]]
+
+
+def dqn_loss(index):
+    from ttrl.algos.dqn.losses import update_loss
+    from ttrl.engine.autograd import Tensor
+    import ttnn
+    out = {}
+    variants = [("vanilla", False, 0, False), ("double", True, 0, False),
+                ("double_mask", True, 6, False), ("double_per", True, 0, True)]
+    for v, (name, double, mask_n, per) in enumerate(variants):
+        rng = np.random.default_rng(200 + v)
+        B, A = 32, 6
+        q = rng.standard_normal((B, A)).astype(np.float32)
+        q_next_online = rng.standard_normal((B, A)).astype(np.float32)
+        q_next_target = (q_next_online + 0.3 * rng.standard_normal((B, A))).astype(np.float32)
+        actions = rng.integers(0, A, B)
+        onehot = np.eye(A, dtype=np.float32)[actions]
+        rewards = rng.choice([-1.0, 0.0, 1.0], B).astype(np.float32).reshape(B, 1)
+        dones = (rng.random(B) < 0.1).astype(np.float32).reshape(B, 1)
+        discounts = np.where(rng.random(B) < 0.2, 0.99 ** 2, 0.99).astype(np.float32).reshape(B, 1)
+        # Large errors on a few rows exercise Huber's linear branch.
+        rewards[:4] *= 5.0
+        dev = ttnn.DEVICE
+        q_leaf = Tensor.from_numpy(q, dev, requires_grad=True)
+        online = _FakeQNet([q_leaf, None])
+        qn_online = Tensor.from_numpy(q_next_online, dev)
+        qn_target = Tensor.from_numpy(q_next_target, dev)
+        # call order inside update_loss: online(obs), target(next), online(next)
+        online.outputs[1] = qn_online
+        target = _FakeQNet([qn_target])
+        inputs = {
+            "rewards": Tensor.from_numpy(rewards, dev),
+            "dones": Tensor.from_numpy(dones, dev),
+            "discounts": Tensor.from_numpy(discounts, dev),
+            "actions_onehot": Tensor.from_numpy(onehot, dev),
+            "obs.x": Tensor.from_numpy(np.zeros((B, 1), np.float32), dev),
+            "next_obs.x": Tensor.from_numpy(np.zeros((B, 1), np.float32), dev),
+        }
+        mask = np.ones((B, A), np.float32)
+        if mask_n:
+            mask = (rng.random((B, A)) < 0.7).astype(np.float32)
+            mask[np.arange(B), rng.integers(0, A, B)] = 1.0  # at least one legal
+            inputs["next_mask"] = Tensor.from_numpy(mask, dev)
+        isw = np.ones((B, 1), np.float32)
+        if per:
+            isw = rng.uniform(0.2, 1.0, (B, 1)).astype(np.float32)
+            inputs["is_weights"] = Tensor.from_numpy(isw, dev)
+        metrics = update_loss(online, target, inputs, leaves=("x",), num_actions=A,
+                              mask_n=mask_n, double=double, huber_delta=1.0, prioritized=per)
+        pre = f"{name}_"
+        out.update({pre + "q": q, pre + "q_next_online": q_next_online,
+                    pre + "q_next_target": q_next_target, pre + "onehot": onehot,
+                    pre + "rewards": rewards, pre + "dones": dones,
+                    pre + "discounts": discounts, pre + "next_mask": mask,
+                    pre + "is_weights": isw,
+                    pre + "flags": np.array([int(double), mask_n, int(per)], np.int64),
+                    pre + "loss": metrics["loss"].numpy(),
+                    pre + "mean_q": metrics["mean_q"].numpy(),
+                    pre + "grad_sq": metrics["grad_sq"].numpy(),
+                    pre + "dq": q_leaf.grad.to_numpy()})
+        if per:
+            out[pre + "td_abs"] = metrics["td_abs"].numpy()
+    _save("dqn_loss", out, index,
+          "ttrl/algos/dqn/losses.py:77-140 with preset Q tensors (B=32, A=6, delta=1)")
+
+
+def ppo_objective(index):
+    from ttrl.algos.ppo.loss import masked_mean, objective
+    from ttrl.algos.ppo.policy import CategoricalPolicy
+    from ttrl.engine.autograd import Tensor
+    from ttrl.engine.ops import mean_all
+    import ttnn
+    out = {}
+    for v, name in enumerate(("mean", "masked")):
+        rng = np.random.default_rng(300 + v)
+        B, A = 256, 6
+        logits = (rng.standard_normal((B, A)) * 1.5).astype(np.float32)
+        value = rng.standard_normal((B, 1)).astype(np.float32)
+        actions = rng.integers(0, A, B)
+        # old log-probs near the current ones, so the ratio hits both clip sides
+        lsm = logits - logits.max(1, keepdims=True)
+        lsm = lsm - np.log(np.exp(lsm).sum(1, keepdims=True))
+        old_logp = (lsm[np.arange(B), actions] + 0.2 * rng.standard_normal(B)).astype(np.float32)
+        adv = rng.standard_normal(B).astype(np.float32)
+        returns = rng.standard_normal(B).astype(np.float32)
+        old_values = (value.reshape(-1) + 0.3 * rng.standard_normal(B)).astype(np.float32)
+        valid = np.ones(B, np.float32)
+        dev = ttnn.DEVICE
+        lg = Tensor.from_numpy(logits, dev, requires_grad=True)
+        val = Tensor.from_numpy(value, dev, requires_grad=True)
+        batch = SimpleNamespace(old_logp=old_logp, actions=actions, mask=None,
+                                advantages=adv, returns=returns, values=old_values)
+        cfg = SimpleNamespace(clip_eps=0.1, value_clip_eps=0.1, value_coef=0.5,
+                              entropy_coef=0.01)
+        if name == "masked":
+            valid = (rng.random(B) < 0.8).astype(np.float32)
+            reduce = masked_mean(Tensor.from_numpy(valid.reshape(B, 1), dev))
+        else:
+            reduce = mean_all
+        policy = CategoricalPolicy(SimpleNamespace(n=A), dev)
+        loss, parts, new_logp = objective(policy, lg, val, batch, cfg, dev, reduce=reduce)
+        loss.backward()
+        pre = f"{name}_"
+        out.update({pre + "logits": logits, pre + "value": value,
+                    pre + "actions": actions.astype(np.int64), pre + "old_logp": old_logp,
+                    pre + "adv": adv, pre + "returns": returns,
+                    pre + "old_values": old_values, pre + "valid": valid,
+                    pre + "loss": loss.numpy(),
+                    pre + "policy_loss": parts["policy_loss"].numpy(),
+                    pre + "value_loss": parts["value_loss"].numpy(),
+                    pre + "entropy": parts["entropy"].numpy(),
+                    pre + "new_logp": new_logp.numpy(),
+                    pre + "dlogits": lg.grad.to_numpy(), pre + "dvalue": val.grad.to_numpy()})
+    _save("ppo_objective", out, index,
+          "ttrl/algos/ppo/loss.py:42-83 (clip 0.1, vclip 0.1, vf 0.5, ent 0.01), B=256, A=6")
+
+
+def linear_mlp(index):
+    from ttrl.engine.autograd import Tensor
+    from ttrl.engine.layers import Flatten, Linear
+    from ttrl.engine.ops import mean_all, mul, relu
+    import ttnn
+    np.random.seed(400)
+    dev = ttnn.DEVICE
+    B = 4
+    fc1 = Linear(3 * 3 * 16, 32, dev)
+    fc2 = Linear(32, 6, dev)
+    rng = np.random.default_rng(401)
+    x_nhwc = rng.uniform(0, 2, (B, 3, 3, 16)).astype(np.float32)
+    upstream = rng.standard_normal((B, 6)).astype(np.float32)
+    x = Tensor.from_numpy(x_nhwc.reshape(1, 1, B * 9, 16), dev, requires_grad=True)
+    flat = Flatten(3, 3, 16)(x)
+    h = relu(fc1(flat))
+    y = fc2(h)
+    # mean(y * G) * B*6 seeds dy = G (the tape's seed is 1.0)
+    loss = mul(mean_all(mul(y, Tensor.from_numpy(upstream, dev))), float(B * 6))
+    loss.backward()
+    _save("linear_mlp", {
+        "x_nhwc": x_nhwc, "upstream": upstream,
+        "w1": fc1.weight.numpy(), "b1": fc1.bias.numpy(),
+        "w2": fc2.weight.numpy(), "b2": fc2.bias.numpy(),
+        "y": y.numpy(), "dw1": fc1.weight.grad.to_numpy(), "db1": fc1.bias.grad.to_numpy(),
+        "dw2": fc2.weight.grad.to_numpy(), "db2": fc2.bias.grad.to_numpy(),
+        "dx": x.grad.to_numpy().reshape(B, 3, 3, 16),
+    }, index, "ttrl/engine/layers.py Flatten(3,3,16) -> Linear(144,32) -> relu -> Linear(32,6), "
+              "fwd and bwd with upstream gradient G")
+
+
+def conv_tower(index):
+    from ttrl.deploy.conv import conv_features
+    from ttrl.engine.conv.geometry import conv_out_size
+    rng = np.random.default_rng(500)
+    out = {}
+    # Nature CNN stages at a reduced width (channels 4->8->16->16) over a
+    # full 84x84 frame, and a padded stride-1 stage.
+    stages_def = [(4, 8, 8, 4, 0), (8, 16, 4, 2, 0), (16, 16, 3, 1, 0)]
+    frames = rng.integers(0, 256, (2, 4, 84, 84)).astype(np.float32)
+    stages = []
+    for i, (cin, cout, k, s, p) in enumerate(stages_def):
+        bound = 1.0 / np.sqrt(cin * k * k)
+        w = rng.uniform(-bound, bound, (cout, cin, k, k)).astype(np.float32)
+        b = rng.uniform(-bound, bound, (cout,)).astype(np.float32)
+        if i == 0:
+            w = w / np.float32(255.0)  # ObsSpec.scale folded into the first stage
+        stages.append((w, b, s, p))
+        out[f"nature_w{i}"] = w
+        out[f"nature_b{i}"] = b
+    out["nature_frames"] = frames.astype(np.uint8)
+    out["nature_features"] = conv_features(frames, stages)
+    x = rng.standard_normal((2, 3, 9, 9)).astype(np.float32)
+    w = rng.standard_normal((5, 3, 3, 3)).astype(np.float32)
+    b = rng.standard_normal(5).astype(np.float32)
+    out["pad_x"] = x
+    out["pad_w"] = w
+    out["pad_b"] = b
+    out["pad_features"] = conv_features(x, [(w, b, 1, 1)])
+    sizes = []
+    # -1 marks a geometry the reference refuses (ragged stride or empty output).
+    for size, k, s, p in [(84, 8, 4, 0), (20, 4, 2, 0), (9, 3, 1, 0), (9, 3, 1, 1),
+                          (64, 8, 4, 2), (11, 3, 2, 1), (85, 8, 4, 0), (10, 4, 2, 0),
+                          (2, 3, 1, 0)]:
+        try:
+            o = conv_out_size(size, k, s, p, axis="h")
+        except ValueError:
+            o = -1
+        sizes.append([size, k, s, p, o])
+    out["geometry"] = np.array(sizes, np.int64)
+    _save("conv_tower", out, index,
+          "ttrl/deploy/conv.py:31-50 conv_features (ReLU after every stage, NHWC flatten) "
+          "and ttrl/engine/conv/geometry.py conv_out_size")
+
+
+def grad_clip(index):
+    from ttrl.algos.grads import clip_grad_norm, grad_sq_device
+    from ttrl.engine.autograd import Tensor
+    import ttnn
+    out = {}
+    for v, max_norm in enumerate((0.5, 1e3)):
+        rng = np.random.default_rng(600 + v)
+        shapes = [(32, 4), (100,), (7, 3)]
+        params = [Tensor.from_numpy(np.zeros(s, np.float32), ttnn.DEVICE, requires_grad=True)
+                  for s in shapes]
+        grads = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+        for p, g in zip(params, grads):
+            p.grad = ttnn.Tensor(g)
+        sq = grad_sq_device(params).to_numpy()
+        norm = clip_grad_norm(params, max_norm)
+        pre = f"c{v}_"
+        out[pre + "max_norm"] = np.float64(max_norm)
+        out[pre + "norm"] = np.float64(norm)
+        out[pre + "grad_sq"] = sq
+        for i, (p, g) in enumerate(zip(params, grads)):
+            out[pre + f"g{i}"] = g
+            out[pre + f"clipped{i}"] = p.grad.to_numpy()
+    _save("grad_clip", out, index,
+          "ttrl/algos/grads.py:29-61 clip_grad_norm (f64 host norm) and grad_sq_device")
+
+
+def gru(index):
+    from ttrl.engine.autograd import Tensor
+    from ttrl.engine.ops import mean_all, mul
+    from ttrl.engine.recurrent import GRUCell
+    import ttnn
+    np.random.seed(700)
+    dev = ttnn.DEVICE
+    B, I, H = 4, 10, 8
+    cell = GRUCell(I, H, dev)
+    rng = np.random.default_rng(701)
+    x = rng.standard_normal((B, I)).astype(np.float32)
+    h = rng.standard_normal((B, H)).astype(np.float32)
+    upstream = rng.standard_normal((B, H)).astype(np.float32)
+    xt = Tensor.from_numpy(x, dev, requires_grad=True)
+    ht = Tensor.from_numpy(h, dev, requires_grad=True)
+    h1 = cell(xt, ht)
+    loss = mul(mean_all(mul(h1, Tensor.from_numpy(upstream, dev))), float(B * H))
+    loss.backward()
+    out = {"x": x, "h": h, "upstream": upstream, "h1": h1.numpy(),
+           "dx": xt.grad.to_numpy(), "dh": ht.grad.to_numpy()}
+    for name, p in cell.named_parameters():
+        out["param." + name] = p.numpy()
+        out["grad." + name] = p.grad.to_numpy()
+    _save("gru_cell", out, index, "ttrl/engine/recurrent.py GRUCell forward and backward")
+
+
+def param_sync(index):
+    from ttrl.engine.autograd import Tensor
+    from ttrl.engine.mesh.sync import ParamSync
+    from ttrl.engine.nn import Module
+    import ttnn
+
+    class Two(Module):
+        def __init__(self, a, b):
+            self.w = Tensor.from_numpy(np.array(a, np.float32), ttnn.DEVICE, requires_grad=True)
+            self.b = Tensor.from_numpy(np.array(b, np.float32), ttnn.DEVICE, requires_grad=True)
+
+    rng = np.random.default_rng(800)
+    out = {}
+    for n in (2, 3, 4):
+        a = [rng.standard_normal(5).astype(np.float32) for _ in range(n)]
+        b = [rng.standard_normal((2, 3)).astype(np.float32) for _ in range(n)]
+        mods = [Two(a[i], b[i]) for i in range(n)]
+        sync = ParamSync(mods, sync_every=1)
+        sync.average()
+        out[f"n{n}_w_in"] = np.stack(a)
+        out[f"n{n}_b_in"] = np.stack(b)
+        out[f"n{n}_w_out"] = np.stack([m.w.numpy() for m in mods])
+        out[f"n{n}_b_out"] = np.stack([m.b.numpy() for m in mods])
+    _save("param_sync", out, index,
+          "ttrl/engine/mesh/sync.py ParamSync.average: exact fp32 sum in replica order, then /N")
+
+
+def main() -> None:
+    reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TTRL_REFERENCE")
+    if not reference or not os.path.isdir(os.path.join(reference, "ttrl")):
+        raise SystemExit("usage: make_golden.py <reference checkout>")
+    _install(reference)
+    index: dict = {}
+    for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
+               grad_clip, gru, param_sync):
+        fn(index)
+        print("wrote", fn.__name__)
+    with open(os.path.join(HERE, "index.json"), "w") as f:
+        json.dump(index, f, indent=1, sort_keys=True)
+
+
+if __name__ == "__main__":
+    main()

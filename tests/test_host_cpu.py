@@ -1,0 +1,172 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports
+every entry point its header declares; ParamSync's averaging, schedule and
+error contract (ttrl/engine/mesh/sync.py, tests/engine/test_mesh_sync.py's
+known answers); the multi-process averaging path over a world-size-2 gloo
+group; and conv geometry validation.
+"""
+
+import os
+import re
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "ttrl_b200.h")
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ttrl_[a-z0-9_]+)\s*\(", text)))
+
+
+def _ensure_built():
+    from ttrl_b200 import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        subprocess.run(["make", "-C", os.path.join(ROOT, "tt-rl_b200", "csrc"), "-j8"],
+                       check=True, capture_output=True)
+    return _lib
+
+
+def test_library_exports_every_header_symbol():
+    _lib = _ensure_built()
+    lib = _lib.lib()  # loads without a GPU: no CUDA call happens at load
+    declared = header_symbols()
+    assert len(declared) >= 25
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+    # ...and the Python binding types every one of them.
+    assert sorted(_lib.EXPORTED_SYMBOLS) == declared
+    assert lib.ttrl_version() >= 1
+
+
+def test_library_refuses_bad_arguments_without_a_gpu():
+    _lib = _ensure_built()
+    lib = _lib.lib()
+    # Argument validation happens on the host before any CUDA call.
+    rc = lib.ttrl_linear_fwd(None, None, None, None, 0, 4, 4, 0, 0, None, 0, None, None)
+    assert rc == 1  # TTRL_EINVAL
+    assert b"bad extents" in lib.ttrl_last_error()
+
+
+# ---------------------------------------------------------------- ParamSync
+
+def _module(values):
+    from ttrl_b200.engine.autograd import Tensor
+    from ttrl_b200.engine.nn import Module
+
+    class Two(Module):
+        def __init__(self, w, b):
+            self.w = Tensor(torch.tensor(np.asarray(w, np.float32)), requires_grad=True)
+            self.b = Tensor(torch.tensor(np.asarray(b, np.float32)), requires_grad=True)
+
+    return Two(*values)
+
+
+def test_param_sync_known_answers():
+    # tests/engine/test_mesh_sync.py:21-46: (1, 3) -> 2 and (10, 20) -> 15.
+    from ttrl_b200.engine.mesh import ParamSync
+    mods = [_module(([1.0], [10.0])), _module(([3.0], [20.0]))]
+    ParamSync(mods, sync_every=1).average()
+    for m in mods:
+        assert m.w.numpy().tolist() == [2.0]
+        assert m.b.numpy().tolist() == [15.0]
+
+
+@pytest.mark.parametrize("n", [2, 3, 4])
+def test_param_sync_matches_reference_golden(n):
+    from ttrl_b200.engine.mesh import ParamSync
+    d = np.load(os.path.join(GOLDEN, "param_sync.npz"))
+    mods = [_module((d[f"n{n}_w_in"][i], d[f"n{n}_b_in"][i])) for i in range(n)]
+    ParamSync(mods, sync_every=1).average()
+    for i, m in enumerate(mods):
+        assert np.array_equal(m.w.numpy(), d[f"n{n}_w_out"][i])
+        assert np.array_equal(m.b.numpy(), d[f"n{n}_b_out"][i])
+
+
+def test_param_sync_schedule():
+    from ttrl_b200.engine.mesh import ParamSync
+    mods = [_module(([0.0], [0.0])), _module(([2.0], [2.0]))]
+    sync = ParamSync(mods, sync_every=3)
+    assert [sync.maybe_average() for _ in range(6)] == [False, False, True, False, False, True]
+    assert mods[0].w.numpy().tolist() == [1.0]
+
+
+def test_param_sync_errors():
+    from ttrl_b200.engine.mesh import ParamSync, ParamSyncError
+    with pytest.raises(ValueError):
+        ParamSync([_module(([0.0], [0.0]))], sync_every=0)
+    with pytest.raises(ParamSyncError):  # schema mismatch by shape
+        ParamSync([_module(([0.0], [0.0])), _module(([0.0, 1.0], [0.0]))])
+
+    def raising(arrays):
+        raise RuntimeError("link down")
+
+    mods = [_module(([1.0], [1.0])), _module(([3.0], [3.0]))]
+    with pytest.raises(ParamSyncError, match="reduction failed on parameter 0"):
+        ParamSync(mods, reduce_fn=raising).average()
+    with pytest.raises(ParamSyncError, match="returned 1 results"):
+        ParamSync(mods, reduce_fn=lambda arrays: arrays[:1]).average()
+    # Nothing was written back by the failed calls.
+    assert mods[0].w.numpy().tolist() == [1.0]
+
+
+_GLOO_WORKER = r"""
+import os, sys, numpy as np, torch, torch.distributed as dist
+sys.path[:0] = [{root!r}, os.path.join({root!r}, "tt-rl_b200")]
+from datetime import timedelta
+rank = int(sys.argv[1])
+dist.init_process_group("gloo", init_method="tcp://127.0.0.1:{port}", rank=rank,
+                        world_size=2, timeout=timedelta(seconds=60))
+from ttrl_b200.engine.autograd import Tensor
+from ttrl_b200.engine.nn import Module
+from ttrl_b200.engine.mesh import ParamSync
+class Net(Module):
+    def __init__(self, r):
+        self.w = Tensor(torch.full((3, 4), float(r + 1)), requires_grad=True)
+        self.b = Tensor(torch.arange(5, dtype=torch.float32) * (10.0 ** r), requires_grad=True)
+net = Net(rank)
+sync = ParamSync([net], sync_every=2, group=dist.group.WORLD)
+assert sync.maybe_average() is False
+assert sync.maybe_average() is True
+np.save(os.path.join({out!r}, f"rank{{rank}}.npy"),
+        np.concatenate([net.w.numpy().ravel(), net.b.numpy().ravel()]))
+dist.destroy_process_group()
+"""
+
+
+def test_param_sync_gloo_world_size_2():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as out:
+        script = os.path.join(out, "worker.py")
+        with open(script, "w") as f:
+            f.write(_GLOO_WORKER.format(root=ROOT, port=port, out=out))
+        procs = [subprocess.Popen([sys.executable, script, str(r)]) for r in range(2)]
+        codes = [p.wait(timeout=180) for p in procs]
+        assert codes == [0, 0]
+        r0 = np.load(os.path.join(out, "rank0.npy"))
+        r1 = np.load(os.path.join(out, "rank1.npy"))
+    want = np.concatenate([np.full(12, 1.5, np.float32),
+                           (np.arange(5, dtype=np.float32) * 11.0) / 2.0])
+    assert np.array_equal(r0, want) and np.array_equal(r1, want)
+
+
+# ---------------------------------------------------------------- geometry
+
+def test_conv_geometry_matches_reference():
+    from ttrl_b200.engine.conv import conv_out_size
+    for size, k, s, p, want in np.load(os.path.join(GOLDEN, "conv_tower.npz"))["geometry"]:
+        if want < 0:
+            with pytest.raises(ValueError):
+                conv_out_size(int(size), int(k), int(s), int(p))
+        else:
+            assert conv_out_size(int(size), int(k), int(s), int(p)) == want

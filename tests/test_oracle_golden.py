@@ -1,0 +1,167 @@
+"""The CPU oracle against golden vectors made by the reference's own code
+(tests/golden/make_golden.py runs ttrl's tape, ops, Adam, losses, GRU,
+ParamSync and deploy conv tower). This pins the oracle; the GPU tests then
+compare the CUDA path with the pinned oracle.
+
+Tolerances: fp32 elementwise chains 1e-6 relative (the spec's bar); float64
+oracle against float32 reference arithmetic through exp/log/softmax 1e-5;
+matmul-bearing chains 1e-5 (both sides are exact fp32/f64 BLAS, no TF32).
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import layers as L
+from oracle import learner as R
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return np.load(os.path.join(GOLDEN, f"{name}.npz"))
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def test_adam_scalars():
+    for lr, b1, b2, eps, t, alpha, eps_t in load("adam_scalars")["rows"]:
+        a, e = L.adam_fused_scalars(lr, b1, b2, eps, int(t))
+        assert a == pytest.approx(alpha, rel=1e-14)
+        assert e == pytest.approx(eps_t, rel=1e-14)
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_adam_steps(case):
+    d = load("adam_steps")
+    pre = f"c{case}_"
+    lr, eps, wd = d[pre + "hyper"]
+    for i in range(3):
+        p = d[pre + f"p{i}_init"].copy()
+        S = np.zeros_like(p)
+        V = np.zeros_like(p)
+        t = 0
+        for step, g in enumerate(d[pre + f"p{i}_grads"]):
+            if i == 1 and step == 2:
+                continue  # no gradient: no update, no step count
+            t += 1
+            p, S, V = L.adam_step_sv(p, g, S, V, t, lr=lr, eps=eps, weight_decay=wd)
+        assert t == d[pre + "steps"][i]
+        assert rel(p, d[pre + f"p{i}_final"]) <= 1e-6
+        assert rel(S, d[pre + f"p{i}_S"]) <= 1e-6
+        assert rel(V, d[pre + f"p{i}_V"]) <= 1e-6
+
+
+@pytest.mark.parametrize("name", ["vanilla", "double", "double_mask", "double_per"])
+def test_dqn_loss_head(name):
+    d = load("dqn_loss")
+    g = {k[len(name) + 1:]: d[k] for k in d.files if k.startswith(name + "_")}
+    double, mask_n, per = (int(v) for v in g["flags"])
+    q = g["q"].astype(np.float64)
+    q_tgt = g["q_next_target"].astype(np.float64)
+    q_sel = g["q_next_online"].astype(np.float64) if double else q_tgt
+    actions = g["onehot"].argmax(1)
+    loss, mean_q, dq, td_abs, _ = R.dqn_loss_head(
+        q, q_sel, q_tgt, actions, g["rewards"].reshape(-1), g["dones"].reshape(-1),
+        g["discounts"].reshape(-1), delta=1.0,
+        next_mask=g["next_mask"] if mask_n else None,
+        is_weights=g["is_weights"].reshape(-1) if per else None)
+    assert rel(loss, g["loss"]) <= 1e-6
+    assert abs(mean_q - float(g["mean_q"].reshape(-1)[0])) <= 1e-6
+    assert rel(dq, g["dq"]) <= 1e-6
+    assert rel(np.sum(dq * dq), g["grad_sq"]) <= 1e-5
+    if per:
+        assert rel(td_abs, g["td_abs"].reshape(-1)) <= 1e-6
+
+
+@pytest.mark.parametrize("name", ["mean", "masked"])
+def test_ppo_objective(name):
+    d = load("ppo_objective")
+    g = {k[len(name) + 1:]: d[k] for k in d.files if k.startswith(name + "_")}
+    loss, parts, new_logp, dlogits, dvalue = R.ppo_objective_and_grads(
+        g["logits"].astype(np.float64), g["value"].astype(np.float64), g["actions"],
+        g["old_logp"].astype(np.float64), g["adv"].astype(np.float64),
+        g["returns"].astype(np.float64), g["old_values"].astype(np.float64),
+        clip=0.1, vclip=0.1, vcoef=0.5, entcoef=0.01,
+        valid=g["valid"] if name == "masked" else None)
+    assert rel(loss, g["loss"]) <= 1e-5
+    for k in ("policy_loss", "value_loss", "entropy"):
+        assert rel(parts[k], g[k]) <= 1e-5, k
+    assert rel(new_logp, g["new_logp"].reshape(-1)) <= 1e-5
+    assert rel(dlogits, g["dlogits"]) <= 1e-5
+    assert rel(dvalue, g["dvalue"]) <= 1e-5
+
+
+def test_linear_mlp():
+    d = load("linear_mlp")
+    x = d["x_nhwc"].astype(np.float64)
+    b = x.shape[0]
+    flat = x.reshape(b, -1)  # (h, w, c) flatten order
+    h_pre = L.linear(flat, d["w1"].astype(np.float64), d["b1"])
+    h = L.relu(h_pre)
+    y = L.linear(h, d["w2"].astype(np.float64), d["b2"])
+    assert rel(y, d["y"]) <= 1e-5
+    dh, dw2, db2 = L.linear_backward(h, d["w2"].astype(np.float64), d["upstream"])
+    dz = dh * (h_pre > 0)
+    dx, dw1, db1 = L.linear_backward(flat, d["w1"].astype(np.float64), dz)
+    assert rel(dw2, d["dw2"]) <= 1e-5
+    assert rel(db2, d["db2"]) <= 1e-5
+    assert rel(dw1, d["dw1"]) <= 1e-5
+    assert rel(db1, d["db1"]) <= 1e-5
+    assert rel(dx.reshape(d["dx"].shape), d["dx"]) <= 1e-5
+
+
+def test_conv_tower_forward():
+    d = load("conv_tower")
+    x = d["nature_frames"].astype(np.float64).transpose(0, 2, 3, 1)
+    for i, s in enumerate((4, 2, 1)):
+        x = L.conv2d_nhwc(x, d[f"nature_w{i}"].astype(np.float64), d[f"nature_b{i}"],
+                          stride=s, apply_relu=True)
+    assert rel(x.reshape(x.shape[0], -1), d["nature_features"]) <= 1e-5
+    y = L.conv2d_nhwc(d["pad_x"].astype(np.float64).transpose(0, 2, 3, 1),
+                      d["pad_w"].astype(np.float64), d["pad_b"], stride=1, padding=1,
+                      apply_relu=True)
+    assert rel(y.reshape(y.shape[0], -1), d["pad_features"]) <= 1e-5
+
+
+def test_conv_geometry():
+    for size, k, s, p, want in load("conv_tower")["geometry"]:
+        if want < 0:
+            with pytest.raises(ValueError):
+                L.conv_out(int(size), int(k), int(s), int(p))
+        else:
+            assert L.conv_out(int(size), int(k), int(s), int(p)) == want
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_grad_clip(case):
+    d = load("grad_clip")
+    pre = f"c{case}_"
+    grads = [d[pre + f"g{i}"] for i in range(3)]
+    norm, scale = R.clip_grad_norm_scale(grads, float(d[pre + "max_norm"]))
+    assert norm == pytest.approx(float(d[pre + "norm"]), rel=1e-12)
+    assert rel(sum(np.sum(np.asarray(g, np.float64) ** 2) for g in grads),
+               d[pre + "grad_sq"]) <= 1e-6
+    for i, g in enumerate(grads):
+        want = d[pre + f"clipped{i}"]
+        got = g if scale is None else g * np.float32(scale)
+        assert rel(got, want) <= 1e-6
+
+
+def test_gru_cell():
+    d = load("gru_cell")
+    p = {k[len("param."):]: d[k].astype(np.float64) for k in d.files if k.startswith("param.")}
+    h1, cache = R.gru_cell_forward(d["x"].astype(np.float64), d["h"].astype(np.float64),
+                                   p["weight_ih"], p["weight_hh"], p["bias_ih"], p["bias_hh"])
+    assert rel(h1, d["h1"]) <= 1e-5
+    g = R.gru_cell_backward(d["upstream"].astype(np.float64), cache, p["weight_ih"],
+                            p["weight_hh"])
+    assert rel(g["dx"], d["dx"]) <= 1e-5
+    assert rel(g["dh"], d["dh"]) <= 1e-5
+    for k in ("weight_ih", "weight_hh", "bias_ih", "bias_hh"):
+        assert rel(g[k], d["grad." + k]) <= 1e-5, k

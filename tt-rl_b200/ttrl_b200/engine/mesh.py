@@ -87,9 +87,11 @@ class ParamSync:
         self._nparams = len(self._schema)
         self._flat = None
         self._world = 1
+        self._nccl = False
         if self.group is not None:
             import torch.distributed as dist
             self._world = dist.get_world_size(self.group)
+            self._nccl = str(dist.get_backend(self.group)).lower() == "nccl"
 
     # -- schedule --------------------------------------------------------
 
@@ -124,14 +126,26 @@ class ParamSync:
         for module in self.modules:
             params = list(module.parameters())
             flat = self._flat_buffer(params)
-            ctx = context(flat.device)
+            # On a GPU the packing runs as this library's copy kernels; host
+            # replicas (gloo process groups) pack with plain tensor copies.
+            if flat.is_cuda:
+                copy = context(flat.device).copy_strided
+            else:
+                def copy(dst, src):
+                    dst.copy_(src)
             off = 0
             for p in params:
                 n = p.data.numel()
-                ctx.copy_strided(flat[off:off + n], p.data.reshape(-1))
+                copy(flat[off:off + n], p.data.reshape(-1))
                 off += n
             try:
-                dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=self.group)
+                if self._nccl:
+                    # NCCL's average: the sum and the 1/N in one collective.
+                    dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=self.group)
+                else:
+                    # gloo has no AVG: sum, then the 1/N (host replicas only).
+                    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+                    flat.div_(self._world)
             except Exception as e:
                 raise ParamSyncError(
                     f"ParamSync.average(): the all-reduce failed: {e}. No parameter was "
@@ -141,7 +155,7 @@ class ParamSync:
             off = 0
             for p in params:
                 n = p.data.numel()
-                ctx.copy_strided(p.data.reshape(-1), flat[off:off + n])
+                copy(p.data.reshape(-1), flat[off:off + n])
                 off += n
 
     # -- in-process path (reference semantics) ---------------------------
