@@ -165,3 +165,24 @@ def test_gru_cell():
     assert rel(g["dh"], d["dh"]) <= 1e-5
     for k in ("weight_ih", "weight_hh", "bias_ih", "bias_hh"):
         assert rel(g[k], d["grad." + k]) <= 1e-5, k
+
+
+@pytest.mark.parametrize("n,h,c,cout,k,s,p", [
+    (2, 84, 4, 8, 8, 4, 0), (2, 20, 8, 16, 4, 2, 0), (2, 9, 16, 16, 3, 1, 0),
+    (1, 9, 3, 5, 3, 1, 1),
+])
+def test_conv_backward_is_the_adjoint_of_the_pinned_forward(n, h, c, cout, k, s, p):
+    """The conv forward is pinned by the deploy tower fixture; dX and dW are
+    its adjoints: <conv(x, W), dY> = <x, dX(dY)> = <W, dW(x, dY)>, in f64.
+    This is the property ttrl/engine/conv/backward.py:33-78 relies on."""
+    rng = np.random.default_rng(n * 1000 + h * 10 + k)
+    x = rng.standard_normal((n, h, h, c))
+    w = rng.standard_normal((cout, c, k, k))
+    oh = L.conv_out(h, k, s, p)
+    dy = rng.standard_normal((n, oh, oh, cout))
+    y = L.conv2d_nhwc(x, w, stride=s, padding=p)
+    lhs = float(np.sum(y * dy))
+    dx = L.conv2d_dgrad(dy, w, x.shape, stride=s, padding=p)
+    dw = L.conv2d_wgrad(x, dy, k, stride=s, padding=p)
+    assert float(np.sum(x * dx)) == pytest.approx(lhs, rel=1e-10)
+    assert float(np.sum(w * dw)) == pytest.approx(lhs, rel=1e-10)
