@@ -35,8 +35,9 @@ def _inputs(rng, m, k, n, dev):
 
 
 @pytest.mark.parametrize("m,k,n,relu,use_bias,prec", [
-    (32, 3136, 512, 1, True, 0),   # Nature-CNN fc1 at batch 32: split-K, separate reduce
-    (256, 512, 64, 0, True, 0),    # split-K reduced inside the GEMM kernel
+    (32, 32768, 128, 1, True, 0),  # long K: 32 splits summed through the fixed scratch
+    (32, 3136, 512, 1, True, 0),   # Nature-CNN fc1 at batch 32: split-K inside a cluster
+    (256, 512, 64, 0, True, 0),    # a few splits inside a cluster
     (128, 512, 512, 1, False, 1),  # single-pass TF32
     (8, 16, 6, 0, True, 0),        # one k-block, no split
 ])
@@ -79,7 +80,7 @@ def test_noalloc_matches_workspace_entry(m, k, n, relu, use_bias, prec):
 def test_noalloc_refuses_oversized_scratch():
     _lib, lib = _setup()
     dev = torch.device("cuda", 0)
-    m, k, n = 1024, 4096, 1024  # 3 splits x 4 MiB of partial sums
+    m, k, n = 256, 32768, 256  # long K: 32 splits x 256 KB of partial sums
     x = torch.zeros((m, k), device=dev)
     w = torch.zeros((k, n), device=dev)
     y = torch.zeros((m, n), device=dev)

@@ -13,12 +13,17 @@
 
 namespace ttrl {
 
-constexpr int kAdamChunk = 8192;   // elements per block
+// Each thread owns kAdamQuads float4 quads of one 4096-element chunk and
+// issues every load of them before its first store: one memory round trip
+// per thread instead of one per element.
 constexpr int kAdamThreads = 256;
+constexpr int kAdamQuads = 4;
+constexpr int kAdamChunk = kAdamThreads * kAdamQuads * 4;  // elements per block
 
 struct AdamArgs {
   ttrl_adam_tensor t[TTRL_ADAM_MAX_TENSORS];
   long long chunk_start[TTRL_ADAM_MAX_TENSORS + 1];
+  uint64_t vec_mask;  // bit i: tensor i's four buffers are 16-byte aligned
   int count;
   int pad0;
   int32_t* steps;
@@ -28,6 +33,48 @@ struct AdamArgs {
   double lr, b1, b2, eps, wd;
 };
 
+__device__ __forceinline__ float4 load4(const float* p, long long i, long long end, bool vec) {
+  if (vec && i + 3 < end) return *reinterpret_cast<const float4*>(p + i);
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (i < end) v.x = p[i];
+  if (i + 1 < end) v.y = p[i + 1];
+  if (i + 2 < end) v.z = p[i + 2];
+  if (i + 3 < end) v.w = p[i + 3];
+  return v;
+}
+
+__device__ __forceinline__ void store4(float* p, long long i, long long end, bool vec, float4 v) {
+  if (vec && i + 3 < end) {
+    *reinterpret_cast<float4*>(p + i) = v;
+    return;
+  }
+  if (i < end) p[i] = v.x;
+  if (i + 1 < end) p[i + 1] = v.y;
+  if (i + 2 < end) p[i + 2] = v.z;
+  if (i + 3 < end) p[i + 3] = v.w;
+}
+
+struct AdamScalars {
+  float alpha_t, eps_t, b1, b2, wd, gs;
+  bool scaled;
+};
+
+// One element of the reference's composed tail, rounding where each of its
+// separate device ops rounds (explicit _rn intrinsics: no FMA contraction).
+__device__ __forceinline__ void adam_elem(const AdamScalars& k, float g, float& p, float& S,
+                                          float& V) {
+  if (k.scaled) g = __fmul_rn(g, k.gs);
+  if (k.wd != 0.f) g = __fadd_rn(g, __fmul_rn(k.wd, p));
+  const float sq = __fmul_rn(g, g);
+  V = __fadd_rn(sq, __fmul_rn(k.b2, V));
+  S = __fadd_rn(g, __fmul_rn(k.b1, S));
+  float d = __fsqrt_rn(V);
+  d = __fadd_rn(d, k.eps_t);
+  d = __fdiv_rn(S, d);
+  d = __fmul_rn(d, k.alpha_t);
+  p = __fsub_rn(p, d);
+}
+
 __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constant__ AdamArgs a) {
   // Locate this block's tensor (count <= 64: a linear scan is cheap).
   const long long chunk = blockIdx.x;
@@ -36,36 +83,42 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
   const ttrl_adam_tensor& T = a.t[ti];
   const long long begin = (chunk - a.chunk_start[ti]) * kAdamChunk;
   const long long end = begin + kAdamChunk < T.numel ? begin + kAdamChunk : T.numel;
+  const bool vec = (a.vec_mask >> ti) & 1ull;
 
   const int step = a.steps[T.step_index] + 1;
   const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
   const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
   const double c = sqrt((1.0 - a.b2) / bc2);
   const double lr = a.lr_device ? *a.lr_device : a.lr;
-  const float alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
-  const float eps_t = static_cast<float>(a.eps / c);
-  const float b1 = static_cast<float>(a.b1), b2 = static_cast<float>(a.b2);
-  const float wd = static_cast<float>(a.wd);
-  const bool scaled = a.grad_scale != nullptr;
-  const float gs = scaled ? *a.grad_scale : 1.f;
+  AdamScalars k;
+  k.alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
+  k.eps_t = static_cast<float>(a.eps / c);
+  k.b1 = static_cast<float>(a.b1);
+  k.b2 = static_cast<float>(a.b2);
+  k.wd = static_cast<float>(a.wd);
+  k.scaled = a.grad_scale != nullptr;
+  k.gs = k.scaled ? *a.grad_scale : 1.f;
 
-  // Explicit round-to-nearest intrinsics: no FMA contraction, so each step
-  // rounds exactly where the reference's separate device ops round.
-  for (long long i = begin + threadIdx.x; i < end; i += blockDim.x) {
-    float g = T.grad[i];
-    if (scaled) g = __fmul_rn(g, gs);
-    const float p = T.param[i];
-    if (wd != 0.f) g = __fadd_rn(g, __fmul_rn(wd, p));
-    const float sq = __fmul_rn(g, g);
-    const float V = __fadd_rn(sq, __fmul_rn(b2, T.v[i]));
-    const float S = __fadd_rn(g, __fmul_rn(b1, T.s[i]));
-    T.v[i] = V;
-    T.s[i] = S;
-    float d = __fsqrt_rn(V);
-    d = __fadd_rn(d, eps_t);
-    d = __fdiv_rn(S, d);
-    d = __fmul_rn(d, alpha_t);
-    T.param[i] = __fsub_rn(p, d);
+  float4 g[kAdamQuads], p[kAdamQuads], S[kAdamQuads], V[kAdamQuads];
+#pragma unroll
+  for (int u = 0; u < kAdamQuads; ++u) {
+    const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+    g[u] = load4(T.grad, i, end, vec);
+    p[u] = load4(T.param, i, end, vec);
+    S[u] = load4(T.s, i, end, vec);
+    V[u] = load4(T.v, i, end, vec);
+  }
+#pragma unroll
+  for (int u = 0; u < kAdamQuads; ++u) {
+    const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+    if (i >= end) continue;
+    adam_elem(k, g[u].x, p[u].x, S[u].x, V[u].x);
+    adam_elem(k, g[u].y, p[u].y, S[u].y, V[u].y);
+    adam_elem(k, g[u].z, p[u].z, S[u].z, V[u].z);
+    adam_elem(k, g[u].w, p[u].w, S[u].w, V[u].w);
+    store4(T.v, i, end, vec, V[u]);
+    store4(T.s, i, end, vec, S[u]);
+    store4(T.param, i, end, vec, p[u]);
   }
 
   // The last block to finish advances every step counter of this launch,
@@ -75,17 +128,19 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
     __threadfence();
     const unsigned int prev = atomicAdd(reinterpret_cast<unsigned int*>(a.ticket), 1u);
     if (prev == gridDim.x - 1) {
-      for (int k = 0; k < a.count; ++k) {
+      for (int q = 0; q < a.count; ++q) {
         // Each tensor's counter advances once even if tensors share an index.
         bool seen = false;
-        for (int q = 0; q < k; ++q) seen |= a.t[q].step_index == a.t[k].step_index;
-        if (!seen) a.steps[a.t[k].step_index] += 1;
+        for (int r = 0; r < q; ++r) seen |= a.t[r].step_index == a.t[q].step_index;
+        if (!seen) a.steps[a.t[q].step_index] += 1;
       }
       *a.ticket = 0;
       __threadfence();
     }
   }
 }
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
               const float* grad_scale, const double* lr_device, double lr, double b1, double b2,
@@ -104,6 +159,7 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
     if (t.numel <= 0 || !t.param || !t.grad || !t.s || !t.v)
       return set_error(TTRL_EINVAL, "adam: tensor %d is empty or has a null buffer", i);
     a.t[i] = t;
+    if (al16(t.param) && al16(t.grad) && al16(t.s) && al16(t.v)) a.vec_mask |= 1ull << i;
     a.chunk_start[i] = chunks;
     chunks += (t.numel + kAdamChunk - 1) / kAdamChunk;
   }
@@ -126,13 +182,15 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
 
 // ------------------------------------------------------ sum of squares
 
-constexpr int kSqChunk = 16384;
 constexpr int kSqThreads = 256;
+constexpr int kSqQuads = 4;
+constexpr int kSqChunk = kSqThreads * kSqQuads * 4;
 
 struct SqArgs {
   const float* g[TTRL_ADAM_MAX_TENSORS];
   long long numel[TTRL_ADAM_MAX_TENSORS];
   long long chunk_start[TTRL_ADAM_MAX_TENSORS + 1];
+  uint64_t vec_mask;
   int count;
   int pad0;
   double* partial;  // one per block
@@ -141,43 +199,66 @@ struct SqArgs {
   float max_norm;
 };
 
-__global__ void __launch_bounds__(kSqThreads) sqnorm_kernel(const __grid_constant__ SqArgs a) {
-  __shared__ double red[kSqThreads];
-  const long long chunk = blockIdx.x;
-  int ti = 0;
-  while (ti + 1 < a.count && a.chunk_start[ti + 1] <= chunk) ++ti;
-  const long long begin = (chunk - a.chunk_start[ti]) * kSqChunk;
-  const long long end = begin + kSqChunk < a.numel[ti] ? begin + kSqChunk : a.numel[ti];
-  const float* g = a.g[ti];
-  double s = 0.0;
-  for (long long i = begin + threadIdx.x; i < end; i += blockDim.x) {
-    const double x = g[i];
-    s += x * x;
-  }
-  red[threadIdx.x] = s;
+// Fixed-shape tree sum of kSqThreads doubles in shared memory.
+__device__ __forceinline__ double block_sum_fixed(double v, double* red) {
+  red[threadIdx.x] = v;
   __syncthreads();
   for (int w = kSqThreads / 2; w > 0; w >>= 1) {
     if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
     __syncthreads();
   }
+  const double total = red[0];
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(kSqThreads) sqnorm_kernel(const __grid_constant__ SqArgs a) {
+  __shared__ double red[kSqThreads];
+  __shared__ int s_last;
+  const long long chunk = blockIdx.x;
+  int ti = 0;
+  while (ti + 1 < a.count && a.chunk_start[ti + 1] <= chunk) ++ti;
+  const long long begin = (chunk - a.chunk_start[ti]) * kSqChunk;
+  const long long end = begin + kSqChunk < a.numel[ti] ? begin + kSqChunk : a.numel[ti];
+  const bool vec = (a.vec_mask >> ti) & 1ull;
+  float4 x[kSqQuads];
+#pragma unroll
+  for (int u = 0; u < kSqQuads; ++u)
+    x[u] = load4(a.g[ti], begin + (static_cast<long long>(u) * kSqThreads + threadIdx.x) * 4,
+                 end, vec);
+  double s = 0.0;
+#pragma unroll
+  for (int u = 0; u < kSqQuads; ++u) {
+    s += static_cast<double>(x[u].x) * x[u].x;
+    s += static_cast<double>(x[u].y) * x[u].y;
+    s += static_cast<double>(x[u].z) * x[u].z;
+    s += static_cast<double>(x[u].w) * x[u].w;
+  }
+  const double block_total = block_sum_fixed(s, red);
   if (threadIdx.x == 0) {
-    a.partial[blockIdx.x] = red[0];
+    a.partial[blockIdx.x] = block_total;
     __threadfence();
     const unsigned int prev = atomicAdd(reinterpret_cast<unsigned int*>(a.ticket), 1u);
-    if (prev == gridDim.x - 1) {
-      __threadfence();
-      double total = 0.0;
-      for (unsigned int b = 0; b < gridDim.x; ++b)
-        total += *(volatile double*)(a.partial + b);
-      a.out[0] = static_cast<float>(total);
-      if (a.max_norm > 0.f) {
-        const double norm = sqrt(total);
-        const double mx = static_cast<double>(a.max_norm);
-        a.out[1] = norm > mx ? static_cast<float>(mx / (norm + 1e-6)) : 1.f;
-      }
-      *a.ticket = 0;
-      __threadfence();
+    s_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  // The last block sums the per-block partials: every thread takes a fixed
+  // strided subset in index order, then the fixed tree, so the total does
+  // not depend on which block finished last.
+  __threadfence();
+  double t = 0.0;
+  for (unsigned int b = threadIdx.x; b < gridDim.x; b += kSqThreads) t += __ldcg(a.partial + b);
+  const double total = block_sum_fixed(t, red);
+  if (threadIdx.x == 0) {
+    a.out[0] = static_cast<float>(total);
+    if (a.max_norm > 0.f) {
+      const double norm = sqrt(total);
+      const double mx = static_cast<double>(a.max_norm);
+      a.out[1] = norm > mx ? static_cast<float>(mx / (norm + 1e-6)) : 1.f;
     }
+    *a.ticket = 0;
+    __threadfence();
   }
 }
 
@@ -204,6 +285,7 @@ int grad_sqnorm(const float* const* grads, const int64_t* numels, int count, flo
     if (numels[i] <= 0 || grads[i] == nullptr)
       return set_error(TTRL_EINVAL, "grad_sqnorm: tensor %d is empty or null", i);
     a.g[i] = grads[i];
+    if (al16(grads[i])) a.vec_mask |= 1ull << i;
     a.numel[i] = numels[i];
     a.chunk_start[i] = chunks;
     chunks += (numels[i] + kSqChunk - 1) / kSqChunk;

@@ -40,6 +40,11 @@ constexpr int kThreads = 256;                       // loader threads
 constexpr int kBlockThreads = kThreads + 32;        // + the MMA warp
 constexpr int kMmaWarp = kLoadWarps;
 
+// Largest cluster (in split CTAs) the split-K reduction may use on each
+// device: 16 where the hardware can co-schedule it, else the portable 8.
+// Written by gemm_init_device.
+static int g_max_cluster[64];
+
 // Constant sources for the synthetic "ones" row an operand may append: a
 // GEMM whose A operand carries a row of ones produces the column sums of B
 // (the bias gradient) in that row of D.
@@ -251,30 +256,207 @@ struct Loader {
   }
 };
 
-__device__ __forceinline__ void epi_store(const ttrl_epilogue& ep, const EpiExtra& ex, int r,
-                                          int c, float acc) {
-  if (ex.row2 >= 0 && r == ex.row2) {
-    // The synthetic ones row: column sums of B, stored unscaled.
-    float* o = ex.out2 + static_cast<long long>(c) * ex.cs2;
-    float v = acc;
-    if (ex.accumulate2) v += *o;
-    *o = v;
-    return;
+// The epilogue over up to U output elements at once. Every global load it
+// needs (bias, ReLU-backward mask, the old output when accumulating) is
+// issued before any store, so the U elements share one memory round trip;
+// one element per iteration would serialise a round trip per element.
+// Rows equal to `ex.row2` are the synthetic ones row: column sums of B,
+// stored unscaled into `ex.out2`.
+template <int U>
+__device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const EpiExtra& ex,
+                                                const int (&r)[U], const int (&c)[U],
+                                                const float (&acc)[U], int n) {
+  float add[U], mk[U], old[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    add[u] = 0.f;
+    mk[u] = 1.f;
+    old[u] = 0.f;
+    if (u < n) {
+      if (ex.row2 >= 0 && r[u] == ex.row2) {
+        if (ex.accumulate2) old[u] = ex.out2[static_cast<long long>(c[u]) * ex.cs2];
+      } else {
+        if (ep.bias_mode == TTRL_BIAS_ROW) {
+          add[u] = ep.bias[r[u]];
+        } else if (ep.bias_mode == TTRL_BIAS_COL) {
+          add[u] = ep.bias[c[u]];
+        }
+        if (ep.mask != nullptr)
+          mk[u] = ep.mask[static_cast<long long>(r[u]) * ep.mrs +
+                          static_cast<long long>(c[u]) * ep.mcs];
+        if (ep.accumulate)
+          old[u] = ep.out[static_cast<long long>(r[u]) * ep.ors +
+                          static_cast<long long>(c[u]) * ep.ocs];
+      }
+    }
   }
-  float v = ep.alpha * acc;
-  if (ep.bias_mode == TTRL_BIAS_ROW) {
-    v += ep.bias[r];
-  } else if (ep.bias_mode == TTRL_BIAS_COL) {
-    v += ep.bias[c];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (u >= n) continue;
+    if (ex.row2 >= 0 && r[u] == ex.row2) {
+      float v = acc[u];
+      if (ex.accumulate2) v += old[u];
+      ex.out2[static_cast<long long>(c[u]) * ex.cs2] = v;
+      continue;
+    }
+    float v = ep.alpha * acc[u];
+    if (ep.bias_mode != TTRL_BIAS_NONE) v += add[u];
+    if (!(mk[u] > 0.f)) v = 0.f;
+    if (ep.relu) v = v > 0.f ? v : 0.f;
+    if (ep.accumulate) v += old[u];
+    ep.out[static_cast<long long>(r[u]) * ep.ors + static_cast<long long>(c[u]) * ep.ocs] = v;
   }
-  if (ep.mask != nullptr) {
-    if (!(ep.mask[static_cast<long long>(r) * ep.mrs + static_cast<long long>(c) * ep.mcs] > 0.f))
-      v = 0.f;
+}
+
+constexpr int kEpiBatch = 8;
+
+template <int BN>
+constexpr int kTileLd = BN + 1;  // padded staging row: conflict-free both ways
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared-memory float at `saddr` in cluster CTA `rank` (DSMEM).
+__device__ __forceinline__ float ld_dsmem(uint32_t saddr, int rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float ld_smem(uint32_t saddr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(saddr) : "memory");
+  return v;
+}
+
+// Stores rows [r_lo, r_hi) x [0, cols) of a staged 128 x BN tile through the
+// epilogue. With nsrc > 1 each value is the sum, in cluster-rank order, of
+// the same element of the nsrc cluster CTAs' staged tiles. The thread ->
+// element map uses only compile-time shifts: columns fastest for row-major
+// outputs, rows fastest for transposed ones (ors == 1), so stores coalesce.
+template <int BN>
+__device__ void store_tile(const GemmArgs& args, uint32_t tile_s, int row0, int col0, int r_lo,
+                           int r_hi, int cols, int nsrc, int tid) {
+  constexpr int LD = kTileLd<BN>;
+  constexpr int U = kEpiBatch;
+  const bool rows_fast = !(args.ep.ocs == 1 || args.ep.ors != 1);
+  int rr[U], cc[U];
+  float acc[U];
+  if (!rows_fast) {
+    constexpr int RSTEP = kThreads / BN;
+    const int c = tid & (BN - 1);
+    for (int rb = r_lo + tid / BN; rb < r_hi; rb += RSTEP * U) {
+      int nv = 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int r = rb + u * RSTEP;
+        rr[u] = row0 + r;
+        cc[u] = col0 + c;
+        acc[u] = 0.f;
+        if (r < r_hi && c < cols) nv = u + 1;
+      }
+      if (c >= cols) nv = 0;
+      if (nsrc == 1) {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (u < nv) acc[u] = ld_smem(tile_s + ((rb + u * RSTEP) * LD + c) * 4);
+      } else {
+#pragma unroll 4
+        for (int q = 0; q < nsrc; ++q)
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (u < nv && rb + u * RSTEP < r_hi)
+              acc[u] += ld_dsmem(tile_s + ((rb + u * RSTEP) * LD + c) * 4, q);
+      }
+      // A row past r_hi inside the batch is not valid even if a later one
+      // were: rows grow with u, so the valid ones are a prefix.
+      int np = 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (u < nv && rb + u * RSTEP < r_hi) np = u + 1;
+      epi_store_batch<U>(args.ep, args.ex, rr, cc, acc, np);
+    }
+  } else {
+    const int r = r_lo + (tid & 127);
+    for (int cb = tid >> 7; cb < cols; cb += 2 * U) {
+      int nv = 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = cb + u * 2;
+        rr[u] = row0 + r;
+        cc[u] = col0 + c;
+        acc[u] = 0.f;
+        if (c < cols && r < r_hi) nv = u + 1;
+      }
+      if (r >= r_hi) nv = 0;
+      if (nsrc == 1) {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (u < nv) acc[u] = ld_smem(tile_s + (r * LD + cb + u * 2) * 4);
+      } else {
+#pragma unroll 4
+        for (int q = 0; q < nsrc; ++q)
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (u < nv) acc[u] += ld_dsmem(tile_s + (r * LD + cb + u * 2) * 4, q);
+      }
+      epi_store_batch<U>(args.ep, args.ex, rr, cc, acc, nv);
+    }
+    // Slices taller than 128 rows do not occur: tiles are 128 rows.
   }
-  if (ep.relu) v = v > 0.f ? v : 0.f;
-  float* o = ep.out + static_cast<long long>(r) * ep.ors + static_cast<long long>(c) * ep.ocs;
-  if (ep.accumulate) v += *o;
-  *o = v;
+}
+
+// Long-K split through global memory: the last split CTA of a tile sums
+// the partial planes in split order (loads batched over planes and
+// elements) and applies the epilogue.
+template <int BN>
+__device__ void reduce_partials(const GemmArgs& args, int row0, int col0, int rows, int cols,
+                                int tid) {
+  const long long plane = static_cast<long long>(args.m) * args.n;
+  const int zs = static_cast<int>(gridDim.z);
+  constexpr int U = 4, Z = 4;
+  constexpr int RSTEP = kThreads / BN;
+  const int c = tid & (BN - 1);
+  if (c >= cols) return;
+  for (int rb = tid / BN; rb < rows; rb += RSTEP * U) {
+    int rr[U], cc[U];
+    float sum[U];
+    int nv = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      rr[u] = row0 + rb + u * RSTEP;
+      cc[u] = col0 + c;
+      sum[u] = 0.f;
+      if (rb + u * RSTEP < rows) nv = u + 1;
+    }
+    for (int z0 = 0; z0 < zs; z0 += Z) {
+      float p[Z][U];
+#pragma unroll
+      for (int z = 0; z < Z; ++z)
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          p[z][u] = (z0 + z < zs && u < nv)
+                        ? __ldcg(args.ws + (z0 + z) * plane +
+                                 static_cast<long long>(rr[u]) * args.n + cc[u])
+                        : 0.f;
+#pragma unroll
+      for (int z = 0; z < Z; ++z)
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (z0 + z < zs) sum[u] += p[z][u];
+    }
+    epi_store_batch<U>(args.ep, args.ex, rr, cc, sum, nv);
+  }
 }
 
 template <int BN, bool SPLIT>
@@ -444,62 +626,64 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     umma_commit(accum_bar);
   }
 
-  // ---- epilogue: TMEM -> registers -> staged tile in shared memory ->
-  // coalesced stores (the pipeline ring is idle once the accumulator is
-  // ready, so the tile reuses it) ----
-  const bool split_k = args.ws != nullptr;
+  // ---- epilogue: TMEM -> registers -> staged tile in shared memory (the
+  // ring is idle once the accumulator is ready, so the tile reuses it) ----
   const int rows = min(128, args.m - row0);
   const int cols = min(BN, args.n - col0);
-  constexpr int LD = BN + 1;  // padded row: conflict-free in both passes
   float* tile = reinterpret_cast<float*>(sgen);
   if (warp < kLoadWarps) {
     if (!mbar_wait(accum_bar, 0)) timed_out = true;
     tc_fence_after();
-    {
-      const int rl = (warp & 3) * 32 + lane;
-      const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-      const int cbeg = (warp >> 2) * (BN / 2);
+    const int rl = (warp & 3) * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const int cbeg = (warp >> 2) * (BN / 2);
 #pragma unroll 1
-      for (int c = cbeg; c < cbeg + BN / 2; c += 8) {
-        if (c >= cols) break;  // uniform across the warp
-        float v[8];
-        tmem_ld8(trow + c, v);
+    for (int c = cbeg; c < cbeg + BN / 2; c += 8) {
+      if (c >= cols) break;  // uniform across the warp
+      float v[8];
+      tmem_ld8(trow + c, v);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) tile[rl * LD + c + q] = v[q];
-      }
+      for (int q = 0; q < 8; ++q) tile[rl * kTileLd<BN> + c + q] = v[q];
     }
-    loader_sync();
-    if (timed_out) {
-      record_error(args.status, kErrWaitTimeout);
-    } else if (split_k) {
-      float* wz = args.ws + static_cast<long long>(blockIdx.z) * args.m * args.n;
-      for (int e = tid; e < rows * cols; e += kThreads) {
-        const int rl = e / cols, c = e - rl * cols;
-        wz[static_cast<long long>(row0 + rl) * args.n + col0 + c] = tile[rl * LD + c];
-      }
-    } else if (args.ep.ocs == 1 || args.ep.ors != 1) {
-      for (int e = tid; e < rows * cols; e += kThreads) {
-        const int rl = e / cols, c = e - rl * cols;
-        epi_store(args.ep, args.ex, row0 + rl, col0 + c, tile[rl * LD + c]);
-      }
+  }
+  tc_fence_before();
+  __syncthreads();  // the staged tile is complete and TMEM is no longer read
+  if (warp == kMmaWarp) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (timed_out) record_error(args.status, kErrWaitTimeout);
+
+  const int csplits = args.cluster_splits;
+  if (csplits > 1) {
+    // The split CTAs of this tile are one cluster. Once every partial is
+    // staged, CTA `rank` sums rows [rank*per, (rank+1)*per) across the
+    // cluster's shared memory in split order and stores them.
+    cluster_sync_all();
+    const int rank = static_cast<int>(cluster_ctarank());
+    const int per = (rows + csplits - 1) / csplits;
+    const int r_lo = min(rows, rank * per);
+    const int r_hi = min(rows, r_lo + per);
+    if (warp < kLoadWarps)
+      store_tile<BN>(args, smem_u32(tile), row0, col0, r_lo, r_hi, cols, csplits, tid);
+    cluster_sync_all();  // peers have finished reading this CTA's tile
+  } else if (warp < kLoadWarps) {
+    if (args.ws == nullptr) {
+      store_tile<BN>(args, smem_u32(tile), row0, col0, 0, rows, cols, 1, tid);
     } else {
-      // Transposed output (ors == 1): walk rows fastest.
-      for (int e = tid; e < rows * cols; e += kThreads) {
-        const int c = e / rows, rl = e - c * rows;
-        epi_store(args.ep, args.ex, row0 + rl, col0 + c, tile[rl * LD + c]);
+      // Long-K split through global memory: this split's partial tile.
+      float* wz = args.ws + static_cast<long long>(blockIdx.z) * args.m * args.n;
+      constexpr int RSTEP = kThreads / BN;
+      const int c = tid & (BN - 1);
+      if (c < cols) {
+#pragma unroll 4
+        for (int r = tid / BN; r < rows; r += RSTEP)
+          wz[static_cast<long long>(row0 + r) * args.n + col0 + c] = tile[r * kTileLd<BN> + c];
       }
     }
-  } else if (timed_out) {
-    record_error(args.status, kErrWaitTimeout);
   }
 
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, Cfg::kTmemCols);
-
-  if (split_k && args.reduce_in_kernel) {
+  if (args.ws != nullptr && csplits <= 1 && args.reduce_in_kernel) {
     // The last split CTA of this tile sums every partial in split order.
     const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
+    __syncthreads();
     if (tid == 0) {
       __threadfence();
       const unsigned prev = atomicAdd(reinterpret_cast<unsigned*>(args.counters) + tile_id, 1u);
@@ -508,14 +692,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     __syncthreads();
     if (s_last) {
       __threadfence();
-      const long long plane = static_cast<long long>(args.m) * args.n;
-      for (int e = tid; e < rows * cols; e += kBlockThreads) {
-        const int rr = row0 + e / cols, cc = col0 + e % cols;
-        const float* p = args.ws + static_cast<long long>(rr) * args.n + cc;
-        float sum = 0.f;
-        for (unsigned z = 0; z < gridDim.z; ++z) sum += __ldcg(p + z * plane);
-        epi_store(args.ep, args.ex, rr, cc, sum);
-      }
+      if (warp < kLoadWarps) reduce_partials<BN>(args, row0, col0, rows, cols, tid);
       if (tid == 0) args.counters[tile_id] = 0;
     }
   }
@@ -526,34 +703,73 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int m, int n,
                                      ttrl_epilogue ep, EpiExtra ex) {
   const long long total = static_cast<long long>(m) * n;
+  constexpr int Z = 8;
   for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(idx / n);
-    const int c = static_cast<int>(idx - static_cast<long long>(r) * n);
-    float s = 0.f;
-    for (int sp = 0; sp < splits; ++sp) s += ws[static_cast<long long>(sp) * total + idx];
-    epi_store(ep, ex, r, c, s);
+    int r[1], c[1];
+    r[0] = static_cast<int>(idx / n);
+    c[0] = static_cast<int>(idx - static_cast<long long>(r[0]) * n);
+    float s[1] = {0.f};
+    for (int z0 = 0; z0 < splits; z0 += Z) {
+      float p[Z];
+#pragma unroll
+      for (int z = 0; z < Z; ++z)
+        p[z] = z0 + z < splits ? ws[static_cast<long long>(z0 + z) * total + idx] : 0.f;
+#pragma unroll
+      for (int z = 0; z < Z; ++z)
+        if (z0 + z < splits) s[0] += p[z];
+    }
+    epi_store_batch<1>(ep, ex, r, c, s, 1);
   }
 }
 
 // ------------------------------------------------------------------ host
 
+// Sets the kernel's shared-memory limit, allows clusters above the portable
+// size 8, and returns the largest split-K cluster (16 or 8) the device can
+// co-schedule at this kernel's footprint.
 template <int BN, bool SPLIT>
-static int set_smem_attr() {
+static int set_smem_attr(int* cluster_cap) {
   using Cfg = TileCfg<BN, SPLIT>;
   cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
-  return e == cudaSuccess ? TTRL_OK : set_cuda_error("cudaFuncSetAttribute(gemm)", e);
+  if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
+  int cap = 8;
+  if (cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT>,
+                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, 16);
+    cfg.blockDim = dim3(kBlockThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 16;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<BN, SPLIT>, &cfg) ==
+            cudaSuccess &&
+        clusters >= 1)
+      cap = 16;
+  }
+  cudaGetLastError();  // a refused probe leaves no sticky error
+  if (cap < *cluster_cap) *cluster_cap = cap;
+  return TTRL_OK;
 }
 
 int gemm_init_device() {
   int rc = TTRL_OK;
-  if ((rc = set_smem_attr<32, true>())) return rc;
-  if ((rc = set_smem_attr<64, true>())) return rc;
-  if ((rc = set_smem_attr<128, true>())) return rc;
-  if ((rc = set_smem_attr<32, false>())) return rc;
-  if ((rc = set_smem_attr<64, false>())) return rc;
-  if ((rc = set_smem_attr<128, false>())) return rc;
+  int cap = 16;
+  if ((rc = set_smem_attr<32, true>(&cap))) return rc;
+  if ((rc = set_smem_attr<64, true>(&cap))) return rc;
+  if ((rc = set_smem_attr<128, true>(&cap))) return rc;
+  if ((rc = set_smem_attr<32, false>(&cap))) return rc;
+  if ((rc = set_smem_attr<64, false>(&cap))) return rc;
+  if ((rc = set_smem_attr<128, false>(&cap))) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) g_max_cluster[dev] = cap;
   return TTRL_OK;
 }
 
@@ -637,46 +853,81 @@ static int pick_bn(int n) {
 
 struct Schedule {
   int bn, kblocks, splits, kb_per_split, tiles;
+  bool cluster;  // the splits of a tile reduce through distributed shared memory
 };
+
+static int max_cluster_for_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 8;
+  return g_max_cluster[dev] > 0 ? g_max_cluster[dev] : 8;
+}
 
 static Schedule make_schedule(const ttrl_gemm_desc& d) {
   Schedule s;
   s.bn = pick_bn(d.n);
   s.kblocks = (d.k + 31) / 32;
   s.tiles = ((d.m + 127) / 128) * ((d.n + s.bn - 1) / s.bn);
+  const int cmax = max_cluster_for_current_device();
   int splits = d.splits;
+  bool global_split = false;
   if (splits <= 0) {
-    // Aim for about one wave of 148 SMs, at least 4 k-blocks per CTA, and
-    // at most 32 partials for the last CTA of a tile to reduce.
+    // Aim for about one wave of 148 SMs with at least 4 k-blocks per CTA.
+    // Up to `cmax` splits reduce inside a cluster; beyond that (very long
+    // K, where each CTA would still walk >= 32 k-blocks) up to 32 splits
+    // reduce through global memory.
     splits = 1;
     if (s.tiles < 120 && s.kblocks >= 8) {
       const int want = (148 + s.tiles - 1) / s.tiles;
       const int most = s.kblocks / 4;
       splits = want < most ? want : most;
-      if (splits > 32) splits = 32;
+      if (splits > cmax) {
+        if (s.kblocks / cmax >= 32) {
+          global_split = true;
+          if (splits > 32) splits = 32;
+        } else {
+          splits = cmax;
+        }
+      }
       if (splits < 1) splits = 1;
     }
+  } else if (splits > cmax) {
+    global_split = true;
   }
   if (splits > s.kblocks) splits = s.kblocks > 0 ? s.kblocks : 1;
   s.kb_per_split = (s.kblocks + splits - 1) / splits;
   if (s.kb_per_split < 1) s.kb_per_split = 1;
   s.splits = (s.kblocks + s.kb_per_split - 1) / s.kb_per_split;
   if (s.splits < 1) s.splits = 1;
+  s.cluster = s.splits > 1 && !global_split;
   return s;
 }
 
 size_t gemm_workspace_bytes(const ttrl_gemm_desc& d) {
   const Schedule s = make_schedule(d);
-  if (s.splits <= 1) return kCounterBytes;
+  if (s.splits <= 1 || s.cluster) return kCounterBytes;
   return kCounterBytes + static_cast<size_t>(s.splits) * d.m * d.n * sizeof(float);
 }
 
 template <int BN, bool SPLIT>
-static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, cudaStream_t stream) {
+static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, int cluster_z, cudaStream_t stream) {
   using Cfg = TileCfg<BN, SPLIT>;
-  gemm_tc_kernel<BN, SPLIT><<<grid, kBlockThreads, Cfg::kSmem, stream>>>(args);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kBlockThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (cluster_z > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, SPLIT>, args);
   note_launch();
-  return cudaGetLastError();
+  return e;
 }
 
 int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* counters,
@@ -705,7 +956,9 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   const Schedule s = make_schedule(d);
   args.kblocks = s.kblocks;
   args.kb_per_split = s.kb_per_split;
-  if (s.splits > 1) {
+  if (s.cluster) {
+    args.cluster_splits = s.splits;
+  } else if (s.splits > 1) {
     const size_t need = static_cast<size_t>(s.splits) * d.m * d.n * sizeof(float);
     if (counters == nullptr || partials == nullptr || partial_bytes < need)
       return set_error(TTRL_EWORKSPACE, "gemm: needs %zu bytes of workspace, got %zu",
@@ -721,14 +974,17 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   }
   dim3 grid((d.m + 127) / 128, (d.n + s.bn - 1) / s.bn, s.splits);
   const bool split3 = d.precision == TTRL_PREC_TF32X3;
+  const int cz = s.cluster ? s.splits : 1;
   cudaError_t e;
   switch (s.bn) {
-    case 32: e = split3 ? launch_bn<32, true>(args, grid, stream) : launch_bn<32, false>(args, grid, stream); break;
-    case 64: e = split3 ? launch_bn<64, true>(args, grid, stream) : launch_bn<64, false>(args, grid, stream); break;
-    default: e = split3 ? launch_bn<128, true>(args, grid, stream) : launch_bn<128, false>(args, grid, stream); break;
+    case 32: e = split3 ? launch_bn<32, true>(args, grid, cz, stream) : launch_bn<32, false>(args, grid, cz, stream); break;
+    case 64: e = split3 ? launch_bn<64, true>(args, grid, cz, stream) : launch_bn<64, false>(args, grid, cz, stream); break;
+    default: e = split3 ? launch_bn<128, true>(args, grid, cz, stream) : launch_bn<128, false>(args, grid, cz, stream); break;
   }
   if (e != cudaSuccess) return set_cuda_error("gemm launch", e);
-  if (s.splits > 1 && !args.reduce_in_kernel) {
+  if (s.splits > 1 && !s.cluster && !args.reduce_in_kernel) {
+    if (args.ws == nullptr)
+      return set_error(TTRL_EUNSUPPORTED, "gemm: split-K reduce without partials");
     const long long total = static_cast<long long>(d.m) * d.n;
     int blocks = static_cast<int>((total + 255) / 256);
     if (blocks > 148 * 8) blocks = 148 * 8;

@@ -56,6 +56,8 @@ struct GemmArgs {
   int32_t kblocks;
   int32_t kb_per_split;
   int32_t reduce_in_kernel;  // last split CTA sums the partials (else a second kernel)
+  int32_t cluster_splits;    // > 1: the splits of a tile form a cluster and reduce in DSMEM
+  int32_t pad0;
   float* ws;      // split-K partials [splits][m][n], or null
   int* counters;  // split-K arrival counter per output tile
   int* status;

@@ -196,23 +196,42 @@ __global__ void col2im_kernel(const float* __restrict__ dxcol, const float* __re
     t /= g.w;
     const int iy = static_cast<int>(t % g.h);
     const int img = static_cast<int>(t / g.h);
+    // The mask and old value load first, and each kernel row's taps load
+    // together (kx unrolled), so a pixel waits on a few memory round trips
+    // rather than one per tap. Taps are summed in (ky, kx) order.
+    const float mk = mask != nullptr ? mask[idx] : 1.f;
+    const float old = accumulate ? dx[idx] : 0.f;
     float s = 0.f;
     for (int ky = 0; ky < g.kh; ++ky) {
       const int ty = iy + g.pad - ky;
       if (ty < 0 || ty % g.stride) continue;
       const int oy = ty / g.stride;
       if (oy >= g.oh) continue;
-      for (int kx = 0; kx < g.kw; ++kx) {
+      const long long row0 = (static_cast<long long>(img) * g.oh + oy) * g.ow;
+      constexpr int kMaxKw = 8;
+      float v[kMaxKw];
+#pragma unroll
+      for (int kx = 0; kx < kMaxKw; ++kx) {
+        v[kx] = 0.f;
+        const int tx = ix + g.pad - kx;
+        if (kx < g.kw && tx >= 0 && tx % g.stride == 0 && tx / g.stride < g.ow)
+          v[kx] = dxcol[(row0 + tx / g.stride) * kk + (ky * g.kw + kx) * g.c + c];
+      }
+#pragma unroll
+      for (int kx = 0; kx < kMaxKw; ++kx) {
+        const int tx = ix + g.pad - kx;
+        if (kx < g.kw && tx >= 0 && tx % g.stride == 0 && tx / g.stride < g.ow) s += v[kx];
+      }
+      for (int kx = kMaxKw; kx < g.kw; ++kx) {  // kernels wider than 8
         const int tx = ix + g.pad - kx;
         if (tx < 0 || tx % g.stride) continue;
         const int ox = tx / g.stride;
         if (ox >= g.ow) continue;
-        const long long row = (static_cast<long long>(img) * g.oh + oy) * g.ow + ox;
-        s += dxcol[row * kk + (ky * g.kw + kx) * g.c + c];
+        s += dxcol[(row0 + ox) * kk + (ky * g.kw + kx) * g.c + c];
       }
     }
-    if (mask != nullptr && !(mask[idx] > 0.f)) s = 0.f;
-    if (accumulate) s += dx[idx];
+    if (!(mk > 0.f) && mask != nullptr) s = 0.f;
+    if (accumulate) s += old;
     dx[idx] = s;
   }
 }
