@@ -69,16 +69,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 
 // 16-byte global->shared copy; src_bytes == 0 zero-fills the destination.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  // No "memory" clobber: the destination is read only after cp_async_wait,
+  // which carries one, and a clobber here would force the compiler to reload
+  // every value it holds from memory after each copy.
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(src_bytes)
-               : "memory");
+               "r"(src_bytes));
 }
 
 // 4-byte global->shared copy; src_bytes == 0 zero-fills the destination.
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
-               "r"(src_bytes)
-               : "memory");
+               "r"(src_bytes));
 }
 
 __device__ __forceinline__ void cp_async_commit() {

@@ -29,6 +29,9 @@
 // epilogue, so results are deterministic and no second kernel is launched.
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "internal.h"
@@ -58,7 +61,7 @@ __device__ __forceinline__ int fdiv(const FastDiv& f, int n) {
 }
 
 // General element address (used by the scalar fallback modes only).
-__device__ const float* opnd_addr(const DevOperand& o, int r, int k, bool& ok) {
+__device__ __forceinline__ const float* opnd_addr(const DevOperand& o, int r, int k, bool& ok) {
   ok = false;
   if (k >= o.kdim) return o.ptr;
   if (r >= o.rows) {
@@ -104,7 +107,7 @@ struct Loader {
   int cky, ckx;
   bool cvalid, cones;
 
-  __device__ void init(const DevOperand& o, int row0, int tid) {
+  __device__ __forceinline__ void init(const DevOperand& o, int row0, int tid) {
     valid = ones = 0;
     coff = 0;
     cky = ckx = 0;
@@ -150,7 +153,8 @@ struct Loader {
     }
   }
 
-  __device__ void issue(const DevOperand& o, uint32_t base, int row0, int k0, int tid) {
+  __device__ __forceinline__ void issue(const DevOperand& o, uint32_t base, int row0, int k0,
+                                        int tid) {
     if (o.mode == kModeKVec) {
       const int kc = tid & 7;
       const int k = k0 + kc * 4;
@@ -220,7 +224,8 @@ struct Loader {
 
   // Split the chunks this thread copied for one stage: hi (tf32-exact) in
   // place in the raw tile, lo = x - hi at the same offset in the low tile.
-  __device__ void split(const DevOperand& o, uint8_t* hi_gen, uint8_t* lo_gen, int tid) const {
+  __device__ __forceinline__ void split(const DevOperand& o, uint8_t* hi_gen, uint8_t* lo_gen,
+                                        int tid) const {
     if (o.mode == kModeKVec || o.mode == kModeMNVec) {
       uint32_t off[P];
       float4 x[P];
@@ -308,10 +313,6 @@ __device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const E
   }
 }
 
-constexpr int kEpiBatch = 8;
-
-template <int BN>
-constexpr int kTileLd = BN + 1;  // padded staging row: conflict-free both ways
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
@@ -324,95 +325,116 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
-// Shared-memory float at `saddr` in cluster CTA `rank` (DSMEM).
-__device__ __forceinline__ float ld_dsmem(uint32_t saddr, int rank) {
-  uint32_t remote;
-  float v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ float ld_smem(uint32_t saddr) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(saddr) : "memory");
-  return v;
-}
-
-// Stores rows [r_lo, r_hi) x [0, cols) of a staged 128 x BN tile through the
-// epilogue. With nsrc > 1 each value is the sum, in cluster-rank order, of
-// the same element of the nsrc cluster CTAs' staged tiles. The thread ->
-// element map uses only compile-time shifts: columns fastest for row-major
-// outputs, rows fastest for transposed ones (ors == 1), so stores coalesce.
+// Staged accumulator tile in shared memory. Its layout follows the output's
+// contiguous dimension so the stores coalesce and the cluster reduction can
+// move 16-byte groups: row-major (column fastest, row pitch BN + 4 floats)
+// for ordinary outputs, column-major (row fastest, column pitch 132) for
+// transposed ones (ors == 1). The +4 padding keeps 16-byte alignment and
+// spreads the per-row writes from TMEM over the banks.
 template <int BN>
-__device__ void store_tile(const GemmArgs& args, uint32_t tile_s, int row0, int col0, int r_lo,
-                           int r_hi, int cols, int nsrc, int tid) {
-  constexpr int LD = kTileLd<BN>;
-  constexpr int U = kEpiBatch;
-  const bool rows_fast = !(args.ep.ocs == 1 || args.ep.ors != 1);
-  int rr[U], cc[U];
-  float acc[U];
-  if (!rows_fast) {
-    constexpr int RSTEP = kThreads / BN;
-    const int c = tid & (BN - 1);
-    for (int rb = r_lo + tid / BN; rb < r_hi; rb += RSTEP * U) {
-      int nv = 0;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int r = rb + u * RSTEP;
-        rr[u] = row0 + r;
-        cc[u] = col0 + c;
-        acc[u] = 0.f;
-        if (r < r_hi && c < cols) nv = u + 1;
-      }
-      if (c >= cols) nv = 0;
+struct Stage {
+  static constexpr int kLdRow = BN + 4;
+  static constexpr int kLdCol = 128 + 4;
+  static constexpr int kBytes = (128 * kLdRow > BN * kLdCol ? 128 * kLdRow : BN * kLdCol) * 4;
+};
+
+__device__ __forceinline__ float4 ld_smem4(uint32_t saddr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(saddr));
+  return v;
+}
+
+// 16 bytes of shared memory at `saddr` in cluster CTA `rank` (DSMEM).
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t saddr, int rank) {
+  uint32_t remote;
+  float4 v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote));
+  return v;
+}
+
+// Stores rows [r_lo, r_hi) x [0, cols) of a staged tile through the
+// epilogue. With nsrc > 1 each value is the sum, in cluster-rank order, of
+// the same element of the nsrc cluster CTAs' staged tiles. Every thread
+// owns 4-element groups along the staged tile's contiguous dimension.
+template <int BN>
+__device__ __forceinline__ void store_tile(const ttrl_epilogue& ep, const EpiExtra& ex,
+                                           uint32_t tile_s, bool colmajor, int row0, int col0,
+                                           int r_lo, int r_hi, int cols, int nsrc, int tid) {
+  using St = Stage<BN>;
+  int rr[4], cc[4];
+  float acc[4];
+  if (!colmajor) {
+    constexpr int G = BN / 4;             // column groups per row
+    constexpr int RSTEP = kThreads / G;   // rows per pass
+    const int c0 = (tid % G) * 4;
+    if (c0 >= cols) return;
+    for (int r = r_lo + tid / G; r < r_hi; r += RSTEP) {
+      const uint32_t off = tile_s + (r * St::kLdRow + c0) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (nsrc == 1) {
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (u < nv) acc[u] = ld_smem(tile_s + ((rb + u * RSTEP) * LD + c) * 4);
+        v = ld_smem4(off);
       } else {
 #pragma unroll 4
-        for (int q = 0; q < nsrc; ++q)
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (u < nv && rb + u * RSTEP < r_hi)
-              acc[u] += ld_dsmem(tile_s + ((rb + u * RSTEP) * LD + c) * 4, q);
+        for (int q = 0; q < nsrc; ++q) {
+          const float4 p = ld_dsmem4(off, q);
+          v.x += p.x;
+          v.y += p.y;
+          v.z += p.z;
+          v.w += p.w;
+        }
       }
-      // A row past r_hi inside the batch is not valid even if a later one
-      // were: rows grow with u, so the valid ones are a prefix.
-      int np = 0;
+      acc[0] = v.x;
+      acc[1] = v.y;
+      acc[2] = v.z;
+      acc[3] = v.w;
+      int nv = 0;
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (u < nv && rb + u * RSTEP < r_hi) np = u + 1;
-      epi_store_batch<U>(args.ep, args.ex, rr, cc, acc, np);
+      for (int u = 0; u < 4; ++u) {
+        rr[u] = row0 + r;
+        cc[u] = col0 + c0 + u;
+        if (c0 + u < cols) nv = u + 1;
+      }
+      epi_store_batch<4>(ep, ex, rr, cc, acc, nv);
     }
   } else {
-    const int r = r_lo + (tid & 127);
-    for (int cb = tid >> 7; cb < cols; cb += 2 * U) {
-      int nv = 0;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int c = cb + u * 2;
-        rr[u] = row0 + r;
-        cc[u] = col0 + c;
-        acc[u] = 0.f;
-        if (c < cols && r < r_hi) nv = u + 1;
-      }
-      if (r >= r_hi) nv = 0;
+    const int r_span = r_hi - r_lo;
+    const int G = (r_span + 3) / 4;       // row groups in the slice (<= 32)
+    const int rg = tid & 31;
+    if (rg >= G) return;
+    const int r = r_lo + rg * 4;
+    for (int c = tid >> 5; c < cols; c += kThreads / 32) {
+      const uint32_t off = tile_s + (c * St::kLdCol + r) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (nsrc == 1) {
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (u < nv) acc[u] = ld_smem(tile_s + (r * LD + cb + u * 2) * 4);
+        v = ld_smem4(off);
       } else {
 #pragma unroll 4
-        for (int q = 0; q < nsrc; ++q)
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            if (u < nv) acc[u] += ld_dsmem(tile_s + (r * LD + cb + u * 2) * 4, q);
+        for (int q = 0; q < nsrc; ++q) {
+          const float4 p = ld_dsmem4(off, q);
+          v.x += p.x;
+          v.y += p.y;
+          v.z += p.z;
+          v.w += p.w;
+        }
       }
-      epi_store_batch<U>(args.ep, args.ex, rr, cc, acc, nv);
+      acc[0] = v.x;
+      acc[1] = v.y;
+      acc[2] = v.z;
+      acc[3] = v.w;
+      int nv = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        rr[u] = row0 + r + u;
+        cc[u] = col0 + c;
+        if (r + u < r_hi) nv = u + 1;
+      }
+      epi_store_batch<4>(ep, ex, rr, cc, acc, nv);
     }
-    // Slices taller than 128 rows do not occur: tiles are 128 rows.
   }
 }
 
@@ -420,9 +442,10 @@ __device__ void store_tile(const GemmArgs& args, uint32_t tile_s, int row0, int 
 // the partial planes in split order (loads batched over planes and
 // elements) and applies the epilogue.
 template <int BN>
-__device__ void reduce_partials(const GemmArgs& args, int row0, int col0, int rows, int cols,
-                                int tid) {
-  const long long plane = static_cast<long long>(args.m) * args.n;
+__device__ __forceinline__ void reduce_partials(const ttrl_epilogue& ep, const EpiExtra& ex,
+                                                const float* ws, int m, int n, int row0, int col0,
+                                                int rows, int cols, int tid) {
+  const long long plane = static_cast<long long>(m) * n;
   const int zs = static_cast<int>(gridDim.z);
   constexpr int U = 4, Z = 4;
   constexpr int RSTEP = kThreads / BN;
@@ -446,8 +469,7 @@ __device__ void reduce_partials(const GemmArgs& args, int row0, int col0, int ro
 #pragma unroll
         for (int u = 0; u < U; ++u)
           p[z][u] = (z0 + z < zs && u < nv)
-                        ? __ldcg(args.ws + (z0 + z) * plane +
-                                 static_cast<long long>(rr[u]) * args.n + cc[u])
+                        ? __ldcg(ws + (z0 + z) * plane + static_cast<long long>(rr[u]) * n + cc[u])
                         : 0.f;
 #pragma unroll
       for (int z = 0; z < Z; ++z)
@@ -455,7 +477,23 @@ __device__ void reduce_partials(const GemmArgs& args, int row0, int col0, int ro
         for (int u = 0; u < U; ++u)
           if (z0 + z < zs) sum[u] += p[z][u];
     }
-    epi_store_batch<U>(args.ep, args.ex, rr, cc, sum, nv);
+    epi_store_batch<U>(ep, ex, rr, cc, sum, nv);
+  }
+}
+
+// One operand tile of R rows x 32 k by TMA, into the same shared-memory
+// layout the cp.async gathers produce: K-major tiles as one box (128-byte
+// swizzle), MN-major tiles as R/32 boxes of 32 rows x 32 k (128-byte swizzle
+// with 32-byte atoms). Coordinates are innermost first; the innermost one is
+// a multiple of 4 floats (16 bytes) by construction.
+template <int R>
+__device__ __forceinline__ void tma_operand(const CUtensorMap* map, bool mn, uint32_t dst,
+                                            int row0, int k0, uint32_t bar) {
+  if (!mn) {
+    tma_load_2d(dst, map, k0, row0, bar);
+  } else {
+#pragma unroll
+    for (int g = 0; g < R / 32; ++g) tma_load_2d(dst + g * 4096, map, row0 + g * 32, k0, bar);
   }
 }
 
@@ -478,7 +516,7 @@ struct TileCfg {
   static constexpr int kSmem =
       (kStages + kLoSlots) * kTile + 1024 /*align slack*/ + 512 /*barriers*/;
   static_assert(kStages >= 3, "at least three pipeline stages");
-  static_assert(kStages * kTile >= 128 * (BN + 1) * 4, "epilogue staging fits in the ring");
+  static_assert(kStages * kTile >= Stage<BN>::kBytes, "epilogue staging fits in the ring");
 };
 
 // Named barrier over the 256 loader threads (the MMA warp does not join).
@@ -503,7 +541,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const uint32_t empty0 = lo_base + L * Cfg::kTile;  // S "raw stage free"
   const uint32_t full0 = empty0 + S * 8;              // S "stage ready for MMA"
   const uint32_t loempty0 = full0 + S * 8;            // L "lo slot free"
-  const uint32_t accum_bar = loempty0 + (L > 0 ? L : 1) * 8;
+  const uint32_t tfull0 = loempty0 + (L > 0 ? L : 1) * 8;  // S "TMA bytes landed"
+  const uint32_t accum_bar = tfull0 + S * 8;
   const uint32_t tmem_slot = accum_bar + 8;
   const uint32_t* tmem_slot_gen =
       reinterpret_cast<const uint32_t*>(sgen + (tmem_slot - sbase));
@@ -520,6 +559,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(empty0 + s * 8, 1);
       mbar_init(full0 + s * 8, kLoadWarps);
+      mbar_init(tfull0 + s * 8, 1);
     }
     for (int l = 0; l < L; ++l) mbar_init(loempty0 + l * 8, 1);
     mbar_init(accum_bar, 1);
@@ -547,16 +587,33 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 
   if (warp < kLoadWarps) {
     // ---- loader warps ----
+    // Operand descriptors in registers: helpers that read them through a
+    // reference to the kernel parameter block would reload every field
+    // (a generic load) after each copy instruction.
+    const DevOperand oa = args.a;
+    const DevOperand ob = args.b;
     Loader<128> la;
     Loader<BN> lb;
-    la.init(args.a, row0, tid);
-    lb.init(args.b, col0, tid);
+    la.init(oa, row0, tid);
+    lb.init(ob, col0, tid);
+    // Dense operands arrive by TMA (thread 0 issues the whole stage and
+    // the bytes complete on tfull); gathered ones by per-thread cp.async.
+    const bool a_tma = args.a_tma != 0, b_tma = args.b_tma != 0;
+    const bool any_tma = a_tma || b_tma;
+    const uint32_t tma_bytes = (a_tma ? Cfg::kABytes : 0) + (b_tma ? Cfg::kBBytes : 0);
+    auto issue_stage = [&](int st, int kb) {
+      const int k0 = kb * 32;
+      if (any_tma && tid == 0) {
+        mbar_arrive_expect_tx(tfull0 + st * 8, tma_bytes);
+        if (a_tma) tma_operand<128>(&args.tma_a, a_mn, raw_a(st), row0, k0, tfull0 + st * 8);
+        if (b_tma) tma_operand<BN>(&args.tma_b, b_mn, raw_b(st), col0, k0, tfull0 + st * 8);
+      }
+      if (!a_tma) la.issue(oa, raw_a(st), row0, k0, tid);
+      if (!b_tma) lb.issue(ob, raw_b(st), col0, k0, tid);
+    };
 #pragma unroll 1
     for (int s = 0; s < AHEAD; ++s) {
-      if (s < nk) {
-        la.issue(args.a, raw_a(s), row0, (kb0 + s) * 32, tid);
-        lb.issue(args.b, raw_b(s), col0, (kb0 + s) * 32, tid);
-      }
+      if (s < nk) issue_stage(s, kb0 + s);
       cp_async_commit();
     }
 #pragma unroll 1
@@ -568,12 +625,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           // Raw stage sj was last read by the MMAs of k-block j - S.
           if (!mbar_wait(empty0 + sj * 8, ((j - S) / S) & 1)) timed_out = true;
         }
-        la.issue(args.a, raw_a(sj), row0, (kb0 + j) * 32, tid);
-        lb.issue(args.b, raw_b(sj), col0, (kb0 + j) * 32, tid);
+        issue_stage(sj, kb0 + j);
       }
       cp_async_commit();
       cp_async_wait<AHEAD>();  // this thread's copies of k-block i have landed
       const int s = i % S;
+      if (any_tma && !mbar_wait(tfull0 + s * 8, (i / S) & 1)) timed_out = true;
       if (split_a || split_b) {
         const int l = i % LL;
         if (i >= L) {
@@ -582,8 +639,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
         uint8_t* hi = sgen + s * Cfg::kTile;
         uint8_t* lo = sgen + (lo_base - sbase) + l * Cfg::kTile;
-        if (split_a) la.split(args.a, hi, lo, tid);
-        if (split_b) lb.split(args.b, hi + Cfg::kABytes, lo + Cfg::kABytes, tid);
+        if (split_a) la.split(oa, hi, lo, tid);
+        if (split_b) lb.split(ob, hi + Cfg::kABytes, lo + Cfg::kABytes, tid);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -631,6 +688,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const int rows = min(128, args.m - row0);
   const int cols = min(BN, args.n - col0);
   float* tile = reinterpret_cast<float*>(sgen);
+  const bool colmajor = args.ep.ors == 1 && args.ep.ocs != 1 && args.ws == nullptr;
   if (warp < kLoadWarps) {
     if (!mbar_wait(accum_bar, 0)) timed_out = true;
     tc_fence_after();
@@ -642,8 +700,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       if (c >= cols) break;  // uniform across the warp
       float v[8];
       tmem_ld8(trow + c, v);
+      if (!colmajor) {
+        float4* dst = reinterpret_cast<float4*>(tile + rl * Stage<BN>::kLdRow + c);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) tile[rl * kTileLd<BN> + c + q] = v[q];
+        for (int q = 0; q < 8; ++q) tile[(c + q) * Stage<BN>::kLdCol + rl] = v[q];
+      }
     }
   }
   tc_fence_before();
@@ -652,21 +716,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   if (timed_out) record_error(args.status, kErrWaitTimeout);
 
   const int csplits = args.cluster_splits;
+  const ttrl_epilogue ep = args.ep;  // in registers, see the operand copies above
+  const EpiExtra ex = args.ex;
   if (csplits > 1) {
     // The split CTAs of this tile are one cluster. Once every partial is
     // staged, CTA `rank` sums rows [rank*per, (rank+1)*per) across the
     // cluster's shared memory in split order and stores them.
     cluster_sync_all();
     const int rank = static_cast<int>(cluster_ctarank());
-    const int per = (rows + csplits - 1) / csplits;
+    // Row slices in multiples of 4 so column-major groups stay aligned.
+    const int per = ((rows + csplits - 1) / csplits + 3) & ~3;
     const int r_lo = min(rows, rank * per);
     const int r_hi = min(rows, r_lo + per);
     if (warp < kLoadWarps)
-      store_tile<BN>(args, smem_u32(tile), row0, col0, r_lo, r_hi, cols, csplits, tid);
+      store_tile<BN>(ep, ex, smem_u32(tile), colmajor, row0, col0, r_lo, r_hi, cols, csplits,
+                     tid);
     cluster_sync_all();  // peers have finished reading this CTA's tile
   } else if (warp < kLoadWarps) {
     if (args.ws == nullptr) {
-      store_tile<BN>(args, smem_u32(tile), row0, col0, 0, rows, cols, 1, tid);
+      store_tile<BN>(ep, ex, smem_u32(tile), colmajor, row0, col0, 0, rows, cols, 1, tid);
     } else {
       // Long-K split through global memory: this split's partial tile.
       float* wz = args.ws + static_cast<long long>(blockIdx.z) * args.m * args.n;
@@ -675,7 +743,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       if (c < cols) {
 #pragma unroll 4
         for (int r = tid / BN; r < rows; r += RSTEP)
-          wz[static_cast<long long>(row0 + r) * args.n + col0 + c] = tile[r * kTileLd<BN> + c];
+          wz[static_cast<long long>(row0 + r) * args.n + col0 + c] =
+              tile[r * Stage<BN>::kLdRow + c];
       }
     }
   }
@@ -692,7 +761,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     __syncthreads();
     if (s_last) {
       __threadfence();
-      if (warp < kLoadWarps) reduce_partials<BN>(args, row0, col0, rows, cols, tid);
+      if (warp < kLoadWarps)
+        reduce_partials<BN>(ep, ex, args.ws, args.m, args.n, row0, col0, rows, cols, tid);
       if (tid == 0) args.counters[tile_id] = 0;
     }
   }
@@ -789,6 +859,59 @@ FastDiv make_fastdiv(int d) {
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// cuTensorMapEncodeTiled, fetched once through the runtime (no link against
+// the driver library).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// The TMA map of a dense operand whose tiles are R rows x 32 k, or false
+// when the operand is gathered instead (conv windows, odd strides or
+// alignment, or an appended ones row that is not in memory).
+static bool encode_operand_map(const DevOperand& o, int R, CUtensorMap* map) {
+  if (o.kind != TTRL_OPND_DENSE || o.ones_row) return false;
+  if (o.mode != kModeKVec && o.mode != kModeMNVec) return false;
+  if (o.rows <= 0 || o.kdim <= 0) return false;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2];
+  cuuint64_t strides[1];
+  cuuint32_t box[2];
+  const cuuint32_t es[2] = {1, 1};
+  CUtensorMapSwizzle sw;
+  if (o.mode == kModeKVec) {  // rows of K contiguous floats
+    dims[0] = static_cast<cuuint64_t>(o.kdim);
+    dims[1] = static_cast<cuuint64_t>(o.rows);
+    strides[0] = static_cast<cuuint64_t>(o.rs) * 4;
+    box[0] = 32;
+    box[1] = static_cast<cuuint32_t>(R);
+    sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  } else {  // k lines of contiguous rows
+    dims[0] = static_cast<cuuint64_t>(o.rows);
+    dims[1] = static_cast<cuuint64_t>(o.kdim);
+    strides[0] = static_cast<cuuint64_t>(o.ks) * 4;
+    box[0] = 32;
+    box[1] = 32;
+    sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  }
+  if (strides[0] % 16 != 0 || strides[0] >= (1ull << 40)) return false;
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(o.ptr), dims,
+                         strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 // Pick the gather mode of an operand from its strides and alignment.
 static int resolve_operand(const ttrl_operand& in, int ones_row, DevOperand& out) {
@@ -956,6 +1079,8 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   const Schedule s = make_schedule(d);
   args.kblocks = s.kblocks;
   args.kb_per_split = s.kb_per_split;
+  args.a_tma = encode_operand_map(args.a, 128, &args.tma_a) ? 1 : 0;
+  args.b_tma = encode_operand_map(args.b, s.bn, &args.tma_b) ? 1 : 0;
   if (s.cluster) {
     args.cluster_splits = s.splits;
   } else if (s.splits > 1) {

@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/ttrl_b200.h"
@@ -49,6 +50,10 @@ struct EpiExtra {
 };
 
 struct GemmArgs {
+  // TMA tile maps of the dense operands (valid when a_tma / b_tma is set);
+  // first, for their 64-byte alignment.
+  CUtensorMap tma_a;
+  CUtensorMap tma_b;
   DevOperand a, b;
   ttrl_epilogue ep;
   EpiExtra ex;
@@ -57,6 +62,7 @@ struct GemmArgs {
   int32_t kb_per_split;
   int32_t reduce_in_kernel;  // last split CTA sums the partials (else a second kernel)
   int32_t cluster_splits;    // > 1: the splits of a tile form a cluster and reduce in DSMEM
+  int32_t a_tma, b_tma;      // the operand's stages arrive by TMA instead of cp.async
   int32_t pad0;
   float* ws;      // split-K partials [splits][m][n], or null
   int* counters;  // split-K arrival counter per output tile
