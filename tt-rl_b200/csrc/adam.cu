@@ -80,10 +80,22 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
   const long long chunk = blockIdx.x;
   int ti = 0;
   while (ti + 1 < a.count && a.chunk_start[ti + 1] <= chunk) ++ti;
-  const ttrl_adam_tensor& T = a.t[ti];
+  const ttrl_adam_tensor T = a.t[ti];  // a register copy, not a reference into the parameter block
   const long long begin = (chunk - a.chunk_start[ti]) * kAdamChunk;
   const long long end = begin + kAdamChunk < T.numel ? begin + kAdamChunk : T.numel;
   const bool vec = (a.vec_mask >> ti) & 1ull;
+
+  // Operands first: their loads are in flight while the scalars below are
+  // computed from the step counter.
+  float4 g[kAdamQuads], p[kAdamQuads], S[kAdamQuads], V[kAdamQuads];
+#pragma unroll
+  for (int u = 0; u < kAdamQuads; ++u) {
+    const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+    g[u] = load4(T.grad, i, end, vec);
+    p[u] = load4(T.param, i, end, vec);
+    S[u] = load4(T.s, i, end, vec);
+    V[u] = load4(T.v, i, end, vec);
+  }
 
   const int step = a.steps[T.step_index] + 1;
   const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
@@ -99,15 +111,6 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
   k.scaled = a.grad_scale != nullptr;
   k.gs = k.scaled ? *a.grad_scale : 1.f;
 
-  float4 g[kAdamQuads], p[kAdamQuads], S[kAdamQuads], V[kAdamQuads];
-#pragma unroll
-  for (int u = 0; u < kAdamQuads; ++u) {
-    const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
-    g[u] = load4(T.grad, i, end, vec);
-    p[u] = load4(T.param, i, end, vec);
-    S[u] = load4(T.s, i, end, vec);
-    V[u] = load4(T.v, i, end, vec);
-  }
 #pragma unroll
   for (int u = 0; u < kAdamQuads; ++u) {
     const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;

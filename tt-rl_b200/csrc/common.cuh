@@ -227,6 +227,11 @@ __device__ __forceinline__ uint32_t mnmajor_off(int row, int k) {
 
 // Split x into a tf32-representable high part (low 13 mantissa bits
 // cleared) and the exact fp32 remainder.
+// x minus its tf32 truncation (the bits a tcgen05 tf32 MMA ignores), exact.
+__device__ __forceinline__ float tf32_low(float x) {
+  return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
   lo = x - hi;

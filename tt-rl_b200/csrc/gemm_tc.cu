@@ -40,8 +40,9 @@ namespace ttrl {
 
 constexpr int kLoadWarps = 8;
 constexpr int kThreads = 256;                       // loader threads
-constexpr int kBlockThreads = kThreads + 32;        // + the MMA warp
+constexpr int kBlockThreads = kThreads + 64;        // + the MMA warp + the TMA producer warp
 constexpr int kMmaWarp = kLoadWarps;
+constexpr int kProducerWarp = kLoadWarps + 1;
 
 // Largest cluster (in split CTAs) the split-K reduction may use on each
 // device: 16 where the hardware can co-schedule it, else the portable 8.
@@ -222,10 +223,13 @@ struct Loader {
     }
   }
 
-  // Split the chunks this thread copied for one stage: hi (tf32-exact) in
-  // place in the raw tile, lo = x - hi at the same offset in the low tile.
-  __device__ __forceinline__ void split(const DevOperand& o, uint8_t* hi_gen, uint8_t* lo_gen,
-                                        int tid) const {
+  // Split the chunks this thread copied for one stage. tcgen05.mma of kind
+  // tf32 reads an fp32 operand as its high 19 bits (the low 13 bits are
+  // ignored, i.e. truncated), so the raw stage already is the high part;
+  // only the remainder lo = x - trunc(x) is written, to the low tile at the
+  // same offset.
+  __device__ __forceinline__ void split(const DevOperand& o, const uint8_t* raw_gen,
+                                        uint8_t* lo_gen, int tid) const {
     if (o.mode == kModeKVec || o.mode == kModeMNVec) {
       uint32_t off[P];
       float4 x[P];
@@ -234,16 +238,15 @@ struct Loader {
         off[i] = o.mode == kModeKVec
                      ? kmajor_off((tid >> 3) + i * 32, (tid & 7) * 4)
                      : mnmajor_off((tid % RC) * 4, tid / RC + i * (kThreads / RC));
-        x[i] = *reinterpret_cast<const float4*>(hi_gen + off[i]);
+        x[i] = *reinterpret_cast<const float4*>(raw_gen + off[i]);
       }
 #pragma unroll
       for (int i = 0; i < P; ++i) {
-        float4 hi, lo;
-        split_tf32(x[i].x, hi.x, lo.x);
-        split_tf32(x[i].y, hi.y, lo.y);
-        split_tf32(x[i].z, hi.z, lo.z);
-        split_tf32(x[i].w, hi.w, lo.w);
-        *reinterpret_cast<float4*>(hi_gen + off[i]) = hi;
+        float4 lo;
+        lo.x = tf32_low(x[i].x);
+        lo.y = tf32_low(x[i].y);
+        lo.z = tf32_low(x[i].z);
+        lo.w = tf32_low(x[i].w);
         *reinterpret_cast<float4*>(lo_gen + off[i]) = lo;
       }
     } else {
@@ -252,10 +255,8 @@ struct Loader {
         const int r = rows_fast ? t % R : t >> 5;
         const int k = rows_fast ? t / R : t & 31;
         const uint32_t off = kmajor_off(r, k);
-        float hi, lo;
-        split_tf32(*reinterpret_cast<const float*>(hi_gen + off), hi, lo);
-        *reinterpret_cast<float*>(hi_gen + off) = hi;
-        *reinterpret_cast<float*>(lo_gen + off) = lo;
+        *reinterpret_cast<float*>(lo_gen + off) =
+            tf32_low(*reinterpret_cast<const float*>(raw_gen + off));
       }
     }
   }
@@ -502,20 +503,22 @@ struct TileCfg {
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = BN * 128;
   static constexpr int kTile = kABytes + kBBytes;  // one raw (or lo) stage
-  // Split-TF32 keeps the low parts in a short ring of their own, so the
-  // raw ring can be deep: more k-blocks in flight per CTA.
-  static constexpr int kLoSlots = SPLIT ? (BN >= 128 ? 2 : 3) : 0;
+  // Split-TF32 keeps the low parts in a ring of their own, freed by the MMA
+  // commits, so neither ring waits on the other's round trip.
+  static constexpr int kLoSlots = SPLIT ? (BN >= 128 ? 3 : 4) : 0;
   static constexpr int kBudget = 196 * 1024 - kLoSlots * kTile;
   static constexpr int kRawFit = kBudget / kTile;
   static constexpr int kStages = kRawFit > 8 ? 8 : kRawFit;
-  // A raw stage is refilled once the MMAs of the k-block two iterations
-  // back have drained, so the tensor pipe's latency stays off the load path.
+  // Gathered (cp.async) operands refill a raw stage once the MMAs of the
+  // k-block two iterations back have drained; TMA operands are refilled by
+  // the producer warp as soon as a stage drains.
   static constexpr int kLag = kStages >= 4 ? 2 : 1;
   static constexpr int kAhead = kStages - kLag;  // k-blocks in flight
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kSmem =
       (kStages + kLoSlots) * kTile + 1024 /*align slack*/ + 512 /*barriers*/;
   static_assert(kStages >= 3, "at least three pipeline stages");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static_assert(kStages * kTile >= Stage<BN>::kBytes, "epilogue staging fits in the ring");
 };
 
@@ -596,39 +599,38 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     Loader<BN> lb;
     la.init(oa, row0, tid);
     lb.init(ob, col0, tid);
-    // Dense operands arrive by TMA (thread 0 issues the whole stage and
+    // Dense operands arrive by TMA (the producer warp issues each stage and
     // the bytes complete on tfull); gathered ones by per-thread cp.async.
     const bool a_tma = args.a_tma != 0, b_tma = args.b_tma != 0;
     const bool any_tma = a_tma || b_tma;
-    const uint32_t tma_bytes = (a_tma ? Cfg::kABytes : 0) + (b_tma ? Cfg::kBBytes : 0);
-    auto issue_stage = [&](int st, int kb) {
+    const bool any_gather = !(a_tma && b_tma);
+    auto issue_gathers = [&](int st, int kb) {
       const int k0 = kb * 32;
-      if (any_tma && tid == 0) {
-        mbar_arrive_expect_tx(tfull0 + st * 8, tma_bytes);
-        if (a_tma) tma_operand<128>(&args.tma_a, a_mn, raw_a(st), row0, k0, tfull0 + st * 8);
-        if (b_tma) tma_operand<BN>(&args.tma_b, b_mn, raw_b(st), col0, k0, tfull0 + st * 8);
-      }
       if (!a_tma) la.issue(oa, raw_a(st), row0, k0, tid);
       if (!b_tma) lb.issue(ob, raw_b(st), col0, k0, tid);
     };
+    if (any_gather) {
 #pragma unroll 1
-    for (int s = 0; s < AHEAD; ++s) {
-      if (s < nk) issue_stage(s, kb0 + s);
-      cp_async_commit();
+      for (int s = 0; s < AHEAD; ++s) {
+        if (s < nk) issue_gathers(s, kb0 + s);
+        cp_async_commit();
+      }
     }
 #pragma unroll 1
     for (int i = 0; i < nk; ++i) {
-      const int j = i + AHEAD;
-      if (j < nk) {
-        const int sj = j % S;
-        if (j >= S) {
-          // Raw stage sj was last read by the MMAs of k-block j - S.
-          if (!mbar_wait(empty0 + sj * 8, ((j - S) / S) & 1)) timed_out = true;
+      if (any_gather) {
+        const int j = i + AHEAD;
+        if (j < nk) {
+          const int sj = j % S;
+          if (j >= S) {
+            // Raw stage sj was last read by the MMAs of k-block j - S.
+            if (!mbar_wait(empty0 + sj * 8, ((j - S) / S) & 1)) timed_out = true;
+          }
+          issue_gathers(sj, kb0 + j);
         }
-        issue_stage(sj, kb0 + j);
+        cp_async_commit();
+        cp_async_wait<AHEAD>();  // this thread's copies of k-block i have landed
       }
-      cp_async_commit();
-      cp_async_wait<AHEAD>();  // this thread's copies of k-block i have landed
       const int s = i % S;
       if (any_tma && !mbar_wait(tfull0 + s * 8, (i / S) & 1)) timed_out = true;
       if (split_a || split_b) {
@@ -637,7 +639,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           // Lo slot l was last read by the MMAs of k-block i - L.
           if (!mbar_wait(loempty0 + l * 8, ((i - L) / LL) & 1)) timed_out = true;
         }
-        uint8_t* hi = sgen + s * Cfg::kTile;
+        const uint8_t* hi = sgen + s * Cfg::kTile;
         uint8_t* lo = sgen + (lo_base - sbase) + l * Cfg::kTile;
         if (split_a) la.split(oa, hi, lo, tid);
         if (split_b) lb.split(ob, hi + Cfg::kABytes, lo + Cfg::kABytes, tid);
@@ -645,6 +647,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(full0 + s * 8);
+    }
+  } else if (warp == kProducerWarp) {
+    // ---- TMA producer: refills each raw stage as soon as its MMAs drain ----
+    const bool a_tma = args.a_tma != 0, b_tma = args.b_tma != 0;
+    if ((a_tma || b_tma) && lane == 0) {
+      const uint32_t tma_bytes = (a_tma ? Cfg::kABytes : 0) + (b_tma ? Cfg::kBBytes : 0);
+#pragma unroll 1
+      for (int j = 0; j < nk; ++j) {
+        const int st = j % S;
+        if (j >= S) {
+          if (!mbar_wait(empty0 + st * 8, ((j - S) / S) & 1)) timed_out = true;
+        }
+        const int k0 = (kb0 + j) * 32;
+        mbar_arrive_expect_tx(tfull0 + st * 8, tma_bytes);
+        if (a_tma) tma_operand<128>(&args.tma_a, a_mn, raw_a(st), row0, k0, tfull0 + st * 8);
+        if (b_tma) tma_operand<BN>(&args.tma_b, b_mn, raw_b(st), col0, k0, tfull0 + st * 8);
+      }
     }
   } else if (lane == 0) {
     // ---- MMA warp: one thread issues every tcgen05.mma of the tile ----
@@ -1000,7 +1019,9 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
     // reduce through global memory.
     splits = 1;
     if (s.tiles < 120 && s.kblocks >= 8) {
-      const int want = (148 + s.tiles - 1) / s.tiles;
+      // Whole waves only: tiles x splits stays within the 148 SMs (one CTA
+      // of this kernel fits per SM), except that a single tile may use all.
+      const int want = 148 / s.tiles;
       const int most = s.kblocks / 4;
       splits = want < most ? want : most;
       if (splits > cmax) {
