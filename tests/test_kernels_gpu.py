@@ -303,3 +303,41 @@ def test_gemm_split_k_cluster_and_global(m, n, k, splits, transposed):
     assert np.isfinite(outs[0]).all()
     assert rel(outs[0], ref) <= TOL_X3
     assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("n,k,prec,transposed", [
+    (32, 256, 0, False), (64, 512, 0, True), (128, 64, 0, False), (96, 2048, 0, False),
+    (32, 256, 1, True), (128, 320, 1, False),
+])
+def test_gemm_many_waves_half_footprint(n, k, prec, transposed):
+    """Grids of several waves run the half-footprint GEMM (two CTAs per
+    SM): every tile, split-TF32 and single-pass TF32, bias + ReLU epilogue,
+    row-major and transposed outputs."""
+    import ctypes
+    from ttrl_b200 import _lib
+    ctx = _ctx()
+    m = 128 * 170 + 37  # > 148 tiles, ragged last tile
+    rng = np.random.default_rng(n + k + prec)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    da, db, dbias = dev(a), dev(b), dev(bias)
+    y = torch.full((n, m) if transposed else (m, n), float("nan"), device="cuda")
+    d = _lib.GemmDesc()
+    d.m, d.n, d.k, d.precision, d.splits = m, n, k, prec, 1
+    d.a.ptr, d.a.kind, d.a.rows, d.a.kdim, d.a.rs, d.a.ks = da.data_ptr(), 0, m, k, k, 1
+    d.b.ptr, d.b.kind, d.b.rows, d.b.kdim, d.b.rs, d.b.ks = db.data_ptr(), 0, n, k, k, 1
+    d.ep.out = y.data_ptr()
+    d.ep.ors, d.ep.ocs = (1, m) if transposed else (n, 1)
+    d.ep.alpha = 1.0
+    d.ep.bias, d.ep.bias_mode = dbias.data_ptr(), _lib.BIAS_COL
+    d.ep.relu = 1
+    ws, wsb = ctx.workspace(_lib.lib().ttrl_gemm_workspace_bytes(ctypes.byref(d)))
+    _lib.check(_lib.lib().ttrl_gemm(ctypes.byref(d), ws, wsb, ctx.status_ptr(), ctx.stream),
+               "ttrl_gemm")
+    got = host(y)
+    got = got.T if transposed else got
+    ctx.check_status()
+    ref = np.maximum(a.astype(np.float64) @ b.astype(np.float64).T + bias, 0.0)
+    assert np.isfinite(got).all()
+    assert rel(got, ref) <= (TOL_X3 if prec == 0 else TOL_TF32)

@@ -498,15 +498,19 @@ __device__ __forceinline__ void tma_operand(const CUtensorMap* map, bool mn, uin
   }
 }
 
-template <int BN, bool SPLIT>
+// SMALL: a half-size footprint (about 100 KB of shared memory, <= 102
+// registers) so two CTAs share an SM; used for grids of several waves, where
+// one CTA's set-up, pipeline fill and epilogue overlap the other's main loop.
+template <int BN, bool SPLIT, bool SMALL>
 struct TileCfg {
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = BN * 128;
   static constexpr int kTile = kABytes + kBBytes;  // one raw (or lo) stage
   // Split-TF32 keeps the low parts in a ring of their own, freed by the MMA
   // commits, so neither ring waits on the other's round trip.
-  static constexpr int kLoSlots = SPLIT ? (BN >= 128 ? 3 : 4) : 0;
-  static constexpr int kBudget = 196 * 1024 - kLoSlots * kTile;
+  static constexpr int kLoSlots =
+      !SPLIT ? 0 : SMALL ? (BN >= 128 ? 1 : 2) : (BN >= 128 ? 3 : 4);
+  static constexpr int kBudget = (SMALL ? 100 : 196) * 1024 - kLoSlots * kTile;
   static constexpr int kRawFit = kBudget / kTile;
   static constexpr int kStages = kRawFit > 8 ? 8 : kRawFit;
   // Gathered (cp.async) operands refill a raw stage once the MMAs of the
@@ -517,9 +521,10 @@ struct TileCfg {
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kSmem =
       (kStages + kLoSlots) * kTile + 1024 /*align slack*/ + 512 /*barriers*/;
-  static_assert(kStages >= 3, "at least three pipeline stages");
+  static_assert(kStages >= 2, "at least two pipeline stages");
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
-  static_assert(kStages * kTile >= Stage<BN>::kBytes, "epilogue staging fits in the ring");
+  static_assert((kStages + kLoSlots) * kTile >= Stage<BN>::kBytes,
+                "epilogue staging fits in the rings");
 };
 
 // Named barrier over the 256 loader threads (the MMA warp does not join).
@@ -527,10 +532,10 @@ __device__ __forceinline__ void loader_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
 }
 
-template <int BN, bool SPLIT>
-__global__ void __launch_bounds__(kBlockThreads, 1)
+template <int BN, bool SPLIT, bool SMALL>
+__global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
     gemm_tc_kernel(const __grid_constant__ GemmArgs args) {
-  using Cfg = TileCfg<BN, SPLIT>;
+  using Cfg = TileCfg<BN, SPLIT, SMALL>;
   constexpr int S = Cfg::kStages;
   constexpr int L = Cfg::kLoSlots;
   constexpr int LL = L > 0 ? L : 1;  // divisor-safe in the non-split build
@@ -819,12 +824,16 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 // co-schedule at this kernel's footprint.
 template <int BN, bool SPLIT>
 static int set_smem_attr(int* cluster_cap) {
-  using Cfg = TileCfg<BN, SPLIT>;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT>,
+  using Cfg = TileCfg<BN, SPLIT, false>;
+  using Small = TileCfg<BN, SPLIT, true>;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT, false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
   if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
+  e = cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Small::kSmem);
+  if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm, small)", e);
   int cap = 8;
-  if (cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT>,
+  if (cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT, false>,
                            cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, 1, 16);
@@ -838,7 +847,7 @@ static int set_smem_attr(int* cluster_cap) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<BN, SPLIT>, &cfg) ==
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<BN, SPLIT, false>, &cfg) ==
             cudaSuccess &&
         clusters >= 1)
       cap = 16;
@@ -1052,9 +1061,9 @@ size_t gemm_workspace_bytes(const ttrl_gemm_desc& d) {
   return kCounterBytes + static_cast<size_t>(s.splits) * d.m * d.n * sizeof(float);
 }
 
-template <int BN, bool SPLIT>
+template <int BN, bool SPLIT, bool SMALL>
 static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, int cluster_z, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, SPLIT>;
+  using Cfg = TileCfg<BN, SPLIT, SMALL>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kBlockThreads, 1, 1);
@@ -1069,7 +1078,7 @@ static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, int cluster_z, cud
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, SPLIT>, args);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, SPLIT, SMALL>, args);
   note_launch();
   return e;
 }
@@ -1121,12 +1130,20 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   dim3 grid((d.m + 127) / 128, (d.n + s.bn - 1) / s.bn, s.splits);
   const bool split3 = d.precision == TTRL_PREC_TF32X3;
   const int cz = s.cluster ? s.splits : 1;
+  // Several waves of CTAs: the half-size variant runs two CTAs per SM.
+  const bool small = !s.cluster && static_cast<long long>(s.tiles) * s.splits > 148;
   cudaError_t e;
+#define TTRL_LAUNCH(BNV)                                                              \
+  (split3 ? (small ? launch_bn<BNV, true, true>(args, grid, cz, stream)                \
+                   : launch_bn<BNV, true, false>(args, grid, cz, stream))              \
+          : (small ? launch_bn<BNV, false, true>(args, grid, cz, stream)               \
+                   : launch_bn<BNV, false, false>(args, grid, cz, stream)))
   switch (s.bn) {
-    case 32: e = split3 ? launch_bn<32, true>(args, grid, cz, stream) : launch_bn<32, false>(args, grid, cz, stream); break;
-    case 64: e = split3 ? launch_bn<64, true>(args, grid, cz, stream) : launch_bn<64, false>(args, grid, cz, stream); break;
-    default: e = split3 ? launch_bn<128, true>(args, grid, cz, stream) : launch_bn<128, false>(args, grid, cz, stream); break;
+    case 32: e = TTRL_LAUNCH(32); break;
+    case 64: e = TTRL_LAUNCH(64); break;
+    default: e = TTRL_LAUNCH(128); break;
   }
+#undef TTRL_LAUNCH
   if (e != cudaSuccess) return set_cuda_error("gemm launch", e);
   if (s.splits > 1 && !s.cluster && !args.reduce_in_kernel) {
     if (args.ws == nullptr)
