@@ -55,11 +55,6 @@ static int g_max_cluster[64];
 __device__ __align__(16) float kOnes4[4] = {1.f, 1.f, 1.f, 1.f};
 __device__ __align__(16) float kOneZeros[4] = {1.f, 0.f, 0.f, 0.f};
 
-__device__ __forceinline__ int fdiv(const FastDiv& f, int n) {
-  if (f.shr == 0) return n;  // divisor 1
-  const uint32_t t = __umulhi(static_cast<uint32_t>(n), f.mul);
-  return static_cast<int>((t + static_cast<uint32_t>(n)) >> f.shr);
-}
 
 // General element address (used by the scalar fallback modes only).
 __device__ __forceinline__ const float* opnd_addr(const DevOperand& o, int r, int k, bool& ok) {

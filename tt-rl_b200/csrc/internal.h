@@ -22,6 +22,14 @@ enum : int32_t {
 struct FastDiv {
   uint32_t d, mul, shr, pad0;
 };
+
+// n / d for 0 <= n < 2^31 by multiply-shift (d from make_fastdiv).
+__device__ __forceinline__ int fdiv(const FastDiv& f, int n) {
+  if (f.shr == 0) return n;  // divisor 1
+  const uint32_t t = __umulhi(static_cast<uint32_t>(n), f.mul);
+  return static_cast<int>((t + static_cast<uint32_t>(n)) >> f.shr);
+}
+
 FastDiv make_fastdiv(int d);
 
 struct DevOperand {

@@ -184,55 +184,102 @@ int conv_fprop(const float* x, const float* w, const float* b, float* y, const t
 
 // dx[n,iy,ix,c] = sum over the kernel taps that saw (iy,ix) of dxcol, in a
 // fixed (ky, kx) order, then the relu mask of the layer below.
-__global__ void col2im_kernel(const float* __restrict__ dxcol, const float* __restrict__ mask,
-                              float* __restrict__ dx, ttrl_conv_geom g, int accumulate) {
-  const long long total = static_cast<long long>(g.n) * g.h * g.w * g.c;
+// dX from the im2col-shaped gradient dxcol[m][(ky, kx, c)]: each input
+// pixel sums, over the kernel taps that saw it, the matching column of the
+// output pixel's row. One thread owns 4 channels of one pixel (C % 4 == 0)
+// or one channel; indices are 32-bit with multiply-shift division, and all
+// tap loads are issued before the sum, which runs in (ky, kx) order.
+struct Col2imArgs {
+  const float* dxcol;
+  const float* mask;
+  float* dx;
+  ttrl_conv_geom g;
+  FastDiv f_cg, f_w, f_h, f_s;
+  int cg;  // channel groups per pixel: C / 4 (vector) or C
+  int vec;
+  int accumulate;
+  int total;  // pixels * cg
+};
+
+constexpr int kCol2imMaxTaps = 16;
+
+template <bool VEC>
+__global__ void __launch_bounds__(256) col2im_kernel(const __grid_constant__ Col2imArgs a) {
+  const ttrl_conv_geom g = a.g;
   const int kk = g.kh * g.kw * g.c;
-  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>(idx % g.c);
-    long long t = idx / g.c;
-    const int ix = static_cast<int>(t % g.w);
-    t /= g.w;
-    const int iy = static_cast<int>(t % g.h);
-    const int img = static_cast<int>(t / g.h);
-    // The mask and old value load first, and each kernel row's taps load
-    // together (kx unrolled), so a pixel waits on a few memory round trips
-    // rather than one per tap. Taps are summed in (ky, kx) order.
-    const float mk = mask != nullptr ? mask[idx] : 1.f;
-    const float old = accumulate ? dx[idx] : 0.f;
-    float s = 0.f;
-    for (int ky = 0; ky < g.kh; ++ky) {
-      const int ty = iy + g.pad - ky;
-      if (ty < 0 || ty % g.stride) continue;
-      const int oy = ty / g.stride;
-      if (oy >= g.oh) continue;
-      const long long row0 = (static_cast<long long>(img) * g.oh + oy) * g.ow;
-      constexpr int kMaxKw = 8;
-      float v[kMaxKw];
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < a.total;
+       idx += gridDim.x * blockDim.x) {
+    const int pix = fdiv(a.f_cg, idx);
+    const int c = (idx - pix * a.cg) * (VEC ? 4 : 1);
+    const int t = fdiv(a.f_w, pix);
+    const int ix = pix - t * g.w;
+    const int img = fdiv(a.f_h, t);
+    const int iy = t - img * g.h;
+    const int ty0 = iy + g.pad, tx0 = ix + g.pad;
+    const int ky0 = ty0 - fdiv(a.f_s, ty0) * g.stride;  // first tap row that saw this pixel
+    const int kx0 = tx0 - fdiv(a.f_s, tx0) * g.stride;
+    const long long base = static_cast<long long>(pix) * g.c + c;
+    float4 old = make_float4(0.f, 0.f, 0.f, 0.f), mk = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (VEC) {
+      if (a.accumulate) old = *reinterpret_cast<const float4*>(a.dx + base);
+      if (a.mask) mk = *reinterpret_cast<const float4*>(a.mask + base);
+    } else {
+      if (a.accumulate) old.x = a.dx[base];
+      if (a.mask) mk.x = a.mask[base];
+    }
+    float4 v[kCol2imMaxTaps];
+    int nt = 0;
 #pragma unroll
-      for (int kx = 0; kx < kMaxKw; ++kx) {
-        v[kx] = 0.f;
-        const int tx = ix + g.pad - kx;
-        if (kx < g.kw && tx >= 0 && tx % g.stride == 0 && tx / g.stride < g.ow)
-          v[kx] = dxcol[(row0 + tx / g.stride) * kk + (ky * g.kw + kx) * g.c + c];
-      }
+    for (int q = 0; q < kCol2imMaxTaps; ++q) v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Taps in (ky, kx) order; at most 16 (enforced on the host).
+    for (int ky = ky0; ky < g.kh; ky += g.stride) {
+      const int oy = fdiv(a.f_s, ty0 - ky);
+      if (ty0 - ky < 0 || oy >= g.oh) continue;
+      for (int kx = kx0; kx < g.kw; kx += g.stride) {
+        const int ox = fdiv(a.f_s, tx0 - kx);
+        if (tx0 - kx < 0 || ox >= g.ow) continue;
+        const long long off =
+            (static_cast<long long>(img * g.oh + oy) * g.ow + ox) * kk + (ky * g.kw + kx) * g.c + c;
 #pragma unroll
-      for (int kx = 0; kx < kMaxKw; ++kx) {
-        const int tx = ix + g.pad - kx;
-        if (kx < g.kw && tx >= 0 && tx % g.stride == 0 && tx / g.stride < g.ow) s += v[kx];
-      }
-      for (int kx = kMaxKw; kx < g.kw; ++kx) {  // kernels wider than 8
-        const int tx = ix + g.pad - kx;
-        if (tx < 0 || tx % g.stride) continue;
-        const int ox = tx / g.stride;
-        if (ox >= g.ow) continue;
-        s += dxcol[(row0 + ox) * kk + (ky * g.kw + kx) * g.c + c];
+        for (int q = 0; q < kCol2imMaxTaps; ++q) {
+          if (q == nt) {
+            if (VEC) {
+              v[q] = *reinterpret_cast<const float4*>(a.dxcol + off);
+            } else {
+              v[q].x = a.dxcol[off];
+            }
+          }
+        }
+        ++nt;
       }
     }
-    if (!(mk > 0.f) && mask != nullptr) s = 0.f;
-    if (accumulate) s += old;
-    dx[idx] = s;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < kCol2imMaxTaps; ++q) {
+      if (q < nt) {
+        s.x += v[q].x;
+        s.y += v[q].y;
+        s.z += v[q].z;
+        s.w += v[q].w;
+      }
+    }
+    if (a.mask) {
+      if (!(mk.x > 0.f)) s.x = 0.f;
+      if (!(mk.y > 0.f)) s.y = 0.f;
+      if (!(mk.z > 0.f)) s.z = 0.f;
+      if (!(mk.w > 0.f)) s.w = 0.f;
+    }
+    if (a.accumulate) {
+      s.x += old.x;
+      s.y += old.y;
+      s.z += old.z;
+      s.w += old.w;
+    }
+    if (VEC) {
+      *reinterpret_cast<float4*>(a.dx + base) = s;
+    } else {
+      a.dx[base] = s.x;
+    }
   }
 }
 
@@ -267,10 +314,34 @@ int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
                 reinterpret_cast<float*>(reinterpret_cast<char*>(dxcol) + col_bytes),
                 wsb - kCounterBytes - col_bytes, status, st);
   if (rc) return rc;
-  const long long total = static_cast<long long>(g->n) * g->h * g->w * g->c;
+  const int taps = ((g->kh + g->stride - 1) / g->stride) * ((g->kw + g->stride - 1) / g->stride);
+  if (taps > kCol2imMaxTaps)
+    return set_error(TTRL_EUNSUPPORTED, "conv_dgrad: %d kernel taps per input pixel exceed %d",
+                     taps, kCol2imMaxTaps);
+  Col2imArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.dxcol = dxcol;
+  a.mask = mask;
+  a.dx = dx;
+  a.g = *g;
+  const bool vec = g->c % 4 == 0 && (reinterpret_cast<uintptr_t>(dx) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+  a.vec = vec ? 1 : 0;
+  a.cg = vec ? g->c / 4 : g->c;
+  a.f_cg = make_fastdiv(a.cg);
+  a.f_w = make_fastdiv(g->w);
+  a.f_h = make_fastdiv(g->h);
+  a.f_s = make_fastdiv(g->stride);
+  a.accumulate = accumulate;
+  const long long total = static_cast<long long>(g->n) * g->h * g->w * a.cg;
+  if (total >= (1ll << 31)) return set_error(TTRL_EUNSUPPORTED, "conv_dgrad: input too large");
+  a.total = static_cast<int>(total);
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  col2im_kernel<<<blocks, 256, 0, st>>>(dxcol, mask, dx, *g, accumulate);
+  if (vec)
+    col2im_kernel<true><<<blocks, 256, 0, st>>>(a);
+  else
+    col2im_kernel<false><<<blocks, 256, 0, st>>>(a);
   note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("col2im launch", e);
@@ -311,13 +382,12 @@ int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl
 __global__ void u8_nchw_to_f32_nhwc_kernel(const uint8_t* __restrict__ in,
                                            const int32_t* __restrict__ index,
                                            float* __restrict__ out, int n, int c, int h, int w,
-                                           float scale) {
-  const long long pixels = static_cast<long long>(n) * h * w;
+                                           float scale, FastDiv f_hw) {
+  const int pixels = n * h * w;
   const int hw = h * w;
-  for (long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; p < pixels;
-       p += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int img = static_cast<int>(p / hw);
-    const int pix = static_cast<int>(p - static_cast<long long>(img) * hw);
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pixels; p += gridDim.x * blockDim.x) {
+    const int img = fdiv(f_hw, p);
+    const int pix = p - img * hw;
     const int src = index ? index[img] : img;
     const uint8_t* base = in + static_cast<long long>(src) * c * hw + pix;
     float* o = out + p * c;
@@ -340,7 +410,10 @@ int u8_to_f32(const uint8_t* in, const int32_t* index, float* out, int n, int c,
   const long long pixels = static_cast<long long>(n) * h * w;
   int blocks = static_cast<int>((pixels + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  u8_nchw_to_f32_nhwc_kernel<<<blocks, 256, 0, st>>>(in, index, out, n, c, h, w, scale);
+  if (pixels * static_cast<long long>(c) >= (1ll << 31))
+    return set_error(TTRL_EUNSUPPORTED, "u8_to_f32: more than 2^31 values");
+  u8_nchw_to_f32_nhwc_kernel<<<blocks, 256, 0, st>>>(in, index, out, n, c, h, w, scale,
+                                                      make_fastdiv(h * w));
   note_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("u8_to_f32 launch", e);
