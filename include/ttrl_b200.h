@@ -169,13 +169,17 @@ int ttrl_linear_dgrad(const float* g, const float* w, const float* mask, float* 
                       size_t workspace_bytes, int* status, ttrl_stream_t stream);
 
 /* dw[K,N] (=|+=) x[M,K]^T @ g[M,N] and, when db != NULL,
- * db[N] (=|+=) sum_m g[m][:] (computed as an extra row of ones in the same
- * GEMM). Replaces matmul's dB = a^T @ g (ttrl/engine/ops/matmul.py:82-84)
+ * db[N] (=|+=) sum_m g[m][:] (an extra row of ones in the same GEMM).
+ * The workspace size comes from ttrl_linear_wgrad_workspace_bytes. Replaces matmul's dB = a^T @ g (ttrl/engine/ops/matmul.py:82-84)
  * and the bias-add backward (ttrl/engine/ops/elementwise.py:36-41 with
  * ttrl/engine/ops/broadcast.py:11-30). */
 int ttrl_linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, int k, int n,
                       int accumulate, int accumulate_db, int precision, float* workspace,
                       size_t workspace_bytes, int* status, ttrl_stream_t stream);
+
+/* Workspace bytes ttrl_linear_wgrad needs for these extents (the weight
+ * GEMM's split-K partials). */
+size_t ttrl_linear_wgrad_workspace_bytes(int m, int k, int n);
 
 /* ------------------------------------------------------------------ Conv */
 

@@ -76,6 +76,8 @@ __device__ __forceinline__ void adam_elem(const AdamScalars& k, float g, float& 
 }
 
 __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constant__ AdamArgs a) {
+  pdl_trigger();
+  pdl_wait();
   // Locate this block's tensor (count <= 64: a linear scan is cheap).
   const long long chunk = blockIdx.x;
   int ti = 0;
@@ -177,9 +179,9 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
   a.b2 = b2;
   a.eps = eps;
   a.wd = wd;
-  adam_kernel<<<static_cast<unsigned>(chunks), kAdamThreads, 0, st>>>(a);
+  const cudaError_t le_ = launch_pdl(adam_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kAdamThreads), 0, st, a);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("adam launch", e);
 }
 
@@ -216,6 +218,8 @@ __device__ __forceinline__ double block_sum_fixed(double v, double* red) {
 }
 
 __global__ void __launch_bounds__(kSqThreads) sqnorm_kernel(const __grid_constant__ SqArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ double red[kSqThreads];
   __shared__ int s_last;
   const long long chunk = blockIdx.x;
@@ -299,9 +303,9 @@ int grad_sqnorm(const float* const* grads, const int64_t* numels, int count, flo
   a.partial = reinterpret_cast<double*>(static_cast<char*>(ws) + 16);
   a.out = out;
   a.max_norm = max_norm;
-  sqnorm_kernel<<<static_cast<unsigned>(chunks), kSqThreads, 0, st>>>(a);
+  const cudaError_t le_ = launch_pdl(sqnorm_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kSqThreads), 0, st, a);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("grad_sqnorm launch", e);
 }
 

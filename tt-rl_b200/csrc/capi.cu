@@ -40,6 +40,7 @@ size_t conv_dgrad_ws(const ttrl_conv_geom*);
 int conv_wgrad(const float*, const float*, float*, float*, const ttrl_conv_geom*, float, int, int,
                int, float*, size_t, int*, cudaStream_t);
 size_t conv_wgrad_ws(const ttrl_conv_geom*);
+size_t linear_wgrad_ws(int, int, int);
 int u8_to_f32(const uint8_t*, const int32_t*, float*, int, int, int, int, float, cudaStream_t);
 int adam_step(const ttrl_adam_tensor*, int, int32_t*, int32_t*, const float*, const double*,
               double, double, double, double, double, cudaStream_t);
@@ -100,6 +101,10 @@ int ttrl_linear_dgrad(const float* g, const float* w, const float* mask, float* 
                       size_t workspace_bytes, int* status, ttrl_stream_t stream) {
   return linear_dgrad(g, w, mask, dx, m, k, n, accumulate, precision, workspace, workspace_bytes,
                       status, TTRL_STREAM(stream));
+}
+
+size_t ttrl_linear_wgrad_workspace_bytes(int m, int k, int n) {
+  return (m > 0 && k > 0 && n > 0) ? linear_wgrad_ws(m, k, n) : 0;
 }
 
 int ttrl_linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, int k, int n,

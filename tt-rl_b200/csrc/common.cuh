@@ -65,6 +65,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// ------------------------------------------------- programmatic launch
+
+// Every kernel of this library is launched with programmatic stream
+// serialization: the next kernel on the stream may start (and do set-up
+// that touches no global data) once every CTA of this one has called
+// pdl_trigger(). pdl_wait() blocks until the previous kernel has finished
+// and its memory is visible; each kernel calls it before its first global
+// read or write, so no data race crosses the boundary.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- cp.async
 
 // 16-byte global->shared copy; src_bytes == 0 zero-fills the destination.

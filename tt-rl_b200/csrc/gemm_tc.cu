@@ -584,6 +584,10 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_gen;
+  // Set-up above touched no global memory; from here on the previous
+  // kernel's results are read and this kernel's outputs written.
+  pdl_trigger();
+  pdl_wait();
 
   auto raw_a = [&](int s) { return sbase + s * Cfg::kTile; };
   auto raw_b = [&](int s) { return sbase + s * Cfg::kTile + Cfg::kABytes; };
@@ -791,6 +795,8 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
 // partial tiles are too large for one CTA to reduce quickly).
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int m, int n,
                                      ttrl_epilogue ep, EpiExtra ex) {
+  pdl_trigger();
+  pdl_wait();
   const long long total = static_cast<long long>(m) * n;
   constexpr int Z = 8;
   for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
@@ -1031,7 +1037,7 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
       if (splits > cmax) {
         if (s.kblocks / cmax >= 32) {
           global_split = true;
-          if (splits > 32) splits = 32;
+          if (splits > 64) splits = 64;
         } else {
           splits = cmax;
         }
@@ -1064,14 +1070,17 @@ static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, int cluster_z, cud
   cfg.blockDim = dim3(kBlockThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (cluster_z > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = static_cast<unsigned>(cluster_z);
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+    cfg.numAttrs = 2;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, SPLIT, SMALL>, args);
   note_launch();
@@ -1146,9 +1155,10 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
     const long long total = static_cast<long long>(d.m) * d.n;
     int blocks = static_cast<int>((total + 255) / 256);
     if (blocks > 148 * 8) blocks = 148 * 8;
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(args.ws, s.splits, d.m, d.n, d.ep, ex);
+    const cudaError_t le_ = launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream,
+                                       args.ws, s.splits, d.m, d.n, d.ep, ex);
     note_launch();
-    e = cudaGetLastError();
+    e = le_ != cudaSuccess ? le_ : cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("gemm split-k reduce launch", e);
   }
   return TTRL_OK;

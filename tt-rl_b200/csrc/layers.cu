@@ -141,10 +141,17 @@ int linear_dgrad(const float* g, const float* w, const float* mask, float* dx, i
   return gemm_run_ws(d, 0, no_extra(), ws, wsb, status, st);
 }
 
+// Workspace of linear_wgrad: [counters | GEMM split-K partials].
+size_t linear_wgrad_ws(int m, int k, int n) {
+  return gemm_workspace_bytes(make_desc(k + 1, n, m, TTRL_PREC_TF32X3));
+}
+
 int linear_wgrad(const float* x, const float* g, float* dw, float* db, int m, int k, int n,
                  int accumulate, int accumulate_db, int precision, float* ws, size_t wsb,
                  int* status, cudaStream_t st) {
   if (m <= 0 || n <= 0 || k <= 0) return set_error(TTRL_EINVAL, "linear_wgrad: bad extents");
+  // db rides along as an extra row of ones appended to x^T: its row of D
+  // is the column sums of g, in the same GEMM and its tile-order reduction.
   ttrl_gemm_desc d = make_desc(k + (db ? 1 : 0), n, m, precision);
   d.a = dense(x, k, m, 1, k);
   d.b = dense(g, n, m, 1, n);
@@ -205,6 +212,8 @@ constexpr int kCol2imMaxTaps = 16;
 
 template <bool VEC>
 __global__ void __launch_bounds__(256) col2im_kernel(const __grid_constant__ Col2imArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const ttrl_conv_geom g = a.g;
   const int kk = g.kh * g.kw * g.c;
   for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < a.total;
@@ -338,12 +347,13 @@ int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
   a.total = static_cast<int>(total);
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
+  cudaError_t le_;
   if (vec)
-    col2im_kernel<true><<<blocks, 256, 0, st>>>(a);
+    le_ = launch_pdl(col2im_kernel<true>, dim3(blocks), dim3(256), 0, st, a);
   else
-    col2im_kernel<false><<<blocks, 256, 0, st>>>(a);
+    le_ = launch_pdl(col2im_kernel<false>, dim3(blocks), dim3(256), 0, st, a);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("col2im launch", e);
 }
 
@@ -369,6 +379,8 @@ int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl
   d.ep.accumulate = accumulate;
   EpiExtra ex = no_extra();
   if (db) {
+    // db (not scaled by alpha) as an extra row of ones appended to the
+    // windows operand: its row of D is the column sums of dY.
     ex.row2 = kk;
     ex.out2 = db;
     ex.cs2 = 1;
@@ -383,6 +395,8 @@ __global__ void u8_nchw_to_f32_nhwc_kernel(const uint8_t* __restrict__ in,
                                            const int32_t* __restrict__ index,
                                            float* __restrict__ out, int n, int c, int h, int w,
                                            float scale, FastDiv f_hw) {
+  pdl_trigger();
+  pdl_wait();
   const int pixels = n * h * w;
   const int hw = h * w;
   for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pixels; p += gridDim.x * blockDim.x) {
@@ -412,10 +426,10 @@ int u8_to_f32(const uint8_t* in, const int32_t* index, float* out, int n, int c,
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (pixels * static_cast<long long>(c) >= (1ll << 31))
     return set_error(TTRL_EUNSUPPORTED, "u8_to_f32: more than 2^31 values");
-  u8_nchw_to_f32_nhwc_kernel<<<blocks, 256, 0, st>>>(in, index, out, n, c, h, w, scale,
+  const cudaError_t le_ = launch_pdl(u8_nchw_to_f32_nhwc_kernel, dim3(blocks), dim3(256), 0, st, in, index, out, n, c, h, w, scale,
                                                       make_fastdiv(h * w));
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("u8_to_f32 launch", e);
 }
 

@@ -48,6 +48,8 @@ __device__ __forceinline__ float clamp_ref(float x, float lo, float hi, float& p
 // ttrl/algos/dqn/losses.py:77-140 (update_loss) with huber from
 // ttrl/engine/ops/functional.py:56-69 and the mean of ops/reduce.py:37-41.
 __global__ void __launch_bounds__(kLossThreads) dqn_loss_kernel(const __grid_constant__ DqnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[kLossThreads];
   const int A = a.actions;
   const float inv_b = 1.0f / static_cast<float>(a.batch);
@@ -116,9 +118,9 @@ int dqn_loss(const DqnArgs& args, cudaStream_t st) {
   if (!args.q || !args.q_sel || !args.q_tgt || !args.onehot || !args.rewards || !args.dones ||
       !args.discounts || !args.loss || !args.mean_q || !args.dq)
     return set_error(TTRL_EINVAL, "dqn_loss: null pointer");
-  dqn_loss_kernel<<<1, kLossThreads, 0, st>>>(args);
+  const cudaError_t le_ = launch_pdl(dqn_loss_kernel, dim3(1), dim3(kLossThreads), 0, st, args);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("dqn_loss launch", e);
 }
 
@@ -129,6 +131,8 @@ int dqn_loss(const DqnArgs& args, cudaStream_t st) {
 // ttrl/algos/ppo/loss.py:42-83 (objective) with log_softmax / entropy of
 // ttrl/engine/ops/functional.py:160-178 and the reducers of loss.py:27-39.
 __global__ void __launch_bounds__(kLossThreads) ppo_loss_kernel(const __grid_constant__ PpoArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[kLossThreads];
   const int A = a.num_actions;
   // Denominator of the reducer: B (mean_all) or sum(valid) (masked mean).
@@ -227,9 +231,9 @@ int ppo_loss(const PpoArgs& args, cudaStream_t st) {
   if (!args.logits || !args.value || !args.actions || !args.old_logp || !args.adv ||
       !args.returns || !args.old_values || !args.metrics || !args.dlogits || !args.dvalue)
     return set_error(TTRL_EINVAL, "ppo_loss: null pointer");
-  ppo_loss_kernel<<<1, kLossThreads, 0, st>>>(args);
+  const cudaError_t le_ = launch_pdl(ppo_loss_kernel, dim3(1), dim3(kLossThreads), 0, st, args);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("ppo_loss launch", e);
 }
 
@@ -237,6 +241,8 @@ int ppo_loss(const PpoArgs& args, cudaStream_t st) {
 // payloads alike): the on-device minibatch gather of per-sample fields.
 __global__ void gather_rows_kernel(const uint32_t* __restrict__ src, const int32_t* __restrict__ idx,
                                    uint32_t* __restrict__ dst, int n, int row) {
+  pdl_trigger();
+  pdl_wait();
   const long long total = static_cast<long long>(n) * row;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -251,10 +257,10 @@ int gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row, 
   const long long total = static_cast<long long>(n) * row;
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
-  gather_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint32_t*>(src), idx,
+  const cudaError_t le_ = launch_pdl(gather_rows_kernel, dim3(blocks), dim3(256), 0, st, static_cast<const uint32_t*>(src), idx,
                                             static_cast<uint32_t*>(dst), n, row);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("gather_rows launch", e);
 }
 

@@ -55,6 +55,8 @@ __device__ __forceinline__ float ew_apply(int op, float x, float y, float s) {
 }
 
 __global__ void ew_kernel(const __grid_constant__ EwArgs a) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < a.n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int64_t rem = i, ao = 0, bo = 0;
@@ -97,9 +99,9 @@ int ew(int op, const float* x, const int64_t* xs, const float* y, const int64_t*
   if (n == 0) return TTRL_OK;
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
-  ew_kernel<<<blocks, 256, 0, st>>>(a);
+  const cudaError_t le_ = launch_pdl(ew_kernel, dim3(blocks), dim3(256), 0, st, a);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("ew launch", e);
 }
 
@@ -108,6 +110,8 @@ int ew(int op, const float* x, const int64_t* xs, const float* y, const int64_t*
 // in viewed as [outer][n][inner]; out [outer][inner].
 __global__ void reduce_thread_kernel(int op, const float* __restrict__ in, float* __restrict__ out,
                                      int64_t outer, int64_t n, int64_t inner) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t total = outer * inner;
   for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < total;
        o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -135,6 +139,8 @@ __global__ void reduce_thread_kernel(int op, const float* __restrict__ in, float
 // One block per output element, fixed-shape tree: for long reductions.
 __global__ void reduce_block_kernel(int op, const float* __restrict__ in, float* __restrict__ out,
                                     int64_t n, int64_t inner) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float vals[256];
   __shared__ int64_t args[256];
   const int64_t o = blockIdx.x;
@@ -181,22 +187,26 @@ int reduce(int op, const float* in, float* out, int64_t outer, int64_t n, int64_
   if (in == nullptr || out == nullptr) return set_error(TTRL_EINVAL, "reduce: null pointer");
   if (outer <= 0 || n <= 0 || inner <= 0) return set_error(TTRL_EINVAL, "reduce: empty extent");
   const int64_t total = outer * inner;
+  cudaError_t le_;
   if (total < 512 && n >= 1024) {
-    reduce_block_kernel<<<static_cast<unsigned>(total), 256, 0, st>>>(op, in, out, n, inner);
+    le_ = launch_pdl(reduce_block_kernel, dim3(static_cast<unsigned>(total)), dim3(256), 0, st,
+                     op, in, out, n, inner);
     note_launch();
   } else {
     int blocks = static_cast<int>((total + 255) / 256);
     if (blocks > 148 * 8) blocks = 148 * 8;
-    reduce_thread_kernel<<<blocks, 256, 0, st>>>(op, in, out, outer, n, inner);
+    le_ = launch_pdl(reduce_thread_kernel, dim3(blocks), dim3(256), 0, st, op, in, out, outer, n, inner);
     note_launch();
   }
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("reduce launch", e);
 }
 
 // ---------------------------------------------------------- strided copy
 
 __global__ void copy_strided_kernel(const __grid_constant__ EwArgs a) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < a.n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int64_t rem = i, so = 0, dof = 0;
@@ -236,9 +246,9 @@ int copy_strided(float* dst, const int64_t* ds, const float* src, const int64_t*
   if (n == 0) return TTRL_OK;
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
-  copy_strided_kernel<<<blocks, 256, 0, st>>>(a);
+  const cudaError_t le_ = launch_pdl(copy_strided_kernel, dim3(blocks), dim3(256), 0, st, a);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("copy launch", e);
 }
 
@@ -246,6 +256,8 @@ int copy_strided(float* dst, const int64_t* ds, const float* src, const int64_t*
 
 __global__ void axpby_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n,
                              float keep, float take) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     // Order of ttrl/algos/sac/targets.py:55-61: add(mul(dst, 1-tau), mul(src, tau)).
@@ -260,9 +272,9 @@ int polyak(float* dst, const float* src, int64_t n, float tau, cudaStream_t st) 
   if (dst == nullptr || src == nullptr) return set_error(TTRL_EINVAL, "polyak: null pointer");
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
-  axpby_kernel<<<blocks, 256, 0, st>>>(dst, src, n, 1.0f - tau, tau);
+  const cudaError_t le_ = launch_pdl(axpby_kernel, dim3(blocks), dim3(256), 0, st, dst, src, n, 1.0f - tau, tau);
   note_launch();
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("polyak launch", e);
 }
 

@@ -100,6 +100,7 @@ _SIGNATURES = {
                                  _vp, _c_size, _vp, _vp]),
     "ttrl_linear_fwd_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                          _c_int, _vp, _vp]),
+    "ttrl_linear_wgrad_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),
     "ttrl_linear_dgrad": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                    _vp, _c_size, _vp, _vp]),
     "ttrl_linear_wgrad": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,

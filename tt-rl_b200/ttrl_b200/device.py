@@ -207,9 +207,7 @@ class DeviceContext:
                      precision: int = PRECISION) -> None:
         m, k = x.shape[-2], x.shape[-1]
         n = g.shape[-1]
-        desc = _lib.GemmDesc()
-        desc.m, desc.n, desc.k, desc.precision = k + (1 if db is not None else 0), n, m, precision
-        need = lib().ttrl_gemm_workspace_bytes(ctypes.byref(desc))
+        need = lib().ttrl_linear_wgrad_workspace_bytes(m, k, n)
         ws, wsb = self.workspace(need)
         with self._timed(f"linear_wgrad[{m}x{k}x{n}]", 2 * m * k * n):
             check(lib().ttrl_linear_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(g, "g")),
