@@ -253,6 +253,8 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # stdout carries exactly one JSON line: keep NCCL's banner off it.
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
         group = dist.group.WORLD
@@ -282,8 +284,10 @@ def run_ours(args):
     K = args.steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    sync_ms = 0.0
     syncs = 0
+    n_sync = K // SYNC_EVERY
+    sync_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_sync)]
+    sync_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_sync)]
     if group is not None:
         import torch.distributed as dist
         dist.barrier()
@@ -294,18 +298,21 @@ def run_ours(args):
             starts[k].record()
             learner.replay()
             if group is not None and (k + 1) % SYNC_EVERY == 0:
+                sync_s[syncs].record()
                 sync.average()
+                sync_e[syncs].record()
                 syncs += 1
             ends[k].record()
         torch.cuda.synchronize(device)
     clock = clocks.summary()
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(per_step)
+    sync_ms = sum(a.elapsed_time(b) for a, b in zip(sync_s[:syncs], sync_e[:syncs]))
     if group is not None:
         import torch.distributed as dist
-        t = torch.tensor([total_ms], device=device)
+        t = torch.tensor([total_ms, sync_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        total_ms, sync_ms = float(t[0].item()), float(t[1].item())
         dist.barrier()
     value = SAMPLES_PER_UPDATE * K * world / (total_ms * 1e-3)
 
@@ -358,6 +365,7 @@ def run_ours(args):
                        "epochs": EPOCHS, "grad_steps_per_step": STEPS_PER_UPDATE,
                        "parallelism": f"dp{world}", "sync_every_updates": SYNC_EVERY,
                        "syncs_in_timed_region": syncs,
+                       "allreduce_ms_total": round(sync_ms, 4),
                        "precision": "split-TF32 tensor cores (tcgen05 kind::tf32 x3), fp32 "
                                     "accumulate and fp32 elementwise",
                        "l2": "flushed (256 MB write) before every timed step"},

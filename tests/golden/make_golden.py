@@ -379,6 +379,114 @@ def param_sync(index):
           "ttrl/engine/mesh/sync.py ParamSync.average: exact fp32 sum in replica order, then /N")
 
 
+class _Batch(dict):
+    """Mapping of named device tensors plus .obs / .next_obs, as the SAC
+    losses read a loaded batch."""
+
+
+class _FakePolicy:
+    """Returns preset (mean, log_std) leaves for obs and next_obs."""
+
+    def __init__(self, cur, nxt):
+        self.cur, self.nxt = cur, nxt
+
+    def __call__(self, obs):
+        return self.nxt if obs == "next" else self.cur
+
+
+class _LinearCritic:
+    """Q(s, a) = sum(a * w) + s_feat: linear in the action, so d Q / d a
+    carries the actor loss back through the reparameterised sample."""
+
+    def __init__(self, w, s_cur, s_next):
+        self.w, self.s_cur, self.s_next = w, s_cur, s_next
+
+    def __call__(self, obs, action):
+        from ttrl.engine.ops import add, mul, sum_dim
+        feat = self.s_next if obs == "next" else self.s_cur
+        return add(sum_dim(mul(action, self.w), dim=-1, keepdim=True), feat)
+
+
+def sac_losses(index):
+    from ttrl.algos.sac.losses import actor_loss, alpha_loss, critic_loss
+    from ttrl.algos.sac.policy import SquashedGaussian
+    from ttrl.engine.autograd import Tensor
+    from ttrl.spaces.action import ActionSpec
+    import ttnn
+    out = {}
+    dev = ttnn.DEVICE
+    for v, (name, per) in enumerate((("uniform", False), ("prioritized", True))):
+        rng = np.random.default_rng(900 + v)
+        B, D = 256, 3
+        low, high = (-1.0, -2.0, -0.5), (1.0, 2.0, 1.5)
+        spec = ActionSpec(kind="continuous", dim=D, low=low, high=high)
+        dist = SquashedGaussian(spec, dev)
+        mean = (rng.standard_normal((B, D)) * 0.8).astype(np.float32)
+        log_std = rng.uniform(-2.0, 0.5, (B, D)).astype(np.float32)
+        mean_n = (rng.standard_normal((B, D)) * 0.8).astype(np.float32)
+        log_std_n = rng.uniform(-2.0, 0.5, (B, D)).astype(np.float32)
+        noise = rng.standard_normal((B, D)).astype(np.float32)
+        next_noise = rng.standard_normal((B, D)).astype(np.float32)
+        q_w = [rng.standard_normal((1, D)).astype(np.float32) for _ in range(4)]
+        s_feat = [rng.standard_normal((B, 1)).astype(np.float32) for _ in range(8)]
+        actions = rng.uniform(-1, 1, (B, D)).astype(np.float32)
+        rewards = rng.standard_normal((B, 1)).astype(np.float32)
+        dones = (rng.random((B, 1)) < 0.05).astype(np.float32)
+        discounts = np.full((B, 1), 0.99, np.float32)
+        isw = rng.uniform(0.3, 1.0, (B, 1)).astype(np.float32) if per else None
+        log_alpha_v = np.array([[np.log(0.2)]], np.float32)
+        T = lambda a, g=False: Tensor.from_numpy(a, dev, requires_grad=g)
+        mean_t, log_std_t = T(mean, True), T(log_std, True)
+        nets = SimpleNamespace(
+            policy=_FakePolicy((mean_t, log_std_t), (T(mean_n), T(log_std_n))),
+            critics=[_LinearCritic(T(q_w[i]), T(s_feat[i]), T(s_feat[2 + i])) for i in range(2)],
+            targets=[_LinearCritic(T(q_w[2 + i]), T(s_feat[4 + i]), T(s_feat[6 + i]))
+                     for i in range(2)])
+        batch = _Batch(rewards=T(rewards), dones=T(dones), discounts=T(discounts),
+                       actions=T(actions), noise=T(noise), next_noise=T(next_noise))
+        batch.obs, batch.next_obs = "cur", "next"
+        log_alpha = T(log_alpha_v, True)
+        alpha = Tensor(ttnn.exp(log_alpha.data), requires_grad=False)
+        # critic loss: gradients reach the critics' outputs (here the action
+        # weights of the online critics and their state features)
+        for i in range(2):
+            nets.critics[i].w.requires_grad = True
+            nets.critics[i].s_cur.requires_grad = True
+        weights = T(isw) if per else None
+        closs, target, errors = critic_loss(nets, dist, batch, alpha, weights)
+        closs.backward()
+        pre = f"{name}_"
+        out.update({pre + "mean": mean, pre + "log_std": log_std, pre + "mean_next": mean_n,
+                    pre + "log_std_next": log_std_n, pre + "noise": noise,
+                    pre + "next_noise": next_noise, pre + "q_w": np.stack(q_w),
+                    pre + "s_feat": np.stack(s_feat), pre + "actions": actions,
+                    pre + "rewards": rewards, pre + "dones": dones, pre + "discounts": discounts,
+                    pre + "is_weights": isw if per else np.ones((B, 1), np.float32),
+                    pre + "log_alpha": log_alpha_v, pre + "low": np.array(low, np.float32),
+                    pre + "high": np.array(high, np.float32),
+                    pre + "critic_loss": closs.numpy(), pre + "q_target": target.numpy()})
+        for i in range(2):
+            out[pre + f"d_critic{i}_w"] = nets.critics[i].w.grad.to_numpy()
+            out[pre + f"d_critic{i}_s"] = nets.critics[i].s_cur.grad.to_numpy()
+        # actor loss (fresh graph; critics' weights now constants again)
+        for i in range(2):
+            nets.critics[i].w.requires_grad = False
+            nets.critics[i].s_cur.requires_grad = False
+            nets.critics[i].w.grad = None
+        aloss, logp = actor_loss(nets, dist, batch, alpha)
+        aloss.backward()
+        dual = alpha_loss(log_alpha, logp, -float(D))
+        dual.backward()
+        out.update({pre + "actor_loss": aloss.numpy(), pre + "logp": logp.numpy(),
+                    pre + "d_mean": mean_t.grad.to_numpy(),
+                    pre + "d_log_std": log_std_t.grad.to_numpy(),
+                    pre + "alpha_loss": dual.numpy(),
+                    pre + "d_log_alpha": log_alpha.grad.to_numpy()})
+    _save("sac_losses", out, index,
+          "ttrl/algos/sac/losses.py:46-94 with SquashedGaussian (ttrl/algos/sac/policy.py:30-40,"
+          " ttrl/algos/gaussian.py:55-167) over preset policy outputs and action-linear critics")
+
+
 def main() -> None:
     reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TTRL_REFERENCE")
     if not reference or not os.path.isdir(os.path.join(reference, "ttrl")):
@@ -386,7 +494,7 @@ def main() -> None:
     _install(reference)
     index: dict = {}
     for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
-               grad_clip, gru, param_sync):
+               grad_clip, gru, param_sync, sac_losses):
         fn(index)
         print("wrote", fn.__name__)
     with open(os.path.join(HERE, "index.json"), "w") as f:

@@ -186,3 +186,46 @@ def test_conv_backward_is_the_adjoint_of_the_pinned_forward(n, h, c, cout, k, s,
     dw = L.conv2d_wgrad(x, dy, k, stride=s, padding=p)
     assert float(np.sum(x * dx)) == pytest.approx(lhs, rel=1e-10)
     assert float(np.sum(w * dw)) == pytest.approx(lhs, rel=1e-10)
+
+
+@pytest.mark.parametrize("name", ["uniform", "prioritized"])
+def test_sac_losses(name):
+    """SAC critic, actor and temperature losses with their gradients against
+    the reference's own ttrl/algos/sac code (preset policy outputs,
+    critics linear in the action: Q_i(s, a) = a . w_i + s_i)."""
+    from oracle import sac as S
+    d = load("sac_losses")
+    g = {k[len(name) + 1:]: d[k] for k in d.files if k.startswith(name + "_")}
+    w, s = g["q_w"].astype(np.float64), g["s_feat"].astype(np.float64)
+    alpha = float(np.exp(g["log_alpha"].astype(np.float32)).reshape(-1)[0])
+    low, high = g["low"], g["high"]
+    # critic loss against the soft target
+    a_n, logp_n, _ = S.squashed_sample(g["mean_next"], g["log_std_next"], g["next_noise"],
+                                       low, high)
+    q_targ = [(a_n * w[2 + i]).sum(-1) + s[6 + i].reshape(-1) for i in range(2)]
+    y = S.soft_target(g["rewards"].reshape(-1), g["dones"].reshape(-1),
+                      g["discounts"].reshape(-1), q_targ, logp_n, alpha)
+    assert rel(y, g["q_target"].reshape(-1)) <= 1e-5
+    acts = g["actions"].astype(np.float64)
+    q = [(acts * w[i]).sum(-1) + s[i].reshape(-1) for i in range(2)]
+    weights = g["is_weights"].reshape(-1) if name == "prioritized" else None
+    loss, dq = S.critic_loss(q, y, weights)
+    assert rel(loss, g["critic_loss"]) <= 1e-5
+    for i in range(2):
+        assert rel((dq[i][:, None] * acts).sum(0), g[f"d_critic{i}_w"].reshape(-1)) <= 1e-5
+        assert rel(dq[i], g[f"d_critic{i}_s"].reshape(-1)) <= 1e-5
+    # actor loss through the reparameterised sample
+    a, logp, cache = S.squashed_sample(g["mean"], g["log_std"], g["noise"], low, high)
+    assert rel(logp, g["logp"].reshape(-1)) <= 1e-5
+    qa = [(a * w[i]).sum(-1) + s[i].reshape(-1) for i in range(2)]
+    aloss, d_logp, d_q = S.actor_loss(logp, qa, alpha)
+    assert rel(aloss, g["actor_loss"]) <= 1e-5
+    d_action = sum(d_q[i][:, None] * w[i] for i in range(2))
+    d_mean, d_log_std = S.squashed_sample_backward(d_action, d_logp, cache)
+    assert rel(d_mean, g["d_mean"]) <= 1e-5
+    assert rel(d_log_std, g["d_log_std"]) <= 1e-5
+    # temperature
+    la = float(g["log_alpha"].reshape(-1)[0])
+    dual, dla = S.alpha_loss(la, logp, -3.0)
+    assert rel(dual, g["alpha_loss"]) <= 1e-5
+    assert rel(dla, g["d_log_alpha"]) <= 1e-5
