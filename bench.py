@@ -48,6 +48,13 @@ SYNC_EVERY = 50
 PPO_FLOP_PER_SAMPLE = 2 * 24_762_880      # 3F' - conv1 dX, 2 per MAC
 DQN_FLOP_PER_UPDATE = 2 * 43_453_440 * 32
 
+# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu
+# capture each (profiles/gemm_tc_conv1_*_b256.md give the command).
+NCU_TRAFFIC_BYTES = {
+    "conv_wgrad[8x8/4 4->32]": 42.10e6,
+    "conv_fprop[8x8/4 4->32]": 29.03e6,
+}
+
 METRIC = "PPO learner samples/sec (Nature-CNN actor-critic, minibatch 256, fwd+bwd+clip+Adam, graph-replayed)"
 
 
@@ -376,7 +383,8 @@ def run_ours(args):
             "roofline": {
                 "bound": "tensor", "kernel": dom[0], "achieved": achieved,
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                "frac": achieved / peaks["bf16_tflops"],
+                "traffic": NCU_TRAFFIC_BYTES.get(dom[0]),
                 "peak_source": f"{peaks['source']} dense bf16 (TF32 dense is half; split-TF32 "
                                "issues 3 MMAs per product)",
                 "whole_step_tflops": step_tflops,
@@ -386,6 +394,7 @@ def run_ours(args):
         }
         if world == 1 and not args.no_dqn:
             out["dqn"] = bench_dqn(device, args)
+            out["sac"] = bench_sac(device, args)
         if world == 1 and not args.no_cpu_baseline:
             times = cpu_ppo_steps(2, seed=2)
             t = statistics.median(times)
@@ -464,6 +473,48 @@ def bench_dqn(device, args):
             "gpu_launches_per_update": launches,
             "achieved_tflops": DQN_FLOP_PER_UPDATE / (ms * 1e-3) / 1e12,
             "target": ">= 5000 updates/s"}
+
+
+def bench_sac(device, args):
+    """SAC MLP update (batch 256, obs 11, action 3: twin critics 14-256-256-1
+    with Polyak targets, actor 11-256-256-(3,3), learned temperature, three
+    Adams) as one graph replay; updates/sec, device time."""
+    import torch
+    from ttrl_b200.algos.sac import SACLearner
+    from ttrl_b200.device import context
+    from ttrl_b200.nets import build_sac_nets
+    B, OBS, ACT = 256, 11, 3
+    np.random.seed(9)
+    nets = build_sac_nets(OBS, ACT, device, batch=B)
+    learner = SACLearner(nets, -np.ones(ACT), np.ones(ACT), B, OBS, device)
+    rng = np.random.default_rng(4)
+    batch = dict(obs=rng.standard_normal((B, OBS)), next_obs=rng.standard_normal((B, OBS)),
+                 actions=np.tanh(rng.standard_normal((B, ACT))), rewards=rng.standard_normal((B, 1)),
+                 dones=(rng.random((B, 1)) < 0.001) * 1.0, discounts=np.full((B, 1), 0.99),
+                 noise=rng.standard_normal((B, ACT)), next_noise=rng.standard_normal((B, ACT)))
+    learner.load_batch(**batch)
+    for _ in range(max(args.warmup, 3)):
+        learner.replay()
+    ctx = context(device)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
+    K = max(50, args.steps * 5)
+    s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize(device)
+    for k in range(K):
+        ctx.ew("fill", None, None, flush, 0.0)
+        s[k].record()
+        learner.replay()
+        e[k].record()
+    torch.cuda.synchronize(device)
+    ms = sum(a.elapsed_time(b) for a, b in zip(s, e)) / K
+    out = {"metric": "SAC MLP batch-256 learner updates/sec (critic + actor + temperature + "
+                     "Polyak, one graph replay per update)",
+           "value": 1000.0 / ms, "unit": "updates/s", "ms_per_update": ms,
+           "gpu_launches_per_update": learner.launches_per_replay,
+           "achieved_tflops": 0.635e9 / (ms * 1e-3) / 1e12}
+    learner.close()
+    return out
 
 
 def main():

@@ -4,6 +4,7 @@ Nature-CNN shapes and launches one kernel family a few times.
 
     python -m ttrl_b200.profile_case conv1_fprop --batch 256 --reps 3
     python -m ttrl_b200.profile_case dqn_update --reps 3
+    python -m ttrl_b200.profile_case ppo_update --reps 2
 """
 
 from __future__ import annotations
@@ -73,6 +74,28 @@ def _dqn_case(reps: int) -> None:
     step.close()
 
 
+def _ppo_case(reps: int) -> None:
+    """One PPO rollout update (8 x 128 frames, 4 epochs x 4 minibatches of
+    256) replayed `reps` times from its CUDA graph."""
+    from ttrl_b200.algos.ppo import PPOConfig, PPOLearner, initial_old_logp
+    from ttrl_b200.nets import build_actor_critic
+    np.random.seed(0)
+    net = build_actor_critic((4, 84, 84), 6, "cuda", batch=256)
+    learner = PPOLearner(net, 1024, (4, 84, 84), "cuda", cfg=PPOConfig(epochs=4, minibatch_size=256))
+    rng = np.random.default_rng(0)
+    obs = rng.integers(0, 256, (1024, 4, 84, 84), dtype=np.uint8)
+    actions = rng.integers(0, 6, 1024)
+    old_logp, values = initial_old_logp(net, obs, actions, "cuda")
+    learner.load_rollout(obs, actions, old_logp, values, rng.standard_normal(1024),
+                         rng.standard_normal(1024))
+    learner.draw_permutations()
+    learner.capture()
+    for _ in range(reps):
+        learner.replay()
+    torch.cuda.synchronize()
+    learner.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case")
@@ -81,6 +104,9 @@ def main() -> None:
     a = ap.parse_args()
     if a.case == "dqn_update":
         _dqn_case(a.reps)
+        return
+    if a.case == "ppo_update":
+        _ppo_case(a.reps)
         return
     if a.case == "fc1_fwd":
         _linear_case(a.reps, a.batch)
