@@ -48,8 +48,9 @@ SYNC_EVERY = 50
 PPO_FLOP_PER_SAMPLE = 2 * 24_762_880      # 3F' - conv1 dX, 2 per MAC
 DQN_FLOP_PER_UPDATE = 2 * 43_453_440 * 32
 
-# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu
-# capture each (profiles/gemm_tc_conv1_*_b256.md give the command).
+# DRAM bytes (read + write) per launch of the dominant kernels, from one
+# `ncu --set full` capture each of `python -m ttrl_b200.profile_case
+# conv1_wgrad|conv1_fprop --batch 256`.
 NCU_TRAFFIC_BYTES = {
     "conv_wgrad[8x8/4 4->32]": 42.10e6,
     "conv_fprop[8x8/4 4->32]": 29.03e6,
