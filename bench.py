@@ -47,6 +47,7 @@ SAMPLES_PER_UPDATE = STEPS_PER_UPDATE * MB
 SYNC_EVERY = 50
 PPO_FLOP_PER_SAMPLE = 2 * 24_762_880      # 3F' - conv1 dX, 2 per MAC
 DQN_FLOP_PER_UPDATE = 2 * 43_453_440 * 32
+RPPO_FLOP_PER_STEP = 2 * 26_526_976 * 512  # 3F_r - conv1 dX per row, 512 rows
 
 # DRAM bytes (read + write) per launch of the dominant kernels, from one
 # `ncu --set full` capture each of `python -m ttrl_b200.profile_case
@@ -396,6 +397,7 @@ def run_ours(args):
         if world == 1 and not args.no_dqn:
             out["dqn"] = bench_dqn(device, args)
             out["sac"] = bench_sac(device, args)
+            out["recurrent_ppo"] = bench_recurrent(device, args)
         if world == 1 and not args.no_cpu_baseline:
             times = cpu_ppo_steps(2, seed=2)
             t = statistics.median(times)
@@ -514,6 +516,58 @@ def bench_sac(device, args):
            "value": 1000.0 / ms, "unit": "updates/s", "ms_per_update": ms,
            "gpu_launches_per_update": learner.launches_per_replay,
            "achieved_tflops": 0.635e9 / (ms * 1e-3) / 1e12}
+    learner.close()
+    return out
+
+
+def bench_recurrent(device, args):
+    """Recurrent PPO rollout update (16 envs x 128 steps, BPTT T=32, GRU 256
+    on the Nature-CNN trunk, minibatch 512 rows = 16 sequences, 4 epochs =
+    16 minibatch steps) as one graph replay; samples/sec over minibatch steps,
+    device time."""
+    import torch
+    from ttrl_b200.algos.ppo import PPOConfig
+    from ttrl_b200.algos.recurrent_ppo import RecurrentPPOLearner, shift_to_starts
+    from ttrl_b200.device import context
+    from ttrl_b200.nets import build_recurrent_actor_critic
+    n_steps, n_envs, T, H, rows = 128, 16, 32, 256, 512
+    np.random.seed(11)
+    net = build_recurrent_actor_critic((4, 84, 84), 6, device, batch=rows, hidden_size=H)
+    learner = RecurrentPPOLearner(net, n_steps, n_envs, (4, 84, 84), device,
+                                  cfg=PPOConfig(minibatch_size=rows), seq_len=T, seed=5)
+    rng = np.random.default_rng(6)
+    shape = (n_steps, n_envs)
+    boundary = (rng.random(shape) < 0.01).astype(np.float32)
+    learner.load_rollout(
+        rng.integers(0, 256, shape + (4, 84, 84), dtype=np.uint8), rng.integers(0, 6, shape),
+        (np.log(1 / 6) + 0.05 * rng.standard_normal(shape)).astype(np.float32),
+        rng.standard_normal(shape).astype(np.float32), rng.standard_normal(shape).astype(np.float32),
+        rng.standard_normal(shape).astype(np.float32),
+        starts=shift_to_starts(boundary, np.zeros(n_envs)),
+        hidden=(0.1 * rng.standard_normal((n_steps // T, n_envs, H))).astype(np.float32))
+    learner.draw_permutations()
+    for _ in range(max(args.warmup, 3)):
+        learner.replay()
+    ctx = context(device)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
+    K = max(3, args.steps // 10)
+    s = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    torch.cuda.synchronize(device)
+    for k in range(K):
+        ctx.ew("fill", None, None, flush, 0.0)
+        s[k].record()
+        learner.replay()
+        e[k].record()
+    torch.cuda.synchronize(device)
+    ms = sum(a.elapsed_time(b) for a, b in zip(s, e)) / K
+    steps = learner.steps_per_update
+    ms_step = ms / steps
+    out = {"metric": "recurrent PPO samples/sec (GRU 256, T=32, minibatch 512 rows, "
+                     "16 minibatch steps per graph replay)",
+           "value": rows * 1000.0 / ms_step, "unit": "samples/s", "ms_per_minibatch_step": ms_step,
+           "gpu_launches_per_step": learner.launches_per_replay / steps,
+           "achieved_tflops": RPPO_FLOP_PER_STEP / (ms_step * 1e-3) / 1e12}
     learner.close()
     return out
 

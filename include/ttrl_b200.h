@@ -355,6 +355,40 @@ int ttrl_ppo_loss(const float* logits, const float* value, const int32_t* action
                   float value_clip_eps, float value_coef, float entropy_coef,
                   ttrl_stream_t stream);
 
+/* --------------------------------------------------------------- recurrent */
+
+/* One GRU step after its recurrent GEMM: with gi = x_t @ W_ih + b_ih and
+ * gh = hm @ W_hh + b_hh (rows [batch][3*hidden], gate columns reset | update |
+ * candidate), r = sigmoid(gi_r + gh_r), z = sigmoid(gi_z + gh_z),
+ * n = tanh(gi_n + r * gh_n), out = (1 - z) * n + z * hm. gates[batch][3*hidden]
+ * receives (r, z, n) for the backward; when hm_next != NULL it receives
+ * out * (1 - start_next[b]) (start_next == NULL: out), the masked state
+ * entering the next step. Each operation rounds as the op-by-op composition
+ * of ttrl/engine/recurrent.py:86-94 does, so equal gi, gh give equal bits.
+ * Replaces the split / sigmoid / tanh / mul / add / sub launches of
+ * GRUCell.forward (ttrl/engine/recurrent.py:88-94) and the
+ * apply_done_mask of GRU.forward (:164-165). */
+int ttrl_gru_gates_fwd(const float* gi, const float* gh, const float* hm, const float* start_next,
+                       float* out, float* gates, float* hm_next, int batch, int hidden,
+                       ttrl_stream_t stream);
+
+/* The backward of one step. dh = dout (NULL: 0) plus, when carry != 0,
+ * dhm * (1 - start_next[b]) (the gradient reaching this step's output
+ * through the next step's masked state). Writes d gi and d gh
+ * ([batch][3*hidden]) and overwrites dhm with dh * z, the direct part of
+ * d hm; the caller accumulates d gh @ W_hh^T onto it (ttrl_linear_dgrad with
+ * accumulate = 1). Replaces the tape backward of the ops in
+ * ttrl/engine/recurrent.py:88-94 and :164-165. */
+int ttrl_gru_gates_bwd(const float* dout, float* dhm, const float* start_next, int carry,
+                       const float* gates, const float* gh, const float* hm, float* dgi,
+                       float* dgh, int batch, int hidden, ttrl_stream_t stream);
+
+/* out[b][:] = h[b][:] * (1 - start[b]) (start == NULL: a copy): the done mask
+ * of ttrl/engine/ops/functional.py:40-46 (apply_done_mask) on a [batch][hidden]
+ * state, used for the state entering step 0 and for d h0. */
+int ttrl_gru_mask(const float* h, const float* start, float* out, int batch, int hidden,
+                  ttrl_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -487,6 +487,69 @@ def sac_losses(index):
           " ttrl/algos/gaussian.py:55-167) over preset policy outputs and action-linear critics")
 
 
+def recurrent_ppo(index):
+    """One recurrent PPO minibatch through the reference's own pieces:
+    build_recurrent_actor_critic (MLP trunk -> GRU -> heads), a
+    RolloutSequenceBatch with resets inside the sequences and padding slots,
+    RecurrentRuntime.forward (zeroing + masked mean) and objective, then
+    backward. Also the unroll's outputs against T acting steps of the cell."""
+    from ttrl.algos.ppo.loss import objective
+    from ttrl.algos.ppo.policy import CategoricalPolicy
+    from ttrl.algos.ppo.recurrent import RecurrentRuntime
+    from ttrl.buffers.types import RolloutSequenceBatch
+    from ttrl.engine.autograd import Tensor
+    from ttrl.nets.obs import ObsPair
+    from ttrl.nets.recurrent import ACTOR, build_recurrent_actor_critic
+    from ttrl.spaces import ActionSpec, ObsGroup, ObsSpec
+    import ttnn
+    np.random.seed(950)
+    dev = ttnn.DEVICE
+    T, S, D, H, A = 6, 4, 9, 8, 5
+    spec = ObsGroup.of(ObsSpec.vector(D))
+    net = build_recurrent_actor_critic(spec, ActionSpec.discrete(A), dev, batch=T * S,
+                                       hidden_size=H, hidden=(16,))
+    rng = np.random.default_rng(951)
+    rows = T * S
+    obs = rng.standard_normal((rows, D)).astype(np.float32)
+    h0 = rng.standard_normal((S, H)).astype(np.float32)
+    starts = (rng.random((T, S, 1)) < 0.25).astype(np.float32)
+    starts[0, 0, 0], starts[3, 1, 0] = 1.0, 1.0
+    valid = (rng.random(rows) < 0.85).astype(np.float32)
+    actions = rng.integers(0, A, rows)
+    old_logp = (np.log(1.0 / A) + 0.3 * rng.standard_normal(rows)).astype(np.float32)
+    values = rng.standard_normal(rows).astype(np.float32)
+    adv = rng.standard_normal(rows).astype(np.float32)
+    returns = rng.standard_normal(rows).astype(np.float32)
+    batch = RolloutSequenceBatch(obs=obs, actions=actions, old_logp=old_logp, values=values,
+                                 advantages=adv, returns=returns, starts=starts, valid=valid,
+                                 h0={ACTOR: h0}, seq_len=T, lanes=np.arange(S))
+
+    def acting(o, h, st, *, seq_len):
+        return net(ObsPair.shared({"obs": Tensor.from_numpy(o, dev)}), h, st, seq_len=seq_len)
+
+    runtime = RecurrentRuntime(net, dev, n_envs=S, seq_len=T)
+    policy_out, value, reduce, masked = runtime.forward(acting, batch, dev)
+    cfg = SimpleNamespace(clip_eps=0.1, value_clip_eps=0.1, value_coef=0.5, entropy_coef=0.01)
+    policy = CategoricalPolicy(SimpleNamespace(n=A), dev)
+    loss, parts, new_logp = objective(policy, policy_out, value, masked, cfg, dev,
+                                      reduce=reduce)
+    loss.backward()
+    out = {"obs": obs, "h0": h0, "starts": starts, "valid": valid,
+           "actions": actions.astype(np.int64), "old_logp": old_logp, "values": values,
+           "advantages": adv, "returns": returns, "logits": policy_out.numpy(),
+           "value": value.numpy(), "loss": loss.numpy(),
+           "policy_loss": parts["policy_loss"].numpy(),
+           "value_loss": parts["value_loss"].numpy(), "entropy": parts["entropy"].numpy(),
+           "new_logp": new_logp.numpy()}
+    for name, p in net.named_parameters():
+        out["param." + name] = p.numpy()
+        out["grad." + name] = p.grad.to_numpy()
+    _save("recurrent_ppo", out, index,
+          "ttrl/algos/ppo/recurrent.py:179-227 + ttrl/nets/recurrent.py:98-123 + "
+          "ttrl/algos/ppo/loss.py:27-83: T=6 x 4 sequences, MLP(9->16) -> GRU(16->8) -> "
+          "(5 logits, value), starts inside sequences, padding slots; loss and every grad")
+
+
 def main() -> None:
     reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TTRL_REFERENCE")
     if not reference or not os.path.isdir(os.path.join(reference, "ttrl")):
@@ -494,7 +557,7 @@ def main() -> None:
     _install(reference)
     index: dict = {}
     for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
-               grad_clip, gru, param_sync, sac_losses):
+               grad_clip, gru, param_sync, sac_losses, recurrent_ppo):
         fn(index)
         print("wrote", fn.__name__)
     with open(os.path.join(HERE, "index.json"), "w") as f:

@@ -26,6 +26,12 @@ class MathFidelity:
     LoFi, HiFi2, HiFi3, HiFi4 = range(4)
 
 
+class TensorMemoryLayout:
+    """Placement names only: imported by modules this shim never runs."""
+    INTERLEAVED, HEIGHT_SHARDED, WIDTH_SHARDED, BLOCK_SHARDED = (
+        "INTERLEAVED", "HEIGHT_SHARDED", "WIDTH_SHARDED", "BLOCK_SHARDED")
+
+
 class _Device:
     def arch(self):
         return "numpy"

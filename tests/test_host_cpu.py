@@ -53,6 +53,60 @@ def test_library_refuses_bad_arguments_without_a_gpu():
     rc = lib.ttrl_linear_fwd(None, None, None, None, 0, 4, 4, 0, 0, None, 0, None, None)
     assert rc == 1  # TTRL_EINVAL
     assert b"bad extents" in lib.ttrl_last_error()
+    rc = lib.ttrl_gru_gates_fwd(None, None, None, None, None, None, None, 0, 8, None)
+    assert rc == 1
+    assert b"gru_gates_fwd" in lib.ttrl_last_error()
+    rc = lib.ttrl_gru_gates_bwd(None, None, None, 0, None, None, None, None, None, 4, 8, None)
+    assert rc == 1
+    assert b"null pointer" in lib.ttrl_last_error()
+
+
+# ------------------------------------------------- recurrent sequence layout
+
+def test_sequence_rows_are_time_major_whole_lanes():
+    """Row t * n_seq + s of a minibatch is timestep chunk_s * seq_len + t of
+    lane_s (ttrl/buffers/sequences.py:129-177 gather + flatten_time_major)."""
+    from ttrl_b200.algos.recurrent_ppo import sequence_rows
+    n_steps, n_envs, seq_len = 12, 4, 3
+    slot_of = np.arange(n_steps * n_envs).reshape(n_steps, n_envs)  # [t, lane] -> slot
+    ids = np.array([5, 0, 14, 9])
+    got = sequence_rows(ids, n_envs, seq_len)
+    want = []
+    for t in range(seq_len):
+        for i in ids:
+            chunk, lane = divmod(int(i), n_envs)
+            want.append(slot_of[chunk * seq_len + t, lane])
+    assert got.tolist() == want
+    # one sequence is one lane and consecutive timesteps
+    rows = got.reshape(seq_len, len(ids))
+    assert (rows % n_envs == (ids % n_envs)[None, :]).all()
+    assert (np.diff(rows // n_envs, axis=0) == 1).all()
+
+
+def test_sequence_helpers_follow_the_reference_contract():
+    from ttrl_b200.algos.recurrent_ppo import (chunk_count, chunks_per_minibatch,
+                                               normalize_valid_advantages, shift_to_starts)
+    assert chunk_count(128, 32) == 4
+    with pytest.raises(ValueError, match="does not divide"):
+        chunk_count(100, 32)
+    with pytest.raises(ValueError, match="seq_len must be >= 1"):
+        chunk_count(8, 0)
+    assert chunks_per_minibatch(512, 32) == 16
+    with pytest.raises(ValueError, match="not a multiple"):
+        chunks_per_minibatch(500, 32)
+    boundary = np.array([[0, 1], [1, 0], [0, 0]], np.float32)
+    starts = shift_to_starts(boundary, [1, 0])
+    assert starts.tolist() == [[1, 0], [0, 1], [1, 0]]
+    with pytest.raises(ValueError, match="carried covers"):
+        shift_to_starts(boundary, [1, 0, 0])
+    adv = np.array([1.0, 2.0, 100.0, 3.0], np.float32)
+    valid = np.array([1, 1, 0, 1], np.float32)
+    out = normalize_valid_advantages(adv, valid)
+    live = adv[valid > 0]
+    assert np.allclose(out, (adv - live.mean()) / (live.std() + 1e-8))
+    assert abs(float(out[valid > 0].mean())) < 1e-6
+    with pytest.raises(ValueError, match="no valid transitions"):
+        normalize_valid_advantages(adv, np.zeros(4))
 
 
 # ---------------------------------------------------------------- ParamSync

@@ -229,3 +229,24 @@ def test_sac_losses(name):
     dual, dla = S.alpha_loss(la, logp, -3.0)
     assert rel(dual, g["alpha_loss"]) <= 1e-5
     assert rel(dla, g["d_log_alpha"]) <= 1e-5
+
+
+def test_recurrent_ppo_minibatch():
+    """The recurrent minibatch (trunk -> GRU with in-sequence resets -> heads,
+    zeroed padding fields, masked-mean objective) and every gradient, against
+    the reference's own RecurrentRuntime.forward + objective."""
+    from oracle.recurrent import recurrent_ppo_minibatch
+    d = load("recurrent_ppo")
+    p = {k[len("param."):]: d[k].astype(np.float64) for k in d.files if k.startswith("param.")}
+    f = lambda k: d[k].astype(np.float64)
+    T = d["starts"].shape[0]
+    out = recurrent_ppo_minibatch(p, f("obs"), f("h0"), f("starts"), f("valid"), d["actions"],
+                                  f("old_logp"), f("values"), f("advantages"), f("returns"),
+                                  seq_len=T)
+    assert rel(out["logits"], d["logits"]) <= 1e-5
+    assert rel(out["value"], d["value"]) <= 1e-5
+    for k in ("loss", "policy_loss", "value_loss", "entropy"):
+        assert rel(out[k], d[k]) <= 1e-5, k
+    for name, g in out["grads"].items():
+        assert rel(g, d["grad." + name]) <= 1e-5, name
+    assert set(out["grads"]) == {k[len("grad."):] for k in d.files if k.startswith("grad.")}

@@ -133,6 +133,9 @@ _SIGNATURES = {
     "ttrl_dqn_loss": (_c_int, [_vp] * 13 + [_c_int, _c_int, _c_float, _c_int, _vp]),
     "ttrl_ppo_loss": (_c_int, [_vp] * 12 + [_c_int, _c_int, _c_float, _c_float, _c_float,
                                              _c_float, _vp]),
+    "ttrl_gru_gates_fwd": (_c_int, [_vp] * 7 + [_c_int, _c_int, _vp]),
+    "ttrl_gru_gates_bwd": (_c_int, [_vp, _vp, _vp, _c_int] + [_vp] * 5 + [_c_int, _c_int, _vp]),
+    "ttrl_gru_mask": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),
 }
 
 # Elementwise / reduction op codes (include/ttrl_b200.h).

@@ -28,7 +28,7 @@ from ttrl_b200.engine.ops import ppo_objective
 from ttrl_b200.engine.optim import Adam
 from ttrl_b200.engine.trace import capture
 
-__all__ = ["PPOConfig", "PPOLearner", "objective", "normalize_advantages"]
+__all__ = ["PPOConfig", "PPOLearner", "ReplayedUpdate", "objective", "normalize_advantages"]
 
 
 @dataclass(frozen=True)
@@ -63,103 +63,12 @@ def objective(logits: Tensor, value: Tensor, batch: dict, cfg: PPOConfig, *, val
         entropy_coef=cfg.entropy_coef, valid=valid)
 
 
-class PPOLearner:
-    """Graph-replayed PPO learner over a device-resident rollout."""
+class ReplayedUpdate:
+    """What a graph-replayed on-policy learner shares: the whole update
+    (`steps_per_update` calls of `_minibatch_step`) run op by op or captured
+    once and replayed, and the per-step metric rows read back once."""
 
     METRICS = ("loss", "policy_loss", "value_loss", "entropy", "grad_sq")
-
-    def __init__(self, net, rollout_size: int, obs_shape, device=None, *,
-                 cfg: PPOConfig = PPOConfig(), seed: int = 0):
-        self.net = net
-        self.cfg = cfg
-        self.device = as_device(device)
-        self.ctx = context(self.device)
-        self.rollout_size = int(rollout_size)
-        self.obs_shape = tuple(int(v) for v in obs_shape)
-        mb = cfg.minibatch_size
-        self.minibatches = self.rollout_size // mb
-        if self.minibatches == 0:
-            raise ValueError(f"rollout of {rollout_size} holds no minibatch of {mb}")
-        self.steps_per_update = cfg.epochs * self.minibatches
-        self.params = list(net.parameters())
-        self.optimizer = Adam(self.params, lr=cfg.lr, eps=cfg.eps)
-        self.rng = np.random.default_rng(seed)
-        dev = self.device
-        c, h, w = self.obs_shape
-        R = self.rollout_size
-        # Device-resident rollout (address-stable: written in place).
-        self.obs = torch.zeros((R, c, h, w), dtype=torch.uint8, device=dev)
-        self.actions = torch.zeros(R, dtype=torch.int32, device=dev)
-        self.old_logp = torch.zeros(R, dtype=torch.float32, device=dev)
-        self.values = torch.zeros(R, dtype=torch.float32, device=dev)
-        self.returns = torch.zeros(R, dtype=torch.float32, device=dev)
-        self.advantages = torch.zeros(R, dtype=torch.float32, device=dev)
-        self.perm = torch.zeros((self.steps_per_update, mb), dtype=torch.int32, device=dev)
-        self.perm_host = torch.zeros((self.steps_per_update, mb), dtype=torch.int32,
-                                     pin_memory=True)
-        # Minibatch staging (gathered per step on the device).
-        self.mb_rows = torch.empty((1, 1, mb * h * w, c), dtype=torch.float32, device=dev)
-        self.mb_actions = torch.empty(mb, dtype=torch.int32, device=dev)
-        self.mb_fields = {k: torch.empty(mb, dtype=torch.float32, device=dev)
-                          for k in ("old_logp", "values", "returns", "advantages")}
-        self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
-                                      dtype=torch.float32, device=dev)
-        self._graph = None
-        self.launches_per_replay = 0
-
-    # -- rollout -----------------------------------------------------------
-
-    def load_rollout(self, obs_u8, actions, old_logp, values, returns, advantages) -> None:
-        """Upload one rollout (host arrays). Advantages are normalised over
-        the rollout here when cfg.normalize_adv, as the reference does."""
-        adv = normalize_advantages(advantages) if self.cfg.normalize_adv else advantages
-        self.obs.copy_(torch.from_numpy(np.ascontiguousarray(obs_u8, np.uint8)))
-        self.actions.copy_(torch.from_numpy(np.asarray(actions, np.int32)))
-        self.old_logp.copy_(torch.from_numpy(np.asarray(old_logp, np.float32)))
-        self.values.copy_(torch.from_numpy(np.asarray(values, np.float32)))
-        self.returns.copy_(torch.from_numpy(np.asarray(returns, np.float32)))
-        self.advantages.copy_(torch.from_numpy(np.asarray(adv, np.float32)))
-
-    def draw_permutations(self) -> None:
-        """One permutation of the rollout per epoch, cut into minibatches."""
-        mb = self.cfg.minibatch_size
-        rows = []
-        for _ in range(self.cfg.epochs):
-            perm = self.rng.permutation(self.rollout_size)
-            for start in range(0, self.minibatches * mb, mb):
-                rows.append(perm[start:start + mb])
-        self.perm_host.numpy()[:] = np.stack(rows).astype(np.int32)
-        self.perm.copy_(self.perm_host, non_blocking=True)
-
-    # -- one gradient step ---------------------------------------------------
-
-    def _minibatch_step(self, k: int) -> None:
-        cfg = self.cfg
-        ctx = self.ctx
-        idx = self.perm[k]
-        c = self.obs_shape[0]
-        ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c), 1.0)
-        ctx.gather_rows(self.actions, idx, self.mb_actions)
-        for name, src in (("old_logp", self.old_logp), ("values", self.values),
-                          ("returns", self.returns), ("advantages", self.advantages)):
-            ctx.gather_rows(src, idx, self.mb_fields[name])
-        self.optimizer.zero_grad()
-        rows = Tensor(self.mb_rows)
-        rows._exact = True  # raw 0..255 frame values
-        logits, value = self.net(rows)
-        loss, parts, _ = ppo_objective(
-            logits, value, self.mb_actions, self.mb_fields["old_logp"],
-            self.mb_fields["advantages"], self.mb_fields["returns"], self.mb_fields["values"],
-            clip_eps=cfg.clip_eps, value_clip_eps=cfg.value_clip_eps,
-            value_coef=cfg.value_coef, entropy_coef=cfg.entropy_coef)
-        loss.backward()
-        norm = clip_grad_norm_device(self.params, cfg.max_grad_norm, self.optimizer)
-        self.optimizer.step()
-        row = self.metric_buf[k]
-        ctx.copy_strided(row[0:1], loss.data.reshape(1))
-        for j, key in enumerate(("policy_loss", "value_loss", "entropy")):
-            ctx.copy_strided(row[j + 1:j + 2], parts[key].data.reshape(1))
-        ctx.copy_strided(row[4:5], norm[0:1])
 
     def _update_body(self) -> None:
         for k in range(self.steps_per_update):
@@ -217,6 +126,113 @@ class PPOLearner:
         if self._graph is not None:
             self._graph.close()
             self._graph = None
+
+    def _record_metrics(self, k: int, loss, parts, norm) -> None:
+        """Step k's metric row: loss, the three parts and the squared grad norm."""
+        ctx = self.ctx
+        row = self.metric_buf[k]
+        ctx.copy_strided(row[0:1], loss.data.reshape(1))
+        for j, key in enumerate(("policy_loss", "value_loss", "entropy")):
+            ctx.copy_strided(row[j + 1:j + 2], parts[key].data.reshape(1))
+        ctx.copy_strided(row[4:5], norm[0:1])
+
+
+class PPOLearner(ReplayedUpdate):
+    """Graph-replayed PPO learner over a device-resident rollout."""
+
+    def __init__(self, net, rollout_size: int, obs_shape, device=None, *,
+                 cfg: PPOConfig = PPOConfig(), seed: int = 0):
+        self.net = net
+        self.cfg = cfg
+        self.device = as_device(device)
+        self.ctx = context(self.device)
+        self.rollout_size = int(rollout_size)
+        self.obs_shape = tuple(int(v) for v in obs_shape)
+        mb = cfg.minibatch_size
+        self.minibatches = self.rollout_size // mb
+        if self.minibatches == 0:
+            raise ValueError(f"rollout of {rollout_size} holds no minibatch of {mb}")
+        self.steps_per_update = cfg.epochs * self.minibatches
+        self.params = list(net.parameters())
+        self.optimizer = Adam(self.params, lr=cfg.lr, eps=cfg.eps)
+        self.rng = np.random.default_rng(seed)
+        dev = self.device
+        c, h, w = self.obs_shape
+        R = self.rollout_size
+        # Device-resident rollout (address-stable: written in place).
+        self.obs = torch.zeros((R, c, h, w), dtype=torch.uint8, device=dev)
+        self.actions = torch.zeros(R, dtype=torch.int32, device=dev)
+        self.old_logp = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.values = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.returns = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.advantages = torch.zeros(R, dtype=torch.float32, device=dev)
+        self.perm = torch.zeros((self.steps_per_update, mb), dtype=torch.int32, device=dev)
+        self.perm_host = torch.zeros((self.steps_per_update, mb), dtype=torch.int32,
+                                     pin_memory=True)
+        # Minibatch staging (gathered per step on the device).
+        self.mb_rows = torch.empty((1, 1, mb * h * w, c), dtype=torch.float32, device=dev)
+        self.mb_actions = torch.empty(mb, dtype=torch.int32, device=dev)
+        self.mb_fields = {k: torch.empty(mb, dtype=torch.float32, device=dev)
+                          for k in ("old_logp", "values", "returns", "advantages")}
+        self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
+                                      dtype=torch.float32, device=dev)
+        self._upload_done = None
+        self._graph = None
+        self.launches_per_replay = 0
+
+    # -- rollout -----------------------------------------------------------
+
+    def load_rollout(self, obs_u8, actions, old_logp, values, returns, advantages) -> None:
+        """Upload one rollout (host arrays). Advantages are normalised over
+        the rollout here when cfg.normalize_adv, as the reference does."""
+        adv = normalize_advantages(advantages) if self.cfg.normalize_adv else advantages
+        self.obs.copy_(torch.from_numpy(np.ascontiguousarray(obs_u8, np.uint8)))
+        self.actions.copy_(torch.from_numpy(np.asarray(actions, np.int32)))
+        self.old_logp.copy_(torch.from_numpy(np.asarray(old_logp, np.float32)))
+        self.values.copy_(torch.from_numpy(np.asarray(values, np.float32)))
+        self.returns.copy_(torch.from_numpy(np.asarray(returns, np.float32)))
+        self.advantages.copy_(torch.from_numpy(np.asarray(adv, np.float32)))
+
+    def draw_permutations(self) -> None:
+        """One permutation of the rollout per epoch, cut into minibatches."""
+        mb = self.cfg.minibatch_size
+        if self._upload_done is not None:
+            self._upload_done.synchronize()  # the previous upload has read perm_host
+        rows = []
+        for _ in range(self.cfg.epochs):
+            perm = self.rng.permutation(self.rollout_size)
+            for start in range(0, self.minibatches * mb, mb):
+                rows.append(perm[start:start + mb])
+        self.perm_host.numpy()[:] = np.stack(rows).astype(np.int32)
+        self.perm.copy_(self.perm_host, non_blocking=True)
+        self._upload_done = torch.cuda.Event()
+        self._upload_done.record()
+
+    # -- one gradient step ---------------------------------------------------
+
+    def _minibatch_step(self, k: int) -> None:
+        cfg = self.cfg
+        ctx = self.ctx
+        idx = self.perm[k]
+        c = self.obs_shape[0]
+        ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c), 1.0)
+        ctx.gather_rows(self.actions, idx, self.mb_actions)
+        for name, src in (("old_logp", self.old_logp), ("values", self.values),
+                          ("returns", self.returns), ("advantages", self.advantages)):
+            ctx.gather_rows(src, idx, self.mb_fields[name])
+        self.optimizer.zero_grad()
+        rows = Tensor(self.mb_rows)
+        rows._exact = True  # raw 0..255 frame values
+        logits, value = self.net(rows)
+        loss, parts, _ = ppo_objective(
+            logits, value, self.mb_actions, self.mb_fields["old_logp"],
+            self.mb_fields["advantages"], self.mb_fields["returns"], self.mb_fields["values"],
+            clip_eps=cfg.clip_eps, value_clip_eps=cfg.value_clip_eps,
+            value_coef=cfg.value_coef, entropy_coef=cfg.entropy_coef)
+        loss.backward()
+        norm = clip_grad_norm_device(self.params, cfg.max_grad_norm, self.optimizer)
+        self.optimizer.step()
+        self._record_metrics(k, loss, parts, norm)
 
 
 def initial_old_logp(net, obs_u8: np.ndarray, actions: np.ndarray, device, chunk: int = 256):

@@ -355,6 +355,27 @@ class DeviceContext:
         check(lib().ttrl_gather_rows(src.data_ptr(), idx.data_ptr(), dst.data_ptr(),
                                      int(idx.numel()), row, self.stream), "ttrl_gather_rows")
 
+    def gru_gates_fwd(self, gi, gh, hm, start_next, out, gates, hm_next) -> None:
+        """One GRU step's gates after its recurrent GEMM (rows [B][3H])."""
+        b, hidden = hm.shape[0], hm.shape[1]
+        check(lib().ttrl_gru_gates_fwd(_ptr(gi), _ptr(gh), _ptr(hm), _ptr(start_next), _ptr(out),
+                                       _ptr(gates), _ptr(hm_next), b, hidden, self.stream),
+              "ttrl_gru_gates_fwd")
+
+    def gru_gates_bwd(self, dout, dhm, start_next, carry: bool, gates, gh, hm, dgi,
+                      dgh) -> None:
+        """One GRU step's backward; leaves dh * z in `dhm`."""
+        b, hidden = hm.shape[0], hm.shape[1]
+        check(lib().ttrl_gru_gates_bwd(_ptr(dout), _ptr(dhm), _ptr(start_next), int(carry),
+                                       _ptr(gates), _ptr(gh), _ptr(hm), _ptr(dgi), _ptr(dgh), b,
+                                       hidden, self.stream), "ttrl_gru_gates_bwd")
+
+    def gru_mask(self, h, start, out) -> None:
+        """out = h * (1 - start) per row (start None: a copy)."""
+        b, hidden = h.shape[0], h.shape[1]
+        check(lib().ttrl_gru_mask(_ptr(h), _ptr(start), _ptr(out), b, hidden, self.stream),
+              "ttrl_gru_mask")
+
     def dqn_loss(self, q, q_sel, q_tgt, onehot, rewards, dones, discounts, next_mask,
                  is_weights, loss, mean_q, td_abs, dq, delta: float,
                  accumulate: bool = False) -> None:

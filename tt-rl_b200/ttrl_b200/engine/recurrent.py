@@ -1,8 +1,17 @@
-"""`GRUCell` and `GRU` (ttrl/engine/recurrent.py), composed from the tape ops
-in the reference's order: gates (reset, update, candidate) in PyTorch's
-column order, weights stored (features, 3*hidden), the done mask applied to
-the state entering each step, and a fixed-length unroll whose backward
-accumulates each weight's gradient T times.
+"""`GRUCell` and `GRU` (ttrl/engine/recurrent.py), with the reference's
+semantics: gates (reset, update, candidate) in PyTorch's column order,
+weights stored (features, 3*hidden), the done mask applied to the state
+entering each step, and a fixed-length unroll whose backward accumulates each
+weight's gradient over all T steps.
+
+The unroll runs as one tape node, `gru_unroll`. Its forward computes the input
+projection x @ W_ih + b_ih of every timestep in one GEMM, then per step one
+recurrent GEMM (hm_t @ W_hh + b_hh) and one fused gate kernel that also writes
+the masked state entering the next step. Its backward walks the steps in
+reverse with one fused gate-backward kernel and one GEMM (d gh_t @ W_hh^T,
+accumulated onto the direct path) per step, then forms dW_hh and db_hh with a
+single GEMM over all T steps. The tape's ordinary `linear` backward turns the
+stacked d gi into dX, dW_ih and db_ih, again one GEMM each.
 """
 
 from __future__ import annotations
@@ -10,13 +19,13 @@ from __future__ import annotations
 import math
 
 import numpy as np
+import torch
 
-from ttrl_b200.engine.autograd import Tensor, as_device
+from ttrl_b200.engine.autograd import Tensor, _detached, _needs, as_device
 from ttrl_b200.engine.nn import Module
-from ttrl_b200.engine.ops import (add, apply_done_mask, concat, linear, mul, reshape,
-                                  sigmoid, split, sub, tanh)
+from ttrl_b200.engine.ops import _ctx, _new, linear, reshape
 
-__all__ = ["GRU", "GRUCell", "GATES"]
+__all__ = ["GRU", "GRUCell", "GATES", "gru_unroll"]
 
 GATES = ("reset", "update", "candidate")
 
@@ -49,14 +58,9 @@ class GRUCell(Module):
 
     def forward(self, x: Tensor, h: Tensor) -> Tensor:
         self._check(x, h)
-        widths = (self.hidden_size,) * len(GATES)
-        # x @ W + b as one fused GEMM each (the reference's matmul + add).
-        gi = split(linear(x, self.weight_ih, self.bias_ih), widths)
-        gh = split(linear(h, self.weight_hh, self.bias_hh), widths)
-        reset = sigmoid(add(gi[0], gh[0]))
-        update = sigmoid(add(gi[1], gh[1]))
-        candidate = tanh(add(gi[2], mul(reset, gh[2])))
-        return add(mul(sub(1.0, update), candidate), mul(update, h))
+        gi = linear(x, self.weight_ih, self.bias_ih)
+        out = gru_unroll(gi, h, None, self.weight_hh, self.bias_hh, steps=1)
+        return reshape(out, (int(h.shape[0]), self.hidden_size))
 
     def _check(self, x: Tensor, h: Tensor) -> None:
         xs, hs = tuple(int(d) for d in x.shape), tuple(int(d) for d in h.shape)
@@ -97,13 +101,104 @@ class GRU(Module):
                 raise ValueError(
                     f"GRU: done must be shaped ({steps}, {batch}, 1), got {dshape}."
                 )
-            done_steps = split(done, (1,) * steps, dim=0)
-        rows = split(x, (1,) * steps, dim=0)
-        h = h0
-        outputs = []
-        for index, row in enumerate(rows):
-            if done is not None:
-                h = apply_done_mask(h, reshape(done_steps[index], (batch, 1)))
-            h = self.cell(reshape(row, (batch, self.in_features)), h)
-            outputs.append(reshape(h, (1, batch, self.hidden_size)))
-        return concat(outputs, dim=0), h
+        cell = self.cell
+        gi = linear(reshape(x, (steps * batch, self.in_features)), cell.weight_ih, cell.bias_ih)
+        outputs = gru_unroll(gi, h0, done, cell.weight_hh, cell.bias_hh, steps=steps)
+        return outputs, _last_step(outputs)
+
+
+def _last_step(outputs: Tensor) -> Tensor:
+    """outputs[T-1] as a view; its backward (taken only when the final state
+    feeds the loss) scatters into a zero gradient of the whole sequence."""
+    steps = int(outputs.shape[0])
+    data = outputs.data[steps - 1]
+    if not _needs(outputs):
+        return _detached(data)
+    out = Tensor(data, True, (outputs,), "gru_final")
+
+    def _backward(grad):
+        if outputs.requires_grad:
+            full = _new(outputs.shape, grad)
+            ctx = _ctx(grad)
+            ctx.ew("fill", None, None, full, 0.0)
+            ctx.copy_strided(full[steps - 1], grad.reshape(full[steps - 1].shape))
+            outputs._accumulate(full)
+
+    out._backward = _backward
+    return out
+
+
+def gru_unroll(gi: Tensor, h0: Tensor, starts, w_hh: Tensor, b_hh: Tensor, *,
+               steps: int) -> Tensor:
+    """The recurrent half of a GRU over `steps` timesteps, as one tape node.
+
+    gi: x @ W_ih + b_ih for every step, rows time-major [steps * batch, 3H];
+    h0: [batch, H]; starts: None or a (steps, batch, 1) {0, 1} mask applied to
+    the state entering each step (ttrl/engine/recurrent.py:163-167);
+    w_hh [H, 3H], b_hh [1, 3H]. -> outputs (steps, batch, H).
+    """
+    batch, hidden = int(h0.shape[0]), int(h0.shape[1])
+    g = gi.data if gi.data.is_contiguous() else gi.data.contiguous()
+    if tuple(g.shape) != (steps * batch, 3 * hidden):
+        raise ValueError(f"gru_unroll: gi has shape {tuple(g.shape)}, expected "
+                         f"({steps * batch}, {3 * hidden})")
+    g = g.reshape(steps, batch, 3 * hidden)
+    hd = h0.data if h0.data.is_contiguous() else h0.data.contiguous()
+    sd = None
+    if starts is not None:
+        sv = starts.data if isinstance(starts, Tensor) else starts
+        sd = sv.contiguous().reshape(steps, batch)
+    ctx = _ctx(g)
+    gh = _new((steps, batch, 3 * hidden), g)
+    gates = _new((steps, batch, 3 * hidden), g)
+    hm = _new((steps, batch, hidden), g)
+    out = _new((steps, batch, hidden), g)
+    ctx.gru_mask(hd, None if sd is None else sd[0], hm[0])
+    for t in range(steps):
+        ctx.linear_fwd(hm[t], w_hh.data, b_hh.data, gh[t], False)
+        nxt = t + 1 < steps
+        ctx.gru_gates_fwd(g[t], gh[t], hm[t], sd[t + 1] if (nxt and sd is not None) else None,
+                          out[t], gates[t], hm[t + 1] if nxt else None)
+    parents = (gi, h0, w_hh, b_hh)
+    if not _needs(*parents):
+        return _detached(out)
+    node = Tensor(out, True, parents, "gru_unroll")
+
+    def _backward(grad):
+        dy = grad if grad.is_contiguous() else grad.contiguous()
+        dy = dy.reshape(steps, batch, hidden)
+        dgi = _new((steps, batch, 3 * hidden), dy)
+        dgh = _new((steps, batch, 3 * hidden), dy)
+        dhm = _new((batch, hidden), dy)
+        need_h0 = h0.requires_grad
+        for t in reversed(range(steps)):
+            nxt = t + 1 < steps
+            ctx.gru_gates_bwd(dy[t], dhm, sd[t + 1] if (nxt and sd is not None) else None, nxt,
+                              gates[t], gh[t], hm[t], dgi[t], dgh[t])
+            if t > 0 or need_h0:
+                ctx.linear_dgrad(dgh[t], w_hh.data, None, dhm, True)
+        if need_h0:
+            d0 = _new((batch, hidden), dy)
+            ctx.gru_mask(dhm, None if sd is None else sd[0], d0)
+            h0._accumulate(d0)
+        wb, bb = w_hh.requires_grad, b_hh.requires_grad
+        if wb or bb:
+            if wb:
+                dw, accw = w_hh._grad_slot()
+            else:
+                dw, accw = torch.empty_like(w_hh.data), False
+            if bb:
+                db, accb = b_hh._grad_slot()
+            else:
+                db, accb = None, False
+            ctx.linear_wgrad(hm.reshape(steps * batch, hidden),
+                             dgh.reshape(steps * batch, 3 * hidden), dw, db, accw, accb)
+            if wb:
+                w_hh._set_grad(dw)
+            if bb:
+                b_hh._set_grad(db)
+        if gi.requires_grad:
+            gi._accumulate(dgi.reshape(steps * batch, 3 * hidden))
+
+    node._backward = _backward
+    return node

@@ -96,6 +96,32 @@ def _ppo_case(reps: int) -> None:
     learner.close()
 
 
+def _rppo_case(reps: int) -> None:
+    """One recurrent PPO rollout update (16 x 128 frames, T=32, GRU 256,
+    4 epochs x 4 minibatches of 16 sequences) replayed `reps` times."""
+    from ttrl_b200.algos.ppo import PPOConfig
+    from ttrl_b200.algos.recurrent_ppo import RecurrentPPOLearner
+    from ttrl_b200.nets import build_recurrent_actor_critic
+    np.random.seed(0)
+    net = build_recurrent_actor_critic((4, 84, 84), 6, "cuda", batch=512, hidden_size=256)
+    learner = RecurrentPPOLearner(net, 128, 16, (4, 84, 84), "cuda",
+                                  cfg=PPOConfig(minibatch_size=512), seq_len=32)
+    rng = np.random.default_rng(0)
+    shape = (128, 16)
+    learner.load_rollout(rng.integers(0, 256, shape + (4, 84, 84), dtype=np.uint8),
+                         rng.integers(0, 6, shape), np.full(shape, np.log(1 / 6), np.float32),
+                         rng.standard_normal(shape), rng.standard_normal(shape),
+                         rng.standard_normal(shape),
+                         starts=(rng.random(shape) < 0.01).astype(np.float32),
+                         hidden=np.zeros((4, 16, 256), np.float32))
+    learner.draw_permutations()
+    learner.capture()
+    for _ in range(reps):
+        learner.replay()
+    torch.cuda.synchronize()
+    learner.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("case")
@@ -107,6 +133,9 @@ def main() -> None:
         return
     if a.case == "ppo_update":
         _ppo_case(a.reps)
+        return
+    if a.case == "rppo_update":
+        _rppo_case(a.reps)
         return
     if a.case == "fc1_fwd":
         _linear_case(a.reps, a.batch)
