@@ -383,6 +383,34 @@ int ttrl_gru_gates_bwd(const float* dout, float* dhm, const float* start_next, i
                        const float* gates, const float* gh, const float* hm, float* dgi,
                        float* dgh, int batch, int hidden, ttrl_stream_t stream);
 
+/* Nonzero when the sequence kernels below take this batch and hidden width
+ * (hidden a multiple of 4, shared-memory slices that fit). Uses the current
+ * device (after ttrl_init). */
+int ttrl_gru_sequence_supported(int batch, int hidden);
+
+/* The recurrent half of a whole GRU unroll in one launch of thread-block
+ * clusters: for t = 0 .. steps-1, hm[t] = (t ? out[t-1] : h0) * (1 -
+ * starts[t]) (starts == NULL: no mask), gh[t] = hm[t] @ W_hh + b_hh, the
+ * gates of ttrl_gru_gates_fwd from gi[t] and gh[t], out[t] = the new state.
+ * gi, gh, gates are [steps][batch][3*hidden]; hm, out [steps][batch][hidden];
+ * starts [steps][batch]; w_hh [hidden][3*hidden]; b_hh [3*hidden]. gh is
+ * summed in fp32 on the CUDA cores. Replaces the T-step loop of GRU.forward
+ * (ttrl/engine/recurrent.py:160-168) after the input projection. */
+int ttrl_gru_sequence_fwd(const float* gi, const float* h0, const float* starts,
+                          const float* w_hh, const float* b_hh, float* gh, float* gates, float* hm,
+                          float* out, int steps, int batch, int hidden, ttrl_stream_t stream);
+
+/* Its backward through time in one launch: from dout [steps][batch][hidden]
+ * (NULL: zero) and the forward's saved gates, gh and hm, writes d gi and d gh
+ * ([steps][batch][3*hidden]) and, when dh0 != NULL, d h0. The weight
+ * gradients are one GEMM each over all steps (ttrl_linear_wgrad of hm against
+ * d gh, and of x against d gi). Replaces the tape backward of the T-step loop
+ * (ttrl/engine/recurrent.py:160-168). */
+int ttrl_gru_sequence_bwd(const float* dout, const float* starts, const float* w_hh,
+                          const float* gates, const float* gh, const float* hm, float* dgi,
+                          float* dgh, float* dh0, int steps, int batch, int hidden,
+                          ttrl_stream_t stream);
+
 /* out[b][:] = h[b][:] * (1 - start[b]) (start == NULL: a copy): the done mask
  * of ttrl/engine/ops/functional.py:40-46 (apply_done_mask) on a [batch][hidden]
  * state, used for the state entering step 0 and for d h0. */

@@ -146,3 +146,55 @@ def test_gru_unroll_matches_torch_reference():
         assert rel(ours.grad.cpu().numpy(), ref.grad.numpy()) <= 1e-4
     assert rel(xs.grad.cpu().numpy(), tx.grad.numpy()) <= 1e-4
     assert rel(hs.grad.cpu().numpy(), th.grad.numpy()) <= 1e-4
+
+
+@pytest.mark.parametrize("T,B,F,H,masked", [(5, 3, 8, 8, True), (32, 16, 64, 256, True),
+                                             (1, 4, 10, 8, False), (7, 2, 5, 12, True),
+                                             (6, 40, 16, 64, False)])
+def test_gru_sequence_kernels_equal_step_by_step(T, B, F, H, masked):
+    """The one-launch cluster unroll (forward and BPTT) against the per-step
+    GEMM + gate-kernel path on the same inputs: outputs and every gradient to
+    2e-5 relative (fp32 CUDA-core dots against split-TF32 GEMMs)."""
+    _need_gpu()
+    from ttrl_b200.device import context
+    from ttrl_b200.engine import ops as o
+    from ttrl_b200.engine.autograd import Tensor
+    from ttrl_b200.engine.recurrent import GRU, gru_unroll
+    from ttrl_b200.engine.ops import linear, reshape
+    ctx = context("cuda")
+    assert ctx.gru_sequence_supported(B, H)
+    rng = np.random.default_rng(T * 100 + H)
+    x = rng.standard_normal((T, B, F)).astype(np.float32)
+    h0 = rng.standard_normal((B, H)).astype(np.float32)
+    done = (rng.random((T, B, 1)) < 0.2).astype(np.float32) if masked else None
+    up = rng.standard_normal((T, B, H)).astype(np.float32)
+    results = []
+    for persistent in (True, False):
+        np.random.seed(4)
+        gru = GRU(F, H, "cuda")
+        c = gru.cell
+        xs = Tensor.from_numpy(x, "cuda", requires_grad=True)
+        hs = Tensor.from_numpy(h0, "cuda", requires_grad=True)
+        gi = linear(reshape(xs, (T * B, F)), c.weight_ih, c.bias_ih)
+        out = gru_unroll(gi, hs, None if done is None else Tensor.from_numpy(done, "cuda"),
+                         c.weight_hh, c.bias_hh, steps=T, persistent=persistent)
+        o.sum_all(o.mul(out, Tensor.from_numpy(up, "cuda"))).backward()
+        results.append([out.numpy(), xs.grad.cpu().numpy(), hs.grad.cpu().numpy()]
+                       + [p.grad.cpu().numpy() for p in (c.weight_ih, c.weight_hh, c.bias_ih,
+                                                         c.bias_hh)])
+    names = ("out", "dx", "dh0", "dW_ih", "dW_hh", "db_ih", "db_hh")
+    for name, a, b in zip(names, *results):
+        assert rel(a, b) <= 2e-5, name
+
+
+def test_gru_sequence_refuses_shapes_without_a_plan():
+    _need_gpu()
+    from ttrl_b200.device import context
+    from ttrl_b200._lib import lib
+    ctx = context("cuda")
+    assert not ctx.gru_sequence_supported(4, 6)   # hidden not a multiple of 4
+    assert not ctx.gru_sequence_supported(0, 8)
+    rc = lib().ttrl_gru_sequence_fwd(None, None, None, None, None, None, None, None, None,
+                                     3, 4, 6, None)
+    assert rc == 4  # TTRL_EUNSUPPORTED
+    assert b"has no plan" in lib().ttrl_last_error()

@@ -76,7 +76,8 @@ unsigned long long ttrl_launch_count(void) {
 int ttrl_init(int device) {
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return set_cuda_error("cudaSetDevice", e);
-  return gemm_init_device();
+  const int rc = gemm_init_device();
+  return rc != TTRL_OK ? rc : gru_init_device();
 }
 
 size_t ttrl_gemm_workspace_bytes(const ttrl_gemm_desc* d) {

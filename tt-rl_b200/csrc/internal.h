@@ -103,6 +103,7 @@ void note_launch();
 int set_cuda_error(const char* what, cudaError_t e);
 
 int gemm_init_device();
+int gru_init_device();
 size_t gemm_workspace_bytes(const ttrl_gemm_desc& d);
 // Launch one GEMM. `counters` (kCounterBytes, zeroed) and `partials` back
 // a split-K schedule; both may be null when K is not split.

@@ -136,6 +136,9 @@ _SIGNATURES = {
     "ttrl_gru_gates_fwd": (_c_int, [_vp] * 7 + [_c_int, _c_int, _vp]),
     "ttrl_gru_gates_bwd": (_c_int, [_vp, _vp, _vp, _c_int] + [_vp] * 5 + [_c_int, _c_int, _vp]),
     "ttrl_gru_mask": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),
+    "ttrl_gru_sequence_supported": (_c_int, [_c_int, _c_int]),
+    "ttrl_gru_sequence_fwd": (_c_int, [_vp] * 9 + [_c_int, _c_int, _c_int, _vp]),
+    "ttrl_gru_sequence_bwd": (_c_int, [_vp] * 9 + [_c_int, _c_int, _c_int, _vp]),
 }
 
 # Elementwise / reduction op codes (include/ttrl_b200.h).

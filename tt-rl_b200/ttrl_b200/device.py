@@ -370,6 +370,25 @@ class DeviceContext:
                                        _ptr(gates), _ptr(gh), _ptr(hm), _ptr(dgi), _ptr(dgh), b,
                                        hidden, self.stream), "ttrl_gru_gates_bwd")
 
+    def gru_sequence_supported(self, batch: int, hidden: int) -> bool:
+        """Whether the one-launch sequence kernels take this shape here."""
+        torch.cuda.set_device(self.index)
+        return bool(lib().ttrl_gru_sequence_supported(int(batch), int(hidden)))
+
+    def gru_sequence_fwd(self, gi, h0, starts, w_hh, b_hh, gh, gates, hm, out) -> None:
+        """The whole recurrent unroll after the input GEMM, one launch."""
+        steps, b, hidden = hm.shape
+        check(lib().ttrl_gru_sequence_fwd(_ptr(gi), _ptr(h0), _ptr(starts), _ptr(w_hh),
+                                          _ptr(b_hh), _ptr(gh), _ptr(gates), _ptr(hm), _ptr(out),
+                                          steps, b, hidden, self.stream), "ttrl_gru_sequence_fwd")
+
+    def gru_sequence_bwd(self, dout, starts, w_hh, gates, gh, hm, dgi, dgh, dh0) -> None:
+        """Its backward through time, one launch."""
+        steps, b, hidden = hm.shape
+        check(lib().ttrl_gru_sequence_bwd(_ptr(dout), _ptr(starts), _ptr(w_hh), _ptr(gates),
+                                          _ptr(gh), _ptr(hm), _ptr(dgi), _ptr(dgh), _ptr(dh0),
+                                          steps, b, hidden, self.stream), "ttrl_gru_sequence_bwd")
+
     def gru_mask(self, h, start, out) -> None:
         """out = h * (1 - start) per row (start None: a copy)."""
         b, hidden = h.shape[0], h.shape[1]

@@ -5,13 +5,16 @@ entering each step, and a fixed-length unroll whose backward accumulates each
 weight's gradient over all T steps.
 
 The unroll runs as one tape node, `gru_unroll`. Its forward computes the input
-projection x @ W_ih + b_ih of every timestep in one GEMM, then per step one
-recurrent GEMM (hm_t @ W_hh + b_hh) and one fused gate kernel that also writes
-the masked state entering the next step. Its backward walks the steps in
-reverse with one fused gate-backward kernel and one GEMM (d gh_t @ W_hh^T,
-accumulated onto the direct path) per step, then forms dW_hh and db_hh with a
-single GEMM over all T steps. The tape's ordinary `linear` backward turns the
-stacked d gi into dX, dW_ih and db_ih, again one GEMM each.
+projection x @ W_ih + b_ih of every timestep in one GEMM. The recurrence then
+runs as one launch over all T steps (one thread-block cluster per slice of
+the sequences, W_hh split across its CTAs' shared memory, the state exchanged
+through distributed shared memory between steps), and its backward through
+time as a second one; dW_hh and db_hh come from a single GEMM over all T
+steps, and the tape's ordinary `linear` backward turns the stacked d gi into
+dX, dW_ih and db_ih. Shapes the sequence kernels have no plan for (hidden not
+a multiple of 4, or slices too large for shared memory) run the same
+arithmetic step by step: one recurrent GEMM and one fused gate kernel per step
+forward, one gate-backward kernel and one GEMM per step backward.
 """
 
 from __future__ import annotations
@@ -129,13 +132,15 @@ def _last_step(outputs: Tensor) -> Tensor:
 
 
 def gru_unroll(gi: Tensor, h0: Tensor, starts, w_hh: Tensor, b_hh: Tensor, *,
-               steps: int) -> Tensor:
+               steps: int, persistent: bool | None = None) -> Tensor:
     """The recurrent half of a GRU over `steps` timesteps, as one tape node.
 
     gi: x @ W_ih + b_ih for every step, rows time-major [steps * batch, 3H];
     h0: [batch, H]; starts: None or a (steps, batch, 1) {0, 1} mask applied to
     the state entering each step (ttrl/engine/recurrent.py:163-167);
     w_hh [H, 3H], b_hh [1, 3H]. -> outputs (steps, batch, H).
+    `persistent` picks the one-launch sequence kernels (None: whenever the
+    shape has a plan) or the step-by-step launches.
     """
     batch, hidden = int(h0.shape[0]), int(h0.shape[1])
     g = gi.data if gi.data.is_contiguous() else gi.data.contiguous()
@@ -153,12 +158,17 @@ def gru_unroll(gi: Tensor, h0: Tensor, starts, w_hh: Tensor, b_hh: Tensor, *,
     gates = _new((steps, batch, 3 * hidden), g)
     hm = _new((steps, batch, hidden), g)
     out = _new((steps, batch, hidden), g)
-    ctx.gru_mask(hd, None if sd is None else sd[0], hm[0])
-    for t in range(steps):
-        ctx.linear_fwd(hm[t], w_hh.data, b_hh.data, gh[t], False)
-        nxt = t + 1 < steps
-        ctx.gru_gates_fwd(g[t], gh[t], hm[t], sd[t + 1] if (nxt and sd is not None) else None,
-                          out[t], gates[t], hm[t + 1] if nxt else None)
+    if persistent is None:
+        persistent = ctx.gru_sequence_supported(batch, hidden)
+    if persistent:
+        ctx.gru_sequence_fwd(g, hd, sd, w_hh.data, b_hh.data, gh, gates, hm, out)
+    else:
+        ctx.gru_mask(hd, None if sd is None else sd[0], hm[0])
+        for t in range(steps):
+            ctx.linear_fwd(hm[t], w_hh.data, b_hh.data, gh[t], False)
+            nxt = t + 1 < steps
+            ctx.gru_gates_fwd(g[t], gh[t], hm[t], sd[t + 1] if (nxt and sd is not None) else None,
+                              out[t], gates[t], hm[t + 1] if nxt else None)
     parents = (gi, h0, w_hh, b_hh)
     if not _needs(*parents):
         return _detached(out)
@@ -169,17 +179,22 @@ def gru_unroll(gi: Tensor, h0: Tensor, starts, w_hh: Tensor, b_hh: Tensor, *,
         dy = dy.reshape(steps, batch, hidden)
         dgi = _new((steps, batch, 3 * hidden), dy)
         dgh = _new((steps, batch, 3 * hidden), dy)
-        dhm = _new((batch, hidden), dy)
         need_h0 = h0.requires_grad
-        for t in reversed(range(steps)):
-            nxt = t + 1 < steps
-            ctx.gru_gates_bwd(dy[t], dhm, sd[t + 1] if (nxt and sd is not None) else None, nxt,
-                              gates[t], gh[t], hm[t], dgi[t], dgh[t])
-            if t > 0 or need_h0:
-                ctx.linear_dgrad(dgh[t], w_hh.data, None, dhm, True)
+        if persistent:
+            d0 = _new((batch, hidden), dy) if need_h0 else None
+            ctx.gru_sequence_bwd(dy, sd, w_hh.data, gates, gh, hm, dgi, dgh, d0)
+        else:
+            dhm = _new((batch, hidden), dy)
+            for t in reversed(range(steps)):
+                nxt = t + 1 < steps
+                ctx.gru_gates_bwd(dy[t], dhm, sd[t + 1] if (nxt and sd is not None) else None,
+                                  nxt, gates[t], gh[t], hm[t], dgi[t], dgh[t])
+                if t > 0 or need_h0:
+                    ctx.linear_dgrad(dgh[t], w_hh.data, None, dhm, True)
+            if need_h0:
+                d0 = _new((batch, hidden), dy)
+                ctx.gru_mask(dhm, None if sd is None else sd[0], d0)
         if need_h0:
-            d0 = _new((batch, hidden), dy)
-            ctx.gru_mask(dhm, None if sd is None else sd[0], d0)
             h0._accumulate(d0)
         wb, bb = w_hh.requires_grad, b_hh.requires_grad
         if wb or bb:
