@@ -201,12 +201,6 @@ __device__ __forceinline__ uint32_t gru_cluster_rank() {
   return r;
 }
 
-__device__ __forceinline__ void st_peer(const float* local, uint32_t rank, float v) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-
 // Threads per output: each sums every kLanes-th float4 of the reduction,
 // then a shuffle tree over the group.
 constexpr int kLanes = 8;
@@ -221,26 +215,27 @@ __device__ __forceinline__ unsigned group_mask() {
   return ((1u << kLanes) - 1u) << (threadIdx.x & (32 - kLanes));
 }
 
-// The per-step inputs of the forward for this CTA's units and the cluster's
-// rows, copied asynchronously: gi of step t ([R][3J]) and the done flag
-// entering step t+1 ([R]).
-__device__ __forceinline__ void fwd_stage(const GruSeqArgs& a, int t, float* gs, float* ss,
-                                          int b0, int rows, int j0) {
-  const int H = a.hidden, J = a.cols, H3 = 3 * H;
-  for (int i = threadIdx.x; i < rows * 3 * J; i += blockDim.x) {
-    const int bl = i / (3 * J), cl = i - bl * 3 * J;
-    const float* src = a.gi + (static_cast<size_t>(t) * a.batch + b0 + bl) * H3 + (cl / J) * H +
-                       j0 + (cl % J);
-    cp_async4(smem_u32(gs + i), src, 4);
-  }
-  if (a.starts != nullptr && t + 1 < a.steps) {
-    for (int i = threadIdx.x; i < rows; i += blockDim.x)
-      cp_async4(smem_u32(ss + i), a.starts + static_cast<size_t>(t + 1) * a.batch + b0 + i, 4);
-  }
-  cp_async_commit();
+// Each lane group of kLanes threads owns one (sequence, unit) pair of its CTA
+// for the whole launch, so every index below is computed once. Within a step
+// the group's lanes share the pair's side work: lane q stages one of the
+// pair's inputs for the next step, stores to the peers q, q + kLanes, ..., and
+// writes one of the pair's saved values to global memory.
+
+// Shared-memory address of `local` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t peer_addr(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  return remote;
 }
 
-__global__ void __launch_bounds__(512) gru_seq_fwd_kernel(const __grid_constant__ GruSeqArgs a) {
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Peers a lane stores to: q and q + kLanes (clusters have at most 16 CTAs).
+constexpr int kPeersPerLane = 2;
+
+__global__ void __launch_bounds__(1024) gru_seq_fwd_kernel(const __grid_constant__ GruSeqArgs a) {
   extern __shared__ __align__(16) float smem[];
   pdl_trigger();
   pdl_wait();
@@ -253,7 +248,6 @@ __global__ void __launch_bounds__(512) gru_seq_fwd_kernel(const __grid_constant_
   float* hs = ws + 3 * J * ld;     // [2][R][ld]: the state entering a step, by parity
   float* gs = hs + 2 * R * ld;     // [2][R][3J]: gi of a step, by parity
   float* ss = gs + 2 * R * 3 * J;  // [2][R]: done flag entering the next step
-  float* res = ss + 2 * R;         // [2][8][R][J]: h, hm next, r, z, n, gh r z n, by parity
   // W_hh row k holds this CTA's J columns of each gate contiguously: read
   // them unit-fastest (coalesced) and transpose into ws.
   for (int i = threadIdx.x; i < 3 * J * H; i += blockDim.x) {
@@ -267,27 +261,48 @@ __global__ void __launch_bounds__(512) gru_seq_fwd_kernel(const __grid_constant_
     hs[bl * ld + k] = v;
     if (k >= j0 && k < j0 + J) a.hm[static_cast<size_t>(b) * H + k] = v;
   }
-  fwd_stage(a, 0, gs, ss, b0, rows, j0);
+  const int q = threadIdx.x & (kLanes - 1);
+  const int p = threadIdx.x / kLanes;
+  const bool active = p < rows * J;
+  const int bl = active ? p / J : 0, jj = p - bl * J, j = j0 + jj, b = b0 + bl;
+  const size_t plane = static_cast<size_t>(a.batch);
+  // Lane q < 3 stages gi[s][b][q*H + j]; lane 3 of the unit-0 pair stages the
+  // done flag entering step s + 1.
+  auto stage = [&](int s, int buf) {
+    if (!active) return;
+    if (q < 3) {
+      cp_async4(smem_u32(gs + (buf * R + bl) * 3 * J + q * J + jj),
+                a.gi + (s * plane + b) * H3 + q * H + j, 4);
+    } else if (q == 3 && jj == 0 && a.starts != nullptr && s + 1 < a.steps) {
+      cp_async4(smem_u32(ss + buf * R + bl), a.starts + (s + 1) * plane + b, 4);
+    }
+  };
+  stage(0, 0);
+  cp_async_commit();
   cp_async_wait<0>();
   gru_cluster_sync();  // every CTA of the cluster is running before any peer store
-  const int q = threadIdx.x & (kLanes - 1);
+  // This pair's element of each parity buffer in peers q and q + kLanes.
+  const bool has0 = q < C, has1 = q + kLanes < C;
+  const uint32_t ra0 = has0 ? peer_addr(hs + bl * ld + j, q) : 0u;
+  const uint32_t rb0 = has0 ? peer_addr(hs + (R + bl) * ld + j, q) : 0u;
+  const uint32_t ra1 = has1 ? peer_addr(hs + bl * ld + j, q + kLanes) : 0u;
+  const uint32_t rb1 = has1 ? peer_addr(hs + (R + bl) * ld + j, q + kLanes) : 0u;
   const unsigned mask = group_mask();
   const int chunks = H >> 2;
-  const size_t plane = static_cast<size_t>(a.batch);
+  const float* wr = ws + jj * ld;
+  const float* wz = ws + (J + jj) * ld;
+  const float* wn = ws + (2 * J + jj) * ld;
+  const float bhr = active ? a.b_hh[j] : 0.f;
+  const float bhz = active ? a.b_hh[H + j] : 0.f;
+  const float bhn = active ? a.b_hh[2 * H + j] : 0.f;
   for (int t = 0; t < a.steps; ++t) {
     const int cur = t & 1;
-    const float* hc = hs + cur * R * ld;
-    float* hn = hs + (cur ^ 1) * R * ld;
-    const float* gc = gs + cur * R * 3 * J;
-    float* rc = res + cur * 8 * R * J;
     const bool more = t + 1 < a.steps;
-    if (more) fwd_stage(a, t + 1, gs + (cur ^ 1) * R * 3 * J, ss + (cur ^ 1) * R, b0, rows, j0);
-    for (int p = threadIdx.x / kLanes; p < rows * J; p += blockDim.x / kLanes) {
-      const int bl = p / J, jj = p - bl * J, j = j0 + jj;
-      const float* hrow = hc + bl * ld;
-      const float* wr = ws + jj * ld;
-      const float* wz = ws + (J + jj) * ld;
-      const float* wn = ws + (2 * J + jj) * ld;
+    if (more) stage(t + 1, cur ^ 1);
+    cp_async_commit();
+    float vq = 0.f;
+    if (active) {
+      const float* hrow = hs + (cur * R + bl) * ld;
       float ar = 0.f, az = 0.f, an = 0.f;
       for (int c = q; c < chunks; c += kLanes) {
         const float4 h4 = *reinterpret_cast<const float4*>(hrow + 4 * c);
@@ -304,12 +319,11 @@ __global__ void __launch_bounds__(512) gru_seq_fwd_kernel(const __grid_constant_
       ar = group_sum(ar, mask);
       az = group_sum(az, mask);
       an = group_sum(an, mask);
-      // Every lane of the group holds the sums; each finishes the gates and
-      // takes a share of the stores.
-      const float* g3 = gc + bl * 3 * J;
-      const float ghr = __fadd_rn(ar, a.b_hh[j]);
-      const float ghz = __fadd_rn(az, a.b_hh[H + j]);
-      const float ghn = __fadd_rn(an, a.b_hh[2 * H + j]);
+      // Every lane of the group holds the sums and finishes the gates.
+      const float* g3 = gs + (cur * R + bl) * 3 * J;
+      const float ghr = __fadd_rn(ar, bhr);
+      const float ghz = __fadd_rn(az, bhz);
+      const float ghn = __fadd_rn(an, bhn);
       const float r = gru_sigmoid(__fadd_rn(g3[jj], ghr));
       const float z = gru_sigmoid(__fadd_rn(g3[J + jj], ghz));
       const float n = tanhf(__fadd_rn(g3[2 * J + jj], __fmul_rn(r, ghn)));
@@ -318,77 +332,34 @@ __global__ void __launch_bounds__(512) gru_seq_fwd_kernel(const __grid_constant_
       const float hnext =
           (a.starts && more) ? __fmul_rn(h, __fsub_rn(1.f, ss[cur * R + bl])) : h;
       if (more) {
-        for (int peer = q; peer < C; peer += kLanes) st_peer(hn + bl * ld + j, peer, hnext);
+        if (has0) st_cluster(cur ? ra0 : rb0, hnext);
+        if (has1) st_cluster(cur ? ra1 : rb1, hnext);
       }
-      float vq;
-      switch (q) {
-        case 0: vq = h; break;
-        case 1: vq = hnext; break;
-        case 2: vq = r; break;
-        case 3: vq = z; break;
-        case 4: vq = n; break;
-        case 5: vq = ghr; break;
-        case 6: vq = ghz; break;
-        default: vq = ghn; break;
-      }
-      rc[(q * R + bl) * J + jj] = vq;
+      vq = q == 0 ? h : q == 1 ? hnext : q == 2 ? r : q == 3 ? z : q == 4 ? n
+         : q == 5 ? ghr : q == 6 ? ghz : ghn;
     }
-    // Publish the exchange (and the staged next-step inputs), then write the
-    // step's saved activations while the barrier completes.
+    // Publish the exchange and the staged inputs, then write this step's
+    // saved activations while the barrier completes.
     cp_async_wait<0>();
-    __syncthreads();
     if (more) gru_cluster_arrive();
-    for (int i = threadIdx.x; i < 8 * rows * J; i += blockDim.x) {
-      const int f = i / (rows * J), rem = i - f * rows * J, bl = rem / J, jj = rem - bl * J;
-      const int b = b0 + bl, j = j0 + jj;
-      const float v = rc[(f * R + bl) * J + jj];
+    if (active) {
       const size_t row = (t * plane + b) * H;
       const size_t row3 = (t * plane + b) * H3;
-      if (f == 0) {
-        a.out[row + j] = v;
-      } else if (f == 1) {
-        if (more) a.hm[row + plane * H + j] = v;
-      } else if (f <= 4) {
-        a.gates[row3 + (f - 2) * H + j] = v;
+      if (q == 0) {
+        a.out[row + j] = vq;
+      } else if (q == 1) {
+        if (more) a.hm[row + plane * H + j] = vq;
+      } else if (q <= 4) {
+        a.gates[row3 + (q - 2) * H + j] = vq;
       } else {
-        a.gh[row3 + (f - 5) * H + j] = v;
+        a.gh[row3 + (q - 5) * H + j] = vq;
       }
     }
     if (more) gru_cluster_wait();
   }
 }
 
-// The per-step inputs of the backward for this CTA's units and the cluster's
-// rows: per row [dout | r | z | n | gh_n | hm] (J each) and the done flag
-// entering step t+1.
-__device__ __forceinline__ void bwd_stage(const GruSeqBwdArgs& a, int t, float* xs, float* ss,
-                                          int b0, int rows, int j0) {
-  const int H = a.hidden, J = a.cols, H3 = 3 * H;
-  for (int i = threadIdx.x; i < rows * 6 * J; i += blockDim.x) {
-    const int bl = i / (6 * J), cl = i - bl * 6 * J, f = cl / J, jj = cl - f * J;
-    const size_t r1 = static_cast<size_t>(t) * a.batch + b0 + bl;
-    const float* src;
-    uint32_t bytes = 4;
-    if (f == 0) {
-      src = a.dout ? a.dout + r1 * H + j0 + jj : a.hm;  // no dout: zero-fill
-      bytes = a.dout ? 4 : 0;
-    } else if (f <= 3) {
-      src = a.gates + r1 * H3 + (f - 1) * H + j0 + jj;
-    } else if (f == 4) {
-      src = a.gh + r1 * H3 + 2 * H + j0 + jj;
-    } else {
-      src = a.hm + r1 * H + j0 + jj;
-    }
-    cp_async4(smem_u32(xs + i), src, bytes);
-  }
-  if (a.starts != nullptr && t + 1 < a.steps) {
-    for (int i = threadIdx.x; i < rows; i += blockDim.x)
-      cp_async4(smem_u32(ss + i), a.starts + static_cast<size_t>(t + 1) * a.batch + b0 + i, 4);
-  }
-  cp_async_commit();
-}
-
-__global__ void __launch_bounds__(512) gru_seq_bwd_kernel(const __grid_constant__ GruSeqBwdArgs a) {
+__global__ void __launch_bounds__(1024) gru_seq_bwd_kernel(const __grid_constant__ GruSeqBwdArgs a) {
   extern __shared__ __align__(16) float smem[];
   pdl_trigger();
   pdl_wait();
@@ -400,20 +371,52 @@ __global__ void __launch_bounds__(512) gru_seq_bwd_kernel(const __grid_constant_
   float* wr = smem;                  // [J][ld]: row j0 + jj of W_hh
   float* ds = wr + J * ld;           // [2][R][ld]: d gh of the step after, by parity
   float* direct = ds + 2 * R * ld;   // [R][J]: dh * z of the step after
-  float* xs = direct + R * J;        // [2][R][6J]: staged per-step inputs
+  float* xs = direct + R * J;        // [2][R][6J]: [dout | r | z | n | gh_n | hm] of a step
   float* ss = xs + 2 * R * 6 * J;    // [2][R]: done flag entering the step after
-  float* res = ss + 2 * R;           // [2][4][R][J]: d a_r, d a_z, d a_n, d gh_n, by parity
   for (int i = threadIdx.x; i < J * H3; i += blockDim.x) {
     const int jj = i / H3, c = i - jj * H3;
     wr[jj * ld + c] = a.w_hh[static_cast<size_t>(j0 + jj) * H3 + c];
   }
-  bwd_stage(a, a.steps - 1, xs, ss, b0, rows, j0);
+  const int q = threadIdx.x & (kLanes - 1);
+  const int p = threadIdx.x / kLanes;
+  const bool active = p < rows * J;
+  const int bl = active ? p / J : 0, jj = p - bl * J, j = j0 + jj, b = b0 + bl;
+  const size_t plane = static_cast<size_t>(a.batch);
+  // Lane q < 6 stages field q of step s; lane 6 of the unit-0 pair stages the
+  // done flag entering step s + 1.
+  auto stage = [&](int s, int buf) {
+    if (!active) return;
+    const size_t r1 = s * plane + b;
+    if (q < 6) {
+      const float* src;
+      uint32_t bytes = 4;
+      if (q == 0) {
+        src = a.dout ? a.dout + r1 * H + j : a.hm;  // no dout: zero-fill
+        bytes = a.dout ? 4 : 0;
+      } else if (q <= 3) {
+        src = a.gates + r1 * H3 + (q - 1) * H + j;
+      } else if (q == 4) {
+        src = a.gh + r1 * H3 + 2 * H + j;
+      } else {
+        src = a.hm + r1 * H + j;
+      }
+      cp_async4(smem_u32(xs + (buf * R + bl) * 6 * J + q * J + jj), src, bytes);
+    } else if (q == 6 && jj == 0 && a.starts != nullptr && s + 1 < a.steps) {
+      cp_async4(smem_u32(ss + buf * R + bl), a.starts + (s + 1) * plane + b, 4);
+    }
+  };
+  stage(a.steps - 1, 0);
+  cp_async_commit();
   cp_async_wait<0>();
   gru_cluster_sync();
-  const int q = threadIdx.x & (kLanes - 1);
+  const bool has0 = q < C, has1 = q + kLanes < C;
+  const uint32_t ra0 = has0 ? peer_addr(ds + bl * ld + j, q) : 0u;
+  const uint32_t rb0 = has0 ? peer_addr(ds + (R + bl) * ld + j, q) : 0u;
+  const uint32_t ra1 = has1 ? peer_addr(ds + bl * ld + j, q + kLanes) : 0u;
+  const uint32_t rb1 = has1 ? peer_addr(ds + (R + bl) * ld + j, q + kLanes) : 0u;
   const unsigned mask = group_mask();
   const int chunks = H3 >> 2;
-  const size_t plane = static_cast<size_t>(a.batch);
+  const float* wrow = wr + jj * ld;
   // Phases T-1 .. 0, then (when d h0 is wanted) a tail that reads step 0's d gh.
   const int phases = a.steps + (a.dh0 != nullptr ? 1 : 0);
   for (int it = 0; it < phases; ++it) {
@@ -422,18 +425,13 @@ __global__ void __launch_bounds__(512) gru_seq_bwd_kernel(const __grid_constant_
     const int cur = it & 1;
     const bool carry = tail || t + 1 < a.steps;
     const bool push = it + 1 < phases;  // a later phase reads this step's d gh
-    const float* dc = ds + cur * R * ld;
-    float* dn_buf = ds + (cur ^ 1) * R * ld;
-    const float* xc = xs + cur * R * 6 * J;
-    float* rc = res + cur * 4 * R * J;
-    if (it + 1 < a.steps)
-      bwd_stage(a, t - 1, xs + (cur ^ 1) * R * 6 * J, ss + (cur ^ 1) * R, b0, rows, j0);
-    for (int p = threadIdx.x / kLanes; p < rows * J; p += blockDim.x / kLanes) {
-      const int bl = p / J, jj = p - bl * J, j = j0 + jj;
+    if (it + 1 < a.steps) stage(t - 1, cur ^ 1);
+    cp_async_commit();
+    float vq = 0.f;
+    if (active) {
       float acc = 0.f;
       if (carry) {
-        const float* drow = dc + bl * ld;
-        const float* wrow = wr + jj * ld;
+        const float* drow = ds + (cur * R + bl) * ld;
         for (int c = q; c < chunks; c += kLanes) {
           const float4 d4 = *reinterpret_cast<const float4*>(drow + 4 * c);
           const float4 w4 = *reinterpret_cast<const float4*>(wrow + 4 * c);
@@ -445,54 +443,46 @@ __global__ void __launch_bounds__(512) gru_seq_bwd_kernel(const __grid_constant_
       const float dhm = carry ? direct[bl * J + jj] + acc : 0.f;
       if (tail) {
         if (q == 0) {
-          const int b = b0 + bl;
           const float s0 = a.starts ? a.starts[b] : 0.f;
           a.dh0[static_cast<size_t>(b) * H + j] = a.starts ? dhm * (1.f - s0) : dhm;
         }
-        continue;
-      }
-      const float* x6 = xc + bl * 6 * J;
-      float dh = x6[jj];
-      if (carry) dh += a.starts ? dhm * (1.f - ss[cur * R + bl]) : dhm;
-      const float r = x6[J + jj], z = x6[2 * J + jj], n = x6[3 * J + jj];
-      const float ghn = x6[4 * J + jj], hp = x6[5 * J + jj];
-      const float dnn = dh * (1.f - z);
-      const float dz = dh * (hp - n);
-      const float dan = dnn * (1.f - n * n);
-      const float dar = (dan * ghn) * r * (1.f - r);
-      const float daz = dz * z * (1.f - z);
-      const float dghn = dan * r;
-      if (push) {
-        float* dst = dn_buf + bl * ld;
-        for (int peer = q; peer < C; peer += kLanes) {
-          st_peer(dst + j, peer, dar);
-          st_peer(dst + H + j, peer, daz);
-          st_peer(dst + 2 * H + j, peer, dghn);
+      } else {
+        const float* x6 = xs + (cur * R + bl) * 6 * J;
+        float dh = x6[jj];
+        if (carry) dh += a.starts ? dhm * (1.f - ss[cur * R + bl]) : dhm;
+        const float r = x6[J + jj], z = x6[2 * J + jj], n = x6[3 * J + jj];
+        const float ghn = x6[4 * J + jj], hp = x6[5 * J + jj];
+        const float dnn = dh * (1.f - z);
+        const float dz = dh * (hp - n);
+        const float dan = dnn * (1.f - n * n);
+        const float dar = (dan * ghn) * r * (1.f - r);
+        const float daz = dz * z * (1.f - z);
+        const float dghn = dan * r;
+        if (push) {
+          if (has0) {
+            const uint32_t base = cur ? ra0 : rb0;
+            st_cluster(base, dar);
+            st_cluster(base + 4u * H, daz);
+            st_cluster(base + 8u * H, dghn);
+          }
+          if (has1) {
+            const uint32_t base = cur ? ra1 : rb1;
+            st_cluster(base, dar);
+            st_cluster(base + 4u * H, daz);
+            st_cluster(base + 8u * H, dghn);
+          }
         }
-      }
-      if (q < 4) {
-        const float vq = q == 0 ? dar : (q == 1 ? daz : (q == 2 ? dan : dghn));
-        rc[(q * R + bl) * J + jj] = vq;
-      } else if (q == 4) {
-        direct[bl * J + jj] = dh * z;
+        if (q == 6) direct[bl * J + jj] = dh * z;
+        // d gi = (d a_r, d a_z, d a_n); d gh = (d a_r, d a_z, d gh_n).
+        vq = q == 0 ? dar : q == 1 ? daz : q == 2 ? dan : q == 3 ? dar : q == 4 ? daz : dghn;
       }
     }
     cp_async_wait<0>();
-    __syncthreads();
     if (push) gru_cluster_arrive();
-    if (!tail) {
-      // d gi = (d a_r, d a_z, d a_n); d gh = (d a_r, d a_z, d gh_n).
-      for (int i = threadIdx.x; i < 6 * rows * J; i += blockDim.x) {
-        const int f = i / (rows * J), rem = i - f * rows * J, bl = rem / J, jj = rem - bl * J;
-        const int b = b0 + bl, j = j0 + jj;
-        const size_t row3 = (t * plane + b) * H3;
-        if (f < 3) {
-          a.dgi[row3 + f * H + j] = rc[(f * R + bl) * J + jj];
-        } else {
-          const int g = f - 3;
-          a.dgh[row3 + g * H + j] = rc[((g == 2 ? 3 : g) * R + bl) * J + jj];
-        }
-      }
+    if (active && !tail && q < 6) {
+      const size_t row3 = (t * plane + b) * H3;
+      if (q < 3) a.dgi[row3 + q * H + j] = vq;
+      else a.dgh[row3 + (q - 3) * H + j] = vq;
     }
     if (push) gru_cluster_wait();
   }
@@ -502,7 +492,7 @@ __global__ void __launch_bounds__(512) gru_seq_bwd_kernel(const __grid_constant_
 // the portable 8), probed once by gru_init_device with both kernels' shared
 // memory ceilings raised.
 static int g_gru_cluster_cap[64];
-constexpr size_t kGruSmemCap = 200u << 10;
+constexpr size_t kGruSmemCap = 227u << 10;  // the per-CTA maximum on B200
 
 struct GruSeqPlan {
   int csize, cols, rows, clusters, threads, ldh, ld3;
@@ -513,30 +503,36 @@ struct GruSeqPlan {
 // lane groups of a quarter-warp reading adjacent rows hit disjoint banks.
 static int gru_pad(int w) { return w + ((16 - w % 32) + 32) % 32; }
 
+// The cluster size is the smallest of 4, 8, 16 whose per-CTA slices fit: a
+// step's exchange costs more the more CTAs a cluster spans (measured on B200:
+// about 0.56, 0.76 and 1.26 us per step at 4, 8 and 16 CTAs), while the
+// per-lane work stays the same because the CTA's lane groups grow with it.
 static bool gru_seq_plan(int batch, int hidden, GruSeqPlan* p) {
   if (batch <= 0 || hidden <= 0 || (hidden & 3) != 0) return false;
   int dev = 0;
   int cap = 8;
   if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64 && g_gru_cluster_cap[dev] > 0)
     cap = g_gru_cluster_cap[dev];
-  int c = cap;
-  while (c > 1 && hidden % c != 0) c >>= 1;
-  const int cols = hidden / c;
-  int most = 148 / c;
-  if (most < 1) most = 1;
-  const int rows = (batch + most - 1) / most;
-  const int clusters = (batch + rows - 1) / rows;
-  long long threads = ((static_cast<long long>(kLanes) * rows * cols + 31) / 32) * 32;
-  if (threads > 512) threads = 512;
   const int ldh = gru_pad(hidden), ld3 = gru_pad(3 * hidden);
-  const size_t rj = static_cast<size_t>(rows) * cols;
-  const size_t fwd = ((static_cast<size_t>(3 * cols) + 2 * rows) * ldh + 2 * rj * 3 + 2 * rows +
-                      2 * 8 * rj) * sizeof(float);
-  const size_t bwd = ((static_cast<size_t>(cols) + 2 * rows) * ld3 + rj + 2 * rj * 6 + 2 * rows +
-                      2 * 4 * rj) * sizeof(float);
-  if (fwd > kGruSmemCap || bwd > kGruSmemCap) return false;
-  *p = GruSeqPlan{c, cols, rows, clusters, static_cast<int>(threads), ldh, ld3, fwd, bwd};
-  return true;
+  for (int c = 4; c <= cap && c <= kLanes * kPeersPerLane; c *= 2) {
+    if (hidden % c != 0) continue;
+    const int cols = hidden / c;
+    const int most = 148 / c;
+    const int rows = (batch + most - 1) / most;
+    const int clusters = (batch + rows - 1) / rows;
+    // One lane group per (sequence, unit) pair, a block of at most 1024 threads.
+    const long long threads = ((static_cast<long long>(kLanes) * rows * cols + 31) / 32) * 32;
+    if (threads > 1024) continue;
+    const size_t rj = static_cast<size_t>(rows) * cols;
+    const size_t fwd = ((static_cast<size_t>(3 * cols) + 2 * rows) * ldh + 2 * rj * 3 +
+                        2 * rows) * sizeof(float);
+    const size_t bwd = ((static_cast<size_t>(cols) + 2 * rows) * ld3 + rj + 2 * rj * 6 +
+                        2 * rows) * sizeof(float);
+    if (fwd > kGruSmemCap || bwd > kGruSmemCap) continue;
+    *p = GruSeqPlan{c, cols, rows, clusters, static_cast<int>(threads), ldh, ld3, fwd, bwd};
+    return true;
+  }
+  return false;
 }
 
 int gru_init_device() {
@@ -555,7 +551,7 @@ int gru_init_device() {
           cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(16);
-    cfg.blockDim = dim3(512);
+    cfg.blockDim = dim3(1024);
     cfg.dynamicSmemBytes = kGruSmemCap;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
