@@ -1,32 +1,45 @@
 // tcgen05 GEMM for the learner update: D[r][c] = sum_k A[r][k] * B[c][k].
 //
 // One CTA owns a 128 x BN tile of D held in TMEM and walks its share of K
-// in 32-wide k-blocks through a ring of shared-memory stages: eight loader
-// warps gather each stage with cp.async (and, for split-TF32, split the
-// chunks they copied), then arrive on the stage's "full" mbarrier; a ninth
-// warp waits on it and issues the tcgen05.mma instructions, whose commit
-// frees the stage again. No block-wide barrier sits in the main loop. Each operand is *gathered* (dense strided matrix, convolution
-// im2col, or transposed im2col for the weight gradient), so one kernel
-// serves Linear fwd/dgrad/wgrad and Conv2d fprop/dgrad/wgrad without
-// materialising any im2col buffer. Tiles land in the canonical swizzled
-// layouts (K-major SWIZZLE_128B, or MN-major SWIZZLE_128B_BASE32B for 32-bit
-// operands) depending on which dimension is contiguous in global memory,
-// and thread 0 issues tcgen05.mma.kind::tf32.
+// in 32-wide k-blocks through a ring of shared-memory stages. Warp roles:
+//   - a TMA producer warp (one elected lane) loads every operand that is a
+//     plain dense matrix with 16-byte-aligned strides with
+//     cp.async.bulk.tensor, refilling a stage as soon as the MMA frees it;
+//   - eight loader warps *gather* the other operands with cp.async: the
+//     convolution im2col, the transposed im2col of the weight gradient, and
+//     dense matrices TMA cannot describe. So one kernel serves Linear
+//     fwd/dgrad/wgrad and Conv2d fprop/dgrad/wgrad without materialising any
+//     im2col buffer. For split-TF32 the loader warps also write each stage's
+//     low part into a separate ring;
+//   - one MMA warp (one elected lane) issues tcgen05.mma.kind::tf32 and
+//     commits each stage back to its "empty" mbarrier.
+// No block-wide barrier sits in the main loop. Tiles land in the canonical
+// swizzled layouts (K-major SWIZZLE_128B, or MN-major SWIZZLE_128B_BASE32B
+// for 32-bit operands) depending on which dimension is contiguous in global
+// memory; TMA writes the same layouts.
 //
 // Gather addressing is split into a per-CTA part (each thread's rows or row
 // chunk, computed once) and a per-k-block part (multiply-shift division, no
 // hardware divides), which keeps the load path a few instructions per
 // 16-byte copy.
 //
-// Precision: TTRL_PREC_TF32X3 splits every operand into a tf32 high part and
-// an fp32 remainder in shared memory and accumulates hi*hi + hi*lo + lo*hi,
-// which reproduces fp32 products to ~1e-6 relative. TTRL_PREC_TF32 issues a
-// single pass on the truncated operands.
+// Precision: TTRL_PREC_TF32X3 accumulates hi*hi + hi*lo + lo*hi. The MMA
+// reads fp32 operands and uses their tf32 part, so the raw stage is the high
+// part and only lo = x - tf32(x) is written; this reproduces fp32 products
+// to ~1e-6 relative. TTRL_PREC_TF32 issues a single pass.
 //
-// K can be split across CTAs (blockIdx.z). Each split writes its partial
-// tile to the workspace; the last CTA of a tile to arrive (a device counter,
-// left at zero afterwards) sums the partials in split order and applies the
-// epilogue, so results are deterministic and no second kernel is launched.
+// Split-K (blockIdx.z): up to 16 splits run as one thread-block cluster and
+// reduce their partial tiles through distributed shared memory in split
+// order. Very long K (>= 32 k-blocks per split at the cluster limit) splits
+// up to 64 ways through a global workspace instead; the last CTA of a tile to
+// arrive (a device counter, left at zero afterwards) sums the partials in
+// split order, or splitk_reduce_kernel does when the partials are large.
+// Either way results are deterministic. Grids of several waves use a
+// half-footprint variant (SMALL) that fits two CTAs per SM.
+//
+// Every launch uses programmatic dependent launch: TMEM allocation and
+// barrier set-up overlap the previous kernel's tail, and griddepcontrol.wait
+// precedes the first global access.
 #include <cstdio>
 #include <cstring>
 #include <mutex>

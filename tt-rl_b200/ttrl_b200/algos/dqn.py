@@ -72,12 +72,25 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
                 leaves=None) -> dict:
     """One DQN update: Huber loss against the (double-)DQN n-step target,
     backward, and device metrics (ttrl/algos/dqn/losses.py:77-140)."""
-    obs = obs_to_rows(inputs["obs"])
     next_obs = obs_to_rows(inputs["next_obs"])
-    q = online(obs)
+    # The two no-grad forwards on s' are independent of the online forward on
+    # s: they run on side lanes, concurrently with it (parallel branches of
+    # the captured graph), and the loss waits for all three.
+    ctx = context(next_obs.data.device)
+    main = torch.cuda.current_stream(ctx.device)
     with no_grad():
-        next_target_q = target(next_obs)
-        selector = online(next_obs) if double else next_target_q
+        with ctx.side(1):
+            next_target_q = target(next_obs)
+            next_target_q.data.record_stream(main)
+        if double:
+            with ctx.side(2):
+                selector = online(next_obs)
+                selector.data.record_stream(main)
+        else:
+            selector = next_target_q
+    obs = obs_to_rows(inputs["obs"])
+    q = online(obs)
+    ctx.join()
     loss, mean_q, td_abs = dqn_td_huber(
         q, selector, next_target_q, inputs["actions_onehot"], inputs["rewards"],
         inputs["dones"], inputs["discounts"], delta=huber_delta,

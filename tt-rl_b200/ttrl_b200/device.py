@@ -14,6 +14,7 @@ that lives as long as the context.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from dataclasses import dataclass
 
@@ -22,7 +23,10 @@ import torch
 from ttrl_b200 import _lib
 from ttrl_b200._lib import check, lib
 
-__all__ = ["DeviceContext", "context", "conv_geom", "PRECISION"]
+__all__ = ["DeviceContext", "context", "conv_geom", "PRECISION", "SIDE_LANES"]
+
+#: Side streams a context keeps (lanes 1..SIDE_LANES).
+SIDE_LANES = 2
 
 #: Precision of every tensor-core contraction. Split-TF32 reproduces fp32
 #: products to ~1e-6 relative, which is what lets gradients match the
@@ -125,12 +129,23 @@ class DeviceContext:
         with torch.cuda.device(self.device):
             check(lib().ttrl_init(self.index), "ttrl_init")
             self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
-        self._ws = None
-        self._ws_bytes = 0
+        # Launch lanes: lane 0 is the caller's current stream, lanes 1.. are
+        # side streams that run independent work concurrently (inside a
+        # captured graph they become parallel branches). Each lane has its own
+        # workspace, so concurrent GEMMs never share split-K scratch.
+        self._lane = 0
+        self._ws: dict = {}
+        self._ws_bytes: dict = {}
         self._retired: list = []
+        self._streams: dict = {}
+        self._joins: set = set()
+        # Weight-gradient GEMMs of leaf parameters run on side lane 1 during
+        # backward, beside the data-gradient chain.
+        self.concurrent = True
         # When a list, every GEMM-family call appends (name, flops, start, end).
         self.profile = None
-        self.reserve(64 << 20)
+        for lane in range(SIDE_LANES + 1):
+            self.reserve(64 << 20, lane=lane)
 
     def _timed(self, name: str, flops: int = 0):
         if self.profile is None or torch.cuda.is_current_stream_capturing():
@@ -139,31 +154,75 @@ class DeviceContext:
 
     # -- workspace -------------------------------------------------------
 
-    def reserve(self, nbytes: int) -> None:
-        """Make the shared workspace at least `nbytes` long. Never shrinks,
-        never frees a buffer a graph may have recorded."""
-        if nbytes <= self._ws_bytes:
+    def reserve(self, nbytes: int, lane: int | None = None) -> None:
+        """Make a lane's workspace at least `nbytes` long. Never shrinks, never
+        frees a buffer a graph may have recorded."""
+        lane = self._lane if lane is None else lane
+        have = self._ws_bytes.get(lane, 0)
+        if nbytes <= have:
             return
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError(
                 f"ttrl_b200: a kernel needs {nbytes} bytes of workspace but only "
-                f"{self._ws_bytes} are reserved, and the stream is being captured, "
+                f"{have} are reserved, and the stream is being captured, "
                 "where allocating would invalidate the graph. Run the step once "
                 "eagerly before capture so the workspace is sized first."
             )
-        size = max(nbytes, 2 * self._ws_bytes)
+        size = max(nbytes, 2 * have)
         size = (size + (1 << 20) - 1) & ~((1 << 20) - 1)
         # zeroed: its first 64 KB hold split-K tile counters the kernels
         # expect at zero (and always leave at zero)
         buf = torch.zeros(size, dtype=torch.uint8, device=self.device)
-        if self._ws is not None:
-            self._retired.append(self._ws)
-        self._ws = buf
-        self._ws_bytes = size
+        if lane in self._ws:
+            self._retired.append(self._ws[lane])
+        self._ws[lane] = buf
+        self._ws_bytes[lane] = size
 
     def workspace(self, nbytes: int = 0):
         self.reserve(nbytes)
-        return self._ws.data_ptr(), self._ws_bytes
+        return self._ws[self._lane].data_ptr(), self._ws_bytes[self._lane]
+
+    # -- lanes -----------------------------------------------------------
+
+    def _side_stream(self, lane: int):
+        if not 1 <= lane <= SIDE_LANES:
+            raise ValueError(f"side lane must be in [1, {SIDE_LANES}], got {lane}")
+        s = self._streams.get(lane)
+        if s is None:
+            s = self._streams[lane] = torch.cuda.Stream(self.device)
+        return s
+
+    @contextlib.contextmanager
+    def side(self, lane: int = 1):
+        """Issue the enclosed launches on side lane `lane`: a stream ordered
+        after everything issued so far on the current stream, with its own
+        workspace. `join()` orders the current stream after it again. Tensors
+        the side work reads or writes that may be freed before `join()` must
+        be `record_stream`-ed to the yielded stream by the caller."""
+        main = torch.cuda.current_stream(self.device)
+        s = self._side_stream(lane)
+        fork = torch.cuda.Event()
+        fork.record(main)
+        s.wait_event(fork)
+        prev = self._lane
+        self._lane = lane
+        try:
+            with torch.cuda.stream(s):
+                yield s
+        finally:
+            self._lane = prev
+            self._joins.add(lane)
+
+    def join(self) -> None:
+        """Order the current stream after all side-lane work issued so far."""
+        if not self._joins:
+            return
+        main = torch.cuda.current_stream(self.device)
+        for lane in sorted(self._joins):
+            done = torch.cuda.Event()
+            done.record(self._streams[lane])
+            main.wait_event(done)
+        self._joins.clear()
 
     @property
     def stream(self) -> int:

@@ -150,6 +150,8 @@ class Tensor:
         if tuple(grad.shape) != tuple(self.data.shape):
             grad = grad.reshape(self.data.shape)
         ctx = context(self.data.device)
+        if self._op == "" and self.grad is not None:
+            ctx.join()  # a parameter's gradient may still be written on a side lane
         if self._premask and not premasked:
             masked = torch.empty_like(grad)
             ctx.ew("relu_bw", grad, self.data, masked)
@@ -259,6 +261,9 @@ class Tensor:
                     node._backward(grad)
         finally:
             _BACKWARD_ROOT = prev_root
+            # Weight gradients issued on side lanes are complete before
+            # anything after backward() runs on the current stream.
+            context(self.data.device).join()
             for node in topo:
                 if node._op:
                     node._backward_done = True

@@ -44,6 +44,21 @@ def _new(shape, like):
     return torch.empty(shape, dtype=torch.float32, device=like.device)
 
 
+def _weight_grad(ctx, receivers, tensors, launch) -> None:
+    """Run a weight-gradient launch on side lane 1, beside the data-gradient
+    chain, when every gradient it writes belongs to a leaf parameter (read
+    only after backward() joins the lanes); otherwise on the current stream.
+    `tensors` are the buffers it touches, kept from reuse until it is done."""
+    if ctx.concurrent and all(t._op == "" for t in receivers):
+        with ctx.side(1) as s:
+            for t in tensors:
+                if t is not None:
+                    t.record_stream(s)
+            launch()
+    else:
+        launch()
+
+
 def _ew(op, a, b=None, scalar=0.0, shape=None):
     """Run one elementwise kernel; a/b are torch tensors (broadcastable)."""
     if shape is None:
@@ -439,10 +454,8 @@ def linear(x: Tensor, w: Tensor, b: Tensor | None, *, relu: bool = False,
 
     def _backward(grad):
         g = grad if grad.is_contiguous() else grad.contiguous()
-        if x.requires_grad:
-            buf, acc = x._grad_slot()
-            ctx.linear_dgrad(g, w.data, xd if x._premask else None, buf, acc)
-            x._set_grad(buf)
+        # The weight gradient is issued first so that, on a side lane, it
+        # starts while the data gradient runs.
         wb = w.requires_grad
         bb = b is not None and b.requires_grad
         if wb or bb:
@@ -454,11 +467,17 @@ def linear(x: Tensor, w: Tensor, b: Tensor | None, *, relu: bool = False,
                 db, accb = b._grad_slot()
             else:
                 db, accb = None, False
-            ctx.linear_wgrad(xd, g, dw, db, accw, accb)
+            receivers = [t for t, want in ((w, wb), (b, bb)) if want]
+            _weight_grad(ctx, receivers, (xd, g, dw, db),
+                         lambda: ctx.linear_wgrad(xd, g, dw, db, accw, accb))
             if wb:
                 w._set_grad(dw)
             if bb:
                 b._set_grad(db)
+        if x.requires_grad:
+            buf, acc = x._grad_slot()
+            ctx.linear_dgrad(g, w.data, xd if x._premask else None, buf, acc)
+            x._set_grad(buf)
 
     out._backward = _backward
     return out
@@ -493,6 +512,25 @@ def conv2d_nhwc(x: Tensor, w: Tensor, b: Tensor | None, geom, *, input_scale: fl
         g = grad.reshape(rows, geom.cout)
         if not g.is_contiguous():
             g = g.contiguous()
+        wb = w.requires_grad
+        bb = b is not None and b.requires_grad
+        if wb or bb:
+            if wb:
+                dw, accw = w._grad_slot()
+            else:
+                dw, accw = torch.empty_like(w.data), False
+            if bb:
+                db, accb = b._grad_slot()
+            else:
+                db, accb = None, False
+            receivers = [t for t, want in ((w, wb), (b, bb)) if want]
+            _weight_grad(ctx, receivers, (xd, g, dw, db),
+                         lambda: ctx.conv_wgrad(xd, g, dw, None if db is None else db.reshape(-1),
+                                                geom, input_scale, accw, accb))
+            if wb:
+                w._set_grad(dw)
+            if bb:
+                b._set_grad(db)
         if x.requires_grad:
             if not needs_input_grad:
                 raise RuntimeError(
@@ -505,23 +543,6 @@ def conv2d_nhwc(x: Tensor, w: Tensor, b: Tensor | None, geom, *, input_scale: fl
             ctx.conv_dgrad(g, w.data, xd if x._premask else None, buf.reshape(-1, geom.c), geom,
                            acc)
             x._set_grad(buf)
-        wb = w.requires_grad
-        bb = b is not None and b.requires_grad
-        if wb or bb:
-            if wb:
-                dw, accw = w._grad_slot()
-            else:
-                dw, accw = torch.empty_like(w.data), False
-            if bb:
-                db, accb = b._grad_slot()
-            else:
-                db, accb = None, False
-            ctx.conv_wgrad(xd, g, dw, None if db is None else db.reshape(-1), geom, input_scale,
-                           accw, accb)
-            if wb:
-                w._set_grad(dw)
-            if bb:
-                b._set_grad(db)
 
     out._backward = _backward
     return out
