@@ -99,19 +99,27 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
     V[u] = load4(T.v, i, end, vec);
   }
 
-  const int step = a.steps[T.step_index] + 1;
-  const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
-  const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
-  const double c = sqrt((1.0 - a.b2) / bc2);
-  const double lr = a.lr_device ? *a.lr_device : a.lr;
-  AdamScalars k;
-  k.alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
-  k.eps_t = static_cast<float>(a.eps / c);
-  k.b1 = static_cast<float>(a.b1);
-  k.b2 = static_cast<float>(a.b2);
-  k.wd = static_cast<float>(a.wd);
-  k.scaled = a.grad_scale != nullptr;
-  k.gs = k.scaled ? *a.grad_scale : 1.f;
+  // The bias-correction scalars depend only on the tensor's step: one thread
+  // computes them (double precision) while the block's loads are in flight.
+  __shared__ AdamScalars ks;
+  if (threadIdx.x == 0) {
+    const int step = a.steps[T.step_index] + 1;
+    const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
+    const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
+    const double c = sqrt((1.0 - a.b2) / bc2);
+    const double lr = a.lr_device ? *a.lr_device : a.lr;
+    AdamScalars k;
+    k.alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
+    k.eps_t = static_cast<float>(a.eps / c);
+    k.b1 = static_cast<float>(a.b1);
+    k.b2 = static_cast<float>(a.b2);
+    k.wd = static_cast<float>(a.wd);
+    k.scaled = a.grad_scale != nullptr;
+    k.gs = k.scaled ? *a.grad_scale : 1.f;
+    ks = k;
+  }
+  __syncthreads();
+  const AdamScalars k = ks;
 
 #pragma unroll
   for (int u = 0; u < kAdamQuads; ++u) {

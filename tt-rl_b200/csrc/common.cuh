@@ -112,6 +112,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // ---------------------------------------------------------------- TMA
 
+// Fetch a tensor map (a kernel parameter) into the TMA unit's descriptor
+// cache ahead of its first use; it touches no global data.
+__device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
 // 2-D tiled TMA load of one box into shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y,
                                             uint32_t bar) {

@@ -571,6 +571,12 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
+  if (warp == kProducerWarp && lane == 0) {
+    // The descriptors are launch parameters, so their fetch can overlap the
+    // previous kernel's tail.
+    if (args.a_tma) prefetch_tensormap(&args.tma_a);
+    if (args.b_tma) prefetch_tensormap(&args.tma_b);
+  }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(empty0 + s * 8, 1);
@@ -1037,8 +1043,8 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
   bool global_split = false;
   if (splits <= 0) {
     // Aim for about one wave of 148 SMs with at least 4 k-blocks per CTA.
-    // Up to `cmax` splits reduce inside a cluster; beyond that (very long
-    // K, where each CTA would still walk >= 32 k-blocks) up to 32 splits
+    // Up to `cmax` splits reduce inside a cluster; beyond that (long K,
+    // where each CTA would still walk >= 16 k-blocks) up to 64 splits
     // reduce through global memory.
     splits = 1;
     if (s.tiles < 120 && s.kblocks >= 8) {
@@ -1048,7 +1054,7 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
       const int most = s.kblocks / 4;
       splits = want < most ? want : most;
       if (splits > cmax) {
-        if (s.kblocks / cmax >= 32) {
+        if (s.kblocks / cmax >= 16) {
           global_split = true;
           if (splits > 64) splits = 64;
         } else {
@@ -1100,6 +1106,92 @@ static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, int cluster_z, cud
   return e;
 }
 
+// ---------------------------------------------------- small dense GEMMs
+//
+// Products of at most kSimtMacs multiply-adds between two dense operands
+// (network heads with a handful of outputs, their gradients, narrow MLP
+// layers) run on the CUDA cores: one warp per output element when the
+// reduction is long (lanes take every 32nd k, then a fixed shuffle tree), one
+// thread per output element when it is short. At these sizes a 128-row
+// tensor-core tile is mostly padding and a launch is bound by the tcgen05
+// pipeline's fixed latency (TMA load, MMA, commit, TMEM read-back), not by
+// math. Only when the caller lets the library choose the schedule
+// (desc.splits == 0). fp32 fused multiply-adds in a fixed order: results are
+// deterministic and at least as accurate as split-TF32.
+constexpr long long kSimtMacs = 1ll << 20;
+constexpr int kSimtWarpK = 64;  // reductions at least this long get a warp per output
+
+struct SimtArgs {
+  DevOperand a, b;
+  ttrl_epilogue ep;
+  EpiExtra ex;
+  int32_t m, n, k;
+  int32_t warp_per_output;
+  int32_t c_fast;  // consecutive threads take consecutive columns (else rows)
+};
+
+__device__ __forceinline__ float simt_a(const DevOperand& o, int r, int k) {
+  if (o.ones_row && r == o.rows) return 1.f;
+  return o.ptr[static_cast<long long>(r) * o.rs + static_cast<long long>(k) * o.ks];
+}
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ SimtArgs p) {
+  pdl_trigger();
+  pdl_wait();
+  const DevOperand a = p.a, b = p.b;
+  const long long outs = static_cast<long long>(p.m) * p.n;
+  const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  long long o;
+  int lane = 0;
+  if (p.warp_per_output) {
+    o = gid >> 5;
+    lane = threadIdx.x & 31;
+  } else {
+    o = gid;
+  }
+  if (o >= outs) return;  // uniform across a warp when it owns one output
+  const int r = p.c_fast ? static_cast<int>(o / p.n) : static_cast<int>(o % p.m);
+  const int c = p.c_fast ? static_cast<int>(o % p.n) : static_cast<int>(o / p.m);
+  float acc = 0.f;
+  if (p.warp_per_output) {
+    for (int k = lane; k < p.k; k += 32) acc = fmaf(simt_a(a, r, k), simt_a(b, c, k), acc);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane != 0) return;
+  } else {
+    for (int k = 0; k < p.k; ++k) acc = fmaf(simt_a(a, r, k), simt_a(b, c, k), acc);
+  }
+  const int rr[1] = {r};
+  const int cc[1] = {c};
+  const float v[1] = {acc};
+  epi_store_batch<1>(p.ep, p.ex, rr, cc, v, 1);
+}
+
+static bool simt_eligible(const ttrl_gemm_desc& d, int a_ones_row) {
+  return d.splits == 0 && d.a.kind == TTRL_OPND_DENSE && d.b.kind == TTRL_OPND_DENSE &&
+         static_cast<long long>(d.m) * d.n * d.k <= kSimtMacs && (a_ones_row == 0 || d.m >= 1);
+}
+
+static int simt_run(const ttrl_gemm_desc& d, const GemmArgs& g, cudaStream_t stream) {
+  SimtArgs p;
+  std::memset(&p, 0, sizeof(p));
+  p.a = g.a;
+  p.b = g.b;
+  p.ep = g.ep;
+  p.ex = g.ex;
+  p.m = d.m;
+  p.n = d.n;
+  p.k = d.k;
+  p.warp_per_output = d.k >= kSimtWarpK ? 1 : 0;
+  p.c_fast = d.ep.ocs <= d.ep.ors ? 1 : 0;
+  const long long threads = static_cast<long long>(d.m) * d.n * (p.warp_per_output ? 32 : 1);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  const cudaError_t le = launch_pdl(gemm_simt_kernel, dim3(blocks), dim3(256), 0, stream, p);
+  note_launch();
+  const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("gemm_simt launch", e);
+}
+
 int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* counters,
              float* partials, size_t partial_bytes, int* status, cudaStream_t stream) {
   if (d.m < 0 || d.n < 0 || d.k < 0) return set_error(TTRL_EINVAL, "gemm: negative extent");
@@ -1122,6 +1214,7 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   args.n = d.n;
   args.k = d.k;
   args.status = status;
+  if (simt_eligible(d, a_ones_row)) return simt_run(d, args, stream);
 
   const Schedule s = make_schedule(d);
   args.kblocks = s.kblocks;

@@ -13,6 +13,8 @@ it) or float rows already in the network's input layout.
 
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 import torch
 
@@ -78,12 +80,13 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
     # the captured graph), and the loss waits for all three.
     ctx = context(next_obs.data.device)
     main = torch.cuda.current_stream(ctx.device)
+    lane = ctx.side if ctx.concurrent else (lambda _k: contextlib.nullcontext())
     with no_grad():
-        with ctx.side(1):
+        with lane(1):
             next_target_q = target(next_obs)
             next_target_q.data.record_stream(main)
         if double:
-            with ctx.side(2):
+            with lane(2):
                 selector = online(next_obs)
                 selector.data.record_stream(main)
         else:

@@ -139,8 +139,9 @@ class DeviceContext:
         self._retired: list = []
         self._streams: dict = {}
         self._joins: set = set()
-        # Weight-gradient GEMMs of leaf parameters run on side lane 1 during
-        # backward, beside the data-gradient chain.
+        self._weight_lanes: dict = {}
+        # Weight-gradient GEMMs of leaf parameters run on the side lanes
+        # during backward, beside the data-gradient chain.
         self.concurrent = True
         # When a list, every GEMM-family call appends (name, flops, start, end).
         self.profile = None
@@ -212,6 +213,16 @@ class DeviceContext:
         finally:
             self._lane = prev
             self._joins.add(lane)
+
+    def weight_lane(self, param) -> int:
+        """The side lane a parameter's weight gradients run on: lanes are
+        dealt round-robin in the order parameters are first seen, and a
+        parameter keeps its lane, so its gradient accumulates in order."""
+        key = param.data_ptr()
+        lane = self._weight_lanes.get(key)
+        if lane is None:
+            lane = self._weight_lanes[key] = 1 + len(self._weight_lanes) % SIDE_LANES
+        return lane
 
     def join(self) -> None:
         """Order the current stream after all side-lane work issued so far."""

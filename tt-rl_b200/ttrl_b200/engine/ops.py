@@ -45,12 +45,13 @@ def _new(shape, like):
 
 
 def _weight_grad(ctx, receivers, tensors, launch) -> None:
-    """Run a weight-gradient launch on side lane 1, beside the data-gradient
+    """Run a weight-gradient launch on a side lane, beside the data-gradient
     chain, when every gradient it writes belongs to a leaf parameter (read
     only after backward() joins the lanes); otherwise on the current stream.
+    Each parameter keeps one lane, so its gradient accumulates in order.
     `tensors` are the buffers it touches, kept from reuse until it is done."""
     if ctx.concurrent and all(t._op == "" for t in receivers):
-        with ctx.side(1) as s:
+        with ctx.side(ctx.weight_lane(receivers[0].data)) as s:
             for t in tensors:
                 if t is not None:
                     t.record_stream(s)
