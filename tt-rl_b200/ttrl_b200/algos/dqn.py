@@ -104,7 +104,10 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
     metrics = {"loss": loss, "mean_q": mean_q}
     if prioritized:
         metrics["td_abs"] = td_abs
-    grad_sq = grad_sq_device(online.parameters())
+    # The gradient norm is a metric only: on side lane 2 it runs beside the
+    # optimizer step that follows.
+    with lane(2):
+        grad_sq = grad_sq_device(online.parameters())
     if grad_sq is not None:
         metrics["grad_sq"] = Tensor(grad_sq.reshape(1, 1), requires_grad=False)
     return metrics

@@ -33,7 +33,7 @@ def _sqnorm(params, max_norm: float):
     ctx = context(dev)
     numels = [g.numel() for g in grads]
     need = ctx.sqnorm_workspace_bytes(numels)
-    key = (str(dev), need)
+    key = (str(dev), need, ctx._lane)  # one per launch lane: lanes may run at once
     ws = _WS.get(key)
     if ws is None:
         if torch.cuda.is_current_stream_capturing():

@@ -121,6 +121,8 @@ class Tensor:
         return Tensor(t, requires_grad)
 
     def numpy(self) -> np.ndarray:
+        if self.data.is_cuda:
+            context(self.data.device).join()  # written on a side lane, perhaps
         out = self.data.detach().to("cpu").numpy()
         return out.astype(np.float32) if out.dtype != np.float32 and out.dtype.kind == "f" else out
 

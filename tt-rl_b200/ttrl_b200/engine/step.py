@@ -16,6 +16,8 @@ arithmetic and the order of operations are unchanged.
 
 from __future__ import annotations
 
+import contextlib
+
 from typing import Callable
 
 import numpy as np
@@ -107,17 +109,23 @@ class MetricPack:
         self.buffer = None
         if self.scalar_keys:
             dev = self.sources[self.scalar_keys[0]].data.device
-            self.buffer = torch.empty(len(self.scalar_keys), dtype=torch.float32, device=dev)
             ctx = context(dev)
-            for i, k in enumerate(self.scalar_keys):
-                src = self.sources[k].data.reshape(1)
-                if src.dtype != torch.float32:
-                    src = src.float()
-                ctx.copy_strided(self.buffer[i:i + 1], src)
+            # On side lane 2 (when lanes are on), beside the optimizer step
+            # that follows on the current stream; the caller joins.
+            lane = ctx.side(2) if ctx.concurrent else contextlib.nullcontext()
+            with lane:
+                self.buffer = torch.empty(len(self.scalar_keys), dtype=torch.float32,
+                                          device=dev)
+                for i, k in enumerate(self.scalar_keys):
+                    src = self.sources[k].data.reshape(1)
+                    if src.dtype != torch.float32:
+                        src = src.float()
+                    ctx.copy_strided(self.buffer[i:i + 1], src)
 
     def read(self) -> dict:
         out = dict(self.passthrough)
         if self.buffer is not None:
+            context(self.buffer.device).join()
             host = self.buffer.detach().to("cpu").numpy()
             for i, k in enumerate(self.scalar_keys):
                 out[k] = host[i:i + 1].reshape(self.sources[k].shape)
@@ -188,9 +196,13 @@ class TrainStep:
         if self.optimizer is not None:
             self.optimizer.zero_grad()
         metrics = self.step_fn(self.inputs)
+        # Packed before the optimizer step so that, on a side lane, the
+        # metric copies run beside it.
+        pack = MetricPack(metrics)
         if self.optimizer is not None:
             self.optimizer.step()
-        return MetricPack(metrics)
+        context(self.device).join()
+        return pack
 
     def _capture(self) -> None:
         # Warm-up pass: real launches (kernel loading, workspace sizing,

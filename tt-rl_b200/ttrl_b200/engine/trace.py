@@ -14,6 +14,7 @@ from typing import Callable, TypeVar
 
 import torch
 
+from ttrl_b200.device import context
 from ttrl_b200.engine.autograd import as_device
 from ttrl_b200.engine.config import DEFAULT, EngineConfig
 
@@ -79,6 +80,8 @@ def capture(device, record: Callable[[], R], *, pool=None) -> tuple[CapturedTrac
             torch.cuda.synchronize(dev)
             with torch.cuda.graph(graph, pool=pool, capture_error_mode="thread_local"):
                 result = record()
+                # Every side lane rejoins the capture stream before it ends.
+                context(dev).join()
     except BaseException as e:
         try:
             graph.reset()
