@@ -13,12 +13,14 @@
 
 namespace ttrl {
 
-// Each thread owns kAdamQuads float4 quads of one 4096-element chunk and
-// issues every load of them before its first store: one memory round trip
-// per thread instead of one per element.
+// A block walks chunks of kAdamChunk elements in a grid-stride loop over a
+// grid of at most kAdamBlocksPerSM blocks per SM (one wave). Each thread owns
+// kAdamQuads float4 quads of a chunk and issues every load of them before
+// its first store: one memory round trip per thread per chunk.
 constexpr int kAdamThreads = 256;
-constexpr int kAdamQuads = 4;
-constexpr int kAdamChunk = kAdamThreads * kAdamQuads * 4;  // elements per block
+constexpr int kAdamQuads = 2;
+constexpr int kAdamChunk = kAdamThreads * kAdamQuads * 4;  // elements per chunk
+constexpr int kAdamBlocksPerSM = 3;
 
 struct AdamArgs {
   ttrl_adam_tensor t[TTRL_ADAM_MAX_TENSORS];
@@ -75,39 +77,50 @@ __device__ __forceinline__ void adam_elem(const AdamScalars& k, float g, float& 
   p = __fsub_rn(p, d);
 }
 
-__global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constant__ AdamArgs a) {
+__device__ __forceinline__ int adam_tensor_of(const AdamArgs& a, long long chunk) {
+  int ti = 0;  // count <= 64: a linear scan is cheap
+  while (ti + 1 < a.count && a.chunk_start[ti + 1] <= chunk) ++ti;
+  return ti;
+}
+
+__global__ void __launch_bounds__(kAdamThreads, kAdamBlocksPerSM)
+    adam_kernel(const __grid_constant__ AdamArgs a) {
   pdl_trigger();
   pdl_wait();
-  // Locate this block's tensor (count <= 64: a linear scan is cheap).
-  const long long chunk = blockIdx.x;
-  int ti = 0;
-  while (ti + 1 < a.count && a.chunk_start[ti + 1] <= chunk) ++ti;
-  const ttrl_adam_tensor T = a.t[ti];  // a register copy, not a reference into the parameter block
-  const long long begin = (chunk - a.chunk_start[ti]) * kAdamChunk;
-  const long long end = begin + kAdamChunk < T.numel ? begin + kAdamChunk : T.numel;
-  const bool vec = (a.vec_mask >> ti) & 1ull;
-
-  // Operands first: their loads are in flight while the scalars below are
-  // computed from the step counter.
+  const long long total = a.chunk_start[a.count];
+  long long chunk = blockIdx.x;
   float4 g[kAdamQuads], p[kAdamQuads], S[kAdamQuads], V[kAdamQuads];
+  int ti = 0;
+  long long begin = 0, end = 0;
+  bool vec = false;
+  auto load = [&](long long c) {
+    ti = adam_tensor_of(a, c);
+    const ttrl_adam_tensor& T = a.t[ti];
+    begin = (c - a.chunk_start[ti]) * kAdamChunk;
+    end = begin + kAdamChunk < T.numel ? begin + kAdamChunk : T.numel;
+    vec = (a.vec_mask >> ti) & 1ull;
 #pragma unroll
-  for (int u = 0; u < kAdamQuads; ++u) {
-    const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
-    g[u] = load4(T.grad, i, end, vec);
-    p[u] = load4(T.param, i, end, vec);
-    S[u] = load4(T.s, i, end, vec);
-    V[u] = load4(T.v, i, end, vec);
-  }
+    for (int u = 0; u < kAdamQuads; ++u) {
+      const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+      g[u] = load4(T.grad, i, end, vec);
+      p[u] = load4(T.param, i, end, vec);
+      S[u] = load4(T.s, i, end, vec);
+      V[u] = load4(T.v, i, end, vec);
+    }
+  };
+  if (chunk < total) load(chunk);
 
-  // The bias-correction scalars depend only on the tensor's step: one thread
-  // computes them (double precision) while the block's loads are in flight.
-  __shared__ AdamScalars ks;
-  if (threadIdx.x == 0) {
-    const int step = a.steps[T.step_index] + 1;
+  // The bias-correction scalars depend only on a tensor's step: one thread
+  // per tensor computes them (double precision) while the first loads are
+  // in flight.
+  __shared__ AdamScalars ks[TTRL_ADAM_MAX_TENSORS];
+  const double lr = a.lr_device ? *a.lr_device : a.lr;
+  const float gs = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
+  for (int q = threadIdx.x; q < a.count; q += blockDim.x) {
+    const int step = a.steps[a.t[q].step_index] + 1;
     const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
     const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
     const double c = sqrt((1.0 - a.b2) / bc2);
-    const double lr = a.lr_device ? *a.lr_device : a.lr;
     AdamScalars k;
     k.alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
     k.eps_t = static_cast<float>(a.eps / c);
@@ -115,23 +128,28 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const __grid_constan
     k.b2 = static_cast<float>(a.b2);
     k.wd = static_cast<float>(a.wd);
     k.scaled = a.grad_scale != nullptr;
-    k.gs = k.scaled ? *a.grad_scale : 1.f;
-    ks = k;
+    k.gs = gs;
+    ks[q] = k;
   }
   __syncthreads();
-  const AdamScalars k = ks;
 
+  while (chunk < total) {
+    const AdamScalars k = ks[ti];
+    const ttrl_adam_tensor& T = a.t[ti];
 #pragma unroll
-  for (int u = 0; u < kAdamQuads; ++u) {
-    const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
-    if (i >= end) continue;
-    adam_elem(k, g[u].x, p[u].x, S[u].x, V[u].x);
-    adam_elem(k, g[u].y, p[u].y, S[u].y, V[u].y);
-    adam_elem(k, g[u].z, p[u].z, S[u].z, V[u].z);
-    adam_elem(k, g[u].w, p[u].w, S[u].w, V[u].w);
-    store4(T.v, i, end, vec, V[u]);
-    store4(T.s, i, end, vec, S[u]);
-    store4(T.param, i, end, vec, p[u]);
+    for (int u = 0; u < kAdamQuads; ++u) {
+      const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+      if (i >= end) continue;
+      adam_elem(k, g[u].x, p[u].x, S[u].x, V[u].x);
+      adam_elem(k, g[u].y, p[u].y, S[u].y, V[u].y);
+      adam_elem(k, g[u].z, p[u].z, S[u].z, V[u].z);
+      adam_elem(k, g[u].w, p[u].w, S[u].w, V[u].w);
+      store4(T.v, i, end, vec, V[u]);
+      store4(T.s, i, end, vec, S[u]);
+      store4(T.param, i, end, vec, p[u]);
+    }
+    chunk += gridDim.x;
+    if (chunk < total) load(chunk);
   }
 
   // The last block to finish advances every step counter of this launch,
@@ -187,7 +205,9 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
   a.b2 = b2;
   a.eps = eps;
   a.wd = wd;
-  const cudaError_t le_ = launch_pdl(adam_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kAdamThreads), 0, st, a);
+  const long long wave = 148LL * kAdamBlocksPerSM;
+  const unsigned blocks = static_cast<unsigned>(chunks < wave ? chunks : wave);
+  const cudaError_t le_ = launch_pdl(adam_kernel, dim3(blocks), dim3(kAdamThreads), 0, st, a);
   note_launch();
   cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("adam launch", e);
