@@ -1033,6 +1033,13 @@ static int max_cluster_for_current_device() {
   return g_max_cluster[dev] > 0 ? g_max_cluster[dev] : 8;
 }
 
+// Non-cluster GEMMs whose CTAs each walk at most this many k-blocks use the
+// half-footprint variant.
+#ifndef TTRL_SMALL_MAX_KBLOCKS
+#define TTRL_SMALL_MAX_KBLOCKS 8
+#endif
+constexpr int kSmallMaxKBlocks = TTRL_SMALL_MAX_KBLOCKS;
+
 static Schedule make_schedule(const ttrl_gemm_desc& d) {
   Schedule s;
   s.bn = pick_bn(d.n);
@@ -1240,8 +1247,11 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   dim3 grid((d.m + 127) / 128, (d.n + s.bn - 1) / s.bn, s.splits);
   const bool split3 = d.precision == TTRL_PREC_TF32X3;
   const int cz = s.cluster ? s.splits : 1;
-  // Several waves of CTAs: the half-size variant runs two CTAs per SM.
-  const bool small = !s.cluster && static_cast<long long>(s.tiles) * s.splits > 148;
+  // Several waves of CTAs, or a short walk along K (where a deep ring buys
+  // little): the half-size variant runs two CTAs per SM, which also lets
+  // GEMMs on concurrent launch lanes share SMs.
+  const bool small = !s.cluster && (static_cast<long long>(s.tiles) * s.splits > 148 ||
+                                    s.kb_per_split <= kSmallMaxKBlocks);
   cudaError_t e;
 #define TTRL_LAUNCH(BNV)                                                              \
   (split3 ? (small ? launch_bn<BNV, true, true>(args, grid, cz, stream)                \
