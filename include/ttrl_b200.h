@@ -230,6 +230,18 @@ size_t ttrl_conv_wgrad_workspace_bytes(const ttrl_conv_geom* g);
 int ttrl_u8_nchw_to_f32_nhwc(const uint8_t* in, const int32_t* index, float* out, int n, int c,
                              int h, int w, float scale, ttrl_stream_t stream);
 
+/* The same frames converted straight into space-to-depth rows for a first
+ * convolution whose stride `fold` divides its kernel and the frame size:
+ * out[(img, Y, X)][(dy*fold + dx)*c + ch] = in[index ? index[img] : img][ch]
+ *   [Y*fold + dy][X*fold + dx] * scale, rows [n*(h/fold)*(w/fold)][fold*fold*c].
+ * That convolution is then a stride-1 convolution with kernel k/fold over
+ * fold*fold*c channels: the same products, whose operand gathers read
+ * contiguous channel runs. Plays the part of ttrl/nets/obs.py:73-75 and the
+ * reference's space-to-depth fold (ttrl/engine/conv/packing.py) for the
+ * Nature-CNN's first layer. */
+int ttrl_u8_nchw_to_f32_s2d(const uint8_t* in, const int32_t* index, float* out, int n, int c,
+                            int h, int w, int fold, float scale, ttrl_stream_t stream);
+
 /* ------------------------------------------------------------------ Adam */
 
 /* One parameter tensor of a multi-tensor Adam launch. */

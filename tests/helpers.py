@@ -75,3 +75,32 @@ def device_gates(net, rows_tensor):
         gates["feat"] = feat.numpy() > 0
     torch.cuda.synchronize()
     return gates
+
+
+def grads_in_state_layout(net):
+    """{parameter name: its gradient in the state_dict layout}: conv weights
+    converted from the device's (possibly space-to-depth) KRSC to OIHW."""
+    from ttrl_b200.engine.conv import Conv2d
+    from ttrl_b200.engine.nn import Module
+    convs = {}
+    stack = [net]
+    seen = set()
+    while stack:
+        v = stack.pop()
+        if id(v) in seen:
+            continue
+        seen.add(id(v))
+        if isinstance(v, Conv2d):
+            convs[id(v.weight)] = v
+        if isinstance(v, Module):
+            stack.extend(val for _, val in v._slot_sources())
+        elif isinstance(v, dict):
+            stack.extend(v.values())
+        elif isinstance(v, (list, tuple)):
+            stack.extend(v)
+    out = {}
+    for name, p in net.named_parameters():
+        g = p.grad.detach().cpu().numpy()
+        conv = convs.get(id(p))
+        out[name] = conv._from_device_layout(g) if conv is not None else g
+    return out

@@ -13,7 +13,8 @@ import pytest
 torch = pytest.importorskip("torch")
 
 from oracle import learner as ref  # noqa: E402
-from tests.helpers import (TOL_GRAD, TOL_PARAM, dqn_batch, nature_state_dict,  # noqa: E402
+from tests.helpers import (TOL_GRAD, TOL_PARAM, dqn_batch, grads_in_state_layout,
+                           nature_state_dict,  # noqa: E402
                            nchw_to_nhwc, rel)
 
 pytestmark = pytest.mark.gpu
@@ -80,13 +81,9 @@ def test_dqn_update_matches_oracle_eager():
     assert abs(float(metrics["mean_q"].reshape(-1)[0]) - m["mean_q"]) <= 1e-6
     assert rel(metrics["grad_sq"], m["grad_sq"]) <= 1e-4
     named_g = nature_state_dict(grads)
-    for name, p in online.named_parameters():
-        g = p.grad.detach().cpu().numpy()
+    for name, g in grads_in_state_layout(online).items():
         want = named_g[name]
-        if name.endswith("weight") and g.ndim == 4:  # KRSC on device -> OIHW
-            g = g.transpose(0, 3, 1, 2)
-        g = g.reshape(want.shape)
-        assert rel(g, want) <= TOL_GRAD, name
+        assert rel(g.reshape(want.shape), want) <= TOL_GRAD, name
     sd = online.state_dict()
     want_p = nature_state_dict(new_p)
     for name in sd:

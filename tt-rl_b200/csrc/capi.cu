@@ -42,6 +42,8 @@ int conv_wgrad(const float*, const float*, float*, float*, const ttrl_conv_geom*
 size_t conv_wgrad_ws(const ttrl_conv_geom*);
 size_t linear_wgrad_ws(int, int, int);
 int u8_to_f32(const uint8_t*, const int32_t*, float*, int, int, int, int, float, cudaStream_t);
+int u8_to_f32_s2d(const uint8_t*, const int32_t*, float*, int, int, int, int, int, float,
+                  cudaStream_t);
 int adam_step(const ttrl_adam_tensor*, int, int32_t*, int32_t*, const float*, const double*,
               double, double, double, double, double, cudaStream_t);
 int grad_sqnorm(const float* const*, const int64_t*, int, float*, float, void*, size_t,
@@ -148,6 +150,11 @@ size_t ttrl_conv_wgrad_workspace_bytes(const ttrl_conv_geom* g) {
 int ttrl_u8_nchw_to_f32_nhwc(const uint8_t* in, const int32_t* index, float* out, int n, int c,
                              int h, int w, float scale, ttrl_stream_t stream) {
   return u8_to_f32(in, index, out, n, c, h, w, scale, TTRL_STREAM(stream));
+}
+
+int ttrl_u8_nchw_to_f32_s2d(const uint8_t* in, const int32_t* index, float* out, int n, int c,
+                            int h, int w, int fold, float scale, ttrl_stream_t stream) {
+  return u8_to_f32_s2d(in, index, out, n, c, h, w, fold, scale, TTRL_STREAM(stream));
 }
 
 int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,

@@ -433,4 +433,85 @@ int u8_to_f32(const uint8_t* in, const int32_t* index, float* out, int n, int c,
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("u8_to_f32 launch", e);
 }
 
+// Frames to space-to-depth rows: out[(img, Y, X)][(dy * f + dx) * c + ch] =
+// in[src][ch][Y * f + dy][X * f + dx] * scale, the input layout of a
+// stride-f convolution whose kernel f divides, rewritten as a stride-1
+// convolution over f*f*c channels (the same products, in another order).
+// One thread per (img, Y, dy, X) when c == 4 and f == 4: four 4-byte loads
+// (one per channel) and four float4 stores.
+__global__ void u8_nchw_to_f32_s2d_kernel(const uint8_t* __restrict__ in,
+                                          const int32_t* __restrict__ index,
+                                          float* __restrict__ out, int n, int c, int h, int w,
+                                          int f, float scale) {
+  pdl_trigger();
+  pdl_wait();
+  const int hf = h / f, wf = w / f, hw = h * w;
+  const int cc = f * f * c;
+  if (c == 4 && f == 4) {
+    const long long items = static_cast<long long>(n) * hf * f * wf;
+    for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < items;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const int X = static_cast<int>(t % wf);
+      long long r = t / wf;
+      const int dy = static_cast<int>(r % f);
+      r /= f;
+      const int Y = static_cast<int>(r % hf);
+      const int img = static_cast<int>(r / hf);
+      const int src = index ? index[img] : img;
+      const uint8_t* base = in + static_cast<long long>(src) * c * hw +
+                            static_cast<long long>(Y * f + dy) * w + X * f;
+      uchar4 px[4];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch)
+        px[ch] = *reinterpret_cast<const uchar4*>(base + static_cast<long long>(ch) * hw);
+      float* o = out + ((static_cast<long long>(img) * hf + Y) * wf + X) * cc + dy * f * c;
+      const float4 v0 = make_float4(px[0].x * scale, px[1].x * scale, px[2].x * scale, px[3].x * scale);
+      const float4 v1 = make_float4(px[0].y * scale, px[1].y * scale, px[2].y * scale, px[3].y * scale);
+      const float4 v2 = make_float4(px[0].z * scale, px[1].z * scale, px[2].z * scale, px[3].z * scale);
+      const float4 v3 = make_float4(px[0].w * scale, px[1].w * scale, px[2].w * scale, px[3].w * scale);
+      reinterpret_cast<float4*>(o)[0] = v0;
+      reinterpret_cast<float4*>(o)[1] = v1;
+      reinterpret_cast<float4*>(o)[2] = v2;
+      reinterpret_cast<float4*>(o)[3] = v3;
+    }
+    return;
+  }
+  const long long total = static_cast<long long>(n) * hf * wf * cc;
+  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(t % cc);
+    const long long pix = t / cc;
+    const int X = static_cast<int>(pix % wf);
+    const long long r = pix / wf;
+    const int Y = static_cast<int>(r % hf);
+    const int img = static_cast<int>(r / hf);
+    const int ch = k % c, dd = k / c, dx = dd % f, dy = dd / f;
+    const int src = index ? index[img] : img;
+    out[t] = in[static_cast<long long>(src) * c * hw + static_cast<long long>(ch) * hw +
+                static_cast<long long>(Y * f + dy) * w + X * f + dx] * scale;
+  }
+}
+
+int u8_to_f32_s2d(const uint8_t* in, const int32_t* index, float* out, int n, int c, int h, int w,
+                  int f, float scale, cudaStream_t st) {
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0 || f <= 0)
+    return set_error(TTRL_EINVAL, "u8_to_f32_s2d: bad extents");
+  if (h % f || w % f) return set_error(TTRL_EINVAL, "u8_to_f32_s2d: fold %d must divide %dx%d", f, h, w);
+  if (in == nullptr || out == nullptr) return set_error(TTRL_EINVAL, "u8_to_f32_s2d: null pointer");
+  const bool fast = c == 4 && f == 4;
+  if (fast && ((reinterpret_cast<uintptr_t>(out) & 15u) || (reinterpret_cast<uintptr_t>(in) & 3u) ||
+               (w & 3) || ((h * w) & 3)))
+    return set_error(TTRL_EINVAL, "u8_to_f32_s2d: unaligned frames or output");
+  const long long values = static_cast<long long>(n) * h * w * c;
+  if (values >= (1ll << 31)) return set_error(TTRL_EUNSUPPORTED, "u8_to_f32_s2d: more than 2^31 values");
+  const long long items = fast ? values / 16 : values;
+  int blocks = static_cast<int>((items + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  const cudaError_t le_ = launch_pdl(u8_nchw_to_f32_s2d_kernel, dim3(blocks), dim3(256), 0, st, in,
+                                     index, out, n, c, h, w, f, scale);
+  note_launch();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("u8_to_f32_s2d launch", e);
+}
+
 }  // namespace ttrl

@@ -21,6 +21,7 @@ import torch
 from ttrl_b200.algos.grads import grad_sq_device
 from ttrl_b200.device import context
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
+from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import dqn_td_huber
 
 __all__ = ["step_inputs", "update_loss", "obs_to_rows"]
@@ -56,16 +57,21 @@ def step_inputs(obs_shape, device, *, batch: int, num_actions: int, mask_n: int 
     return inputs
 
 
-def obs_to_rows(obs: Tensor) -> Tensor:
+def obs_to_rows(obs: Tensor, fold: int = 1) -> Tensor:
     """uint8 [B, C, H, W] frames -> fp32 NHWC rows [1, 1, B*H*W, C] (raw 0..255;
-    the 1/255 is conv1's input scale). Float inputs pass through."""
+    the 1/255 is conv1's input scale), in the space-to-depth order of `fold`
+    when the first convolution reads that (`input_fold(net)`). Float inputs
+    pass through."""
     if obs.data.dtype != torch.uint8:
         return obs
     b, c, h, w = obs.shape
-    out = torch.empty((1, 1, b * h * w, c), dtype=torch.float32, device=obs.data.device)
-    context(obs.data.device).u8_to_f32(obs.data, None, out.reshape(-1, c), 1.0)
+    out = torch.empty((1, 1, b * h * w // (fold * fold), c * fold * fold), dtype=torch.float32,
+                      device=obs.data.device)
+    context(obs.data.device).u8_to_f32(obs.data, None, out.reshape(-1, c * fold * fold), 1.0,
+                                       fold=fold)
     rows = Tensor(out, requires_grad=False)
     rows._exact = True  # raw 0..255 values
+    rows._fold = fold
     return rows
 
 
@@ -74,7 +80,8 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
                 leaves=None) -> dict:
     """One DQN update: Huber loss against the (double-)DQN n-step target,
     backward, and device metrics (ttrl/algos/dqn/losses.py:77-140)."""
-    next_obs = obs_to_rows(inputs["next_obs"])
+    fold = input_fold(online)
+    next_obs = obs_to_rows(inputs["next_obs"], fold)
     # The two no-grad forwards on s' are independent of the online forward on
     # s: they run on side lanes, concurrently with it (parallel branches of
     # the captured graph), and the loss waits for all three.
@@ -91,7 +98,7 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
                 selector.data.record_stream(main)
         else:
             selector = next_target_q
-    obs = obs_to_rows(inputs["obs"])
+    obs = obs_to_rows(inputs["obs"], fold)
     q = online(obs)
     ctx.join()
     loss, mean_q, td_abs = dqn_td_huber(

@@ -24,6 +24,7 @@ import torch
 from ttrl_b200.algos.grads import clip_grad_norm_device
 from ttrl_b200.device import context
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
+from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import ppo_objective
 from ttrl_b200.engine.optim import Adam
 from ttrl_b200.engine.trace import capture
@@ -170,7 +171,12 @@ class PPOLearner(ReplayedUpdate):
         self.perm_host = torch.zeros((self.steps_per_update, mb), dtype=torch.int32,
                                      pin_memory=True)
         # Minibatch staging (gathered per step on the device).
-        self.mb_rows = torch.empty((1, 1, mb * h * w, c), dtype=torch.float32, device=dev)
+        # Frame rows in the order the first convolution reads (space-to-depth
+        # when it folds), gathered and converted from the uint8 rollout.
+        self.fold = input_fold(net)
+        f2 = self.fold * self.fold
+        self.mb_rows = torch.empty((1, 1, mb * h * w // f2, c * f2), dtype=torch.float32,
+                                   device=dev)
         self.mb_actions = torch.empty(mb, dtype=torch.int32, device=dev)
         self.mb_fields = {k: torch.empty(mb, dtype=torch.float32, device=dev)
                           for k in ("old_logp", "values", "returns", "advantages")}
@@ -215,7 +221,8 @@ class PPOLearner(ReplayedUpdate):
         ctx = self.ctx
         idx = self.perm[k]
         c = self.obs_shape[0]
-        ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c), 1.0)
+        f2 = self.fold * self.fold
+        ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c * f2), 1.0, fold=self.fold)
         ctx.gather_rows(self.actions, idx, self.mb_actions)
         for name, src in (("old_logp", self.old_logp), ("values", self.values),
                           ("returns", self.returns), ("advantages", self.advantages)):
@@ -223,6 +230,7 @@ class PPOLearner(ReplayedUpdate):
         self.optimizer.zero_grad()
         rows = Tensor(self.mb_rows)
         rows._exact = True  # raw 0..255 frame values
+        rows._fold = self.fold
         logits, value = self.net(rows)
         loss, parts, _ = ppo_objective(
             logits, value, self.mb_actions, self.mb_fields["old_logp"],
@@ -244,15 +252,18 @@ def initial_old_logp(net, obs_u8: np.ndarray, actions: np.ndarray, device, chunk
     logp = np.zeros(n, np.float32)
     vals = np.zeros(n, np.float32)
     frames = torch.from_numpy(np.ascontiguousarray(obs_u8)).to(dev)
-    rows = torch.empty((1, 1, chunk * h * w, c), dtype=torch.float32, device=dev)
+    fold = input_fold(net)
+    f2 = fold * fold
+    rows = torch.empty((1, 1, chunk * h * w // f2, c * f2), dtype=torch.float32, device=dev)
     with no_grad():
         for s in range(0, n, chunk):
             e = min(n, s + chunk)
             if e - s != chunk:
                 raise ValueError("rollout size must be a multiple of the chunk")
-            ctx.u8_to_f32(frames[s:e], None, rows.reshape(-1, c), 1.0)
+            ctx.u8_to_f32(frames[s:e], None, rows.reshape(-1, c * f2), 1.0, fold=fold)
             x = Tensor(rows)
             x._exact = True
+            x._fold = fold
             logits, value = net(x)
             lg = logits.numpy().astype(np.float64)
             mx = lg.max(axis=1, keepdims=True)

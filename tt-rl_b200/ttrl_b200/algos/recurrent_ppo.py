@@ -33,6 +33,7 @@ from ttrl_b200.algos.grads import clip_grad_norm_device
 from ttrl_b200.algos.ppo import PPOConfig, ReplayedUpdate
 from ttrl_b200.device import context
 from ttrl_b200.engine.autograd import Tensor, as_device
+from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import ppo_objective
 from ttrl_b200.engine.optim import Adam
 from ttrl_b200.nets.recurrent import ACTOR
@@ -151,10 +152,12 @@ class RecurrentPPOLearner(ReplayedUpdate):
         dev = self.device
         slots = self.n_steps * self.n_envs
         f32 = dict(dtype=torch.float32, device=dev)
+        self.fold = input_fold(net) if self.image else 1
         if self.image:
             self.obs = torch.zeros((slots,) + self.obs_shape, dtype=torch.uint8, device=dev)
             c, h, w = self.obs_shape
-            self.mb_rows = torch.empty((1, 1, self.rows * h * w, c), **f32)
+            f2 = self.fold * self.fold
+            self.mb_rows = torch.empty((1, 1, self.rows * h * w // f2, c * f2), **f32)
         else:
             self.obs = torch.zeros((slots,) + self.obs_shape, **f32)
             self.mb_rows = torch.empty((self.rows,) + self.obs_shape, **f32)
@@ -256,7 +259,8 @@ class RecurrentPPOLearner(ReplayedUpdate):
         idx = self.row_idx[k]
         if self.image:
             c = self.obs_shape[0]
-            ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c), 1.0)
+            f2 = self.fold * self.fold
+            ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c * f2), 1.0, fold=self.fold)
         else:
             ctx.gather_rows(self.obs, idx, self.mb_rows)
         ctx.gather_rows(self.actions, idx, self.mb_actions)
@@ -266,6 +270,7 @@ class RecurrentPPOLearner(ReplayedUpdate):
         self.optimizer.zero_grad()
         rows = Tensor(self.mb_rows)
         rows._exact = self.image  # raw 0..255 frame values
+        rows._fold = self.fold
         f = self.mb_fields
         starts = Tensor(f["starts"].reshape(self.seq_len, self.n_seq, 1))
         logits, value = self.net(rows, {ACTOR: Tensor(self.mb_h0)}, starts, seq_len=self.seq_len)

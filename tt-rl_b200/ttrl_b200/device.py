@@ -323,7 +323,9 @@ class DeviceContext:
                                         precision, ws, wsb, self.status_ptr(), self.stream),
                   "ttrl_conv_wgrad")
 
-    def u8_to_f32(self, frames, index, out, scale: float = 1.0) -> None:
+    def u8_to_f32(self, frames, index, out, scale: float = 1.0, fold: int = 1) -> None:
+        """uint8 NCHW frames (optionally gathered by `index`) to fp32 NHWC rows,
+        or, with fold > 1, to space-to-depth rows [n*(h/fold)*(w/fold)][fold²c]."""
         if frames.dtype != torch.uint8 or frames.dim() != 4:
             raise ValueError("frames must be a uint8 [N, C, H, W] CUDA tensor")
         n = frames.shape[0]
@@ -332,6 +334,11 @@ class DeviceContext:
                 raise ValueError("index must be int32")
             n = index.shape[0]
         c, h, w = frames.shape[1], frames.shape[2], frames.shape[3]
+        if fold > 1:
+            check(lib().ttrl_u8_nchw_to_f32_s2d(_ptr(frames), _ptr(index), _ptr(_f32(out, "out")),
+                                                n, c, h, w, int(fold), float(scale), self.stream),
+                  "ttrl_u8_nchw_to_f32_s2d")
+            return
         check(lib().ttrl_u8_nchw_to_f32_nhwc(_ptr(frames), _ptr(index), _ptr(_f32(out, "out")),
                                              n, c, h, w, float(scale), self.stream),
               "ttrl_u8_nchw_to_f32_nhwc")

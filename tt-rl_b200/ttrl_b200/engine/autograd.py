@@ -89,7 +89,7 @@ class Tensor:
 
     __slots__ = ("data", "requires_grad", "grad", "_backward", "_parents", "_op",
                  "_backward_done", "_premask", "_grad_buf", "_grad_owned", "_exact",
-                 "__weakref__")
+                 "_fold", "__weakref__")
 
     def __init__(self, data, requires_grad: bool = False, _parents=(), _op: str = ""):
         self.data = data
@@ -105,6 +105,9 @@ class Tensor:
         # Every value is exactly representable in tf32 (raw 0..255 pixels):
         # a convolution reading it skips the split-TF32 low part.
         self._exact = False
+        # Rows already in space-to-depth order for this fold factor (a first
+        # convolution reads them directly); 1: plain NHWC rows.
+        self._fold = 1
 
     # -- construction ------------------------------------------------------
 

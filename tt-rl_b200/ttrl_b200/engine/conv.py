@@ -8,9 +8,16 @@ OIHW form, as the reference's do, so checkpoints are interchangeable.
 Geometry rules follow ttrl/engine/conv/geometry.py: output sizes, and a
 refusal of ragged strides (the input gradient is only the exact adjoint for
 exactly divisible strides). A space-to-depth `fold` is accepted and checked
-like the reference's, and computes the identical convolution (the fold is a
-re-indexing the reference needs for its hardware; the GEMM here gathers the
-unfolded window directly).
+like the reference's.
+
+Space-to-depth on the device: a layer that needs no input gradient (the
+first layer over frames) and whose stride s divides its kernel and input
+runs as the stride-1 convolution with kernel k/s over s*s*C channels, on
+rows in space-to-depth order (channel (dy*s + dx)*C + c, the reference's
+fold order, ttrl/engine/conv/packing.py:152-160). The products are the same;
+the operand gathers then read contiguous runs of s*s*C channels instead of C.
+Its weight is stored in that folded KRSC order. Input rows arrive folded
+straight from the frame conversion (`Tensor._fold`), or are folded here.
 """
 
 from __future__ import annotations
@@ -19,14 +26,15 @@ import math
 from dataclasses import dataclass
 
 import numpy as np
+import torch
 
-from ttrl_b200.device import conv_geom
+from ttrl_b200.device import context, conv_geom
 from ttrl_b200.engine.autograd import Tensor, as_device
 from ttrl_b200.engine.nn import Module
 from ttrl_b200.engine.ops import conv2d_nhwc
 from ttrl_b200.engine.tensor import restore_in_place
 
-__all__ = ["Conv2d", "ConvGeometry", "ConvDoesNotFit", "conv_out_size"]
+__all__ = ["Conv2d", "ConvGeometry", "ConvDoesNotFit", "conv_out_size", "input_fold"]
 
 
 class ConvDoesNotFit(ValueError):
@@ -138,15 +146,65 @@ class Conv2d(Module):
             if weight.shape != want:
                 raise ValueError(f"Conv2d: weight must have shape {want}, got {weight.shape}")
         self._oihw_shape = weight.shape
-        self.weight = Tensor.from_numpy(np.ascontiguousarray(weight.transpose(0, 2, 3, 1)),
-                                        self.device, requires_grad=True)
+        self.s2d = self._space_to_depth_factor()
+        self.weight = Tensor.from_numpy(self._to_device_layout(weight), self.device,
+                                        requires_grad=True)
         if bias:
             bound = 1.0 / math.sqrt(in_channels * kernel * kernel)
             b = np.random.uniform(-bound, bound, (1, 1, 1, out_channels)).astype(np.float32)
             self.bias = Tensor.from_numpy(b, self.device, requires_grad=True)
         else:
             self.bias = None
-        self._kgeom = self.geom.kernel_geom()
+        self._kgeom = self._kernel_geom()
+
+    # -- space-to-depth --------------------------------------------------
+
+    def _space_to_depth_factor(self) -> int:
+        g = self.geom
+        f = g.stride
+        if (not self.needs_input_grad and f > 1 and g.padding == 0 and g.kernel % f == 0
+                and g.in_h % f == 0 and g.in_w % f == 0):
+            return f
+        return 1
+
+    def _to_device_layout(self, w_oihw: np.ndarray) -> np.ndarray:
+        """OIHW -> KRSC over the (folded) kernel: [O][k/f][k/f][(dy*f+dx)*C + c]."""
+        o, c, k, _ = w_oihw.shape
+        f, kb = self.s2d, k // self.s2d
+        return np.ascontiguousarray(
+            w_oihw.reshape(o, c, kb, f, kb, f).transpose(0, 2, 4, 3, 5, 1)
+            .reshape(o, kb, kb, f * f * c))
+
+    def _from_device_layout(self, w_dev: np.ndarray) -> np.ndarray:
+        o, c, k, _ = self._oihw_shape
+        f, kb = self.s2d, k // self.s2d
+        return np.ascontiguousarray(
+            w_dev.reshape(o, kb, kb, f, f, c).transpose(0, 5, 1, 3, 2, 4).reshape(o, c, k, k))
+
+    def _kernel_geom(self):
+        g, f = self.geom, self.s2d
+        if f == 1:
+            return g.kernel_geom()
+        return conv_geom(g.batch, g.in_h // f, g.in_w // f, g.in_channels * f * f, g.out_channels,
+                         g.kernel // f, g.kernel // f, 1, 0)
+
+    def input_fold(self) -> int:
+        """The space-to-depth factor this layer reads its input rows in."""
+        return self.s2d
+
+    def _fold_input(self, x: Tensor) -> Tensor:
+        """Plain NHWC rows -> space-to-depth rows (one strided copy)."""
+        g, f = self.geom, self.s2d
+        a = g.batch * (g.in_h // f)
+        src = x.data.reshape(a, f, g.in_w // f, f * g.in_channels)  # (a, dy, X, dx*C + c)
+        out = torch.empty((1, 1, a * (g.in_w // f), f * f * g.in_channels),
+                          dtype=torch.float32, device=x.data.device)
+        dst = out.reshape(a, g.in_w // f, f, f * g.in_channels).permute(0, 2, 1, 3)
+        context(x.data.device).copy_strided(dst, src)
+        folded = Tensor(out, requires_grad=False)
+        folded._exact = x._exact
+        folded._fold = f
+        return folded
 
     @property
     def out_shape(self) -> tuple[int, int, int]:
@@ -164,13 +222,13 @@ class Conv2d(Module):
     # -- parameters ------------------------------------------------------
 
     def weight_numpy(self) -> np.ndarray:
-        return np.ascontiguousarray(self.weight.numpy().transpose(0, 3, 1, 2))
+        return self._from_device_layout(self.weight.numpy())
 
     def weight_grad_numpy(self) -> np.ndarray:
         if self.weight.grad is None:
             raise ValueError("Conv2d.weight_grad_numpy: no gradient has been accumulated")
-        g = self.weight.grad.detach().to("cpu").numpy()
-        return np.ascontiguousarray(g.transpose(0, 3, 1, 2))
+        context(self.weight.data.device).join()
+        return self._from_device_layout(self.weight.grad.detach().to("cpu").numpy())
 
     def load_weight_numpy(self, w_oihw) -> None:
         w = np.asarray(w_oihw, np.float32)
@@ -178,7 +236,7 @@ class Conv2d(Module):
             raise ValueError(
                 f"Conv2d.load_weight_numpy: expected shape {self._oihw_shape}, got {w.shape}"
             )
-        restore_in_place(self.weight.data, w.transpose(0, 2, 3, 1))
+        restore_in_place(self.weight.data, self._to_device_layout(w))
 
     def state_dict(self) -> dict:
         state = {"weight": self.weight_numpy()}
@@ -214,7 +272,7 @@ class Conv2d(Module):
         view.geom = ConvGeometry(batch=int(batch), in_channels=g.in_channels, in_h=g.in_h,
                                  in_w=g.in_w, out_channels=g.out_channels, kernel=g.kernel,
                                  stride=g.stride, padding=g.padding, fold=g.fold)
-        view._kgeom = view.geom.kernel_geom()
+        view._kgeom = view._kernel_geom()
         view.needs_input_grad = False
         return view
 
@@ -231,12 +289,47 @@ class Conv2d(Module):
                 "different input."
             )
 
-    def forward(self, x: Tensor) -> Tensor:
+    def _prepare(self, x: Tensor) -> Tensor:
         self._check_input(x)
-        return conv2d_nhwc(x, self.weight, self.bias, self._kgeom, input_scale=self.input_scale,
-                           relu=False, needs_input_grad=self.needs_input_grad)
+        if x._fold == self.s2d:
+            return x
+        if x._fold != 1:
+            raise ValueError(f"conv2d: input rows are folded by {x._fold}, this layer reads "
+                             f"fold {self.s2d}")
+        return self._fold_input(x)
+
+    def forward(self, x: Tensor) -> Tensor:
+        return conv2d_nhwc(self._prepare(x), self.weight, self.bias, self._kgeom,
+                           input_scale=self.input_scale, relu=False,
+                           needs_input_grad=self.needs_input_grad)
 
     def forward_relu(self, x: Tensor) -> Tensor:
-        self._check_input(x)
-        return conv2d_nhwc(x, self.weight, self.bias, self._kgeom, input_scale=self.input_scale,
-                           relu=True, needs_input_grad=self.needs_input_grad)
+        return conv2d_nhwc(self._prepare(x), self.weight, self.bias, self._kgeom,
+                           input_scale=self.input_scale, relu=True,
+                           needs_input_grad=self.needs_input_grad)
+
+
+def _first_conv(value):
+    if isinstance(value, Conv2d):
+        return value
+    if isinstance(value, Module):
+        items = [v for _, v in value._slot_sources()]
+    elif isinstance(value, dict):
+        items = list(value.values())
+    elif isinstance(value, (list, tuple)):
+        items = list(value)
+    else:
+        return None
+    for item in items:
+        found = _first_conv(item)
+        if found is not None:
+            return found
+    return None
+
+
+def input_fold(net) -> int:
+    """The space-to-depth factor `net`'s first convolution reads its input
+    rows in (1 when it has none): frame conversions for this net produce
+    rows in that order directly (`DeviceContext.u8_to_f32(..., fold=)`)."""
+    conv = _first_conv(net)
+    return 1 if conv is None else conv.input_fold()
