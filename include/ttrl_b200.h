@@ -367,6 +367,51 @@ int ttrl_ppo_loss(const float* logits, const float* value, const int32_t* action
                   float value_clip_eps, float value_coef, float entropy_coef,
                   ttrl_stream_t stream);
 
+/* ------------------------------------------------------------------ acting */
+
+/* The DQN acting choice over q[batch][n_actions]: greedy = the first maximum
+ * over the columns with mask > 0.5 (mask == NULL: all columns), then
+ * actions[b] = draws[b] < *eps ? alt_actions[b] : greedy. draws (uniform in
+ * [0, 1), double) and alt_actions (exploring actions) are drawn by the caller
+ * in the reference's order; draws == NULL acts greedily. eps is a device
+ * double so a captured acting graph replays with the current epsilon.
+ * Replaces the argmax_dim_detached + host np.where of
+ * ttrl/algos/dqn/agent.py:97-119 and ttrl/algos/mask.py:95-110. */
+int ttrl_epsilon_greedy(const float* q, const float* mask, const double* draws,
+                        const int32_t* alt_actions, const double* eps, int32_t* actions, int batch,
+                        int n_actions, ttrl_stream_t stream);
+
+/* The PPO acting draw over logits[batch][n_actions]: log-softmax with the
+ * operations of ttrl_ppo_loss, then the first maximum (uniforms == NULL) or
+ * the inverse-CDF draw against uniforms[b] (probs = exp(logp) normalised,
+ * action = number of cumulative probabilities below the uniform, clipped to
+ * n_actions - 1); logp[b] (may be NULL) receives the chosen action's
+ * log-prob. Replaces CategoricalPolicy.sample (ttrl/algos/ppo/policy.py:36-62)
+ * after its device log_softmax. */
+int ttrl_categorical_sample(const float* logits, const double* uniforms, int32_t* actions,
+                            float* logp, int batch, int n_actions, ttrl_stream_t stream);
+
+/* ----------------------------------------------------------------- rollout */
+
+/* GAE-lambda over a [n_steps][n_envs] rollout, one lane per thread walking
+ * t = n_steps-1 .. 0 in the reference's float32 operation order (bit-exact
+ * with ttrl/buffers/rollout.py:195-227): delta = r + gamma*next*(1-done) - v;
+ * gae = (delta + gamma_lam*(1-done)*gae) * valid (valid == NULL: 1);
+ * advantages = gae, returns = gae + v, next = v; `next` starts at
+ * last_values[n_envs]. gamma_lam is float32(gamma * lambda) as the reference
+ * rounds it. */
+int ttrl_gae(const float* rewards, const float* values, const float* dones, const float* valid,
+             const float* last_values, float* advantages, float* returns, int n_steps,
+             int n_envs, float gamma, float gamma_lam, ttrl_stream_t stream);
+
+/* out = (adv - mean) / (std + 1e-8) with mean and (population) std over the
+ * slots whose valid > 0 (valid == NULL: all), applied to every slot
+ * (ttrl/buffers/rollout.py:269-270, ttrl/buffers/seqbatch.py:86-101). The
+ * statistics accumulate in double in a fixed order; a rollout with no valid
+ * slot writes 1002 into `status` and leaves `out` untouched. */
+int ttrl_normalize_advantages(const float* advantages, const float* valid, float* out,
+                              long long n, int* status, ttrl_stream_t stream);
+
 /* --------------------------------------------------------------- recurrent */
 
 /* One GRU step after its recurrent GEMM: with gi = x_t @ W_ih + b_ih and

@@ -550,6 +550,39 @@ def recurrent_ppo(index):
           "(5 logits, value), starts inside sequences, padding slots; loss and every grad")
 
 
+def rollout_gae(index):
+    """ttrl/buffers/rollout.py's compute_gae and the minibatch advantage
+    normalisation over valid slots, on a buffer with terminations and
+    autoreset padding slots."""
+    from ttrl.buffers.rollout import RolloutBuffer
+    from ttrl.spaces import ActionSpec, ObsGroup, ObsSpec
+    out = {}
+    for case, (T, E, gamma, lam) in enumerate([(16, 5, 0.99, 0.95), (9, 3, 0.9, 0.8)]):
+        rng = np.random.default_rng(1100 + case)
+        buf = RolloutBuffer(ObsGroup.of(ObsSpec.vector(2)), ActionSpec.discrete(3), n_envs=E,
+                            n_steps=T, seed=5)
+        rewards = rng.standard_normal((T, E)).astype(np.float32)
+        values = rng.standard_normal((T, E)).astype(np.float32)
+        dones = (rng.random((T, E)) < 0.15).astype(np.float32)
+        valid = (rng.random((T, E)) > 0.1).astype(np.float32)
+        for t in range(T):
+            buf.add({"obs": np.zeros((E, 2), np.float32)}, np.zeros(E, np.int64),
+                    np.zeros(E, np.float32), values[t], rewards[t], dones[t], valid[t])
+        last = rng.standard_normal(E).astype(np.float32)
+        buf.compute_gae(gamma, lam, last)
+        keep = valid.reshape(-1) > 0
+        adv = buf.advantages.reshape(-1)[keep]
+        norm = (adv - adv.mean()) / (adv.std() + 1e-8)
+        pre = f"c{case}_"
+        out.update({pre + "rewards": rewards, pre + "values": values, pre + "dones": dones,
+                    pre + "valid": valid, pre + "last_values": last,
+                    pre + "gamma_lam": np.array([gamma, lam]),
+                    pre + "advantages": buf.advantages.copy(), pre + "returns": buf.returns.copy(),
+                    pre + "normalized_valid": norm})
+    _save("rollout_gae", out, index,
+          "ttrl/buffers/rollout.py:195-227 compute_gae and :269-270 normalisation over valid")
+
+
 def main() -> None:
     reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TTRL_REFERENCE")
     if not reference or not os.path.isdir(os.path.join(reference, "ttrl")):
@@ -557,7 +590,7 @@ def main() -> None:
     _install(reference)
     index: dict = {}
     for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
-               grad_clip, gru, param_sync, sac_losses, recurrent_ppo):
+               grad_clip, gru, param_sync, sac_losses, recurrent_ppo, rollout_gae):
         fn(index)
         print("wrote", fn.__name__)
     with open(os.path.join(HERE, "index.json"), "w") as f:

@@ -250,3 +250,18 @@ def test_recurrent_ppo_minibatch():
     for name, g in out["grads"].items():
         assert rel(g, d["grad." + name]) <= 1e-5, name
     assert set(out["grads"]) == {k[len("grad."):] for k in d.files if k.startswith("grad.")}
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_rollout_gae(case):
+    """GAE-lambda and the valid-slot normalisation, bit-exact against the
+    reference's RolloutBuffer (same float32 operations)."""
+    from oracle import rollout as ro
+    d = load("rollout_gae")
+    g = {k[3:]: d[k] for k in d.files if k.startswith(f"c{case}_")}
+    gamma, lam = (float(v) for v in g["gamma_lam"])
+    adv, ret = ro.gae(g["rewards"], g["values"], g["dones"], g["valid"], g["last_values"],
+                      gamma, lam)
+    assert np.array_equal(adv, g["advantages"])
+    assert np.array_equal(ret, g["returns"])
+    assert np.array_equal(ro.normalize(adv, g["valid"]), g["normalized_valid"])

@@ -21,6 +21,7 @@ constexpr int kSpinLimit = 1 << 22;
 
 // Device status codes written into the optional status word.
 constexpr int kErrWaitTimeout = 1001;
+constexpr int kErrNoValidSlots = 1002;  // a reduction over valid slots found none
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

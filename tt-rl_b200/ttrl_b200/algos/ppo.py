@@ -45,6 +45,8 @@ class PPOConfig:
     epochs: int = 4
     minibatch_size: int = 256
     normalize_adv: bool = True
+    gamma: float = 0.99
+    lam: float = 0.95
 
 
 def normalize_advantages(adv: np.ndarray) -> np.ndarray:
@@ -142,7 +144,10 @@ class PPOLearner(ReplayedUpdate):
     """Graph-replayed PPO learner over a device-resident rollout."""
 
     def __init__(self, net, rollout_size: int, obs_shape, device=None, *,
-                 cfg: PPOConfig = PPOConfig(), seed: int = 0):
+                 cfg: PPOConfig = PPOConfig(), seed: int = 0, minibatches: int | None = None):
+        """`minibatches` per epoch fixes the captured graph; it defaults to
+        rollout_size // minibatch_size, the count of a rollout without
+        autoreset padding (a padded rollout yields valid_slots // size)."""
         self.net = net
         self.cfg = cfg
         self.device = as_device(device)
@@ -150,8 +155,8 @@ class PPOLearner(ReplayedUpdate):
         self.rollout_size = int(rollout_size)
         self.obs_shape = tuple(int(v) for v in obs_shape)
         mb = cfg.minibatch_size
-        self.minibatches = self.rollout_size // mb
-        if self.minibatches == 0:
+        self.minibatches = self.rollout_size // mb if minibatches is None else int(minibatches)
+        if self.minibatches == 0 or self.minibatches * mb > self.rollout_size:
             raise ValueError(f"rollout of {rollout_size} holds no minibatch of {mb}")
         self.steps_per_update = cfg.epochs * self.minibatches
         self.params = list(net.parameters())
@@ -182,6 +187,7 @@ class PPOLearner(ReplayedUpdate):
                           for k in ("old_logp", "values", "returns", "advantages")}
         self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
                                       dtype=torch.float32, device=dev)
+        self.keep = None  # valid slot indices when the rollout has padding slots
         self._upload_done = None
         self._graph = None
         self.launches_per_replay = 0
@@ -192,6 +198,7 @@ class PPOLearner(ReplayedUpdate):
         """Upload one rollout (host arrays). Advantages are normalised over
         the rollout here when cfg.normalize_adv, as the reference does."""
         adv = normalize_advantages(advantages) if self.cfg.normalize_adv else advantages
+        self.keep = None
         self.obs.copy_(torch.from_numpy(np.ascontiguousarray(obs_u8, np.uint8)))
         self.actions.copy_(torch.from_numpy(np.asarray(actions, np.int32)))
         self.old_logp.copy_(torch.from_numpy(np.asarray(old_logp, np.float32)))
@@ -199,16 +206,57 @@ class PPOLearner(ReplayedUpdate):
         self.returns.copy_(torch.from_numpy(np.asarray(returns, np.float32)))
         self.advantages.copy_(torch.from_numpy(np.asarray(adv, np.float32)))
 
+    def load_rollout_raw(self, obs_u8, actions, old_logp, values, rewards, dones, last_values,
+                         valid=None) -> None:
+        """Upload one collected rollout ([n_steps, n_envs] arrays, slot
+        t * n_envs + lane; obs [n_steps, n_envs, C, H, W]) and derive the
+        advantages and returns on the device: GAE-lambda with cfg.gamma and
+        cfg.lam (ttrl/buffers/rollout.py:195-227), then, when
+        cfg.normalize_adv, normalisation over the valid slots (:269-270).
+        Minibatches then draw only valid slots, as the reference's do."""
+        values = np.asarray(values, np.float32)
+        steps, envs = values.shape
+        if steps * envs != self.rollout_size:
+            raise ValueError(f"load_rollout_raw: {steps} x {envs} slots, the learner holds "
+                             f"{self.rollout_size}")
+        dev = self.device
+        up = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+        self.obs.copy_(torch.from_numpy(np.ascontiguousarray(obs_u8, np.uint8)).reshape(
+            self.obs.shape))
+        self.actions.copy_(torch.from_numpy(np.asarray(actions, np.int32).reshape(-1)))
+        self.old_logp.copy_(up(old_logp).reshape(-1))
+        self.values.copy_(up(values).reshape(-1))
+        valid_d = None if valid is None else up(valid)
+        ctx = self.ctx
+        ctx.gae(up(rewards), self.values.reshape(steps, envs), up(dones), valid_d,
+                up(last_values).reshape(envs), self.advantages.reshape(steps, envs),
+                self.returns.reshape(steps, envs), self.cfg.gamma, self.cfg.lam)
+        if self.cfg.normalize_adv:
+            ctx.normalize_advantages(self.advantages, None if valid_d is None else
+                                     valid_d.reshape(-1), self.advantages)
+        self.keep = (None if valid is None else
+                     np.flatnonzero(np.asarray(valid, np.float32).reshape(-1) > 0.0))
+        total = self.rollout_size if self.keep is None else len(self.keep)
+        if total // self.cfg.minibatch_size != self.minibatches:
+            raise ValueError(
+                f"load_rollout_raw: {total} valid transitions make "
+                f"{total // self.cfg.minibatch_size} minibatches of {self.cfg.minibatch_size}, "
+                f"and this learner's captured graph holds {self.minibatches} per epoch")
+
     def draw_permutations(self) -> None:
-        """One permutation of the rollout per epoch, cut into minibatches."""
+        """One permutation of the (valid) rollout slots per epoch, cut into
+        minibatches (ttrl/buffers/rollout.py:241-283)."""
         mb = self.cfg.minibatch_size
         if self._upload_done is not None:
             self._upload_done.synchronize()  # the previous upload has read perm_host
+        keep = self.keep
+        total = self.rollout_size if keep is None else len(keep)
         rows = []
         for _ in range(self.cfg.epochs):
-            perm = self.rng.permutation(self.rollout_size)
+            perm = self.rng.permutation(total)
             for start in range(0, self.minibatches * mb, mb):
-                rows.append(perm[start:start + mb])
+                idx = perm[start:start + mb]
+                rows.append(idx if keep is None else keep[idx])
         self.perm_host.numpy()[:] = np.stack(rows).astype(np.int32)
         self.perm.copy_(self.perm_host, non_blocking=True)
         self._upload_done = torch.cuda.Event()

@@ -18,6 +18,7 @@ import contextlib
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from ttrl_b200 import _lib
@@ -446,6 +447,34 @@ class DeviceContext:
         check(lib().ttrl_gru_gates_bwd(_ptr(dout), _ptr(dhm), _ptr(start_next), int(carry),
                                        _ptr(gates), _ptr(gh), _ptr(hm), _ptr(dgi), _ptr(dgh), b,
                                        hidden, self.stream), "ttrl_gru_gates_bwd")
+
+    def epsilon_greedy(self, q, mask, draws, alt, eps, actions) -> None:
+        """actions = draws < eps ? alt : first argmax of q over legal columns."""
+        b, a = q.shape
+        check(lib().ttrl_epsilon_greedy(_ptr(q), _ptr(mask), _ptr(draws), _ptr(alt), _ptr(eps),
+                                        _ptr(actions), b, a, self.stream), "ttrl_epsilon_greedy")
+
+    def categorical_sample(self, logits, uniforms, actions, logp) -> None:
+        """Inverse-CDF draw (uniforms None: argmax) from the log-softmax."""
+        b, a = logits.shape
+        check(lib().ttrl_categorical_sample(_ptr(logits), _ptr(uniforms), _ptr(actions),
+                                            _ptr(logp), b, a, self.stream),
+              "ttrl_categorical_sample")
+
+    def gae(self, rewards, values, dones, valid, last_values, advantages, returns,
+            gamma: float, lam: float) -> None:
+        """GAE-lambda over [n_steps, n_envs] device arrays (bit-exact with the
+        reference's float32 recursion)."""
+        steps, envs = values.shape
+        gamma_lam = float(np.float32(float(gamma) * float(lam)))
+        check(lib().ttrl_gae(_ptr(rewards), _ptr(values), _ptr(dones), _ptr(valid),
+                             _ptr(last_values), _ptr(advantages), _ptr(returns), steps, envs,
+                             float(np.float32(gamma)), gamma_lam, self.stream), "ttrl_gae")
+
+    def normalize_advantages(self, advantages, valid, out) -> None:
+        check(lib().ttrl_normalize_advantages(_ptr(advantages), _ptr(valid), _ptr(out),
+                                              int(advantages.numel()), self.status_ptr(),
+                                              self.stream), "ttrl_normalize_advantages")
 
     def gru_sequence_supported(self, batch: int, hidden: int) -> bool:
         """Whether the one-launch sequence kernels take this shape here."""
