@@ -391,6 +391,35 @@ int ttrl_epsilon_greedy(const float* q, const float* mask, const double* draws,
 int ttrl_categorical_sample(const float* logits, const double* uniforms, int32_t* actions,
                             float* logp, int batch, int n_actions, ttrl_stream_t stream);
 
+/* ------------------------------------------------------- prioritized replay */
+
+/* Write back one batch's priorities into the float64 table [lanes][columns]
+ * of (p + eps)^alpha: table[lanes[b]][cols[b]] = (|td_abs[b]| + eps)^alpha,
+ * a pair drawn twice taking its last value, and *max_priority = max(
+ * *max_priority, max |td_abs|). from_max != 0 writes (*max_priority +
+ * eps)^alpha instead (a freshly written column; td_abs unused). A non-finite
+ * |td| writes 1003 into `status` and leaves the table unchanged. td_abs is the
+ * device output of ttrl_dqn_loss, so nothing is read back to the host.
+ * Replaces PrioritySampler.update / on_write (ttrl/buffers/sampling.py:131-203)
+ * behind write_back_priorities (ttrl/algos/offpolicy.py:136-145). */
+int ttrl_per_update(double* table, int columns, const int32_t* lanes, const int32_t* cols,
+                    const float* td_abs, int batch, double alpha, double eps,
+                    double* max_priority, int from_max, int* status, ttrl_stream_t stream);
+
+/* Each lane's run (positions p = 0 .. counts[l]-1, oldest first, column
+ * (start[l] + p) % columns) summed in order into cdf[l][p] (float64, numpy's
+ * cumsum order); totals[l] = the lane's sum. */
+int ttrl_per_cdf(const double* table, int n_lanes, int columns, const int32_t* counts,
+                 const int32_t* start, double* cdf, double* totals, ttrl_stream_t stream);
+
+/* One draw per sample b within lane lane_of[b]: the first position whose cdf
+ * exceeds uniforms[b] * (the lane's total), clipped to the run
+ * (ttrl/buffers/sampling.py:221-227); writes the position, its column and its
+ * table value (for the importance-sampling weight). */
+int ttrl_per_draw(const double* cdf, const double* table, int columns, const int32_t* counts,
+                  const int32_t* start, const int32_t* lane_of, const double* uniforms, int batch,
+                  int32_t* positions, int32_t* cols, double* picked, ttrl_stream_t stream);
+
 /* ----------------------------------------------------------------- rollout */
 
 /* GAE-lambda over a [n_steps][n_envs] rollout, one lane per thread walking

@@ -583,6 +583,45 @@ def rollout_gae(index):
           "ttrl/buffers/rollout.py:195-227 compute_gae and :269-270 normalisation over valid")
 
 
+def priority_replay(index):
+    """ttrl/buffers/sampling.py's PrioritySampler (pure numpy) through a
+    scripted sequence: fresh columns, two write-backs (one with a column drawn
+    twice), and draws over wrapped ring runs."""
+    from ttrl.buffers.sampling import PriorityConfig, PrioritySampler
+    from ttrl.buffers.window import SampleWindow
+    lanes, columns = 3, 40
+    cfg = PriorityConfig(alpha=0.6, epsilon=1e-6)
+    s = PrioritySampler(cfg, lanes=lanes, columns=columns)
+    rng = np.random.default_rng(1200)
+    out = {}
+    fresh = [(l, c) for l in range(lanes) for c in range(columns)]
+    for l, c in fresh:
+        s.on_write(l, c)
+    for phase in range(2):
+        n = 24
+        ul = rng.integers(0, lanes, n)
+        uc = rng.integers(0, columns, n)
+        ul[-1], uc[-1] = ul[0], uc[0]  # one pair twice: the last value wins
+        td = (np.abs(rng.standard_normal(n)) * (3.0 if phase else 1.0)).astype(np.float32)
+        s.update(ul, uc, td)
+        out[f"u{phase}_lanes"], out[f"u{phase}_cols"], out[f"u{phase}_td"] = ul, uc, td
+        out[f"u{phase}_weight"] = s._weight.copy()
+        out[f"u{phase}_max"] = np.float64(s._max_priority)
+    s.on_write(1, 7)
+    out["fresh_weight"] = s._weight.copy()
+    window = SampleWindow(counts=np.array([40, 25, 31]), start=np.array([0, 30, 12]),
+                          capacity=columns)
+    for k, beta in enumerate((0.4, 0.9)):
+        draw_rng = np.random.default_rng(1300 + k)
+        d = s.draw(draw_rng, window, batch_size=64, beta=beta)
+        out[f"d{k}_lanes"], out[f"d{k}_offsets"], out[f"d{k}_weights"] = d.lanes, d.offsets, d.weights
+        out[f"d{k}_beta"] = np.float64(beta)
+    out["window_counts"], out["window_start"] = window.counts, window.start
+    _save("priority_replay", out, index,
+          "ttrl/buffers/sampling.py PrioritySampler: on_write, update (duplicate pair), draw "
+          "(multinomial lane quota, searchsorted, IS weights) over wrapped runs")
+
+
 def main() -> None:
     reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TTRL_REFERENCE")
     if not reference or not os.path.isdir(os.path.join(reference, "ttrl")):
@@ -590,7 +629,8 @@ def main() -> None:
     _install(reference)
     index: dict = {}
     for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
-               grad_clip, gru, param_sync, sac_losses, recurrent_ppo, rollout_gae):
+               grad_clip, gru, param_sync, sac_losses, recurrent_ppo, rollout_gae,
+               priority_replay):
         fn(index)
         print("wrote", fn.__name__)
     with open(os.path.join(HERE, "index.json"), "w") as f:

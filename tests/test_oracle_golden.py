@@ -265,3 +265,26 @@ def test_rollout_gae(case):
     assert np.array_equal(adv, g["advantages"])
     assert np.array_equal(ret, g["returns"])
     assert np.array_equal(ro.normalize(adv, g["valid"]), g["normalized_valid"])
+
+
+def test_priority_replay():
+    """The prioritized-replay restatement against the reference's own
+    PrioritySampler on the same scripted sequence."""
+    from oracle.priority import PriorityTable
+    d = load("priority_replay")
+    t = PriorityTable(3, 40, 0.6, 1e-6)
+    for l in range(3):
+        for c in range(40):
+            t.on_write(l, c)
+    for phase in range(2):
+        t.update(d[f"u{phase}_lanes"], d[f"u{phase}_cols"], d[f"u{phase}_td"])
+        assert np.array_equal(t.weight, d[f"u{phase}_weight"])
+        assert t.max_priority == float(d[f"u{phase}_max"])
+    t.on_write(1, 7)
+    assert np.array_equal(t.weight, d["fresh_weight"])
+    for k in range(2):
+        lanes, offsets, weights = t.draw(np.random.default_rng(1300 + k), d["window_counts"],
+                                         d["window_start"], 40, 64, float(d[f"d{k}_beta"]))
+        assert np.array_equal(lanes, d[f"d{k}_lanes"])
+        assert np.array_equal(offsets, d[f"d{k}_offsets"])
+        assert np.array_equal(weights, d[f"d{k}_weights"])

@@ -140,6 +140,11 @@ _SIGNATURES = {
     "ttrl_gru_mask": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),
     "ttrl_epsilon_greedy": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp]),
     "ttrl_categorical_sample": (_c_int, [_vp] * 4 + [_c_int, _c_int, _vp]),
+    "ttrl_per_update": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _c_int, ctypes.c_double,
+                                 ctypes.c_double, _vp, _c_int, _vp, _vp]),
+    "ttrl_per_cdf": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),
+    "ttrl_per_draw": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp,
+                               _vp]),
     "ttrl_gae": (_c_int, [_vp] * 7 + [_c_int, _c_int, _c_float, _c_float, _vp]),
     "ttrl_normalize_advantages": (_c_int, [_vp, _vp, _vp, ctypes.c_longlong, _vp, _vp]),
     "ttrl_gru_sequence_supported": (_c_int, [_c_int, _c_int]),
