@@ -3,7 +3,9 @@
 Run in a container that has the reference checkout (its path is the first
 argument, or TTRL_REFERENCE):
 
-    python tests/golden/make_golden.py /path/to/tt-rl
+    python tests/golden/make_golden.py /path/to/tt-rl [case ...]
+
+(naming cases regenerates only those).
 
 The reference's device code imports `ttnn` at module scope; this script
 installs `ttnn_numpy` (a float32 numpy stand-in) under that name first, so
@@ -622,18 +624,185 @@ def priority_replay(index):
           "(multinomial lane quota, searchsorted, IS weights) over wrapped runs")
 
 
+#: A small image DQN: the Nature-CNN stages over 4x36x36 frames (36 -> 8 -> 3
+#: -> 1), a 16-wide feature layer and 6 actions.
+CKPT_OBS = (4, 36, 36)
+CKPT_HIDDEN, CKPT_ACTIONS = 16, 6
+CKPT_CONV = ((32, 4, 8, 8), (64, 32, 4, 4), (64, 64, 3, 3))
+
+
+def _ckpt_q_state(rng):
+    """The names and shapes `EncoderHead.state_dict()` of the reference's
+    build_q_net has for this spec (every encoder a MultiEncoder, Sequential
+    numbering ReLUs and the Flatten), values on a 1/1024 grid so the file
+    compresses."""
+    sd = {}
+    grid = lambda shape: (rng.integers(-48, 49, shape) / 1024.0).astype(np.float32)
+    for layer, shape in zip((0, 2, 4), CKPT_CONV):
+        sd[f"encoder.towers.obs.layers.{layer}.weight"] = grid(shape)
+        sd[f"encoder.towers.obs.layers.{layer}.bias"] = grid((1, 1, 1, shape[0]))
+    sd["encoder.towers.obs.layers.7.weight"] = grid((64, CKPT_HIDDEN))
+    sd["encoder.towers.obs.layers.7.bias"] = grid((1, CKPT_HIDDEN))
+    sd["head.q.weight"] = grid((CKPT_HIDDEN, CKPT_ACTIONS))
+    sd["head.q.bias"] = grid((1, CKPT_ACTIONS))
+    return sd
+
+
+def _ckpt_layout(shape):
+    """The prepared layout the reference's device library gives this conv
+    (cp: channels rounded up to 8; the 4-channel 8x8 case is pinned by the
+    reference's own tests at (1, 1, 512, 32))."""
+    from ttrl.engine.conv.packing import candidate_layouts
+    o, c, kh, kw = shape
+    cp = (c + 7) // 8 * 8
+    rows = kh * ((kw * cp + 31) // 32 * 32)
+    cols = (o + 31) // 32 * 32
+    return next(lay for lay in candidate_layouts(rows, cols, o, c, kh, kw) if lay.cp == cp)
+
+
+def checkpoint_dqn(index):
+    """A DQN-shaped L1 checkpoint written by the reference's own
+    save_checkpoint (ttrl/train/checkpoint/file.py:112-218), with the Adam
+    moments of each conv weight in the reference's prepared matrix
+    (ttrl/engine/conv/packing.py:24-108) as its optimizer stores them, read
+    back by its load_checkpoint and exported by its ttrl.deploy path; then the
+    same file rewritten by ttrl_b200.checkpoint with changed weights and
+    moments, and THAT file read and exported by the reference too."""
+    import tempfile
+    from ttrl.algos.dqn.config import DQNConfig
+    from ttrl.deploy.export import export_policy
+    from ttrl.deploy.read import load_policy
+    from ttrl.spaces import ActionSpec, ObsSpec
+    from ttrl.train.checkpoint import L1, load_checkpoint, save_checkpoint
+    from ttrl.train.config import TrainConfig
+    sys.path.insert(0, os.path.join(os.path.dirname(HERE), "..", "tt-rl_b200"))
+    from ttrl_b200.checkpoint import Checkpoint
+    from ttrl_b200.engine.packing import solve_cp
+
+    rng = np.random.default_rng(1500)
+    online, target = _ckpt_q_state(rng), _ckpt_q_state(rng)
+    names = list(online)
+    m, v, layouts = [], [], {}
+    for i, name in enumerate(names):
+        shape = online[name].shape
+        mi = (rng.integers(-32, 33, shape) / 4096.0).astype(np.float32)
+        vi = (rng.integers(1, 64, shape) / 2.0 ** 20).astype(np.float32)
+        if len(shape) == 4 and shape[2] > 1:  # a conv weight: prepared matrix
+            lay = _ckpt_layout(shape)
+            layouts[i] = lay
+            mi, vi = lay.pack(mi), lay.pack(vi)
+        m.append(mi)
+        v.append(vi)
+    optimizer = {"t": 7, "steps": [7] * len(names), "lr": 1e-4, "betas": (0.9, 0.999),
+                 "eps": 1.5e-4, "weight_decay": 0.0, "m": m, "v": v}
+    state = {"config": DQNConfig(), "online": online, "target": target,
+             "optimizer": optimizer, "frame_count": 2800, "update_count": 7,
+             "rng_state": np.random.default_rng(3).bit_generator.state,
+             "autoreset": {}, "clock": {}}
+    obs = rng.integers(0, 256, (3,) + CKPT_OBS, dtype=np.uint8)
+    out = {"obs": obs}
+    with tempfile.TemporaryDirectory() as tmp:
+        ref_path = os.path.join(tmp, "ref.npz")
+        save_checkpoint(ref_path, agent_state=state, obs_spec=ObsSpec.image(*CKPT_OBS),
+                        action_spec=ActionSpec.discrete(CKPT_ACTIONS), level=L1, frame=2800,
+                        config=TrainConfig(), env_policy_state=[])
+        loaded = load_checkpoint(ref_path)["agent_state"]
+        assert set(loaded["online"]) == set(names)
+        export_policy(ref_path, os.path.join(tmp, "ref_policy.npz"))
+        out["deploy_q"] = load_policy(os.path.join(tmp, "ref_policy.npz")).head(obs)
+
+        # Our reader and writer on the reference's file.
+        ours = Checkpoint.read(ref_path)
+        tree = ours.agent_state()
+        for name in names:
+            assert np.array_equal(tree["online"][name], loaded["online"][name])
+        assert ours.to_bytes() is not None
+        for i, lay in layouts.items():
+            mine = solve_cp(tree["optimizer"]["m"][i].shape, CKPT_CONV[list(layouts).index(i)],
+                            v=tree["optimizer"]["v"][i])
+            assert (mine.cp, mine.rows, mine.cols) == (lay.cp, lay.rows, lay.cols)
+            assert np.array_equal(mine.unpack(tree["optimizer"]["m"][i]),
+                                  lay.unpack(tree["optimizer"]["m"][i]))
+        # Changed weights and moments written back in the stored forms.
+        upd_online = {k: (a + np.float32(1.0 / 512)).astype(np.float32)
+                      for k, a in tree["online"].items()}
+        opt = dict(tree["optimizer"])
+        opt["t"], opt["steps"] = 8, [8] * len(names)
+        opt["m"] = [a * np.float32(0.5) for a in opt["m"]]
+        tree["online"] = upd_online
+        tree["optimizer"] = opt
+        tree["update_count"] = 8
+        upd_path = os.path.join(tmp, "ours.npz")
+        ours.with_agent_state(tree).write(upd_path)
+        back = load_checkpoint(upd_path)
+        for name in names:
+            assert np.array_equal(back["agent_state"]["online"][name], upd_online[name])
+        assert back["agent_state"]["optimizer"]["t"] == 8
+        for i, lay in layouts.items():
+            got = back["agent_state"]["optimizer"]["m"][i]
+            assert got.shape == lay.shape and np.array_equal(got, opt["m"][i])
+        export_policy(upd_path, os.path.join(tmp, "ours_policy.npz"))
+        out["deploy_q_updated"] = load_policy(os.path.join(tmp, "ours_policy.npz")).head(obs)
+        with open(ref_path, "rb") as f:
+            out["ref_file"] = np.frombuffer(f.read(), np.uint8)
+    out["layouts"] = np.array([[i, lay.rows, lay.cols, lay.cp] for i, lay in layouts.items()],
+                              np.int64)
+    _save("checkpoint_dqn", out, index,
+          "ttrl/train/checkpoint/file.py save_checkpoint (L1) of a 4x36x36 DQN with prepared "
+          "conv Adam moments (engine/conv/packing.py); deploy_q: ttrl.deploy export -> head "
+          "of that file; deploy_q_updated: the same after ttrl_b200.checkpoint rewrote it")
+
+
+def state_names(index):
+    """state_dict names and shapes of the reference's builders over vector
+    observations (ttrl/nets/build.py: build_q_net, build_actor_critic,
+    build_sac_nets; ttrl/nets/recurrent.py), built on the numpy stand-in. An
+    image net's names are pinned by the checkpoint_dqn file."""
+    from ttrl.nets.build import build_actor_critic, build_q_net, build_sac_nets
+    from ttrl.nets.recurrent import build_recurrent_actor_critic
+    from ttrl.spaces import ActionSpec, ObsGroup, ObsSpec
+    import ttnn
+    dev = ttnn.DEVICE
+    np.random.seed(1600)
+    spec = ObsGroup.of(ObsSpec.vector(11))
+    nets = {
+        "q": build_q_net(spec, ActionSpec.discrete(5), dev, batch=8, hidden=(32, 24)),
+        "ac": build_actor_critic(spec, ActionSpec.discrete(5), dev, batch=8, hidden=(32, 24)),
+        "sac": build_sac_nets(spec, ActionSpec.continuous([-1.0] * 3, [1.0] * 3), dev, batch=8,
+                              critic_hidden=(20, 12), encoder_kwargs={"hidden": (24, 16)}),
+        "rec": build_recurrent_actor_critic(spec, ActionSpec.discrete(5), dev, batch=8,
+                                            hidden_size=10, hidden=(16,)),
+    }
+    out = {}
+    for family, net in nets.items():
+        sd = net.state_dict()
+        out[f"{family}.names"] = np.array(list(sd), dtype=np.str_)
+        out[f"{family}.shapes"] = np.array(
+            [",".join(str(d) for d in np.asarray(a).shape) for a in sd.values()], dtype=np.str_)
+    _save("state_names", out, index,
+          "state_dict names/shapes of build_q_net, build_actor_critic, build_sac_nets, "
+          "build_recurrent_actor_critic over an 11-dim vector observation")
+
+
 def main() -> None:
     reference = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TTRL_REFERENCE")
     if not reference or not os.path.isdir(os.path.join(reference, "ttrl")):
         raise SystemExit("usage: make_golden.py <reference checkout>")
     _install(reference)
+    index_path = os.path.join(HERE, "index.json")
+    only = set(sys.argv[2:])
     index: dict = {}
+    if only and os.path.exists(index_path):
+        with open(index_path) as f:
+            index = json.load(f)
     for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
                grad_clip, gru, param_sync, sac_losses, recurrent_ppo, rollout_gae,
-               priority_replay):
+               priority_replay, checkpoint_dqn, state_names):
+        if only and fn.__name__ not in only:
+            continue
         fn(index)
         print("wrote", fn.__name__)
-    with open(os.path.join(HERE, "index.json"), "w") as f:
+    with open(index_path, "w") as f:
         json.dump(index, f, indent=1, sort_keys=True)
 
 

@@ -18,7 +18,7 @@ def rel(a, b):
 def nature_state_dict(p, heads=("q",)):
     """Oracle parameter dict -> the state_dict of ttrl_b200's Nature-CNN nets
     (EncoderHead for heads=('q',), ActorCritic for ('pi', 'v'))."""
-    enc = "encoder" if heads == ("q",) else "encoders.actor"
+    enc = ("encoder" if heads == ("q",) else "encoders.actor") + ".towers.obs"
     sd = {}
     for i, layer in enumerate((0, 2, 4)):
         sd[f"{enc}.layers.{layer}.weight"] = p[f"conv{i}.w"]
@@ -61,7 +61,7 @@ def device_gates(net, rows_tensor):
     import torch
     from ttrl_b200.engine.autograd import no_grad
     enc = net.encoder if hasattr(net, "encoder") else net.encoders["actor"]
-    layers = list(enc.layers)
+    layers = list(enc["obs"].layers)
     gates = {}
     x = rows_tensor
     with no_grad():

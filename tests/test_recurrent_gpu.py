@@ -27,21 +27,11 @@ from tests.helpers import rel  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-REF_TRUNK = "encoders.actor.towers.obs.layers."
-OUR_TRUNK = "encoders.actor.layers."
 
 
 def _need_gpu():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-
-
-def _ours(name: str) -> str:
-    return OUR_TRUNK + name[len(REF_TRUNK):] if name.startswith(REF_TRUNK) else name
-
-
-def _theirs(name: str) -> str:
-    return REF_TRUNK + name[len(OUR_TRUNK):] if name.startswith(OUR_TRUNK) else name
 
 
 def _vector_net(d, a, hidden, trunk=(16,), batch=24, seed=0):
@@ -62,7 +52,7 @@ def test_recurrent_minibatch_matches_reference_golden():
     H = g["h0"].shape[1]
     A = g["logits"].shape[1]
     net = _vector_net(D, A, H)
-    net.load_state_dict({_ours(k[len("param."):]): g[k] for k in g.files
+    net.load_state_dict({k[len("param."):]: g[k] for k in g.files
                          if k.startswith("param.")})
     cu = lambda a, dt=torch.float32: torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dt)
     keep = g["valid"].astype(np.float32)
@@ -80,8 +70,8 @@ def test_recurrent_minibatch_matches_reference_golden():
         assert rel(parts[k].numpy(), g[k]) <= 1e-4, k
     names = set()
     for name, p in net.named_parameters():
-        names.add(_theirs(name))
-        assert rel(p.grad.detach().cpu().numpy(), g["grad." + _theirs(name)]) <= 1e-4, name
+        names.add(name)
+        assert rel(p.grad.detach().cpu().numpy(), g["grad." + name]) <= 1e-4, name
     assert names == {k[len("grad."):] for k in g.files if k.startswith("grad.")}
 
 
@@ -149,7 +139,7 @@ def test_recurrent_learner_replay_equals_eager_and_oracle():
     ro = _vector_rollout(rng, n_steps, n_envs, d, a, hidden, n_steps // seq_len)
     eager = _learner(5, cfg, n_steps, n_envs, d, a, hidden, seq_len)
     graph = _learner(5, cfg, n_steps, n_envs, d, a, hidden, seq_len)
-    init = {_theirs(k): v.astype(np.float64) for k, v in eager.net.state_dict().items()}
+    init = {k: v.astype(np.float64) for k, v in eager.net.state_dict().items()}
     for lrn in (eager, graph):
         lrn.load_rollout(**ro)
         lrn.draw_permutations()
@@ -183,7 +173,7 @@ def test_recurrent_learner_replay_equals_eager_and_oracle():
     assert rel(got["loss"], np.mean(losses)) <= 1e-4
     sd = graph.net.state_dict()
     for name in sd:
-        assert rel(sd[name], params[_theirs(name)]) <= 1e-3, name
+        assert rel(sd[name], params[name]) <= 1e-3, name
     for lrn in (eager, graph):
         lrn.close()
 

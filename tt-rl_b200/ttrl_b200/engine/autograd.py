@@ -89,7 +89,7 @@ class Tensor:
 
     __slots__ = ("data", "requires_grad", "grad", "_backward", "_parents", "_op",
                  "_backward_done", "_premask", "_grad_buf", "_grad_owned", "_exact",
-                 "_fold", "__weakref__")
+                 "_fold", "_layout", "__weakref__")
 
     def __init__(self, data, requires_grad: bool = False, _parents=(), _op: str = ""):
         self.data = data
@@ -108,6 +108,10 @@ class Tensor:
         # Rows already in space-to-depth order for this fold factor (a first
         # convolution reads them directly); 1: plain NHWC rows.
         self._fold = 1
+        # A parameter stored in a device layout other than its portable one
+        # (a convolution's KRSC weight): converts optimizer state to and from
+        # the portable layout. None: the device layout is the portable one.
+        self._layout = None
 
     # -- construction ------------------------------------------------------
 

@@ -32,6 +32,7 @@ from ttrl_b200.device import context, conv_geom
 from ttrl_b200.engine.autograd import Tensor, as_device
 from ttrl_b200.engine.nn import Module
 from ttrl_b200.engine.ops import conv2d_nhwc
+from ttrl_b200.engine.packing import default_layout, solve_cp
 from ttrl_b200.engine.tensor import restore_in_place
 
 __all__ = ["Conv2d", "ConvGeometry", "ConvDoesNotFit", "conv_out_size", "input_fold"]
@@ -149,6 +150,7 @@ class Conv2d(Module):
         self.s2d = self._space_to_depth_factor()
         self.weight = Tensor.from_numpy(self._to_device_layout(weight), self.device,
                                         requires_grad=True)
+        self.weight._layout = ConvWeightLayout(self)
         if bias:
             bound = 1.0 / math.sqrt(in_channels * kernel * kernel)
             b = np.random.uniform(-bound, bound, (1, 1, 1, out_channels)).astype(np.float32)
@@ -307,6 +309,44 @@ class Conv2d(Module):
         return conv2d_nhwc(self._prepare(x), self.weight, self.bias, self._kgeom,
                            input_scale=self.input_scale, relu=True,
                            needs_input_grad=self.needs_input_grad)
+
+
+class ConvWeightLayout:
+    """Optimizer state of a convolution weight between this layer's device
+    layout (KRSC over the possibly folded kernel) and the portable forms:
+    logical OIHW, which `Adam.state_dict` writes, and the reference's
+    prepared `[1, 1, rows, cols]` matrix (ttrl_b200.engine.packing), which
+    its checkpoints hold the moments in."""
+
+    def __init__(self, conv: "Conv2d"):
+        self.oihw = tuple(int(d) for d in conv._oihw_shape)
+        self._to_device = conv._to_device_layout
+        self._from_device = conv._from_device_layout
+
+    def to_portable(self, device_array) -> np.ndarray:
+        return self._from_device(np.asarray(device_array, np.float32))
+
+    def from_stored(self, array, *, v=None) -> np.ndarray:
+        """A stored moment (OIHW or prepared) -> this layer's device layout.
+        `v`: the stored second moment beside it, which fixes a prepared
+        matrix's channel stride."""
+        a = np.asarray(array, np.float32)
+        if a.shape == self.oihw:
+            return self._to_device(a)
+        layout = solve_cp(a.shape, self.oihw, v=v)
+        return self._to_device(layout.unpack(a))
+
+    def to_stored(self, device_array, like=None, *, v_like=None) -> np.ndarray:
+        """The device moment in the form of `like` (a stored array of the
+        same moment): prepared when `like` is, OIHW otherwise."""
+        w = self.to_portable(device_array)
+        if like is None or np.shape(like) == self.oihw:
+            return w
+        return solve_cp(np.shape(like), self.oihw, v=v_like).pack(w)
+
+    def prepared(self, device_array) -> np.ndarray:
+        """The moment in the reference device library's default prepared layout."""
+        return default_layout(*self.oihw).pack(self.to_portable(device_array))
 
 
 def _first_conv(value):

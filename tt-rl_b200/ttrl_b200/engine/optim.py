@@ -142,9 +142,15 @@ class Adam(Optimizer):
             "betas": (self.b1, self.b2),
             "eps": self.eps,
             "weight_decay": self.weight_decay,
-            "m": [to_host(m) * self._m_scale for m in self.m],
-            "v": [to_host(v) * self._v_scale for v in self.v],
+            "m": [self._portable(i, to_host(m) * self._m_scale) for i, m in enumerate(self.m)],
+            "v": [self._portable(i, to_host(v) * self._v_scale) for i, v in enumerate(self.v)],
         }
+
+    def _portable(self, i: int, array: np.ndarray) -> np.ndarray:
+        """A moment in its parameter's portable layout (a convolution weight's
+        in OIHW, every other parameter's as stored)."""
+        layout = getattr(self.params[i], "_layout", None)
+        return array if layout is None else layout.to_portable(array)
 
     def load_state_dict(self, state: dict, device=None) -> None:
         if len(state["m"]) != len(self.m) or len(state["v"]) != len(self.v):
@@ -152,14 +158,27 @@ class Adam(Optimizer):
                 f"Adam.load_state_dict: checkpoint has {len(state['m'])} m and "
                 f"{len(state['v'])} v buffers, expected {len(self.m)} of each."
             )
+        device_form = {"m": [], "v": []}
         for key, buffers in (("m", self.m), ("v", self.v)):
             for i, (arr, buf) in enumerate(zip(state[key], buffers)):
+                layout = getattr(self.params[i], "_layout", None)
                 got = tuple(np.asarray(arr).shape)
-                if got != tuple(buf.shape):
+                if layout is not None:
+                    # Logical OIHW or the reference's prepared matrix; the
+                    # stored v fixes the latter's channel stride.
+                    try:
+                        arr = layout.from_stored(arr, v=state["v"][i])
+                    except ValueError as exc:
+                        raise ValueError(
+                            f"Adam.load_state_dict: {key}[{i}] has shape {got}, which is "
+                            f"neither its convolution weight's OIHW shape {layout.oihw} nor "
+                            f"a prepared matrix holding it ({exc})") from None
+                elif got != tuple(buf.shape):
                     raise ValueError(
                         f"Adam.load_state_dict: {key}[{i}] has shape {got}, which does "
                         f"not match its parameter's shape {tuple(buf.shape)}."
                     )
+                device_form[key].append(arr)
         t = int(state["t"])
         steps = [int(s) for s in state.get("steps", [t] * len(self.params))]
         lr = state.get("lr", self._lr)
@@ -186,8 +205,8 @@ class Adam(Optimizer):
         self.eps = eps
         self.weight_decay = weight_decay
         ms, vs = self._m_scale, self._v_scale
-        for i, arr in enumerate(state["m"]):
+        for i, arr in enumerate(device_form["m"]):
             restore_in_place(self.m[i], np.asarray(arr) / ms)
-        for i, arr in enumerate(state["v"]):
+        for i, arr in enumerate(device_form["v"]):
             restore_in_place(self.v[i], np.asarray(arr) / vs)
         self._dev_steps.copy_(torch.tensor(steps, dtype=torch.int32))

@@ -10,18 +10,23 @@ from ttrl_b200.nets.encoders import Encoder, image_encoder, vector_encoder
 from ttrl_b200.nets.heads import CategoricalHead, GaussianHead, QHead, ValueHead
 from ttrl_b200.nets.models import (ActorCritic, ConcatEncoder, ContinuousCritic, EncoderHead,
                                    SacNets)
+from ttrl_b200.nets.multi import MultiEncoder, single_leaf
 
 __all__ = ["build_q_net", "build_actor_critic", "build_sac_nets", "build_encoder"]
 
 
-def build_encoder(obs_shape, device=None, *, batch: int, hidden=None, scale=None, **kw):
+def build_encoder(obs_shape, device=None, *, batch: int, hidden=None, scale=None,
+                  **kw) -> MultiEncoder:
+    """The tower for one observation leaf, wrapped as the reference's
+    `MultiEncoder` (ttrl/nets/multi.py:108-145) so parameters are named
+    `towers.obs.layers.<i>.*`."""
     shape = tuple(int(v) for v in obs_shape)
     if len(shape) == 3:
-        return image_encoder(shape, device, batch=batch, hidden=hidden or 512,
-                             scale=(1.0 / 255.0) if scale is None else scale, **kw)
+        return single_leaf(image_encoder(shape, device, batch=batch, hidden=hidden or 512,
+                                         scale=(1.0 / 255.0) if scale is None else scale, **kw))
     if len(shape) == 1:
-        return vector_encoder(shape[0], device, hidden=hidden or (256, 256),
-                              scale=1.0 if scale is None else scale)
+        return single_leaf(vector_encoder(shape[0], device, hidden=hidden or (256, 256),
+                                          scale=1.0 if scale is None else scale))
     raise ValueError(f"observation shape {shape} is neither (C, H, W) nor (D,)")
 
 
@@ -45,7 +50,7 @@ def build_sac_nets(obs_dim: int, action_dim: int, device=None, *, batch: int,
         raise ValueError(f"build_sac_nets: n_critics must be >= 2, got {n_critics}")
 
     def one_critic():
-        joint = ConcatEncoder(Encoder((), obs_dim), action_dim)
+        joint = ConcatEncoder(single_leaf(Encoder((), obs_dim)), action_dim)
         layers = []
         prev = joint.out_features
         for width in critic_hidden:
@@ -54,7 +59,7 @@ def build_sac_nets(obs_dim: int, action_dim: int, device=None, *, batch: int,
         layers.append(ValueHead(prev, device))
         return ContinuousCritic(joint, Sequential(*layers))
 
-    policy_tower = vector_encoder(obs_dim, device, hidden=policy_hidden)
+    policy_tower = single_leaf(vector_encoder(obs_dim, device, hidden=policy_hidden))
     policy = EncoderHead(policy_tower, GaussianHead(policy_tower.out_features, action_dim, device))
     nets = SacNets(policy=policy,
                    critics=ModuleList([one_critic() for _ in range(n_critics)]),

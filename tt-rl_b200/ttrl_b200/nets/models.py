@@ -48,14 +48,13 @@ class ActorCritic(Module):
 class ConcatEncoder(Module):
     """concat(obs features, action) -> one row (ttrl/nets/fusion.py)."""
 
-    def __init__(self, tower, action_dim: int):
-        self.tower = tower
+    def __init__(self, encoder, action_dim: int):
+        self.encoder = encoder
         self.action_dim = int(action_dim)
-        self.out_features = int(tower.out_features) + self.action_dim
+        self.out_features = int(encoder.out_features) + self.action_dim
 
     def forward(self, obs, action):
-        feats = self.tower(_leaf(obs)) if len(self.tower) else _leaf(obs)
-        return concat([feats, action], dim=-1)
+        return concat([self.encoder(_leaf(obs)), action], dim=-1)
 
 
 class ContinuousCritic(Module):
