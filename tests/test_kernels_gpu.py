@@ -106,6 +106,10 @@ CONV_CASES = [
     (2, 9, 9, 64, 64, 3, 1, 0),      # Nature conv3
     (2, 10, 10, 8, 16, 3, 1, 1),     # padded
     (3, 9, 9, 3, 5, 3, 2, 1),        # odd channels: scalar gather path
+    # C a multiple of 32: windows by TMA im2col mode
+    (2, 21, 21, 64, 32, 2, 1, 0),    # Nature conv1 in space-to-depth form
+    (3, 11, 11, 32, 48, 3, 1, 1),    # padded; 363 pixels, 288 wgrad rows (partial tiles)
+    (2, 13, 13, 64, 32, 5, 2, 2),    # 5x5 stride 2, padded
 ]
 
 

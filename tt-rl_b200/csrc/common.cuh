@@ -129,14 +129,19 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
-// 4-D tiled TMA load, used for the sliding-window (im2col) view of an NHWC
-// activation: {inner span, output column, output row, image}.
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1,
-                                            int c2, int c3, uint32_t bar) {
+// 4-D TMA load in im2col mode from an NHWC activation: the tensor map's
+// pixelsPerColumn pixels starting at window origin (w, h) of image n, walked
+// W, then H, then N through the map's bounding box of window origins with its
+// traversal strides, each pixel displaced by the filter tap (tap_w, tap_h)
+// and contributing channelsPerPixel channels from channel c. Pixels outside
+// the tensor read as zeros.
+__device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const void* tmap, int c, int w,
+                                                   int h, int n, uint16_t tap_w, uint16_t tap_h,
+                                                   uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
+      "l"(tmap), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar), "h"(tap_w), "h"(tap_h)
       : "memory");
 }
 

@@ -41,6 +41,7 @@
 // barrier set-up overlap the previous kernel's tail, and griddepcontrol.wait
 // precedes the first global access.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -228,6 +229,21 @@ struct Loader {
         const float* src = opnd_addr(o, row0 + r, k0 + k, ok);
         cp_async4(base + kmajor_off(r, k), src, ok ? 4u : 0u);
       }
+    }
+  }
+
+  // The synthetic ones row of an MN-major operand whose stage arrived by TMA
+  // (which cannot produce it): 1.0 at every valid k of tile row
+  // `o.rows - row0`, 0.0 past the end of K. Written by the threads that split
+  // those chunks, before they read them.
+  __device__ __forceinline__ void fill_ones_row(const DevOperand& o, uint8_t* raw_gen, int row0,
+                                                int k0, int tid) const {
+    const int r = o.rows - row0;
+    if (r < 0 || r >= R || (tid % RC) != (r >> 2)) return;
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      const int k = tid / RC + i * (kThreads / RC);
+      *reinterpret_cast<float*>(raw_gen + mnmajor_off(r, k)) = k0 + k < o.kdim ? 1.f : 0.f;
     }
   }
 
@@ -506,6 +522,54 @@ __device__ __forceinline__ void tma_operand(const CUtensorMap* map, bool mn, uin
   }
 }
 
+// Window origin (input column, input row, image) of output pixel `p` of a
+// convolution operand.
+struct WindowOrigin {
+  int w, h, n;
+};
+__device__ __forceinline__ WindowOrigin window_origin(const DevOperand& o, int p) {
+  const int img = fdiv(o.f_ohw, p);
+  const int rem = p - img * o.oh * o.ow;
+  const int oy = fdiv(o.f_ow, rem);
+  const int ox = rem - oy * o.ow;
+  return {ox * o.stride - o.pad, oy * o.stride - o.pad, img};
+}
+
+// One stage of a convolution operand by TMA im2col mode. The map's pixel
+// box is 32 channels, so each load covers one filter tap (C is a multiple of
+// 32 whenever this path is taken).
+//  - conv fprop windows (K-major): 128 output pixels from `row0`, reduction
+//    columns k0 .. k0+31 = tap k0 / C, channels k0 % C .. +31.
+//  - weight-gradient windows (MN-major): R rows of (tap, channel) from
+//    `row0` in groups of 32, each group the 32 pixels k0 .. k0+31 of one
+//    tap; groups past the last row repeat the last tap (those rows of D are
+//    never stored; the bias gradient's ones row is written over them).
+template <int R>
+__device__ __forceinline__ void tma_im2col_operand(const CUtensorMap* map, const DevOperand& o,
+                                                   bool mn, uint32_t dst, int row0, int k0,
+                                                   uint32_t bar) {
+  if (!mn) {
+    const WindowOrigin wo = window_origin(o, row0);
+    const int t = fdiv(o.f_c, k0);
+    const int ky = fdiv(o.f_kw, t);
+    tma_load_im2col_4d(dst, map, k0 - t * o.c, wo.w, wo.h, wo.n,
+                       static_cast<uint16_t>(t - ky * o.kw), static_cast<uint16_t>(ky), bar);
+  } else {
+    const WindowOrigin wo = window_origin(o, k0);
+    const int last = o.kh * o.kw - 1;
+#pragma unroll
+    for (int g = 0; g < R / 32; ++g) {
+      const int r = row0 + g * 32;
+      int t = fdiv(o.f_c, r);
+      const int c = r - t * o.c;
+      if (t > last) t = last;
+      const int ky = fdiv(o.f_kw, t);
+      tma_load_im2col_4d(dst + g * 4096, map, c, wo.w, wo.h, wo.n,
+                         static_cast<uint16_t>(t - ky * o.kw), static_cast<uint16_t>(ky), bar);
+    }
+  }
+}
+
 // SMALL: a half-size footprint (about 100 KB of shared memory, <= 102
 // registers) so two CTAs share an SM; used for grids of several waves, where
 // one CTA's set-up, pipeline fill and epilogue overlap the other's main loop.
@@ -627,6 +691,7 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
     const bool a_tma = args.a_tma != 0, b_tma = args.b_tma != 0;
     const bool any_tma = a_tma || b_tma;
     const bool any_gather = !(a_tma && b_tma);
+    const bool a_ones_by_loader = (args.im2col & 1) && a_mn && oa.ones_row;
     auto issue_gathers = [&](int st, int kb) {
       const int k0 = kb * 32;
       if (!a_tma) la.issue(oa, raw_a(st), row0, k0, tid);
@@ -656,6 +721,7 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
       }
       const int s = i % S;
       if (any_tma && !mbar_wait(tfull0 + s * 8, (i / S) & 1)) timed_out = true;
+      if (a_ones_by_loader) la.fill_ones_row(oa, sgen + s * Cfg::kTile, row0, (kb0 + i) * 32, tid);
       if (split_a || split_b) {
         const int l = i % LL;
         if (i >= L) {
@@ -684,8 +750,20 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
         }
         const int k0 = (kb0 + j) * 32;
         mbar_arrive_expect_tx(tfull0 + st * 8, tma_bytes);
-        if (a_tma) tma_operand<128>(&args.tma_a, a_mn, raw_a(st), row0, k0, tfull0 + st * 8);
-        if (b_tma) tma_operand<BN>(&args.tma_b, b_mn, raw_b(st), col0, k0, tfull0 + st * 8);
+        if (a_tma) {
+          if (args.im2col & 1)
+            tma_im2col_operand<128>(&args.tma_a, args.a, a_mn, raw_a(st), row0, k0,
+                                    tfull0 + st * 8);
+          else
+            tma_operand<128>(&args.tma_a, a_mn, raw_a(st), row0, k0, tfull0 + st * 8);
+        }
+        if (b_tma) {
+          if (args.im2col & 2)
+            tma_im2col_operand<BN>(&args.tma_b, args.b, b_mn, raw_b(st), col0, k0,
+                                   tfull0 + st * 8);
+          else
+            tma_operand<BN>(&args.tma_b, b_mn, raw_b(st), col0, k0, tfull0 + st * 8);
+        }
       }
     }
   } else if (lane == 0) {
@@ -923,6 +1001,71 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     cudaGetLastError();
   });
   return fn;
+}
+
+// cuTensorMapEncodeIm2col, fetched the same way.
+static PFN_cuTensorMapEncodeIm2col_v12000 im2col_map_encoder() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Convolution operands whose windows TMA im2col mode loads (bit 0: conv
+// fprop A, bit 1: conv wgrad B). TTRL_IM2COL_TMA overrides (0 = gather both
+// with cp.async).
+static int im2col_modes() {
+  static int modes = [] {
+    const char* e = std::getenv("TTRL_IM2COL_TMA");
+    return e ? std::atoi(e) : 3;
+  }();
+  return modes;
+}
+
+// The im2col TMA map of a convolution operand (NHWC activation, C a multiple
+// of 32): pixel box of 32 channels; 128 pixels per load for fprop's windows
+// (one K-major stage), 32 for the weight gradient's (one 32-row group of an
+// MN-major stage); bounding box of window origins
+// [-pad, extent - 1 + pad - (kernel - 1)] walked with the conv stride. False
+// when the operand does not qualify (it is then gathered).
+static bool encode_im2col_map(const DevOperand& o, CUtensorMap* map) {
+  const bool fprop = o.kind == TTRL_OPND_CONV_FPROP && o.mode == kModeKVec && !o.ones_row;
+  // A weight gradient's windows operand may carry the ones row of the bias
+  // gradient: the loader warps write it into each stage after the TMA lands.
+  const bool wgrad = o.kind == TTRL_OPND_CONV_WGRAD && o.mode == kModeMNVec;
+  if (!(fprop && (im2col_modes() & 1)) && !(wgrad && (im2col_modes() & 2))) return false;
+  const int pixels = fprop ? 128 : 32;
+  if (o.c % 32 != 0 || !aligned16(o.ptr)) return false;
+  if (o.stride < 1 || o.stride > 8 || o.pad > 127 || o.kh != o.kw) return false;
+  const int upper = o.pad - (o.kw - 1);
+  if (upper < -128 || o.w + 2 * o.pad < o.kw || o.h + 2 * o.pad < o.kh) return false;
+  PFN_cuTensorMapEncodeIm2col_v12000 enc = im2col_map_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(o.c), static_cast<cuuint64_t>(o.w),
+                              static_cast<cuuint64_t>(o.h), static_cast<cuuint64_t>(o.n)};
+  const cuuint64_t row = static_cast<cuuint64_t>(o.c) * 4;
+  const cuuint64_t strides[3] = {row, row * o.w, row * o.w * o.h};
+  if (strides[2] >= (1ull << 40)) return false;
+  const int lower_corner[2] = {-o.pad, -o.pad};
+  const int upper_corner[2] = {upper, upper};
+  const cuuint32_t es[4] = {1, static_cast<cuuint32_t>(o.stride),
+                            static_cast<cuuint32_t>(o.stride), 1};
+  const CUtensorMapSwizzle sw =
+      fprop ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  const CUresult r =
+      enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(o.ptr), dims, strides,
+          lower_corner, upper_corner, 32, static_cast<cuuint32_t>(pixels), es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 // The TMA map of a dense operand whose tiles are R rows x 32 k, or false
@@ -1228,6 +1371,14 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   args.kb_per_split = s.kb_per_split;
   args.a_tma = encode_operand_map(args.a, 128, &args.tma_a) ? 1 : 0;
   args.b_tma = encode_operand_map(args.b, s.bn, &args.tma_b) ? 1 : 0;
+  if (!args.a_tma && encode_im2col_map(args.a, &args.tma_a)) {
+    args.a_tma = 1;
+    args.im2col |= 1;
+  }
+  if (!args.b_tma && !args.b.ones_row && encode_im2col_map(args.b, &args.tma_b)) {
+    args.b_tma = 1;
+    args.im2col |= 2;
+  }
   if (s.cluster) {
     args.cluster_splits = s.splits;
   } else if (s.splits > 1) {

@@ -71,7 +71,8 @@ struct GemmArgs {
   int32_t reduce_in_kernel;  // last split CTA sums the partials (else a second kernel)
   int32_t cluster_splits;    // > 1: the splits of a tile form a cluster and reduce in DSMEM
   int32_t a_tma, b_tma;      // the operand's stages arrive by TMA instead of cp.async
-  int32_t pad0;
+  int32_t im2col;            // bit 0: A (conv fprop windows), bit 1: B (conv wgrad
+                             // windows) by TMA im2col mode rather than a tiled map
   float* ws;      // split-K partials [splits][m][n], or null
   int* counters;  // split-K arrival counter per output tile
   int* status;

@@ -16,7 +16,10 @@ import torch
 
 from ttrl_b200.device import context, conv_geom
 
-CONV = {"conv1": (84, 4, 32, 8, 4), "conv2": (20, 32, 64, 4, 2), "conv3": (9, 64, 64, 3, 1)}
+#: (input extent, in channels, out channels, kernel, stride). conv1s2d is
+#: conv1 in the space-to-depth form the nets run it in (fold 4).
+CONV = {"conv1": (84, 4, 32, 8, 4), "conv1s2d": (21, 64, 32, 2, 1),
+        "conv2": (20, 32, 64, 4, 2), "conv3": (9, 64, 64, 3, 1)}
 
 
 def _conv_case(layer: str, kind: str, batch: int, reps: int) -> None:
