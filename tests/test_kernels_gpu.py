@@ -110,6 +110,9 @@ CONV_CASES = [
     (2, 21, 21, 64, 32, 2, 1, 0),    # Nature conv1 in space-to-depth form
     (3, 11, 11, 32, 48, 3, 1, 1),    # padded; 363 pixels, 288 wgrad rows (partial tiles)
     (2, 13, 13, 64, 32, 5, 2, 2),    # 5x5 stride 2, padded
+    # data gradient as one sub-pixel GEMM (no padding, stride | kernel)
+    (3, 14, 14, 32, 64, 4, 2, 0),    # 147 window rows, 4 parity classes
+    (2, 12, 12, 16, 24, 4, 2, 0),    # dY channels not a multiple of 32: gathered windows
 ]
 
 
@@ -152,6 +155,26 @@ def test_conv_dgrad_masked(case):
     dx = torch.empty((n * h * w, c), device="cuda")
     ctx.conv_dgrad(dev(dy.reshape(-1, cout)), dev(ol.oihw_to_krsc(wt)),
                    dev(mask.reshape(-1, c)), dx, geom, accumulate=False)
+    assert rel(host(dx).reshape(ref.shape), ref) <= TOL_X3
+
+
+@pytest.mark.parametrize("case", [CONV_CASES[1], CONV_CASES[2]])
+def test_conv_dgrad_accumulates_unmasked(case):
+    """The sub-pixel data gradient adding into an existing dX (a tensor read
+    by two consumers), without a mask."""
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    n, h, w, c, cout, k, s, p = case
+    _, wt, _ = _conv_inputs(case, 4)
+    geom = conv_geom(n, h, w, c, cout, k, k, s, p)
+    rng = np.random.default_rng(6)
+    dy = rng.standard_normal((n, geom.oh, geom.ow, cout)).astype(np.float32)
+    prior = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    ref = ol.conv2d_dgrad(dy.astype(np.float64), wt.astype(np.float64), (n, h, w, c), stride=s,
+                          padding=p) + prior
+    dx = dev(prior.reshape(-1, c))
+    ctx.conv_dgrad(dev(dy.reshape(-1, cout)), dev(ol.oihw_to_krsc(wt)), None, dx, geom,
+                   accumulate=True)
     assert rel(host(dx).reshape(ref.shape), ref) <= TOL_X3
 
 

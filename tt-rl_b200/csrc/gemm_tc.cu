@@ -297,6 +297,28 @@ __device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const E
                                                 const int (&r)[U], const int (&c)[U],
                                                 const float (&acc)[U], int n) {
   float add[U], mk[U], old[U];
+  long long oo[U], mo[U];  // output and mask offsets of each element
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (ex.scatter_s) {
+      const int q = fdiv(ex.f_sc, c[u]);
+      const int ch = c[u] - q * ex.scatter_c;
+      const int py = fdiv(ex.f_s, q);
+      const int px = q - py * ex.scatter_s;
+      const int img = fdiv(ex.f_ghw, r[u]);
+      const int rem = r[u] - img * ex.scatter_gh * ex.scatter_gw;
+      const int i = fdiv(ex.f_gw, rem);
+      const int j = rem - i * ex.scatter_gw;
+      const long long pix =
+          (static_cast<long long>(img) * ex.scatter_h + ex.scatter_s * i + py) * ex.scatter_w +
+          ex.scatter_s * j + px;
+      oo[u] = pix * ep.ors + static_cast<long long>(ch) * ep.ocs;
+      mo[u] = pix * ep.mrs + static_cast<long long>(ch) * ep.mcs;
+    } else {
+      oo[u] = static_cast<long long>(r[u]) * ep.ors + static_cast<long long>(c[u]) * ep.ocs;
+      mo[u] = static_cast<long long>(r[u]) * ep.mrs + static_cast<long long>(c[u]) * ep.mcs;
+    }
+  }
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     add[u] = 0.f;
@@ -311,12 +333,8 @@ __device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const E
         } else if (ep.bias_mode == TTRL_BIAS_COL) {
           add[u] = ep.bias[c[u]];
         }
-        if (ep.mask != nullptr)
-          mk[u] = ep.mask[static_cast<long long>(r[u]) * ep.mrs +
-                          static_cast<long long>(c[u]) * ep.mcs];
-        if (ep.accumulate)
-          old[u] = ep.out[static_cast<long long>(r[u]) * ep.ors +
-                          static_cast<long long>(c[u]) * ep.ocs];
+        if (ep.mask != nullptr) mk[u] = ep.mask[mo[u]];
+        if (ep.accumulate) old[u] = ep.out[oo[u]];
       }
     }
   }
@@ -334,7 +352,7 @@ __device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const E
     if (!(mk[u] > 0.f)) v = 0.f;
     if (ep.relu) v = v > 0.f ? v : 0.f;
     if (ep.accumulate) v += old[u];
-    ep.out[static_cast<long long>(r[u]) * ep.ors + static_cast<long long>(c[u]) * ep.ocs] = v;
+    ep.out[oo[u]] = v;
   }
 }
 

@@ -55,6 +55,13 @@ struct EpiExtra {
   int32_t accumulate2;
   float* out2;   // out2[c * cs2]
   int64_t cs2;
+  // Sub-pixel scatter of a transposed convolution (the direct data
+  // gradient), off when scatter_s == 0: row r = (image, i, j) of a gh x gw
+  // grid and column q * sc + ch of D is pixel (image, s*i + q / s,
+  // s*j + q % s) of an h x w output, channel ch; the output and mask
+  // addresses are pixel * (ors | mrs) + ch * (ocs | mcs).
+  int32_t scatter_s, scatter_c, scatter_h, scatter_w, scatter_gh, scatter_gw;
+  FastDiv f_sc, f_s, f_gw, f_ghw;
 };
 
 struct GemmArgs {
@@ -168,6 +175,8 @@ inline EpiExtra no_extra() {
   e.accumulate2 = 0;
   e.out2 = nullptr;
   e.cs2 = 0;
+  e.scatter_s = e.scatter_c = e.scatter_h = e.scatter_w = e.scatter_gh = e.scatter_gw = 0;
+  e.f_sc = e.f_s = e.f_gw = e.f_ghw = FastDiv{};
   return e;
 }
 

@@ -2,6 +2,7 @@
 // epilogues, plus the two non-GEMM pieces they need: the col2im gather
 // that finishes the convolution input gradient, and the uint8 frame
 // normalisation that feeds the first convolution.
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -292,7 +293,133 @@ __global__ void __launch_bounds__(256) col2im_kernel(const __grid_constant__ Col
   }
 }
 
+// ------------------------------------------- direct (sub-pixel) data gradient
+//
+// For a convolution with no padding, a stride s that divides the kernel k
+// and an input covered exactly by the windows (h = (oh - 1) s + k), the data
+// gradient splits by input-pixel parity q = (py, px) into s^2 stride-1
+// correlations of dY with sub-kernels of extent kb = k / s:
+//   dX[n, s i + py, s j + px, c]
+//     = sum_{ty, tx < kb, co} dY[n, i - (kb-1) + ty, j - (kb-1) + tx, co]
+//                              * W[co, s (kb-1-ty) + py, s (kb-1-tx) + px, c]
+// for i < h / s, j < w / s (dY read as zero outside its extent). All s^2
+// classes read the same dY windows, so the whole gradient is ONE implicit
+// GEMM: A = the windows of dY (a stride-1 conv operand, padding kb - 1),
+// B = the s^2 sub-kernels stacked into an (s^2 C) x (kb^2 Cout) matrix, and
+// the epilogue scatters column q * C + c of row (n, i, j) to its pixel. No
+// column buffer and no col2im pass.
+
+static bool direct_dgrad_enabled() {
+  static int on = [] {
+    const char* e = std::getenv("TTRL_DIRECT_DGRAD");
+    return e ? std::atoi(e) : 1;
+  }();
+  return on != 0;
+}
+
+static bool direct_dgrad_applies(const ttrl_conv_geom* g) {
+  if (!direct_dgrad_enabled()) return false;
+  const int s = g->stride, k = g->kh;
+  return g->pad == 0 && g->kh == g->kw && k % s == 0 && g->h == (g->oh - 1) * s + k &&
+         g->w == (g->ow - 1) * s + k;
+}
+
+static size_t dgrad_weights_bytes(const ttrl_conv_geom* g) {
+  const size_t n = static_cast<size_t>(g->kh) * g->kw * g->c * g->cout;
+  return (n * sizeof(float) + 255) & ~static_cast<size_t>(255);
+}
+
+static ttrl_conv_geom dgrad_window_geom(const ttrl_conv_geom* g) {
+  const int kb = g->kh / g->stride;
+  ttrl_conv_geom a;
+  std::memset(&a, 0, sizeof(a));
+  a.n = g->n;
+  a.h = g->oh;
+  a.w = g->ow;
+  a.c = g->cout;
+  a.cout = g->stride * g->stride * g->c;
+  a.kh = a.kw = kb;
+  a.stride = 1;
+  a.pad = kb - 1;
+  a.oh = g->h / g->stride;
+  a.ow = g->w / g->stride;
+  return a;
+}
+
+static ttrl_gemm_desc direct_dgrad_desc(const ttrl_conv_geom* g, int precision) {
+  const ttrl_conv_geom a = dgrad_window_geom(g);
+  const int kb = a.kh;
+  return make_desc(a.n * a.oh * a.ow, g->stride * g->stride * g->c, kb * kb * g->cout,
+                   precision);
+}
+
+// out[(q*C + c) * kb^2*Cout + (ty*kb + tx) * Cout + co]
+//   = w[co][s (kb-1-ty) + q / s][s (kb-1-tx) + q % s][c]   (w in KRSC)
+__global__ void dgrad_weights_kernel(const float* __restrict__ w, float* __restrict__ out,
+                                     int cout, int k, int c, int s, int total) {
+  pdl_trigger();
+  pdl_wait();
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int kb = k / s;
+  const int co = idx % cout;
+  int t = idx / cout;
+  const int tx = t % kb;
+  t /= kb;
+  const int ty = t % kb;
+  t /= kb;
+  const int ch = t % c;
+  const int q = t / c;
+  const int ky = s * (kb - 1 - ty) + q / s;
+  const int kx = s * (kb - 1 - tx) + q % s;
+  out[idx] = w[((static_cast<long long>(co) * k + ky) * k + kx) * c + ch];
+}
+
+static int conv_dgrad_direct(const float* dy, const float* w, const float* mask, float* dx,
+                             const ttrl_conv_geom* g, int accumulate, int precision, float* ws,
+                             size_t wsb, int* status, cudaStream_t st) {
+  const size_t wb = dgrad_weights_bytes(g);
+  float* wt = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
+  const int total = g->kh * g->kw * g->c * g->cout;
+  cudaError_t le = launch_pdl(dgrad_weights_kernel, dim3((total + 255) / 256), dim3(256), 0, st,
+                              w, wt, g->cout, g->kh, g->c, g->stride, total);
+  note_launch();
+  cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("dgrad weights launch", e);
+  const ttrl_conv_geom a = dgrad_window_geom(g);
+  ttrl_gemm_desc d = direct_dgrad_desc(g, precision);
+  d.a = conv_operand(dy, TTRL_OPND_CONV_FPROP, a);
+  d.b = dense(wt, d.n, d.k, d.k, 1);
+  d.ep = epi(dx, g->c, 1);
+  d.ep.accumulate = accumulate;
+  if (mask) {
+    d.ep.mask = mask;
+    d.ep.mrs = g->c;
+    d.ep.mcs = 1;
+  }
+  EpiExtra ex = no_extra();
+  if (g->stride > 1) {
+    ex.scatter_s = g->stride;
+    ex.scatter_c = g->c;
+    ex.scatter_h = g->h;
+    ex.scatter_w = g->w;
+    ex.scatter_gh = a.oh;
+    ex.scatter_gw = a.ow;
+    ex.f_sc = make_fastdiv(g->c);
+    ex.f_s = make_fastdiv(g->stride);
+    ex.f_gw = make_fastdiv(a.ow);
+    ex.f_ghw = make_fastdiv(a.oh * a.ow);
+  }
+  char* partials = reinterpret_cast<char*>(wt) + wb;
+  return gemm_run(d, 0, ex, reinterpret_cast<int*>(ws), reinterpret_cast<float*>(partials),
+                  wsb - kCounterBytes - wb, status, st);
+}
+
 size_t conv_dgrad_ws(const ttrl_conv_geom* g) {
+  if (direct_dgrad_applies(g)) {
+    // [counters | stacked sub-kernels | the GEMM's split-K partials]
+    return gemm_workspace_bytes(direct_dgrad_desc(g, TTRL_PREC_TF32X3)) + dgrad_weights_bytes(g);
+  }
   const size_t m = static_cast<size_t>(g->n) * g->oh * g->ow;
   const size_t kk = static_cast<size_t>(g->kh) * g->kw * g->c;
   ttrl_gemm_desc d = make_desc(static_cast<int>(m), static_cast<int>(kk), g->cout,
@@ -312,6 +439,8 @@ int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
   if (ws == nullptr || wsb < need)
     return set_error(TTRL_EWORKSPACE, "conv_dgrad: needs %zu bytes of workspace, got %zu", need,
                      wsb);
+  if (direct_dgrad_applies(g))
+    return conv_dgrad_direct(dy, w, mask, dx, g, accumulate, precision, ws, wsb, status, st);
   const size_t col_bytes =
       (static_cast<size_t>(m) * kk * sizeof(float) + 255) & ~static_cast<size_t>(255);
   float* dxcol = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
