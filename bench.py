@@ -68,7 +68,20 @@ def _args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dqn", action="store_true")
+    # tf32x3: split-TF32 (~1e-6 relative; gradients within 1e-4 of float64);
+    # tf32: one TF32 pass over round-to-nearest operands (the accuracy class
+    # of the reference's HiFi4 matmuls; ill-conditioned reductions reach
+    # ~1.5e-3 of float64).
+    ap.add_argument("--precision", choices=("tf32", "tf32x3"), default="tf32x3")
     return ap.parse_args()
+
+
+PRECISION_TEXT = {
+    "tf32": "TF32 tensor cores (tcgen05 kind::tf32, one pass), fp32 accumulate and fp32 "
+            "elementwise",
+    "tf32x3": "split-TF32 tensor cores (tcgen05 kind::tf32 x3), fp32 accumulate and fp32 "
+              "elementwise",
+}
 
 
 # ---------------------------------------------------------------- clocks
@@ -271,6 +284,7 @@ def run_ours(args):
     from ttrl_b200.engine.mesh import ParamSync
 
     ctx = context(device)
+    ctx.set_precision(args.precision)
     seed = 1234 + rank * 1_000_003
     learner, host = build_ppo(device, seed)
     sync = ParamSync([learner.net], sync_every=SYNC_EVERY, group=group)
@@ -366,7 +380,8 @@ def run_ours(args):
         out = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": K,
             "warmup": max(args.warmup, 3), "ms_per_step": total_ms / K,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.precision,
             "data": "synthetic (seeded uint8 frames U{0..255}, actions U[0,6), advantages and "
                     "returns N(0,1), old log-probs and values from the initial policy)",
             "config": {"workload": "ppo_nature_cnn_rollout8x128_mb256_epochs4",
@@ -375,8 +390,7 @@ def run_ours(args):
                        "parallelism": f"dp{world}", "sync_every_updates": SYNC_EVERY,
                        "syncs_in_timed_region": syncs,
                        "allreduce_ms_total": round(sync_ms, 4),
-                       "precision": "split-TF32 tensor cores (tcgen05 kind::tf32 x3), fp32 "
-                                    "accumulate and fp32 elementwise",
+                       "precision": PRECISION_TEXT[args.precision],
                        "l2": "flushed (256 MB write) before every timed step"},
             "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "steps": E},
@@ -387,8 +401,9 @@ def run_ours(args):
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"],
                 "traffic": NCU_TRAFFIC_BYTES.get(dom[0]),
-                "peak_source": f"{peaks['source']} dense bf16 (TF32 dense is half; split-TF32 "
-                               "issues 3 MMAs per product)",
+                "peak_source": f"{peaks['source']} dense bf16 (TF32 dense is half"
+                               + ("; split-TF32 issues 3 MMAs per product)"
+                                  if args.precision == "tf32x3" else ")"),
                 "whole_step_tflops": step_tflops,
             },
             "kernel_times_us": {f"{n}#{i}": round(t * 1e6, 2) for i, (n, _, t) in enumerate(prof)},
@@ -396,8 +411,18 @@ def run_ours(args):
         }
         if world == 1 and not args.no_dqn:
             out["dqn"] = bench_dqn(device, args)
+            # The same update at the other contraction precision, for reference.
+            other = "tf32x3" if args.precision == "tf32" else "tf32"
+            ctx.set_precision(other)
+            alt = bench_dqn(device, args)
+            ctx.set_precision(args.precision)
+            out["dqn"]["precision"] = args.precision
+            out["dqn"]["other_precision"] = {"precision": other, "value": alt["value"],
+                                             "ms_per_update": alt["ms_per_update"]}
             out["sac"] = bench_sac(device, args)
+            out["sac"]["precision"] = args.precision
             out["recurrent_ppo"] = bench_recurrent(device, args)
+            out["recurrent_ppo"]["precision"] = args.precision
         if world == 1 and not args.no_cpu_baseline:
             times = cpu_ppo_steps(2, seed=2)
             t = statistics.median(times)

@@ -134,16 +134,17 @@ def dqn_loss_head(q, q_sel, q_tgt, actions, rewards, dones, discounts, *, delta=
 
 
 def dqn_update(online, target, obs, next_obs, actions, rewards, dones, discounts, *,
-               double=True, delta=1.0, adam_state=None, lr=1e-4, eps=1.5e-4, t=1):
+               double=True, delta=1.0, adam_state=None, lr=1e-4, eps=1.5e-4, t=1, gates=None):
     """One DQN update. obs/next_obs are raw NHWC [B, H, W, C]. Returns
-    (metrics, grads, new_params, new_adam_state)."""
+    (metrics, grads, new_params, new_adam_state). `gates`: the device's ReLU
+    masks of the online forward on obs (see nature_backward)."""
     outs, cache = nature_forward(online, obs)
     q = outs["q"]
     q_tgt = nature_forward(target, next_obs)[0]["q"]
     q_sel = nature_forward(online, next_obs)[0]["q"] if double else q_tgt
     loss, mean_q, dq, _, nxt = dqn_loss_head(q, q_sel, q_tgt, actions, rewards, dones,
                                              discounts, delta=delta)
-    grads = nature_backward(online, cache, {"q": dq})
+    grads = nature_backward(online, cache, {"q": dq}, gates=gates)
     grad_sq = sum(float(np.sum(np.asarray(g, np.float64) ** 2)) for g in grads.values())
     new_params, new_state = {}, {}
     for k in online:

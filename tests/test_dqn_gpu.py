@@ -60,11 +60,42 @@ def _step_fn(online, target):
                                           huber_delta=1.0)
 
 
-def test_dqn_update_matches_oracle_eager():
+@pytest.mark.parametrize("precision,mode", [("tf32x3", "eager"), ("tf32", "traced_fwd_bwd")])
+def test_dqn_update_matches_oracle(precision, mode):
+    """Split-TF32 eagerly at the tolerances above; one TF32 pass replayed
+    from the graph (the bench's configuration) at the spec's 1e-3 for TF32
+    GEMM paths, the accuracy class of the reference's own HiFi4 matmuls
+    (ttrl/engine/ops/matmul.py:14-20), for loss, gradients and post-Adam
+    parameters alike."""
+    from ttrl_b200.device import context
+    ctx = context("cuda") if torch.cuda.is_available() else None
+    saved = ctx.precision if ctx else None
+    try:
+        if ctx:
+            ctx.set_precision(precision)
+        _dqn_update_check(mode, *((1e-5, 1e-4, TOL_GRAD, TOL_PARAM) if precision == "tf32x3"
+                                  else (1e-3, 1e-3, 1e-3, 1e-3)),
+                          device_relu=precision == "tf32")
+    finally:
+        if ctx:
+            ctx.precision = saved
+
+
+def _dqn_update_check(mode, tol_loss, tol_sq, tol_grad, tol_param, device_relu=False):
     from ttrl_b200.engine.step import TrainStep
     rng, online_p, target_p, online, target, opt, inputs = _setup()
     batch = dqn_batch(rng)
-    step = TrainStep(_step_fn(online, target), inputs, "cuda", optimizer=opt, mode="eager")
+    gates = None
+    if device_relu:
+        # The device's own ReLU masks (before the update changes the weights):
+        # at ~1e-4 forward error a pre-activation within rounding of zero may
+        # take the other side than in float64, and the oracle follows the
+        # device there instead of charging that rank-1 term to the GEMMs.
+        from ttrl_b200.engine.autograd import Tensor
+        from tests.helpers import device_gates
+        x = nchw_to_nhwc(batch[0]).astype(np.float32)
+        gates = device_gates(online, Tensor(torch.from_numpy(x.reshape(1, 1, -1, 4)).cuda()))
+    step = TrainStep(_step_fn(online, target), inputs, "cuda", optimizer=opt, mode=mode)
     _load(step, batch)
     grads_before = None
     metrics = step.run()
@@ -74,20 +105,21 @@ def test_dqn_update_matches_oracle_eager():
     m, grads, new_p, _ = ref.dqn_update(
         f64, t64, nchw_to_nhwc(obs).astype(np.float64), nchw_to_nhwc(next_obs).astype(np.float64),
         act, rewards.astype(np.float64), dones.astype(np.float64), discounts.astype(np.float64),
-        lr=LR, eps=EPS)
-    assert rel(metrics["loss"], m["loss"]) <= 1e-5
+        lr=LR, eps=EPS, gates=gates)
+    assert rel(metrics["loss"], m["loss"]) <= tol_loss
     # mean Q sits near zero (a mean of mixed-sign values): compare on the
     # scale of the Q values rather than of their mean.
-    assert abs(float(metrics["mean_q"].reshape(-1)[0]) - m["mean_q"]) <= 1e-6
-    assert rel(metrics["grad_sq"], m["grad_sq"]) <= 1e-4
+    assert abs(float(metrics["mean_q"].reshape(-1)[0]) - m["mean_q"]) <= tol_loss * 0.1
+    assert rel(metrics["grad_sq"], m["grad_sq"]) <= tol_sq
     named_g = nature_state_dict(grads)
     for name, g in grads_in_state_layout(online).items():
         want = named_g[name]
-        assert rel(g.reshape(want.shape), want) <= TOL_GRAD, name
+        assert rel(g.reshape(want.shape), want) <= tol_grad, name
     sd = online.state_dict()
     want_p = nature_state_dict(new_p)
     for name in sd:
-        assert rel(sd[name], want_p[name]) <= TOL_PARAM, name
+        assert rel(sd[name], want_p[name]) <= tol_param, name
+    step.close()
     del grads_before
 
 

@@ -216,6 +216,21 @@ def test_conv_wgrad_split_k_is_deterministic():
         assert np.array_equal(dw, outs[0][0]) and np.array_equal(db, outs[0][1])
 
 
+def test_tf32_single_pass_rounds_to_nearest():
+    """All-positive operands: a truncating tf32 conversion would bias every
+    product low by about 2^-10 and the sums by ~1e-3 relative; rounding to
+    nearest leaves an unbiased error orders of magnitude smaller."""
+    from ttrl_b200 import _lib
+    ctx = _ctx()
+    rng = np.random.default_rng(12)
+    x = rng.random((128, 2048)).astype(np.float32)
+    w = rng.random((2048, 64)).astype(np.float32)
+    ref = x.astype(np.float64) @ w.astype(np.float64)
+    y = torch.empty((128, 64), device="cuda")
+    ctx.linear_fwd(dev(x), dev(w), None, y, relu=False, precision=_lib.PREC_TF32)
+    assert rel(host(y), ref) <= 2e-4
+
+
 def test_tf32_single_pass_mode_is_looser_but_close():
     from ttrl_b200 import _lib
     ctx = _ctx()

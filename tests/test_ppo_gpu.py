@@ -78,13 +78,32 @@ def test_ppo_rollout_update_matches_oracle(epochs):
     learner.close()
 
 
-def test_ppo_minibatch_gradients_match_oracle():
+@pytest.mark.parametrize("precision", ["tf32x3", "tf32"])
+def test_ppo_minibatch_gradients_match_oracle(precision):
+    """Split-TF32 to 1e-4 (gradients) and 1e-5 (loss terms). One TF32 pass
+    (the accuracy class of the reference's own HiFi4 matmuls,
+    ttrl/engine/ops/matmul.py:14-20) to 1e-3 on the loss terms and 2e-3 on
+    the gradients: the value head's weight gradient sums 256 mixed-sign
+    value errors against non-negative features, a reduction that turns the
+    ~1e-4 forward error into 1.4e-3 of the float64 result."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from ttrl_b200.algos.ppo import PPOConfig, objective
+    from ttrl_b200.device import context
     from ttrl_b200.engine.autograd import Tensor
     from ttrl_b200.nets import build_actor_critic
     from tests.helpers import TOL_GRAD
+    tol_grad, tol_loss = (TOL_GRAD, 1e-5) if precision == "tf32x3" else (2e-3, 1e-3)
+    ctx = context("cuda")
+    saved = ctx.precision
+    ctx.set_precision(precision)
+    try:
+        _minibatch_check(PPOConfig, objective, Tensor, build_actor_critic, tol_grad, tol_loss)
+    finally:
+        ctx.precision = saved
+
+
+def _minibatch_check(PPOConfig, objective, Tensor, build_actor_critic, tol_grad, tol_loss):
 
     rng = np.random.default_rng(21)
     p = ref.nature_params(rng, heads=(("pi", 6), ("v", 1)))
@@ -111,10 +130,10 @@ def test_ppo_minibatch_gradients_match_oracle():
     from tests.helpers import device_gates
     gates = device_gates(net, rows)
     grads = ref.nature_backward(f64, cache, {"pi": dl, "v": dv}, gates=gates)
-    assert rel(loss.numpy(), rl) <= 1e-5
+    assert rel(loss.numpy(), rl) <= tol_loss
     for k in ("policy_loss", "value_loss", "entropy"):
-        assert rel(parts[k].numpy(), rparts[k]) <= 1e-5, k
-    assert rel(new_logp.numpy().reshape(-1), rlogp) <= 1e-5
+        assert rel(parts[k].numpy(), rparts[k]) <= tol_loss, k
+    assert rel(new_logp.numpy().reshape(-1), rlogp) <= tol_loss
     named = nature_state_dict(grads, heads=("pi", "v"))
     for name, g in grads_in_state_layout(net).items():
-        assert rel(g.reshape(named[name].shape), named[name]) <= TOL_GRAD, name
+        assert rel(g.reshape(named[name].shape), named[name]) <= tol_grad, name

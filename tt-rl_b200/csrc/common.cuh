@@ -257,6 +257,15 @@ __device__ __forceinline__ float tf32_low(float x) {
   return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
+// x rounded to the nearest tf32 value (ties away from zero), as an fp32
+// bit pattern with the low 13 mantissa bits clear. A single-pass tf32 MMA
+// would otherwise truncate, a bias that accumulates along the reduction.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
   lo = x - hi;

@@ -26,7 +26,9 @@
 // Precision: TTRL_PREC_TF32X3 accumulates hi*hi + hi*lo + lo*hi. The MMA
 // reads fp32 operands and uses their tf32 part, so the raw stage is the high
 // part and only lo = x - tf32(x) is written; this reproduces fp32 products
-// to ~1e-6 relative. TTRL_PREC_TF32 issues a single pass.
+// to ~1e-6 relative. TTRL_PREC_TF32 issues a single pass over operands the
+// loader warps first round to the nearest tf32 in shared memory (the MMA's
+// own truncation is biased and its error would accumulate along K).
 //
 // Split-K (blockIdx.z): up to 16 splits run as one thread-block cluster and
 // reduce their partial tiles through distributed shared memory in split
@@ -244,6 +246,35 @@ struct Loader {
     for (int i = 0; i < P; ++i) {
       const int k = tid / RC + i * (kThreads / RC);
       *reinterpret_cast<float*>(raw_gen + mnmajor_off(r, k)) = k0 + k < o.kdim ? 1.f : 0.f;
+    }
+  }
+
+  // Single-pass precision: round the chunks this thread owns (the ones
+  // `split` would read) to tf32 in place.
+  __device__ __forceinline__ void round_in_place(const DevOperand& o, uint8_t* raw_gen,
+                                                 int tid) const {
+    if (o.mode == kModeKVec || o.mode == kModeMNVec) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const uint32_t off = o.mode == kModeKVec
+                                 ? kmajor_off((tid >> 3) + i * 32, (tid & 7) * 4)
+                                 : mnmajor_off((tid % RC) * 4, tid / RC + i * (kThreads / RC));
+        float4* p = reinterpret_cast<float4*>(raw_gen + off);
+        float4 x = *p;
+        x.x = tf32_round(x.x);
+        x.y = tf32_round(x.y);
+        x.z = tf32_round(x.z);
+        x.w = tf32_round(x.w);
+        *p = x;
+      }
+    } else {
+      const bool rows_fast = o.mode == kModeScalarR;
+      for (int t = tid; t < R * 32; t += kThreads) {
+        const int r = rows_fast ? t % R : t >> 5;
+        const int k = rows_fast ? t / R : t & 31;
+        float* p = reinterpret_cast<float*>(raw_gen + kmajor_off(r, k));
+        *p = tf32_round(*p);
+      }
     }
   }
 
@@ -679,6 +710,8 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
   const bool b_mn = args.b.mode == kModeMNVec;
   const bool split_a = SPLIT && !args.a.exact;
   const bool split_b = SPLIT && !args.b.exact;
+  const bool round_a = !SPLIT && !args.a.exact;
+  const bool round_b = !SPLIT && !args.b.exact;
   bool timed_out = false;
 
   tc_fence_before();
@@ -740,6 +773,8 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
       const int s = i % S;
       if (any_tma && !mbar_wait(tfull0 + s * 8, (i / S) & 1)) timed_out = true;
       if (a_ones_by_loader) la.fill_ones_row(oa, sgen + s * Cfg::kTile, row0, (kb0 + i) * 32, tid);
+      if (round_a) la.round_in_place(oa, sgen + s * Cfg::kTile, tid);
+      if (round_b) lb.round_in_place(ob, sgen + s * Cfg::kTile + Cfg::kABytes, tid);
       if (split_a || split_b) {
         const int l = i % LL;
         if (i >= L) {

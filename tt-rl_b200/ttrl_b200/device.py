@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -29,10 +30,12 @@ __all__ = ["DeviceContext", "context", "conv_geom", "PRECISION", "SIDE_LANES"]
 #: Side streams a context keeps (lanes 1..SIDE_LANES).
 SIDE_LANES = 2
 
-#: Precision of every tensor-core contraction. Split-TF32 reproduces fp32
-#: products to ~1e-6 relative, which is what lets gradients match the
-#: fp32 reference well inside the 1e-3 budget.
-PRECISION = _lib.PREC_TF32X3
+#: Precision of every tensor-core contraction. Split-TF32 (the default)
+#: reproduces fp32 products to ~1e-6 relative, well inside the 1e-3 budget
+#: for TF32 GEMM paths; TTRL_PRECISION=tf32 selects one TF32 pass (about
+#: 1e-3 relative per product, half the tensor-core work).
+PRECISION = (_lib.PREC_TF32 if os.environ.get("TTRL_PRECISION", "").lower() == "tf32"
+             else _lib.PREC_TF32X3)
 
 _CONTEXTS: dict[int, "DeviceContext"] = {}
 
@@ -144,6 +147,9 @@ class DeviceContext:
         # Weight-gradient GEMMs of leaf parameters run on the side lanes
         # during backward, beside the data-gradient chain.
         self.concurrent = True
+        # Contraction precision of every GEMM this context launches (a call
+        # may override it); set_precision changes it.
+        self.precision = PRECISION
         # When a list, every GEMM-family call appends (name, flops, start, end).
         self.profile = None
         for lane in range(SIDE_LANES + 1):
@@ -253,29 +259,44 @@ class DeviceContext:
 
     # -- linear ----------------------------------------------------------
 
-    def linear_fwd(self, x, w, b, y, relu: bool, precision: int = PRECISION) -> None:
+    def _prec(self, precision: int | None) -> int:
+        return self.precision if precision is None else int(precision)
+
+    def set_precision(self, name: str) -> None:
+        """'tf32x3' (split-TF32, ~1e-6 relative) or 'tf32' (one pass, ~1e-3
+        relative: the accuracy class of the reference's HiFi4 matmuls,
+        ttrl/engine/ops/matmul.py:14-20). Affects launches recorded after it."""
+        table = {"tf32x3": _lib.PREC_TF32X3, "tf32": _lib.PREC_TF32}
+        if name not in table:
+            raise ValueError(f"precision must be one of {sorted(table)}, got {name!r}")
+        self.precision = table[name]
+
+    def linear_fwd(self, x, w, b, y, relu: bool, precision: int | None = None) -> None:
+        prec = self._prec(precision)
         m, k = x.shape[-2], x.shape[-1]
         n = w.shape[1]
         ws, wsb = self.workspace()
         with self._timed(f"linear_fwd[{m}x{k}x{n}]", 2 * m * k * n):
             check(lib().ttrl_linear_fwd(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")),
                                         _ptr(_f32(b, "b")), _ptr(_f32(y, "y")), m, k, n,
-                                        int(relu), precision, ws, wsb, self.status_ptr(),
+                                        int(relu), prec, ws, wsb, self.status_ptr(),
                                         self.stream), "ttrl_linear_fwd")
 
     def linear_dgrad(self, g, w, mask, dx, accumulate: bool,
-                     precision: int = PRECISION) -> None:
+                     precision: int | None = None) -> None:
+        prec = self._prec(precision)
         m, n = g.shape[-2], g.shape[-1]
         k = w.shape[0]
         ws, wsb = self.workspace()
         with self._timed(f"linear_dgrad[{m}x{k}x{n}]", 2 * m * k * n):
             check(lib().ttrl_linear_dgrad(_ptr(_f32(g, "g")), _ptr(_f32(w, "w")),
                                           _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")), m, k, n,
-                                          int(accumulate), precision, ws, wsb, self.status_ptr(),
+                                          int(accumulate), prec, ws, wsb, self.status_ptr(),
                                           self.stream), "ttrl_linear_dgrad")
 
     def linear_wgrad(self, x, g, dw, db, accumulate: bool, accumulate_db: bool,
-                     precision: int = PRECISION) -> None:
+                     precision: int | None = None) -> None:
+        prec = self._prec(precision)
         m, k = x.shape[-2], x.shape[-1]
         n = g.shape[-1]
         need = lib().ttrl_linear_wgrad_workspace_bytes(m, k, n)
@@ -283,24 +304,26 @@ class DeviceContext:
         with self._timed(f"linear_wgrad[{m}x{k}x{n}]", 2 * m * k * n):
             check(lib().ttrl_linear_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(g, "g")),
                                           _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), m, k, n,
-                                          int(accumulate), int(accumulate_db), precision, ws, wsb,
+                                          int(accumulate), int(accumulate_db), prec, ws, wsb,
                                           self.status_ptr(), self.stream), "ttrl_linear_wgrad")
 
     # -- conv ------------------------------------------------------------
 
     def conv_fprop(self, x, w, b, y, geom: Geom, alpha: float, relu: bool,
-                   precision: int = PRECISION) -> None:
+                   precision: int | None = None) -> None:
+        prec = self._prec(precision)
         g = geom.c_struct()
         ws, wsb = self.workspace()
         with self._timed(f"conv_fprop[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
                          _conv_flops(geom)):
             check(lib().ttrl_conv_fprop(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")), _ptr(_f32(b, "b")),
                                         _ptr(_f32(y, "y")), ctypes.byref(g), float(alpha),
-                                        int(relu), precision, ws, wsb, self.status_ptr(),
+                                        int(relu), prec, ws, wsb, self.status_ptr(),
                                         self.stream), "ttrl_conv_fprop")
 
     def conv_dgrad(self, dy, w, mask, dx, geom: Geom, accumulate: bool,
-                   precision: int = PRECISION) -> None:
+                   precision: int | None = None) -> None:
+        prec = self._prec(precision)
         g = geom.c_struct()
         need = lib().ttrl_conv_dgrad_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
@@ -308,11 +331,12 @@ class DeviceContext:
                          _conv_flops(geom)):
             check(lib().ttrl_conv_dgrad(_ptr(_f32(dy, "dy")), _ptr(_f32(w, "w")),
                                         _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
-                                        ctypes.byref(g), int(accumulate), precision, ws, wsb,
+                                        ctypes.byref(g), int(accumulate), prec, ws, wsb,
                                         self.status_ptr(), self.stream), "ttrl_conv_dgrad")
 
     def conv_wgrad(self, x, dy, dw, db, geom: Geom, alpha: float, accumulate: bool,
-                   accumulate_db: bool, precision: int = PRECISION) -> None:
+                   accumulate_db: bool, precision: int | None = None) -> None:
+        prec = self._prec(precision)
         g = geom.c_struct()
         need = lib().ttrl_conv_wgrad_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
@@ -321,7 +345,7 @@ class DeviceContext:
             check(lib().ttrl_conv_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(dy, "dy")),
                                         _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), ctypes.byref(g),
                                         float(alpha), int(accumulate), int(accumulate_db),
-                                        precision, ws, wsb, self.status_ptr(), self.stream),
+                                        prec, ws, wsb, self.status_ptr(), self.stream),
                   "ttrl_conv_wgrad")
 
     def u8_to_f32(self, frames, index, out, scale: float = 1.0, fold: int = 1) -> None:
