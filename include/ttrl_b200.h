@@ -213,6 +213,25 @@ int ttrl_conv_dgrad(const float* dy, const float* w, const float* mask, float* d
                     size_t workspace_bytes, int* status, ttrl_stream_t stream);
 size_t ttrl_conv_dgrad_workspace_bytes(const ttrl_conv_geom* g);
 
+/* The same data gradient in two steps, for a caller that prepares the
+ * weights off its critical path (they change only at optimizer steps).
+ * Applies to unpadded convolutions whose stride divides the kernel and whose
+ * windows cover the input exactly; other geometries return TTRL_EUNSUPPORTED
+ * (and ttrl_conv_dgrad_weights_bytes returns 0). out receives the s^2
+ * stacked, flipped sub-kernels ((s*s*Cin) x (kb*kb*Cout), kb = KH / s) of
+ * w[Cout][KH][KW][Cin]; ttrl_conv_dgrad_prepared then computes dx from dy and
+ * them as one sub-pixel GEMM, with ttrl_conv_dgrad's mask and accumulate
+ * semantics. Replace input_grad (ttrl/engine/conv/backward.py:33-42) and
+ * the weight transform inside it (ttrl/engine/conv/transform.py:71-129). */
+size_t ttrl_conv_dgrad_weights_bytes(const ttrl_conv_geom* g);
+int ttrl_conv_dgrad_weights(const float* w, float* out, const ttrl_conv_geom* g,
+                            ttrl_stream_t stream);
+int ttrl_conv_dgrad_prepared(const float* dy, const float* wt, const float* mask, float* dx,
+                             const ttrl_conv_geom* g, int accumulate, int precision,
+                             float* workspace, size_t workspace_bytes, int* status,
+                             ttrl_stream_t stream);
+size_t ttrl_conv_dgrad_prepared_workspace_bytes(const ttrl_conv_geom* g);
+
 /* dw[Cout][KH][KW][Cin] (=|+=) alpha * sum_m dy[m][o] * x_col[m][(ky,kx,c)]
  * and, when db != NULL, db[Cout] (=|+=) sum_m dy[m][o].
  * Replaces weight_grad (ttrl/engine/conv/backward.py:45-78) and the bias

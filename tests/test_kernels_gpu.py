@@ -179,6 +179,34 @@ def test_conv_dgrad_accumulates_unmasked(case):
 
 
 @pytest.mark.parametrize("case", CONV_CASES)
+def test_conv_dgrad_two_step_equals_one_call(case):
+    """ttrl_conv_dgrad_weights + ttrl_conv_dgrad_prepared reproduce
+    ttrl_conv_dgrad bit for bit where the sub-pixel path applies, and refuse
+    (0 bytes) where it does not."""
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    n, h, w, c, cout, k, s, p = case
+    _, wt, _ = _conv_inputs(case, 7)
+    geom = conv_geom(n, h, w, c, cout, k, k, s, p)
+    nbytes = ctx.conv_dgrad_weights_bytes(geom)
+    direct = p == 0 and k % s == 0 and h == (geom.oh - 1) * s + k and w == (geom.ow - 1) * s + k
+    assert (nbytes > 0) == direct
+    if not direct:
+        return
+    rng = np.random.default_rng(8)
+    dy = dev(rng.standard_normal((n * geom.oh * geom.ow, cout)).astype(np.float32))
+    mask = dev(rng.standard_normal((n * h * w, c)).astype(np.float32))
+    krsc = dev(ol.oihw_to_krsc(wt))
+    one = torch.empty((n * h * w, c), device="cuda")
+    ctx.conv_dgrad(dy, krsc, mask, one, geom, accumulate=False)
+    stacked = torch.empty(nbytes // 4, device="cuda")
+    ctx.conv_dgrad_weights(krsc, stacked, geom)
+    two = torch.empty_like(one)
+    ctx.conv_dgrad_prepared(dy, stacked, mask, two, geom, accumulate=False)
+    assert torch.equal(one, two)
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
 def test_conv_wgrad_with_bias_grad(case):
     from ttrl_b200.device import conv_geom
     ctx = _ctx()

@@ -37,6 +37,11 @@ int conv_fprop(const float*, const float*, const float*, float*, const ttrl_conv
 int conv_dgrad(const float*, const float*, const float*, float*, const ttrl_conv_geom*, int, int,
                float*, size_t, int*, cudaStream_t);
 size_t conv_dgrad_ws(const ttrl_conv_geom*);
+int conv_dgrad_weights(const float*, float*, const ttrl_conv_geom*, cudaStream_t);
+size_t conv_dgrad_weights_bytes(const ttrl_conv_geom*);
+int conv_dgrad_prepared(const float*, const float*, const float*, float*, const ttrl_conv_geom*,
+                        int, int, float*, size_t, int*, cudaStream_t);
+size_t conv_dgrad_prepared_ws(const ttrl_conv_geom*);
 int conv_wgrad(const float*, const float*, float*, float*, const ttrl_conv_geom*, float, int, int,
                int, float*, size_t, int*, cudaStream_t);
 size_t conv_wgrad_ws(const ttrl_conv_geom*);
@@ -133,6 +138,27 @@ int ttrl_conv_dgrad(const float* dy, const float* w, const float* mask, float* d
 
 size_t ttrl_conv_dgrad_workspace_bytes(const ttrl_conv_geom* g) {
   return g ? conv_dgrad_ws(g) : 0;
+}
+
+size_t ttrl_conv_dgrad_weights_bytes(const ttrl_conv_geom* g) {
+  return g ? conv_dgrad_weights_bytes(g) : 0;
+}
+
+int ttrl_conv_dgrad_weights(const float* w, float* out, const ttrl_conv_geom* g,
+                            ttrl_stream_t stream) {
+  return conv_dgrad_weights(w, out, g, TTRL_STREAM(stream));
+}
+
+int ttrl_conv_dgrad_prepared(const float* dy, const float* wt, const float* mask, float* dx,
+                             const ttrl_conv_geom* g, int accumulate, int precision,
+                             float* workspace, size_t workspace_bytes, int* status,
+                             ttrl_stream_t stream) {
+  return conv_dgrad_prepared(dy, wt, mask, dx, g, accumulate, precision, workspace,
+                             workspace_bytes, status, TTRL_STREAM(stream));
+}
+
+size_t ttrl_conv_dgrad_prepared_workspace_bytes(const ttrl_conv_geom* g) {
+  return g ? conv_dgrad_prepared_ws(g) : 0;
 }
 
 int ttrl_conv_wgrad(const float* x, const float* dy, float* dw, float* db,

@@ -375,17 +375,76 @@ __global__ void dgrad_weights_kernel(const float* __restrict__ w, float* __restr
   out[idx] = w[((static_cast<long long>(co) * k + ky) * k + kx) * c + ch];
 }
 
+int conv_dgrad_weights(const float* w, float* out, const ttrl_conv_geom* g, cudaStream_t st) {
+  int rc = check_conv(g);
+  if (rc) return rc;
+  if (!direct_dgrad_applies(g))
+    return set_error(TTRL_EUNSUPPORTED, "conv_dgrad_weights: this geometry takes the column path");
+  if (!w || !out) return set_error(TTRL_EINVAL, "conv_dgrad_weights: null pointer");
+  const int total = g->kh * g->kw * g->c * g->cout;
+  const cudaError_t le = launch_pdl(dgrad_weights_kernel, dim3((total + 255) / 256), dim3(256), 0,
+                                    st, w, out, g->cout, g->kh, g->c, g->stride, total);
+  note_launch();
+  const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("dgrad weights launch", e);
+}
+
+size_t conv_dgrad_weights_bytes(const ttrl_conv_geom* g) {
+  return direct_dgrad_applies(g) ? dgrad_weights_bytes(g) : 0;
+}
+
+size_t conv_dgrad_prepared_ws(const ttrl_conv_geom* g) {
+  return direct_dgrad_applies(g) ? gemm_workspace_bytes(direct_dgrad_desc(g, TTRL_PREC_TF32X3))
+                                 : 0;
+}
+
+// The sub-pixel GEMM over stacked sub-kernels `wt` (conv_dgrad_weights);
+// workspace [counters | split-K partials].
+int conv_dgrad_prepared(const float* dy, const float* wt, const float* mask, float* dx,
+                        const ttrl_conv_geom* g, int accumulate, int precision, float* ws,
+                        size_t wsb, int* status, cudaStream_t st) {
+  int rc = check_conv(g);
+  if (rc) return rc;
+  if (!direct_dgrad_applies(g))
+    return set_error(TTRL_EUNSUPPORTED, "conv_dgrad_prepared: this geometry takes the column path");
+  const size_t need = conv_dgrad_prepared_ws(g);
+  if (ws == nullptr || wsb < need)
+    return set_error(TTRL_EWORKSPACE, "conv_dgrad_prepared: needs %zu bytes of workspace, got %zu",
+                     need, wsb);
+  const ttrl_conv_geom a = dgrad_window_geom(g);
+  ttrl_gemm_desc d = direct_dgrad_desc(g, precision);
+  d.a = conv_operand(dy, TTRL_OPND_CONV_FPROP, a);
+  d.b = dense(wt, d.n, d.k, d.k, 1);
+  d.ep = epi(dx, g->c, 1);
+  d.ep.accumulate = accumulate;
+  if (mask) {
+    d.ep.mask = mask;
+    d.ep.mrs = g->c;
+    d.ep.mcs = 1;
+  }
+  EpiExtra ex = no_extra();
+  if (g->stride > 1) {
+    ex.scatter_s = g->stride;
+    ex.scatter_c = g->c;
+    ex.scatter_h = g->h;
+    ex.scatter_w = g->w;
+    ex.scatter_gh = a.oh;
+    ex.scatter_gw = a.ow;
+    ex.f_sc = make_fastdiv(g->c);
+    ex.f_s = make_fastdiv(g->stride);
+    ex.f_gw = make_fastdiv(a.ow);
+    ex.f_ghw = make_fastdiv(a.oh * a.ow);
+  }
+  return gemm_run_ws(d, 0, ex, ws, wsb, status, st);
+}
+
 static int conv_dgrad_direct(const float* dy, const float* w, const float* mask, float* dx,
                              const ttrl_conv_geom* g, int accumulate, int precision, float* ws,
                              size_t wsb, int* status, cudaStream_t st) {
   const size_t wb = dgrad_weights_bytes(g);
   float* wt = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kCounterBytes);
-  const int total = g->kh * g->kw * g->c * g->cout;
-  cudaError_t le = launch_pdl(dgrad_weights_kernel, dim3((total + 255) / 256), dim3(256), 0, st,
-                              w, wt, g->cout, g->kh, g->c, g->stride, total);
-  note_launch();
-  cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error("dgrad weights launch", e);
+  int rc = conv_dgrad_weights(w, wt, g, st);
+  if (rc) return rc;
   const ttrl_conv_geom a = dgrad_window_geom(g);
   ttrl_gemm_desc d = direct_dgrad_desc(g, precision);
   d.a = conv_operand(dy, TTRL_OPND_CONV_FPROP, a);

@@ -110,6 +110,11 @@ _SIGNATURES = {
     "ttrl_conv_dgrad": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ConvGeom), _c_int, _c_int,
                                  _vp, _c_size, _vp, _vp]),
     "ttrl_conv_dgrad_workspace_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),
+    "ttrl_conv_dgrad_weights_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),
+    "ttrl_conv_dgrad_weights": (_c_int, [_vp, _vp, ctypes.POINTER(ConvGeom), _vp]),
+    "ttrl_conv_dgrad_prepared": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ConvGeom), _c_int,
+                                          _c_int, _vp, _c_size, _vp, _vp]),
+    "ttrl_conv_dgrad_prepared_workspace_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),
     "ttrl_conv_wgrad": (_c_int, [_vp, _vp, _vp, _vp, ctypes.POINTER(ConvGeom), _c_float, _c_int,
                                  _c_int, _c_int, _vp, _c_size, _vp, _vp]),
     "ttrl_conv_wgrad_workspace_bytes": (_c_size, [ctypes.POINTER(ConvGeom)]),

@@ -25,10 +25,15 @@ import torch
 from ttrl_b200 import _lib
 from ttrl_b200._lib import check, lib
 
-__all__ = ["DeviceContext", "context", "conv_geom", "PRECISION", "SIDE_LANES"]
+__all__ = ["DeviceContext", "context", "conv_geom", "PRECISION", "SIDE_LANES", "WEIGHT_LANES",
+           "PREP_LANE"]
 
-#: Side streams a context keeps (lanes 1..SIDE_LANES).
-SIDE_LANES = 2
+#: Side streams a context keeps (lanes 1..SIDE_LANES). Weight gradients are
+#: dealt over lanes 1..WEIGHT_LANES; the last lane (PREP_LANE) carries the
+#: short weight-only preparations a forward issues for its backward.
+SIDE_LANES = 3
+WEIGHT_LANES = 2
+PREP_LANE = 3
 
 #: Precision of every tensor-core contraction. Split-TF32 (the default)
 #: reproduces fp32 products to ~1e-6 relative, well inside the 1e-3 budget
@@ -152,7 +157,7 @@ class DeviceContext:
         self.precision = PRECISION
         # When a list, every GEMM-family call appends (name, flops, start, end).
         self.profile = None
-        for lane in range(SIDE_LANES + 1):
+        for lane in range(WEIGHT_LANES + 1):  # the preparation lane needs none up front
             self.reserve(64 << 20, lane=lane)
 
     def _timed(self, name: str, flops: int = 0):
@@ -187,7 +192,7 @@ class DeviceContext:
         self._ws_bytes[lane] = size
 
     def workspace(self, nbytes: int = 0):
-        self.reserve(nbytes)
+        self.reserve(max(int(nbytes), 64 << 10))  # at least the split-K counters
         return self._ws[self._lane].data_ptr(), self._ws_bytes[self._lane]
 
     # -- lanes -----------------------------------------------------------
@@ -228,7 +233,7 @@ class DeviceContext:
         key = param.data_ptr()
         lane = self._weight_lanes.get(key)
         if lane is None:
-            lane = self._weight_lanes[key] = 1 + len(self._weight_lanes) % SIDE_LANES
+            lane = self._weight_lanes[key] = 1 + len(self._weight_lanes) % WEIGHT_LANES
         return lane
 
     def join(self) -> None:
@@ -333,6 +338,32 @@ class DeviceContext:
                                         _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
                                         ctypes.byref(g), int(accumulate), prec, ws, wsb,
                                         self.status_ptr(), self.stream), "ttrl_conv_dgrad")
+
+    def conv_dgrad_weights_bytes(self, geom: Geom) -> int:
+        """Bytes of the stacked sub-kernels of the two-step data gradient, or
+        0 when the geometry takes the column path (ttrl_conv_dgrad)."""
+        g = geom.c_struct()
+        return int(lib().ttrl_conv_dgrad_weights_bytes(ctypes.byref(g)))
+
+    def conv_dgrad_weights(self, w, out, geom: Geom) -> None:
+        g = geom.c_struct()
+        check(lib().ttrl_conv_dgrad_weights(_ptr(_f32(w, "w")), _ptr(_f32(out, "out")),
+                                            ctypes.byref(g), self.stream),
+              "ttrl_conv_dgrad_weights")
+
+    def conv_dgrad_prepared(self, dy, wt, mask, dx, geom: Geom, accumulate: bool,
+                            precision: int | None = None) -> None:
+        prec = self._prec(precision)
+        g = geom.c_struct()
+        need = lib().ttrl_conv_dgrad_prepared_workspace_bytes(ctypes.byref(g))
+        ws, wsb = self.workspace(need)
+        with self._timed(f"conv_dgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom)):
+            check(lib().ttrl_conv_dgrad_prepared(_ptr(_f32(dy, "dy")), _ptr(_f32(wt, "wt")),
+                                                 _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
+                                                 ctypes.byref(g), int(accumulate), prec, ws, wsb,
+                                                 self.status_ptr(), self.stream),
+                  "ttrl_conv_dgrad_prepared")
 
     def conv_wgrad(self, x, dy, dw, db, geom: Geom, alpha: float, accumulate: bool,
                    accumulate_db: bool, precision: int | None = None) -> None:

@@ -18,7 +18,7 @@ import numpy as np
 import torch
 
 from ttrl_b200 import _lib
-from ttrl_b200.device import context
+from ttrl_b200.device import PREP_LANE, context
 from ttrl_b200.engine.autograd import Tensor, _detached, _is_scalar, _needs, backward_root
 
 __all__ = [
@@ -508,6 +508,19 @@ def conv2d_nhwc(x: Tensor, w: Tensor, b: Tensor | None, geom, *, input_scale: fl
         return _detached(y)
     out = Tensor(y, True, parents, "conv2d_relu" if relu else "conv2d")
     out._premask = bool(relu)
+    # The data gradient's stacked sub-kernels depend on the weights alone:
+    # prepared now on a side lane, beside the rest of the forward, instead of
+    # on the backward's critical path.
+    wt, wt_ready = None, None
+    wt_bytes = ctx.conv_dgrad_weights_bytes(geom) if x.requires_grad and ctx.concurrent else 0
+    if wt_bytes:
+        wt = torch.empty(wt_bytes // 4, dtype=torch.float32, device=xd.device)
+        with ctx.side(PREP_LANE) as s:
+            w.data.record_stream(s)
+            wt.record_stream(s)
+            ctx.conv_dgrad_weights(w.data, wt, geom)
+            wt_ready = torch.cuda.Event()
+            wt_ready.record(s)
 
     def _backward(grad):
         g = grad.reshape(rows, geom.cout)
@@ -541,8 +554,12 @@ def conv2d_nhwc(x: Tensor, w: Tensor, b: Tensor | None, geom, *, input_scale: fl
                     "the activation it is given."
                 )
             buf, acc = x._grad_slot()
-            ctx.conv_dgrad(g, w.data, xd if x._premask else None, buf.reshape(-1, geom.c), geom,
-                           acc)
+            mask = xd if x._premask else None
+            if wt is not None:
+                torch.cuda.current_stream(xd.device).wait_event(wt_ready)
+                ctx.conv_dgrad_prepared(g, wt, mask, buf.reshape(-1, geom.c), geom, acc)
+            else:
+                ctx.conv_dgrad(g, w.data, mask, buf.reshape(-1, geom.c), geom, acc)
             x._set_grad(buf)
 
     out._backward = _backward
