@@ -45,16 +45,18 @@ EPOCHS = 4
 STEPS_PER_UPDATE = EPOCHS * (ROLLOUT // MB)
 SAMPLES_PER_UPDATE = STEPS_PER_UPDATE * MB
 SYNC_EVERY = 50
-PPO_FLOP_PER_SAMPLE = 2 * 24_762_880      # 3F' - conv1 dX, 2 per MAC
+# Algorithmic work per sample: three times the forward MACs less conv1's
+# data gradient (which no layer needs), two FLOP per MAC.
+PPO_FLOP_PER_SAMPLE = 2 * 24_762_880
 DQN_FLOP_PER_UPDATE = 2 * 43_453_440 * 32
 RPPO_FLOP_PER_STEP = 2 * 26_526_976 * 512  # 3F_r - conv1 dX per row, 512 rows
 
 # DRAM bytes (read + write) per launch of the dominant kernels, from one
 # `ncu --set full` capture each of `python -m ttrl_b200.profile_case
-# conv1_wgrad|conv1_fprop --batch 256`.
+# conv1s2d_wgrad|conv1s2d_fprop --batch 256`.
 NCU_TRAFFIC_BYTES = {
-    "conv_wgrad[8x8/4 4->32]": 42.10e6,
-    "conv_fprop[8x8/4 4->32]": 29.03e6,
+    "conv_wgrad[2x2/1 64->32]": 42.106624e6 + 512,
+    "conv_fprop[2x2/1 64->32]": 29.039872e6,
 }
 
 METRIC = "PPO learner samples/sec (Nature-CNN actor-critic, minibatch 256, fwd+bwd+clip+Adam, graph-replayed)"
