@@ -352,17 +352,26 @@ def run_ours(args):
     if group is not None:
         dist.barrier()
     torch.cuda.synchronize(device)
+    staged = (pinned["obs"], pinned["actions"], pinned["old_logp"], pinned["values"],
+              pinned["returns"], pinned["adv"])
     t0 = time.perf_counter()
-    for _ in range(E):
-        learner.obs.copy_(pinned["obs"], non_blocking=True)
-        learner.actions.copy_(pinned["actions"], non_blocking=True)
-        learner.old_logp.copy_(pinned["old_logp"], non_blocking=True)
-        learner.values.copy_(pinned["values"], non_blocking=True)
-        learner.returns.copy_(pinned["returns"], non_blocking=True)
-        learner.advantages.copy_(pinned["adv"], non_blocking=True)
+    # Each step's rollout crosses host -> device and its metric rows device ->
+    # host inside the timed region. The upload of step k+1 runs on a copy
+    # stream beside the replay of step k, and step k+1 is enqueued before the
+    # host waits for step k's metrics.
+    learner.stage_rollout(*staged)
+    pending = None
+    for k in range(E):
+        learner.commit_staged()
         learner.draw_permutations()
         learner.replay()
-        learner.read_metrics()  # device -> host, synchronises
+        handle = learner.fetch_metrics()
+        if k + 1 < E:
+            learner.stage_rollout(*staged)
+        if pending is not None:
+            learner.metrics_of(pending)
+        pending = handle
+    learner.metrics_of(pending)
     e2e_s = time.perf_counter() - t0
     if group is not None:
         t = torch.tensor([e2e_s], device=device)

@@ -137,3 +137,39 @@ def _minibatch_check(PPOConfig, objective, Tensor, build_actor_critic, tol_grad,
     named = nature_state_dict(grads, heads=("pi", "v"))
     for name, g in grads_in_state_layout(net).items():
         assert rel(g.reshape(named[name].shape), named[name]) <= tol_grad, name
+
+
+def test_staged_rollout_upload_equals_direct_load():
+    """stage_rollout (copy stream, overlapping the running update) then
+    commit_staged leaves the learner's rollout buffers bit-identical to a
+    direct upload, and the following update reads them."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from ttrl_b200.algos.ppo import PPOConfig, PPOLearner, normalize_advantages
+    from ttrl_b200.nets import build_actor_critic
+    rng = np.random.default_rng(31)
+    net = build_actor_critic((4, 84, 84), 6, "cuda", batch=256)
+    n = 512
+    learner = PPOLearner(net, n, (4, 84, 84), "cuda", cfg=PPOConfig(epochs=1,
+                                                                   minibatch_size=256), seed=3)
+    rollouts = []
+    for _ in range(3):
+        obs, actions, adv, returns = _rollout(rng, n)
+        logp = rng.standard_normal(n).astype(np.float32)
+        values = rng.standard_normal(n).astype(np.float32)
+        rollouts.append((obs, actions.astype(np.int32), logp, values, returns,
+                         normalize_advantages(adv).astype(np.float32)))
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    learner.stage_rollout(*[pin(a) for a in rollouts[0]])
+    for k in range(3):
+        learner.commit_staged()
+        learner.draw_permutations()
+        learner.replay()
+        if k + 1 < 3:
+            learner.stage_rollout(*[pin(a) for a in rollouts[k + 1]])
+        learner.read_metrics()
+        got = [learner.obs, learner.actions, learner.old_logp, learner.values, learner.returns,
+               learner.advantages]
+        for g, want in zip(got, rollouts[k]):
+            assert np.array_equal(g.cpu().numpy().reshape(-1), np.asarray(want).reshape(-1))
+    learner.close()

@@ -119,7 +119,25 @@ class ReplayedUpdate:
 
     def read_metrics(self) -> dict:
         """Mean over the rollout update's steps, like ttrl/algos/ppo/learn.py:69-73."""
-        host = self.metric_buf.detach().to("cpu").numpy().astype(np.float64)
+        return self._metrics_of(self.metric_buf.detach().to("cpu").numpy())
+
+    def fetch_metrics(self):
+        """Start copying this update's metric rows to pinned host memory on the
+        current stream and return a handle; `metrics_of(handle)` waits for that
+        copy only, so the next update can be enqueued before the host blocks."""
+        host = torch.empty(self.metric_buf.shape, dtype=self.metric_buf.dtype, pin_memory=True)
+        host.copy_(self.metric_buf, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.device))
+        return host, done
+
+    def metrics_of(self, handle) -> dict:
+        host, done = handle
+        done.synchronize()
+        return self._metrics_of(host.numpy())
+
+    def _metrics_of(self, rows) -> dict:
+        host = np.asarray(rows, np.float64)
         out = {k: float(host[:, j].mean()) for j, k in enumerate(self.METRICS)}
         out["grad_norm"] = float(np.sqrt(host[:, 4]).mean())
         out["minibatches"] = float(self.steps_per_update)
@@ -205,6 +223,44 @@ class PPOLearner(ReplayedUpdate):
         self.values.copy_(torch.from_numpy(np.asarray(values, np.float32)))
         self.returns.copy_(torch.from_numpy(np.asarray(returns, np.float32)))
         self.advantages.copy_(torch.from_numpy(np.asarray(adv, np.float32)))
+
+    # -- overlapped upload -------------------------------------------------
+
+    _STAGED = ("obs", "actions", "old_logp", "values", "returns", "advantages")
+
+    def stage_rollout(self, obs_u8, actions, old_logp, values, returns, advantages) -> None:
+        """Start uploading the NEXT rollout (pinned host tensors, already
+        normalised advantages) into device staging buffers on a copy stream,
+        beside whatever update is running; `commit_staged()` makes it the
+        rollout the next replay reads."""
+        if getattr(self, "_staging", None) is None:
+            self._staging = {k: torch.empty_like(getattr(self, k)) for k in self._STAGED}
+            self._copy_stream = torch.cuda.Stream(self.device)
+            self._staged = None
+            self._committed = None
+        src = dict(zip(self._STAGED, (obs_u8, actions, old_logp, values, returns, advantages)))
+        with torch.cuda.stream(self._copy_stream):
+            if self._committed is not None:
+                # The previous commit has read the staging buffers.
+                self._copy_stream.wait_event(self._committed)
+            for k, t in src.items():
+                self._staging[k].copy_(t.reshape(self._staging[k].shape), non_blocking=True)
+            self._staged = torch.cuda.Event()
+            self._staged.record(self._copy_stream)
+
+    def commit_staged(self) -> None:
+        """Order the current stream after the staged upload and copy it into
+        the buffers the captured update reads (device to device)."""
+        if getattr(self, "_staged", None) is None:
+            raise RuntimeError("commit_staged: no rollout was staged")
+        main = torch.cuda.current_stream(self.device)
+        main.wait_event(self._staged)
+        for k in self._STAGED:
+            getattr(self, k).copy_(self._staging[k], non_blocking=True)
+        self.keep = None
+        self._committed = torch.cuda.Event()
+        self._committed.record(main)
+        self._staged = None
 
     def load_rollout_raw(self, obs_u8, actions, old_logp, values, rewards, dones, last_values,
                          valid=None) -> None:
