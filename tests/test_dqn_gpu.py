@@ -157,3 +157,38 @@ def test_dqn_replays_are_deterministic():
         step.close()
     for name in finals[0]:
         assert np.array_equal(finals[0][name], finals[1][name]), name
+
+
+def test_dqn_pipelined_metric_reads_match_run():
+    """launch + fetch_metrics / metrics_of, with update k+1 enqueued before
+    update k's metrics are waited on, reads the same losses as run()."""
+    from ttrl_b200.engine.step import TrainStep
+    runs = []
+    for pipelined in (False, True):
+        rng, online_p, target_p, online, target, opt, inputs = _setup(seed=13)
+        step = TrainStep(_step_fn(online, target), inputs, "cuda", optimizer=opt,
+                         mode="traced_fwd_bwd")
+        batches = [dqn_batch(rng) for _ in range(4)]
+        losses = []
+        if not pipelined:
+            for b in batches:
+                _load(step, b)
+                losses.append(float(step.run()["loss"].reshape(-1)[0]))
+        else:
+            _load(step, batches[0])
+            step.run()  # capture: the first call is a whole step
+            losses.append(float(step.metrics()["loss"].reshape(-1)[0]))
+            pending = None
+            for b in batches[1:]:
+                _load(step, b)
+                step.launch()
+                handle = step.fetch_metrics()
+                if pending is not None:
+                    losses.append(float(step.metrics_of(pending)["loss"].reshape(-1)[0]))
+                pending = handle
+            losses.append(float(step.metrics_of(pending)["loss"].reshape(-1)[0]))
+        runs.append((losses, online.state_dict()))
+        step.close()
+    assert runs[0][0] == runs[1][0]
+    for name in runs[0][1]:
+        assert np.array_equal(runs[0][1][name], runs[1][1][name]), name

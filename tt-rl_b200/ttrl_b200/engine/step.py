@@ -133,6 +133,41 @@ class MetricPack:
             out[k] = self.sources[k].numpy()
         return out
 
+    def fetch(self):
+        """Start copying every metric to pinned host memory on the current
+        stream; `result(handle)` waits for those copies only."""
+        copies = {}
+        dev = None
+        if self.buffer is not None:
+            dev = self.buffer.device
+            context(dev).join()
+            copies[None] = torch.empty(self.buffer.shape, dtype=self.buffer.dtype,
+                                       pin_memory=True)
+            copies[None].copy_(self.buffer, non_blocking=True)
+        for k in self.vector_keys:
+            src = self.sources[k].data
+            dev = src.device
+            copies[k] = torch.empty(src.shape, dtype=src.dtype, pin_memory=True)
+            copies[k].copy_(src, non_blocking=True)
+        done = None
+        if dev is not None:
+            done = torch.cuda.Event()
+            done.record(torch.cuda.current_stream(dev))
+        return copies, done
+
+    def result(self, handle) -> dict:
+        copies, done = handle
+        if done is not None:
+            done.synchronize()
+        out = dict(self.passthrough)
+        if None in copies:
+            host = copies[None].numpy()
+            for i, k in enumerate(self.scalar_keys):
+                out[k] = host[i:i + 1].reshape(self.sources[k].shape)
+        for k in self.vector_keys:
+            out[k] = copies[k].numpy().reshape(self.sources[k].shape)
+        return out
+
 
 def read_metrics(metrics: dict | None) -> dict:
     """Download every tensor-valued metric; scalars in one transfer."""
@@ -179,6 +214,14 @@ class TrainStep:
 
     def metrics(self) -> dict:
         return self._pack.read() if self._pack is not None else {}
+
+    def fetch_metrics(self):
+        """Start the metric read of the last replay without waiting (a handle
+        for `metrics_of`), so the next step can be enqueued first."""
+        return self._pack.fetch() if self._pack is not None else ({}, None)
+
+    def metrics_of(self, handle) -> dict:
+        return self._pack.result(handle) if self._pack is not None else {}
 
     def _run_eager(self) -> dict:
         if self.optimizer is not None:
