@@ -1323,6 +1323,7 @@ static cudaError_t launch_bn(const GemmArgs& args, dim3 grid, int cluster_z, cud
 // deterministic and at least as accurate as split-TF32.
 constexpr long long kSimtMacs = 1ll << 20;
 constexpr int kSimtWarpK = 64;  // reductions at least this long get a warp per output
+constexpr int kSimtBatch = 8;   // reduction steps whose loads are issued together
 
 struct SimtArgs {
   DevOperand a, b;
@@ -1355,14 +1356,27 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ 
   if (o >= outs) return;  // uniform across a warp when it owns one output
   const int r = p.c_fast ? static_cast<int>(o / p.n) : static_cast<int>(o % p.m);
   const int c = p.c_fast ? static_cast<int>(o % p.n) : static_cast<int>(o / p.m);
+  // The loads of kSimtBatch consecutive reduction steps are issued before
+  // their multiply-adds, which stay in sequential order: one memory round
+  // trip per batch instead of per step, the same result bit for bit.
   float acc = 0.f;
+  const int step = p.warp_per_output ? 32 : 1;
+  int k = p.warp_per_output ? lane : 0;
+  for (; k + (kSimtBatch - 1) * step < p.k; k += kSimtBatch * step) {
+    float av[kSimtBatch], bv[kSimtBatch];
+#pragma unroll
+    for (int u = 0; u < kSimtBatch; ++u) {
+      av[u] = simt_a(a, r, k + u * step);
+      bv[u] = simt_a(b, c, k + u * step);
+    }
+#pragma unroll
+    for (int u = 0; u < kSimtBatch; ++u) acc = fmaf(av[u], bv[u], acc);
+  }
+  for (; k < p.k; k += step) acc = fmaf(simt_a(a, r, k), simt_a(b, c, k), acc);
   if (p.warp_per_output) {
-    for (int k = lane; k < p.k; k += 32) acc = fmaf(simt_a(a, r, k), simt_a(b, c, k), acc);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane != 0) return;
-  } else {
-    for (int k = 0; k < p.k; ++k) acc = fmaf(simt_a(a, r, k), simt_a(b, c, k), acc);
   }
   const int rr[1] = {r};
   const int cc[1] = {c};
