@@ -347,6 +347,12 @@ int ttrl_copy_strided(float* dst, const int64_t* dst_strides, const float* src,
                       const int64_t* src_strides, const int64_t* shape, int ndim, int accumulate,
                       ttrl_stream_t stream);
 
+/* Self-check of the bounded waits every kernel uses: a wait on a barrier
+ * that nothing completes gives up after about a second and records
+ * the code 1001 in status[0]; the context stays usable.
+ * No reference counterpart (ttnn ops do not time out). */
+int ttrl_wait_probe(int* status, ttrl_stream_t stream);
+
 /* dst = (1 - tau) * dst + tau * src, elementwise, in that operation order
  * (ttrl/algos/sac/targets.py:55-61, the Polyak blend). */
 int ttrl_polyak(float* dst, const float* src, int64_t n, float tau, ttrl_stream_t stream);

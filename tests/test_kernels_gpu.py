@@ -411,3 +411,25 @@ def test_gemm_many_waves_half_footprint(n, k, prec, transposed):
     ref = np.maximum(a.astype(np.float64) @ b.astype(np.float64).T + bias, 0.0)
     assert np.isfinite(got).all()
     assert rel(got, ref) <= (TOL_X3 if prec == 0 else TOL_TF32)
+
+
+def test_bounded_wait_gives_up_and_the_context_stays_usable():
+    """A wait on a barrier that nothing completes (ttrl_wait_probe) gives up
+    after the library's bound, records status 1001, and the next launches on
+    the same context run normally."""
+    import time
+    from ttrl_b200._lib import lib
+    ctx = _ctx()
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert lib().ttrl_wait_probe(status.data_ptr(), ctx.stream) == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert int(status[0].item()) == 1001
+    assert 1.0 < waited < 10.0  # the bound is two seconds of wall time
+    x = torch.randn(64, 32, device="cuda")
+    w = torch.randn(32, 16, device="cuda")
+    y = torch.empty(64, 16, device="cuda")
+    ctx.linear_fwd(x, w, None, y, relu=False)
+    assert rel(host(y), host(x).astype(np.float64) @ host(w).astype(np.float64)) <= TOL_X3

@@ -60,6 +60,7 @@ int reduce(int, const float*, float*, int64_t, int64_t, int64_t, cudaStream_t);
 int copy_strided(float*, const int64_t*, const float*, const int64_t*, const int64_t*, int, int,
                  cudaStream_t);
 int polyak(float*, const float*, int64_t, float, cudaStream_t);
+int wait_probe(int*, cudaStream_t);
 int gather_rows(const void*, const int32_t*, void*, int, int, cudaStream_t);
 
 
@@ -217,6 +218,10 @@ int ttrl_copy_strided(float* dst, const int64_t* dst_strides, const float* src,
                       ttrl_stream_t stream) {
   return copy_strided(dst, dst_strides, src, src_strides, shape, ndim, accumulate,
                       TTRL_STREAM(stream));
+}
+
+int ttrl_wait_probe(int* status, ttrl_stream_t stream) {
+  return wait_probe(status, TTRL_STREAM(stream));
 }
 
 int ttrl_polyak(float* dst, const float* src, int64_t n, float tau, ttrl_stream_t stream) {

@@ -2,8 +2,8 @@
 // bounded mbarrier waits, cp.async gathers, TMA, and the tcgen05
 // (TMEM allocation, UMMA descriptors, MMA issue, TMEM loads) primitives.
 //
-// Every spin-wait in this library is bounded: after kSpinLimit polls it
-// records an error code in the caller-supplied device status word and the
+// Every wait in this library is bounded: after kWaitTimeoutNs of wall time
+// it records an error code in the caller-supplied device status word and the
 // kernel unwinds (frees TMEM and returns) instead of hanging the GPU.
 #pragma once
 
@@ -14,10 +14,19 @@
 
 namespace ttrl {
 
-// Poll budget for one mbarrier wait. try_wait itself suspends for a
-// hardware-chosen interval per poll, so this bounds a wait to well under a
-// second on B200 while never tripping on a healthy pipeline.
-constexpr int kSpinLimit = 1 << 22;
+// One mbarrier wait: polls that each suspend the thread until the phase
+// completes or at most kWaitPollNs pass (try_wait's suspend-time hint, which
+// the hardware may cut short), so waiting warps sleep instead of spinning on
+// the issue slots the working warps need; the global timer, read every 64
+// polls, ends the wait after kWaitTimeoutNs.
+constexpr uint32_t kWaitPollNs = 100000;
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 // Device status codes written into the optional status word.
 constexpr int kErrWaitTimeout = 1001;
@@ -37,24 +46,28 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+
+// Bounded wait on phase `parity` of the barrier. Returns false on timeout.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t ns) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred P1;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, P1;\n\t}"
       : "=r"(done)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(ns)
       : "memory");
   return done != 0;
 }
 
-// Bounded wait on phase `parity` of the barrier. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (int i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait_sleep(bar, parity, kWaitPollNs)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, kWaitPollNs)) return true;
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitTimeoutNs) return false;
   }
-  return false;
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {

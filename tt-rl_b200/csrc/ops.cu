@@ -278,4 +278,26 @@ int polyak(float* dst, const float* src, int64_t n, float tau, cudaStream_t st) 
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("polyak launch", e);
 }
 
+// ------------------------------------------------------- bounded-wait check
+
+// Self-check of the library's bounded waits: one thread waits on an
+// mbarrier that nothing arrives on, gives up after the wait bound (about a
+// second), records kErrWaitTimeout in *status and returns, leaving the
+// context usable. Nothing traps or faults.
+__global__ void wait_probe_kernel(int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t a = smem_u32(&bar);
+  mbar_init(a, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  if (!mbar_wait(a, 0)) record_error(status, kErrWaitTimeout);
+}
+
+int wait_probe(int* status, cudaStream_t st) {
+  if (status == nullptr) return set_error(TTRL_EINVAL, "wait_probe: null status");
+  wait_probe_kernel<<<1, 1, 0, st>>>(status);
+  note_launch();
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("wait_probe launch", e);
+}
+
 }  // namespace ttrl

@@ -132,6 +132,7 @@ _SIGNATURES = {
                          _c_int, _c_float, _vp]),
     "ttrl_reduce": (_c_int, [_c_int, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                              _vp]),
+    "ttrl_wait_probe": (_c_int, [_vp, _vp]),
     "ttrl_copy_strided": (_c_int, [_vp, ctypes.POINTER(ctypes.c_int64), _vp,
                                    ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
                                    _c_int, _c_int, _vp]),
