@@ -118,7 +118,11 @@ int dqn_loss(const DqnArgs& args, cudaStream_t st) {
   if (!args.q || !args.q_sel || !args.q_tgt || !args.onehot || !args.rewards || !args.dones ||
       !args.discounts || !args.loss || !args.mean_q || !args.dq)
     return set_error(TTRL_EINVAL, "dqn_loss: null pointer");
-  const cudaError_t le_ = launch_pdl(dqn_loss_kernel, dim3(1), dim3(kLossThreads), 0, st, args);
+  // One thread per sample (a power of two for the reduction tree): the sums
+  // are bit-identical to a full-width block's, whose extra levels add zeros.
+  int threads = 32;
+  while (threads < args.batch && threads < kLossThreads) threads *= 2;
+  const cudaError_t le_ = launch_pdl(dqn_loss_kernel, dim3(1), dim3(threads), 0, st, args);
   note_launch();
   cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("dqn_loss launch", e);

@@ -64,6 +64,25 @@ def _no_backward(grad):
     return None
 
 
+_UNIT_SEEDS: dict = {}
+
+
+def _unit_seed(like):
+    """d(loss)/d(loss) = 1, shaped like the scalar root: one constant per
+    device and shape, made outside any capture (no fill launch per
+    backward); inside a first capture, filled by a kernel instead."""
+    key = (like.device, tuple(like.shape))
+    seed = _UNIT_SEEDS.get(key)
+    if seed is None:
+        if torch.cuda.is_current_stream_capturing():
+            seed = torch.empty_like(like, dtype=GRAD_ACCUM_DTYPE)
+            context(like.device).ew("fill", None, None, seed, 1.0)
+            return seed
+        seed = torch.ones(like.shape, dtype=GRAD_ACCUM_DTYPE, device=like.device)
+        _UNIT_SEEDS[key] = seed
+    return seed
+
+
 def _default_device():
     if not torch.cuda.is_available():
         raise RuntimeError("ttrl_b200 needs a CUDA device; there is no CPU fallback")
@@ -250,10 +269,10 @@ class Tensor:
                 f"(numel={numel}); there is no `gradient=` kwarg to seed a "
                 "non-scalar backward pass, so reduce to a scalar first."
             )
-        seed = torch.empty_like(self.data, dtype=GRAD_ACCUM_DTYPE)
-        context(self.data.device).ew("fill", None, None, seed, 1.0)
-        self.grad = seed
-        self._grad_owned = True
+        self.grad = _unit_seed(self.data)
+        # Not owned: an op that accumulates into the root's gradient copies
+        # it first, so the shared constant is never written.
+        self._grad_owned = False
         global _BACKWARD_ROOT
         prev_root, _BACKWARD_ROOT = _BACKWARD_ROOT, self
         try:
