@@ -216,8 +216,12 @@ def run_reference(args):
         "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": 1000 * total / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded uint8 frames, N(0,1) advantages/returns)",
-        "config": {"workload": "ppo_nature_cnn_minibatch256", "minibatch": MB,
-                   "note": "each reference step is one PPO minibatch step of 256 samples"},
+        "config": {"workload": "ppo_nature_cnn_rollout8x128_mb256_epochs4",
+                   "global_batch": MB * world, "minibatch": MB, "rollout": ROLLOUT,
+                   "epochs": EPOCHS, "parallelism": f"dp{world}",
+                   "note": "the same workload and metric as the CUDA arm; each reference "
+                           "step is a bounded sample of it, one PPO minibatch step of 256 "
+                           "samples, in samples/s"},
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
                          "sample": f"{steps} PPO minibatch steps of 256 (numpy fp32 restatement "
                                    "of the reference's tape, objective, clip and Adam)"},
