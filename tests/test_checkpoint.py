@@ -153,3 +153,38 @@ def test_load_learner_names_missing_parts():
     from ttrl_b200.checkpoint import load_learner
     with pytest.raises(KeyError, match="online"):
         load_learner({"net": {}}, online=object())
+
+
+def test_learner_state_packs_conv_moments_into_the_stored_layout(ref_path):
+    """learner_state puts an optimizer's OIHW convolution moments back into
+    the prepared matrices the file holds them in (and leaves the others as
+    they are), with a host-only stand-in for the B200 Adam."""
+    from types import SimpleNamespace
+    from ttrl_b200.checkpoint import Checkpoint, learner_state
+    from ttrl_b200.engine.packing import solve_cp
+    stored = Checkpoint.read(ref_path).agent_state()
+    names = list(stored["online"])
+    rng = np.random.default_rng(5)
+    params, m, v = [], [], []
+    for name in names:
+        shape = stored["online"][name].shape
+        conv = len(shape) == 4 and shape[2] > 1
+        params.append(SimpleNamespace(_layout=SimpleNamespace(oihw=shape) if conv else None))
+        m.append(rng.standard_normal(shape).astype(np.float32))
+        v.append(np.abs(rng.standard_normal(shape)).astype(np.float32) + 1e-3)
+    opt = SimpleNamespace(params=params, m=m,
+                          state_dict=lambda: {"t": 8, "steps": [8] * len(names), "lr": 1e-4,
+                                              "betas": (0.9, 0.999), "eps": 1.5e-4,
+                                              "weight_decay": 0.0, "m": list(m), "v": list(v)})
+    out = learner_state(like=stored, optimizer=opt)["optimizer"]
+    assert out["t"] == 8
+    for i, name in enumerate(names):
+        want_shape = stored["optimizer"]["m"][i].shape
+        assert out["m"][i].shape == want_shape and out["v"][i].shape == want_shape, name
+        if want_shape != m[i].shape:
+            lay = solve_cp(want_shape, m[i].shape, v=stored["optimizer"]["v"][i])
+            assert np.array_equal(lay.unpack(out["m"][i]), m[i])
+            assert np.array_equal(lay.unpack(out["v"][i]), v[i])
+            assert lay.padding_is_zero(out["m"][i])
+        else:
+            assert np.array_equal(out["m"][i], m[i])
