@@ -52,7 +52,7 @@ DQN_FLOP_PER_UPDATE = 2 * 43_453_440 * 32
 RPPO_FLOP_PER_STEP = 2 * 26_526_976 * 512  # 3F_r - conv1 dX per row, 512 rows
 
 # DRAM bytes (read + write) per launch of the dominant kernels, from one
-# `ncu --set full` capture each of `python -m ttrl_b200.profile_case
+# `ncu --set full` capture each of `python bench.py --profile-case
 # conv1s2d_wgrad|conv1s2d_fprop --batch 256`.
 NCU_TRAFFIC_BYTES = {
     "conv_wgrad[2x2/1 64->32]": 42.106624e6 + 512,
@@ -75,6 +75,11 @@ def _args():
     # of the reference's HiFi4 matmuls; ill-conditioned reductions reach
     # ~1.5e-3 of float64).
     ap.add_argument("--precision", choices=("tf32", "tf32x3"), default="tf32x3")
+    # Profiling cases (for ncu): run one kernel family of the Nature-CNN
+    # shapes a few times and exit without timing or printing a bench line.
+    ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES), default=None)
+    ap.add_argument("--batch", type=int, default=256, help="batch of a --profile-case")
+    ap.add_argument("--reps", type=int, default=3, help="repetitions of a --profile-case")
     return ap.parse_args()
 
 
@@ -178,6 +183,15 @@ def _dist():
     return world, rank, local
 
 
+def sync_points(k: int) -> set:
+    """Indices of the updates (0-based) after which a multi-GPU run averages
+    its replicas: every SYNC_EVERY-th update, and the last one."""
+    points = {i for i in range(k) if (i + 1) % SYNC_EVERY == 0}
+    if k > 0:
+        points.add(k - 1)
+    return points
+
+
 # ----------------------------------------------------------- CPU arms
 
 def cpu_ppo_steps(n_steps: int, seed: int = 0):
@@ -265,7 +279,8 @@ def kernel_profile(learner, device):
         torch.cuda.synchronize(device)
     finally:
         ctx.profile = None
-    # roll back the optimizer step this profiling pass took
+    # This pass is one more optimizer step on the learner; it runs after the
+    # timed regions, and nothing after it is timed.
     return [(name, flops, s.elapsed_time(e) * 1e-3) for name, flops, s, e in records]
 
 
@@ -281,8 +296,11 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        # stdout carries exactly one JSON line: keep NCCL's banner off it.
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        # NCCL's communicator log (ranks, transports, NVLS) goes to stderr:
+        # stdout carries exactly one JSON line.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
         group = dist.group.WORLD
@@ -309,12 +327,16 @@ def run_ours(args):
         sync.average()
     torch.cuda.synchronize(device)
 
-    # timed region: K rollout updates, each bracketed by its own events
+    # timed region: K rollout updates, each bracketed by its own events. At
+    # N > 1 the parameters are averaged after every 50th update and once more
+    # after the last one, so every timed region holds ceil(K / 50) averages
+    # (one per update at most 50 -- never fewer than the reference's rate).
     K = args.steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     syncs = 0
-    n_sync = K // SYNC_EVERY
+    sync_after = sync_points(K) if group is not None else set()
+    n_sync = len(sync_after)
     sync_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_sync)]
     sync_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_sync)]
     if group is not None:
@@ -326,7 +348,7 @@ def run_ours(args):
             do_flush()
             starts[k].record()
             learner.replay()
-            if group is not None and (k + 1) % SYNC_EVERY == 0:
+            if k in sync_after:
                 sync_s[syncs].record()
                 sync.average()
                 sync_e[syncs].record()
@@ -365,10 +387,13 @@ def run_ours(args):
     # host waits for step k's metrics.
     learner.stage_rollout(*staged)
     pending = None
+    e2e_sync = sync_points(E) if group is not None else set()
     for k in range(E):
         learner.commit_staged()
         learner.draw_permutations()
         learner.replay()
+        if k in e2e_sync:
+            sync.average()
         handle = learner.fetch_metrics()
         if k + 1 < E:
             learner.stage_rollout(*staged)
@@ -404,7 +429,11 @@ def run_ours(args):
                        "epochs": EPOCHS, "grad_steps_per_step": STEPS_PER_UPDATE,
                        "parallelism": f"dp{world}", "sync_every_updates": SYNC_EVERY,
                        "syncs_in_timed_region": syncs,
+                       "sync_rule": "after every 50th update and after the last one "
+                                    "(ceil(steps / 50) averages)" if world > 1 else "none (N=1)",
                        "allreduce_ms_total": round(sync_ms, 4),
+                       "allreduce_bytes": int(sync.arena.numel() * 4) if group is not None
+                       else 0,
                        "precision": PRECISION_TEXT[args.precision],
                        "l2": "flushed (256 MB write) before every timed step"},
             "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
@@ -421,7 +450,10 @@ def run_ours(args):
                                   if args.precision == "tf32x3" else ")"),
                 "whole_step_tflops": step_tflops,
             },
-            "kernel_times_us": {f"{n}#{i}": round(t * 1e6, 2) for i, (n, _, t) in enumerate(prof)},
+            # Each call timed alone, eagerly, with its own launch latency: not
+            # a share of the graph replay (whose kernels overlap on lanes).
+            "kernel_times_us_isolated_eager": {f"{n}#{i}": round(t * 1e6, 2)
+                                               for i, (n, _, t) in enumerate(prof)},
             "clocks": clock,
         }
         if world == 1 and not args.no_dqn:
@@ -456,21 +488,18 @@ def run_ours(args):
 
 def bench_dqn(device, args):
     """Nature-DQN batch-32 update (forward x3, double-DQN Huber, backward,
-    grad_sq, Adam) as one graph replay; updates/sec, device time."""
+    grad_sq, Adam) as one graph replay through `DQNLearner` (its
+    target_sync_interval of 8,000 updates falls outside the timed region);
+    updates/sec, device time."""
     import torch
-    from ttrl_b200.algos import dqn
+    from ttrl_b200.algos.dqn import DQNLearner
     from ttrl_b200.device import context
-    from ttrl_b200.engine.optim import Adam
-    from ttrl_b200.engine.step import TrainStep
     from ttrl_b200.nets import build_q_net
     np.random.seed(7)
     online = build_q_net((4, 84, 84), 6, device, batch=32)
     target = build_q_net((4, 84, 84), 6, device, batch=32)
-    target.copy_from(online)
-    opt = Adam(list(online.parameters()), lr=1e-4, eps=1.5e-4)
-    inputs = dqn.step_inputs((4, 84, 84), device, batch=32, num_actions=6)
-    step = TrainStep(lambda i: dqn.update_loss(online, target, i, num_actions=6, double=True),
-                     inputs, device, optimizer=opt, mode="traced_fwd_bwd")
+    learner = DQNLearner(online, target, (4, 84, 84), 6, device, batch=32, lr=1e-4, eps=1.5e-4,
+                         double=True, target_sync_interval=8_000)
     rng = np.random.default_rng(3)
     obs = rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8)
     nxt = rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8)
@@ -479,12 +508,11 @@ def bench_dqn(device, args):
               "rewards": rng.choice([-1.0, 0.0, 1.0], (32, 1)).astype(np.float32),
               "dones": (rng.random((32, 1)) < 0.01).astype(np.float32),
               "discounts": np.full((32, 1), 0.99, np.float32)}
-    for k, v in arrays.items():
-        step.load_input(k, v)
-    step.run()
+    learner.update(**arrays)
+    step = learner.step
     launches = step.launches_per_replay
     for _ in range(10):
-        step.launch()
+        learner.launch()
     ctx = context(device)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
     K = max(50, args.steps * 5)
@@ -494,21 +522,27 @@ def bench_dqn(device, args):
     for k in range(K):
         ctx.ew("fill", None, None, flush, 0.0)
         s[k].record()
-        step.launch()
+        learner.launch()
         e[k].record()
     torch.cuda.synchronize(device)
     ms = sum(a.elapsed_time(b) for a, b in zip(s, e)) / K
-    # end to end: host arrays -> pinned staging -> device, replay, metric read
+    # end to end: the batch sits in pinned host memory laid out like the
+    # device inputs (TrainStep.pinned_inputs: where a replay sampler writes
+    # its rows), and every update uploads it in ONE host-to-device copy
+    # (the inputs share one device allocation), replays, reads the metrics.
+    pinned = step.pinned_inputs()
+    for k, v in arrays.items():
+        pinned[k].copy_(torch.from_numpy(np.ascontiguousarray(v)).reshape(pinned[k].shape))
     E = 50
+    torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     # Every update's inputs go host -> device and its metrics device -> host
-    # inside the timed region; update k+1 is enqueued (its uploads ordered
+    # inside the timed region; update k+1 is enqueued (its upload ordered
     # after replay k on the same stream) before the host waits for update k.
     pending = None
     for _ in range(E):
-        for k, v in arrays.items():
-            step.load_input(k, v)
-        step.launch()
+        learner.load(**pinned)
+        learner.launch()
         handle = step.fetch_metrics()
         if pending is not None:
             step.metrics_of(pending)
@@ -516,7 +550,7 @@ def bench_dqn(device, args):
     step.metrics_of(pending)
     e2e_ms = (time.perf_counter() - t0) * 1000 / E
     h2d = sum(v.nbytes for v in arrays.values())
-    step.close()
+    learner.close()
     return {"metric": "Nature-DQN batch-32 learner updates/sec (fwd x3 + bwd + Adam, one graph "
                       "replay per update)",
             "value": 1000.0 / ms, "unit": "updates/s", "ms_per_update": ms,
@@ -621,8 +655,213 @@ def bench_recurrent(device, args):
     return out
 
 
+# ------------------------------------------------------ profiling cases
+#
+# `python bench.py --profile-case NAME [--batch B] [--reps R]` runs one kernel
+# family of the Nature-CNN shapes R times on seeded inputs and exits; the
+# ncu summaries under profiles/ name the exact command they came from.
+
+#: (input extent, in channels, out channels, kernel, stride). conv1s2d is
+#: conv1 in the space-to-depth form the nets run it in (fold 4).
+PROFILE_CONV = {"conv1": (84, 4, 32, 8, 4), "conv1s2d": (21, 64, 32, 2, 1),
+                "conv2": (20, 32, 64, 4, 2), "conv3": (9, 64, 64, 3, 1)}
+
+#: The Nature-DQN parameter shapes as the device holds them (conv weights
+#: KRSC, conv1 folded): 1,687,206 floats.
+DQN_PARAM_SHAPES = ((32, 2, 2, 64), (32,), (64, 4, 4, 32), (64,), (64, 3, 3, 64), (64,),
+                    (3136, 512), (512,), (512, 6), (6,))
+
+
+def _profile_conv(layer: str, kind: str):
+    def run(args):
+        import torch
+        from ttrl_b200.device import context, conv_geom
+        hw, c, co, k, st = PROFILE_CONV[layer]
+        g = conv_geom(args.batch, hw, hw, c, co, k, k, st, 0)
+        rng = np.random.default_rng(0)
+        dev = torch.device("cuda", 0)
+        x = torch.from_numpy(rng.standard_normal((args.batch * hw * hw, c)).astype(np.float32)).to(dev)
+        w = torch.from_numpy(rng.standard_normal((co, k, k, c)).astype(np.float32)).to(dev)
+        b = torch.zeros(co, device=dev)
+        y = torch.empty((args.batch * g.oh * g.ow, co), device=dev)
+        ctx = context(dev)
+        for _ in range(args.reps):
+            if kind == "fprop":
+                ctx.conv_fprop(x, w, b, y, g, 1.0, True)
+            elif kind == "dgrad":
+                ctx.conv_dgrad(y, w, x, torch.empty_like(x), g, False)
+            else:
+                ctx.conv_wgrad(x, y, torch.empty_like(w), b, g, 1.0, False, False)
+        torch.cuda.synchronize()
+    return run
+
+
+def _profile_fc1(args):
+    import torch
+    from ttrl_b200.device import context
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy(rng.standard_normal((args.batch, 3136)).astype(np.float32)).to(dev)
+    w = torch.from_numpy(rng.standard_normal((3136, 512)).astype(np.float32)).to(dev)
+    b = torch.zeros(512, device=dev)
+    y = torch.empty((args.batch, 512), device=dev)
+    ctx = context(dev)
+    for _ in range(args.reps):
+        ctx.linear_fwd(x, w, b, y, True)
+    torch.cuda.synchronize()
+
+
+def _dqn_param_tensors(sets: int):
+    """`sets` copies of the Nature-DQN parameter list with seeded gradients."""
+    import torch
+    from ttrl_b200.engine.autograd import Tensor
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    params = []
+    for _ in range(sets):
+        for shape in DQN_PARAM_SHAPES:
+            p = Tensor(torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(dev),
+                       requires_grad=True)
+            p.grad = torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(dev)
+            params.append(p)
+    return params
+
+
+def _profile_adam(sets: int):
+    def run(args):
+        import torch
+        from ttrl_b200.engine.optim import Adam
+        params = _dqn_param_tensors(sets)
+        opt = Adam(params, lr=1e-4, eps=1.5e-4)
+        for _ in range(args.reps):
+            opt.step()
+        torch.cuda.synchronize()
+    return run
+
+
+def _profile_sqnorm(sets: int):
+    def run(args):
+        import torch
+        from ttrl_b200.algos.grads import grad_sq_device
+        params = _dqn_param_tensors(sets)
+        for _ in range(args.reps):
+            grad_sq_device(params)
+        torch.cuda.synchronize()
+    return run
+
+
+def _profile_u8_s2d(args):
+    import torch
+    from ttrl_b200.device import context
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    frames = torch.from_numpy(rng.integers(0, 256, (args.batch, 4, 84, 84),
+                                           dtype=np.uint8)).to(dev)
+    out = torch.empty((args.batch * 21 * 21, 64), device=dev)
+    ctx = context(dev)
+    for _ in range(args.reps):
+        ctx.u8_to_f32(frames, None, out, 1.0, fold=4)
+    torch.cuda.synchronize()
+
+
+def _profile_dqn(args):
+    import torch
+    from ttrl_b200.algos import dqn
+    from ttrl_b200.engine.optim import Adam
+    from ttrl_b200.engine.step import TrainStep
+    from ttrl_b200.nets import build_q_net
+    np.random.seed(0)
+    online = build_q_net((4, 84, 84), 6, "cuda", batch=32)
+    target = build_q_net((4, 84, 84), 6, "cuda", batch=32)
+    opt = Adam(list(online.parameters()), lr=1e-4, eps=1.5e-4)
+    inputs = dqn.step_inputs((4, 84, 84), "cuda", batch=32, num_actions=6)
+    step = TrainStep(lambda i: dqn.update_loss(online, target, i, num_actions=6), inputs,
+                     "cuda", optimizer=opt, mode="traced_fwd_bwd")
+    rng = np.random.default_rng(1)
+    step.load_input("obs", rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8))
+    step.load_input("next_obs", rng.integers(0, 256, (32, 4, 84, 84), dtype=np.uint8))
+    step.load_input("actions_onehot", np.eye(6, dtype=np.float32)[rng.integers(0, 6, 32)])
+    for _ in range(args.reps):
+        step.launch()
+    torch.cuda.synchronize()
+    step.close()
+
+
+def _profile_ppo(args):
+    """One PPO rollout update (8 x 128 frames, 4 epochs x 4 minibatches of
+    256) replayed `reps` times from its CUDA graph."""
+    import torch
+    learner, _ = build_ppo(torch.device("cuda", 0), 0)
+    learner.capture()
+    for _ in range(args.reps):
+        learner.replay()
+    torch.cuda.synchronize()
+    learner.close()
+
+
+def _profile_rppo(args):
+    """One recurrent PPO rollout update (16 x 128 frames, T=32, GRU 256,
+    4 epochs x 4 minibatches of 16 sequences) replayed `reps` times."""
+    import torch
+    from ttrl_b200.algos.ppo import PPOConfig
+    from ttrl_b200.algos.recurrent_ppo import RecurrentPPOLearner
+    from ttrl_b200.nets import build_recurrent_actor_critic
+    np.random.seed(0)
+    net = build_recurrent_actor_critic((4, 84, 84), 6, "cuda", batch=512, hidden_size=256)
+    learner = RecurrentPPOLearner(net, 128, 16, (4, 84, 84), "cuda",
+                                  cfg=PPOConfig(minibatch_size=512), seq_len=32)
+    rng = np.random.default_rng(0)
+    shape = (128, 16)
+    learner.load_rollout(rng.integers(0, 256, shape + (4, 84, 84), dtype=np.uint8),
+                         rng.integers(0, 6, shape), np.full(shape, np.log(1 / 6), np.float32),
+                         rng.standard_normal(shape), rng.standard_normal(shape),
+                         rng.standard_normal(shape),
+                         starts=(rng.random(shape) < 0.01).astype(np.float32),
+                         hidden=np.zeros((4, 16, 256), np.float32))
+    learner.draw_permutations()
+    learner.capture()
+    for _ in range(args.reps):
+        learner.replay()
+    torch.cuda.synchronize()
+    learner.close()
+
+
+def _profile_sac(args):
+    import torch
+    from ttrl_b200.algos.sac import SACLearner
+    from ttrl_b200.nets import build_sac_nets
+    B, OBS, ACT = 256, 11, 3
+    np.random.seed(9)
+    nets = build_sac_nets(OBS, ACT, "cuda", batch=B)
+    learner = SACLearner(nets, -np.ones(ACT), np.ones(ACT), B, OBS, "cuda")
+    rng = np.random.default_rng(4)
+    learner.load_batch(obs=rng.standard_normal((B, OBS)), next_obs=rng.standard_normal((B, OBS)),
+                       actions=np.tanh(rng.standard_normal((B, ACT))),
+                       rewards=rng.standard_normal((B, 1)),
+                       dones=(rng.random((B, 1)) < 0.001) * 1.0,
+                       discounts=np.full((B, 1), 0.99), noise=rng.standard_normal((B, ACT)),
+                       next_noise=rng.standard_normal((B, ACT)))
+    for _ in range(args.reps):
+        learner.replay()
+    torch.cuda.synchronize()
+    learner.close()
+
+
+PROFILE_CASES = {f"{layer}_{kind}": _profile_conv(layer, kind)
+                 for layer in PROFILE_CONV for kind in ("fprop", "dgrad", "wgrad")}
+PROFILE_CASES.update({
+    "fc1_fwd": _profile_fc1, "adam_dqn": _profile_adam(1), "adam_dqn_x4": _profile_adam(4),
+    "sqnorm_dqn": _profile_sqnorm(1), "sqnorm_dqn_x4": _profile_sqnorm(4),
+    "u8_s2d": _profile_u8_s2d, "dqn_update": _profile_dqn, "ppo_update": _profile_ppo,
+    "rppo_update": _profile_rppo, "sac_update": _profile_sac,
+})
+
+
 def main():
     args = _args()
+    if args.profile_case is not None:
+        PROFILE_CASES[args.profile_case](args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -357,6 +357,23 @@ int ttrl_wait_probe(int* status, ttrl_stream_t stream);
  * (ttrl/algos/sac/targets.py:55-61, the Polyak blend). */
 int ttrl_polyak(float* dst, const float* src, int64_t n, float tau, ttrl_stream_t stream);
 
+/* Multi-tensor target-network update over `count` (dst, src, n) pairs in
+ * one launch (a network's parameters need not be contiguous):
+ *   TTRL_BLEND_COPY:   dst = src, bit for bit -- the DQN hard target copy
+ *     (ttrl/algos/dqn/agent.py:205-208 -> ttrl/engine/nn/module.py:164-189,
+ *     one ttnn.add(src, 0) per parameter in ttrl/engine/tensor/arena.py:35-47);
+ *   TTRL_BLEND_POLYAK: dst = (1 - tau) * dst + tau * src, in the operation
+ *     order of ttrl/algos/sac/targets.py:55-61 (PolyakSync._blend).
+ * Pairs must not overlap one another. */
+enum { TTRL_BLEND_COPY = 0, TTRL_BLEND_POLYAK = 1 };
+typedef struct {
+  float* dst;
+  const float* src;
+  int64_t n;
+} ttrl_blend_pair;
+int ttrl_blend_multi(const ttrl_blend_pair* pairs, int count, int mode, float tau,
+                     ttrl_stream_t stream);
+
 /* dst[i][:] = src[idx[i]][:] for n rows of `row` 4-byte words (fp32 or
  * int32 payloads): the minibatch gather of
  * ttrl/buffers/rollout.py:271-282, done on the device. */

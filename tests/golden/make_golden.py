@@ -489,6 +489,136 @@ def sac_losses(index):
           " ttrl/algos/gaussian.py:55-167) over preset policy outputs and action-linear critics")
 
 
+def sac_update(index):
+    """Three whole SAC updates in the reference agent's order
+    (ttrl/algos/sac/agent.py:218-238): critic_region then the critic Adam,
+    actor_region (actor and temperature losses) then the policy and
+    temperature Adams, then PolyakSync's blend (ttrl/algos/sac/targets.py:
+    45-96) -- each region zeroing all three optimizers first, as
+    RegionOptimizers does (ttrl/algos/sac/step.py:28-55). The nets are the
+    reference's build_sac_nets at BASELINE configs[2]: obs 11, actions 3 in
+    [-1, 1], twin critics 14-256-256-1 with targets, actor 11-256-256-(3, 3),
+    batch 256, tau 0.005, lr 3e-4, target entropy -3."""
+    from ttrl.algos.sac.policy import SquashedGaussian
+    from ttrl.algos.sac.step import actor_region, critic_region
+    from ttrl.algos.sac.targets import _blend
+    from ttrl.engine.autograd import Tensor
+    from ttrl.engine.optim import Adam
+    from ttrl.nets.build import build_sac_nets
+    from ttrl.nets.obs import ObsPair
+    from ttrl.spaces import ActionSpec, ObsGroup, ObsSpec
+    import ttnn
+    dev = ttnn.DEVICE
+    B, OBS, D, UPDATES = 256, 11, 3, 3
+    np.random.seed(2024)
+    spec = ObsGroup.of(ObsSpec.vector(OBS))
+    action_spec = ActionSpec.continuous([-1.0] * D, [1.0] * D)
+    nets = build_sac_nets(spec, action_spec, dev, batch=B, critic_hidden=(256, 256),
+                          encoder_kwargs={"hidden": (256, 256)})
+    dist = SquashedGaussian(action_spec, dev)
+    log_alpha = Tensor.from_numpy(np.full((1, 1), np.log(0.2), np.float32), dev,
+                                  requires_grad=True)
+    actor_opt = Adam(nets.policy_parameters(), lr=3e-4)
+    critic_opt = Adam(nets.critic_parameters(), lr=3e-4)
+    alpha_opt = Adam([log_alpha], lr=3e-4)
+    out = {f"init.{k}": v for k, v in nets.state_dict().items()}
+    out["init.log_alpha"] = log_alpha.numpy()
+    rng = np.random.default_rng(2025)
+    T = lambda a: Tensor.from_numpy(np.asarray(a, np.float32), dev)  # noqa: E731
+    for u in range(UPDATES):
+        b = {"obs": rng.standard_normal((B, OBS)), "next_obs": rng.standard_normal((B, OBS)),
+             "actions": np.tanh(rng.standard_normal((B, D))),
+             "rewards": rng.standard_normal((B, 1)),
+             "dones": (rng.random((B, 1)) < 0.05).astype(np.float64),
+             "discounts": np.full((B, 1), 0.99), "noise": rng.standard_normal((B, D)),
+             "next_noise": rng.standard_normal((B, D))}
+        b = {k: np.asarray(v, np.float32) for k, v in b.items()}
+        for k, v in b.items():
+            out[f"batch{u}.{k}"] = v
+        batch = _Batch(actions=T(b["actions"]), rewards=T(b["rewards"]), dones=T(b["dones"]),
+                       discounts=T(b["discounts"]), noise=T(b["noise"]),
+                       next_noise=T(b["next_noise"]))
+        batch.obs = ObsPair.shared({"obs": T(b["obs"])})
+        batch.next_obs = ObsPair.shared({"obs": T(b["next_obs"])})
+        for opt in (actor_opt, critic_opt, alpha_opt):
+            opt.zero_grad()
+        critic = critic_region(nets, dist, batch, log_alpha, prioritized=False)
+        critic_opt.step()
+        for opt in (actor_opt, critic_opt, alpha_opt):
+            opt.zero_grad()
+        actor = actor_region(nets, dist, batch, log_alpha, -float(D), learn_alpha=True)
+        actor_opt.step()
+        alpha_opt.step()
+        _blend(nets, 0.005)
+        for key in ("critic_loss", "alpha"):
+            out[f"update{u}.{key}"] = critic[key].numpy()
+        out[f"update{u}.q_target"] = critic["q_target"].numpy()
+        for key in ("actor_loss", "alpha_loss", "logp"):
+            out[f"update{u}.{key}"] = actor[key].numpy()
+    out.update({f"final.{k}": v for k, v in nets.state_dict().items()})
+    out["final.log_alpha"] = log_alpha.numpy()
+    _save("sac_update", out, index,
+          "three SAC updates of build_sac_nets (obs 11, act 3, hidden 256) in the agent's "
+          "order: critic_region + critic Adam, actor_region + policy and alpha Adams, "
+          "PolyakSync blend tau 0.005 (ttrl/algos/sac/{agent,step,targets}.py)")
+
+
+def conv_backward(index):
+    """The reference's own convolution backward (ttrl/engine/conv/backward.py):
+    weight_grad (k*k strided slices of X, concat, one (M, k*k*C)^T @ (M, K)
+    matmul, scaled by input_scale, into the prepared layout by
+    dw_to_prepared, transform.py:232-254) and input_grad (transpose_weight,
+    transform.py:71-100: the master unpadded, mirrored in both kernel axes,
+    channel pair swapped and padded into the transposed layout, then one
+    conv_transpose2d with mirror_kernel, transform.py:103-129) at the three
+    Nature-CNN geometries and conv1's space-to-depth form, batch 2. The
+    prepared layouts use the default padding rule (channels to 8, a kernel
+    row to 32 rows, outputs to 32 columns)."""
+    from ttrl.engine.conv.backward import input_grad, weight_grad
+    from ttrl.engine.conv.geometry import ConvGeometry
+    from ttrl.engine.conv.packing import PreparedLayout
+    from ttrl.engine.conv.transform import TransposeSpec
+    import ttnn
+    dev = ttnn.DEVICE
+
+    def layout(out_ch, in_ch, k):
+        cp = (in_ch + 7) // 8 * 8
+        row_block = (k * cp + 31) // 32 * 32
+        return PreparedLayout(rows=k * row_block, cols=(out_ch + 31) // 32 * 32, cp=cp,
+                              row_block=row_block, out_channels=out_ch, in_channels=in_ch,
+                              kernel_h=k, kernel_w=k)
+
+    out = {}
+    cases = (("conv1", 84, 4, 32, 8, 4, 1.0 / 255.0), ("conv1s2d", 21, 64, 32, 2, 1, 1.0 / 255.0),
+             ("conv2", 20, 32, 64, 4, 2, 1.0), ("conv3", 9, 64, 64, 3, 1, 1.0))
+    for i, (name, hw, c, co, k, st, scale) in enumerate(cases):
+        rng = np.random.default_rng(700 + i)
+        n = 2
+        geom = ConvGeometry(batch=n, in_channels=c, in_h=hw, in_w=hw, out_channels=co,
+                            kernel=k, stride=st, padding=0)
+        oh = geom.out_h
+        x = rng.standard_normal((n, hw, hw, c)).astype(np.float32)
+        w = (rng.standard_normal((co, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
+        dy = rng.standard_normal((n, oh, oh, co)).astype(np.float32)
+        lay = layout(co, c, k)
+        rows = lambda a: ttnn.Tensor(a.reshape(1, 1, -1, a.shape[-1]), _dev=dev)  # noqa: E731
+        dw = weight_grad(rows(x), rows(dy), geom, lay, dev, input_scale=scale)
+        tspec = TransposeSpec(batch=n, in_channels=co, out_channels=c, in_h=oh, in_w=oh,
+                              kernel=k, stride=st, padding=0, layout=layout(c, co, k),
+                              shard_layout=None, conv_cfg=None)
+        master = ttnn.Tensor(lay.pack(w), _dev=dev)
+        dx = input_grad(rows(dy), master, SimpleNamespace(layout=lay), tspec, dev,
+                        input_scale=scale)
+        out.update({f"{name}.x": x, f"{name}.w": w, f"{name}.dy": dy,
+                    f"{name}.scale": np.float32(scale),
+                    f"{name}.dw": lay.unpack(dw.to_numpy()),
+                    f"{name}.dx": dx.to_numpy().reshape(n, hw, hw, c)})
+    _save("conv_backward", out, index,
+          "ttrl/engine/conv/backward.py weight_grad and input_grad (with transform.py's "
+          "dw_to_prepared / transpose_weight) over the stand-in's conv_transpose2d; "
+          "x/dy NHWC, w/dw OIHW, dx NHWC")
+
+
 def recurrent_ppo(index):
     """One recurrent PPO minibatch through the reference's own pieces:
     build_recurrent_actor_critic (MLP trunk -> GRU -> heads), a
@@ -796,7 +926,8 @@ def main() -> None:
         with open(index_path) as f:
             index = json.load(f)
     for fn in (adam_scalars, adam_steps, dqn_loss, ppo_objective, linear_mlp, conv_tower,
-               grad_clip, gru, param_sync, sac_losses, recurrent_ppo, rollout_gae,
+               grad_clip, gru, param_sync, sac_losses, sac_update, conv_backward,
+               recurrent_ppo, rollout_gae,
                priority_replay, checkpoint_dqn, state_names):
         if only and fn.__name__ not in only:
             continue

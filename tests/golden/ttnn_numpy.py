@@ -69,6 +69,9 @@ class Tensor:
     def to_numpy(self):
         return self.array.copy()
 
+    def get_layout(self):
+        return getattr(self, "_layout", ROW_MAJOR_LAYOUT)
+
     def __repr__(self):
         return f"ttnn_numpy.Tensor(shape={self.shape}, dtype={self.dtype})"
 
@@ -261,3 +264,55 @@ def is_device_tensor(t):
 def copy_host_to_device_tensor(host, dst, **_):
     dst.array[...] = _arr(host)
     return dst
+
+
+def to_layout(a, layout, **_):
+    """Layouts only tag the tensor here: the values are the same numbers."""
+    out = Tensor(_arr(a), getattr(a, "dtype", float32), _dev=_dev_of(a))
+    out._layout = layout
+    return out
+
+
+def permute(a, dims, **_):
+    return _out(np.transpose(_arr(a), tuple(dims)), a)
+
+
+def conv_transpose2d(*, input_tensor, weight_tensor, in_channels, out_channels, batch_size,
+                     input_height, input_width, kernel_size, stride, padding,
+                     output_padding=(0, 0), dilation=(1, 1), groups=1, mirror_kernel=True, **_):
+    """Transposed convolution, as documented: the adjoint of a convolution
+    with the same kernel, stride and padding (PyTorch's conv_transpose2d
+    arithmetic), over row-major NHWC rows [1, 1, N*H*W, Cin]; with
+    mirror_kernel the op first mirrors the kernel in both spatial axes.
+
+    The weight is a prepared matrix [1, 1, rows, cols] indexed
+    M[r * row_block + q * cp + c, k] = W[r, q, c, k] (c: input channel, k:
+    output channel), with the default padding rule of this stand-in's device
+    library: cp = in_channels rounded up to 8, row_block = rows / kernel."""
+    if tuple(dilation) != (1, 1) or groups != 1 or tuple(output_padding) != (0, 0):
+        raise NotImplementedError("conv_transpose2d stand-in: dilation, groups and "
+                                  "output_padding are not modelled")
+    kh, kw = kernel_size
+    sh, sw = stride
+    ph, pw = padding
+    n, h, w, ci, co = batch_size, input_height, input_width, in_channels, out_channels
+    x = _arr(input_tensor).astype(np.float64).reshape(n, h, w, ci)
+    m = _arr(weight_tensor).astype(np.float64)
+    rows, cols = m.shape[-2], m.shape[-1]
+    cp = (ci + 7) // 8 * 8
+    row_block = rows // kh
+    if rows % kh or row_block < kw * cp or cols < co:
+        raise ValueError(f"conv_transpose2d stand-in: weight {m.shape} is not a prepared "
+                         f"{kh}x{kw} kernel for {ci} -> {co} channels")
+    wk = m.reshape(kh, row_block, cols)[:, :kw * cp].reshape(kh, kw, cp, cols)[:, :, :ci, :co]
+    if mirror_kernel:
+        wk = wk[::-1, ::-1]
+    oh = (h - 1) * sh - 2 * ph + kh
+    ow = (w - 1) * sw - 2 * pw + kw
+    full = np.zeros((n, (h - 1) * sh + kh, (w - 1) * sw + kw, co))
+    for r in range(kh):
+        for q in range(kw):
+            full[:, r:r + (h - 1) * sh + 1:sh, q:q + (w - 1) * sw + 1:sw, :] += \
+                x @ wk[r, q]
+    out = full[:, ph:ph + oh, pw:pw + ow, :]
+    return _out(out.reshape(1, 1, n * oh * ow, co).astype(np.float32), input_tensor)

@@ -188,3 +188,19 @@ def test_learner_state_packs_conv_moments_into_the_stored_layout(ref_path):
             assert lay.padding_is_zero(out["m"][i])
         else:
             assert np.array_equal(out["m"][i], m[i])
+
+
+def test_ambiguous_prepared_layout_is_refused_not_guessed():
+    """A prepared matrix wider than the default whose second moment is all
+    zero (a weight that never had a gradient) fits several channel strides:
+    the strict solver refuses instead of picking one."""
+    from ttrl_b200.engine.packing import AmbiguousLayout, candidate_layouts, solve_cp
+    oihw = (32, 4, 8, 8)
+    shape = (1, 1, 8 * 64, 32)  # row_block 64 holds cp = 4..8 for an 8-wide kernel row
+    assert len(candidate_layouts(shape[2], shape[3], *oihw)) > 1
+    with pytest.raises(AmbiguousLayout):
+        solve_cp(shape, oihw, v=np.zeros(shape, np.float32), strict=True)
+    # A trained v (non-zero on every live entry of one layout) resolves it.
+    lay = candidate_layouts(shape[2], shape[3], *oihw)[-1]
+    v = lay.pack(np.full(oihw, 0.5, np.float32))
+    assert solve_cp(shape, oihw, v=v, strict=True) == lay

@@ -165,7 +165,7 @@ def test_param_sync_errors():
     mods = [_module(([1.0], [1.0])), _module(([3.0], [3.0]))]
     with pytest.raises(ParamSyncError, match="reduction failed on parameter 0"):
         ParamSync(mods, reduce_fn=raising).average()
-    with pytest.raises(ParamSyncError, match="returned 1 results"):
+    with pytest.raises(ParamSyncError, match="1 result.* for 2 replica"):
         ParamSync(mods, reduce_fn=lambda arrays: arrays[:1]).average()
     # Nothing was written back by the failed calls.
     assert mods[0].w.numpy().tolist() == [1.0]
@@ -224,3 +224,58 @@ def test_conv_geometry_matches_reference():
                 conv_out_size(int(size), int(k), int(s), int(p))
         else:
             assert conv_out_size(int(size), int(k), int(s), int(p)) == want
+
+
+_GLOO_FAULT_WORKER = r"""
+import os, sys, torch, torch.distributed as dist
+sys.path[:0] = [{root!r}, os.path.join({root!r}, "tt-rl_b200")]
+from datetime import timedelta
+rank = int(sys.argv[1])
+dist.init_process_group("gloo", init_method="tcp://127.0.0.1:{port}", rank=rank,
+                        world_size=2, timeout=timedelta(seconds=30))
+from ttrl_b200.engine.autograd import Tensor
+from ttrl_b200.engine.nn import Module
+from ttrl_b200.engine.mesh import ParamSync, ParamSyncError
+class Net(Module):
+    def __init__(self, r):
+        self.w = Tensor(torch.full((3, 4), float(r + 1)), requires_grad=True)
+net = Net(rank)
+sync = ParamSync([net], sync_every=1, group=dist.group.WORLD, timeout_s=5.0)
+# The arena is what the collective reduces: no packing copies.
+assert sync.arena.data_ptr() == net.w.data.data_ptr()
+dist.barrier()
+if rank == 1:
+    # This rank fails between updates and never joins the average.
+    os._exit(3)
+try:
+    sync.average()
+    outcome = "averaged"
+except ParamSyncError as exc:
+    outcome = "ParamSyncError " + str(exc).splitlines()[0][:200]
+with open(os.path.join({out!r}, "rank0.txt"), "w") as f:
+    f.write(outcome + "\n" + repr(net.w.numpy().ravel().tolist()))
+os._exit(0)
+"""
+
+
+def test_param_sync_gloo_rank_that_fails_mid_run():
+    """A rank that dies instead of joining an average: the surviving rank's
+    average() ends with ParamSyncError within its bound, its parameters
+    untouched (tests/engine/test_mesh_sync.py:47-118 holds the in-process
+    counterparts)."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as out:
+        script = os.path.join(out, "worker.py")
+        with open(script, "w") as f:
+            f.write(_GLOO_FAULT_WORKER.format(root=ROOT, port=port, out=out))
+        procs = [subprocess.Popen([sys.executable, script, str(r)]) for r in range(2)]
+        codes = [p.wait(timeout=180) for p in procs]
+        assert codes == [0, 3]
+        with open(os.path.join(out, "rank0.txt")) as f:
+            outcome, values = f.read().splitlines()
+    assert outcome.startswith("ParamSyncError"), outcome
+    assert "all-reduce over 2 ranks did not complete" in outcome
+    assert values == repr([1.0] * 12)

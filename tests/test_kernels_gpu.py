@@ -433,3 +433,37 @@ def test_bounded_wait_gives_up_and_the_context_stays_usable():
     y = torch.empty(64, 16, device="cuda")
     ctx.linear_fwd(x, w, None, y, relu=False)
     assert rel(host(y), host(x).astype(np.float64) @ host(w).astype(np.float64)) <= TOL_X3
+
+
+_REF_CONV = (("conv1", 4), ("conv1s2d", 1), ("conv2", 2), ("conv3", 1))
+
+
+@pytest.mark.parametrize("name,stride", _REF_CONV)
+def test_conv_backward_matches_the_reference_composition(name, stride):
+    """The tcgen05 weight and data gradients against the reference's own
+    conv backward (tests/golden/conv_backward.npz: ttrl/engine/conv/
+    backward.py weight_grad -- k*k strided slices, one matmul, x input_scale,
+    dw_to_prepared -- and input_grad -- transpose_weight then
+    conv_transpose2d), at the Nature geometries and conv1's space-to-depth
+    form. Split-TF32 against the fixture's fp32: 1e-4 relative."""
+    import os
+    from ttrl_b200.device import conv_geom
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                             "conv_backward.npz"))
+    x, wt, dy = d[name + ".x"], d[name + ".w"], d[name + ".dy"]
+    scale = float(d[name + ".scale"])
+    n, h, w, c = x.shape
+    cout, k = wt.shape[0], wt.shape[2]
+    ctx = _ctx()
+    geom = conv_geom(n, h, w, c, cout, k, k, stride, 0)
+    dw = torch.empty((cout, k, k, c), device="cuda")
+    db = torch.empty((cout,), device="cuda")
+    ctx.conv_wgrad(dev(x.reshape(-1, c)), dev(dy.reshape(-1, cout)), dw, db, geom, scale,
+                   accumulate=False, accumulate_db=False)
+    assert rel(ol.krsc_to_oihw(host(dw)), d[name + ".dw"]) <= TOL_X3
+    # The reference scales the transposed weight by input_scale; the data
+    # gradient is linear in it, so the same scale goes on the weight here.
+    dx = torch.empty((n * h * w, c), device="cuda")
+    ctx.conv_dgrad(dev(dy.reshape(-1, cout)), dev(ol.oihw_to_krsc(wt * np.float32(scale))),
+                   None, dx, geom, accumulate=False)
+    assert rel(host(dx).reshape(x.shape), d[name + ".dx"]) <= TOL_X3

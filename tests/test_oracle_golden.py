@@ -288,3 +288,43 @@ def test_priority_replay():
         assert np.array_equal(lanes, d[f"d{k}_lanes"])
         assert np.array_equal(offsets, d[f"d{k}_offsets"])
         assert np.array_equal(weights, d[f"d{k}_weights"])
+
+
+def test_sac_whole_update():
+    """The oracle's whole SAC update (critic step, actor and temperature
+    steps, Polyak) against three updates of the reference's own
+    build_sac_nets / critic_region / actor_region / Adam / PolyakSync blend
+    at BASELINE configs[2] shapes. The fixture is float32; the oracle is
+    float64: losses to 1e-6, every parameter to 1e-5 relative Frobenius."""
+    from oracle import sac
+    d = load("sac_update")
+    p = {k[len("init."):]: d[k] for k in d.files if k.startswith("init.")}
+    adam, steps = {}, {}
+    for u in range(3):
+        batch = {k.split(".", 1)[1]: d[k] for k in d.files if k.startswith(f"batch{u}.")}
+        p, adam, steps, m = sac.sac_update(p, adam, steps, batch, low=-np.ones(3),
+                                           high=np.ones(3))
+        for key in ("critic_loss", "actor_loss", "alpha_loss", "alpha"):
+            want = float(d[f"update{u}.{key}"].reshape(-1)[0])
+            assert abs(m[key] - want) <= 1e-6 * max(1.0, abs(want)), (u, key)
+        assert np.allclose(m["logp"], d[f"update{u}.logp"][:, 0], rtol=0, atol=5e-5)
+    assert steps == {"critic": 3, "policy": 3, "alpha": 3}
+    for name, value in p.items():
+        want = d["final." + name]
+        err = np.linalg.norm(value.reshape(want.shape) - want) / np.linalg.norm(want)
+        assert err <= 1e-5, (name, err)
+
+
+@pytest.mark.parametrize("name,stride", [("conv1", 4), ("conv1s2d", 1), ("conv2", 2),
+                                         ("conv3", 1)])
+def test_conv_backward_against_the_reference(name, stride):
+    """The oracle's conv dW and dX against the reference's own weight_grad
+    and input_grad (ttrl/engine/conv/backward.py:33-78 with transform.py's
+    weight transforms) run over the stand-in: 1e-5 of the largest entry."""
+    d = load("conv_backward")
+    x, w, dy = (d[f"{name}.{k}"].astype(np.float64) for k in ("x", "w", "dy"))
+    scale = float(d[f"{name}.scale"])
+    dw = L.conv2d_wgrad(x, dy, w.shape[2], stride=stride, input_scale=scale)
+    dx = L.conv2d_dgrad(dy, w, x.shape, stride=stride, input_scale=scale)
+    assert rel(np.asarray(dw).reshape(w.shape), d[f"{name}.dw"]) <= 1e-5
+    assert rel(np.asarray(dx).reshape(x.shape), d[f"{name}.dx"]) <= 1e-5

@@ -173,3 +173,62 @@ def test_staged_rollout_upload_equals_direct_load():
         for g, want in zip(got, rollouts[k]):
             assert np.array_equal(g.cpu().numpy().reshape(-1), np.asarray(want).reshape(-1))
     learner.close()
+
+
+def test_ppo_update_at_the_timed_configuration():
+    """BASELINE configs[1] exactly, the workload bench.py times: a rollout of
+    8 envs x 128 steps (1,024 samples), 4 epochs x 4 minibatches of 256 =
+    16 graph-replayed gradient steps, clip 0.1, value clip 0.1, vf 0.5, ent
+    0.01, Adam 2.5e-4 with grad-norm clip 0.5, against the float64 oracle on
+    the same permutations.
+
+    Every step's loss and gradient norm (from the metric rows the graph
+    writes) to 1e-4 relative; the norm sums every gradient, including those
+    whose ReLU kinks the float64 oracle places differently. Parameters after the 16 Adam steps to 3e-3
+    relative Frobenius: with eps = 1e-8 Adam moves an element by about lr
+    whatever its gradient's size, so the few elements whose gradient sits
+    near zero carry fp32-versus-float64 rounding into full-size steps, and
+    that grows with the step count (1e-3 after 4 steps of one epoch, 2e-3
+    after 8 steps of two)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from ttrl_b200.algos.ppo import PPOConfig, PPOLearner, initial_old_logp
+    from ttrl_b200.nets import build_actor_critic
+
+    rng = np.random.default_rng(101)
+    p = ref.nature_params(rng, heads=(("pi", 6), ("v", 1)))
+    net = build_actor_critic((4, 84, 84), 6, "cuda", batch=256)
+    net.load_state_dict(nature_state_dict(p, heads=("pi", "v")))
+    n = 8 * 128
+    obs, actions, adv, returns = _rollout(rng, n)
+    old_logp, values = initial_old_logp(net, obs, actions, "cuda")
+    cfg = PPOConfig(epochs=4, minibatch_size=256)
+    learner = PPOLearner(net, n, (4, 84, 84), "cuda", cfg=cfg, seed=5)
+    assert learner.steps_per_update == 16
+    learner.load_rollout(obs, actions, old_logp, values, returns, adv)
+    learner.draw_permutations()
+    perms = learner.perm_host.numpy().copy()
+    assert perms.shape == (16, 256)
+    learner.replay()
+    rows = learner.metric_buf.detach().cpu().numpy()
+    torch.cuda.synchronize()
+
+    adv_n = (adv - adv.mean()) / (adv.std() + 1e-8)
+    params = {k: v.astype(np.float64) for k, v in p.items()}
+    state = {}
+    x_all = nchw_to_nhwc(obs).astype(np.float64)
+    for t, idx in enumerate(perms, start=1):
+        m, _, params, state, _ = ref.ppo_minibatch_step(
+            params, state, t, x_all[idx], actions[idx], old_logp[idx].astype(np.float64),
+            adv_n[idx].astype(np.float64), returns[idx].astype(np.float64),
+            values[idx].astype(np.float64), lr=cfg.lr, eps=cfg.eps,
+            max_grad_norm=cfg.max_grad_norm)
+        assert rel(rows[t - 1, 0], m["loss"]) <= 1e-4, (t, rows[t - 1, 0], m["loss"])
+        norm = float(np.sqrt(rows[t - 1, 4]))
+        assert rel(norm, m["grad_norm"]) <= 1e-4, (t, norm, m["grad_norm"])
+    sd = net.state_dict()
+    want = nature_state_dict(params, heads=("pi", "v"))
+    for name in sd:
+        assert rel(sd[name], want[name]) <= 3e-3, name
+    assert learner.optimizer.steps == [16] * len(learner.params)
+    learner.close()

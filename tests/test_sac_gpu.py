@@ -157,3 +157,46 @@ def test_sac_learner_graph_replay_equals_eager():
     eager.close()
     graph.close()
     one.close()
+
+
+def test_sac_learner_matches_the_reference_update():
+    """SACLearner at BASELINE configs[2] (obs 11, actions 3, twin critics and
+    actor with 256-wide layers, batch 256, tau 0.005, lr 3e-4, learned
+    temperature with target entropy -3), three graph-replayed updates,
+    against three updates of the reference's own SAC code
+    (tests/golden/sac_update.npz: ttrl/algos/sac/agent.py:218-238 order --
+    critic step, then actor and temperature steps, then the Polyak blend).
+
+    Losses to 1e-5 relative. Every parameter (policy, critics, targets,
+    log alpha) to 1e-4 relative Frobenius after the three Adam steps: the
+    contractions are split-TF32 against the fixture's fp32."""
+    _need_gpu()
+    from ttrl_b200.algos.sac import SACConfig, SACLearner
+    from ttrl_b200.nets import build_sac_nets
+    d = np.load(os.path.join(GOLDEN, "sac_update.npz"))
+    B, OBS, ACT = 256, 11, 3
+    nets = build_sac_nets(OBS, ACT, "cuda", batch=B)
+    init = {k[len("init."):]: d[k] for k in d.files
+            if k.startswith("init.") and k != "init.log_alpha"}
+    nets.load_state_dict(init)
+    learner = SACLearner(nets, -np.ones(ACT), np.ones(ACT), B, OBS, "cuda",
+                         cfg=SACConfig(init_alpha=0.2, target_entropy=-3.0))
+    learner.log_alpha.data.copy_(torch.from_numpy(d["init.log_alpha"]))
+    for u in range(3):
+        batch = {k.split(".", 1)[1]: d[k] for k in d.files if k.startswith(f"batch{u}.")}
+        learner.load_batch(**batch)
+        learner.replay()
+        got = learner.read_metrics()
+        for key in ("critic_loss", "actor_loss", "alpha_loss"):
+            want = float(d[f"update{u}.{key}"].reshape(-1)[0])
+            assert rel(got[key], want) <= 1e-5, (u, key, got[key], want)
+    sd = nets.state_dict()
+    assert set(sd) == set(init)
+    for name, value in sd.items():
+        want = d["final." + name]
+        err = np.linalg.norm(value.reshape(want.shape) - want) / np.linalg.norm(want)
+        assert err <= 1e-4, (name, err)
+    la = learner.log_alpha.numpy().reshape(1, 1)
+    assert rel(la, d["final.log_alpha"]) <= 1e-5
+    assert learner.critic_opt.steps == [3] * len(learner.critic_opt.params)
+    learner.close()

@@ -85,10 +85,14 @@ def test_noalloc_refuses_oversized_scratch():
     w = torch.zeros((k, n), device=dev)
     y = torch.zeros((m, n), device=dev)
     status = torch.zeros(4, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    launched = lib.ttrl_launch_count()
     rc = lib.ttrl_linear_fwd_noalloc(x.data_ptr(), w.data_ptr(), None, y.data_ptr(), m, k, n,
                                      0, 0, status.data_ptr(),
                                      torch.cuda.current_stream(dev).cuda_stream)
     assert rc == EWORKSPACE
+    # Refused before anything was enqueued: no kernel of the library ran.
+    assert lib.ttrl_launch_count() == launched
     msg = lib.ttrl_last_error().decode()
     assert "ttrl_linear_fwd_noalloc" in msg and str(NOALLOC_SCRATCH_BYTES) in msg
     torch.cuda.synchronize(dev)

@@ -60,6 +60,7 @@ int reduce(int, const float*, float*, int64_t, int64_t, int64_t, cudaStream_t);
 int copy_strided(float*, const int64_t*, const float*, const int64_t*, const int64_t*, int, int,
                  cudaStream_t);
 int polyak(float*, const float*, int64_t, float, cudaStream_t);
+int blend_multi(const ttrl_blend_pair*, int, int, float, cudaStream_t);
 int wait_probe(int*, cudaStream_t);
 int gather_rows(const void*, const int32_t*, void*, int, int, cudaStream_t);
 
@@ -226,6 +227,11 @@ int ttrl_wait_probe(int* status, ttrl_stream_t stream) {
 
 int ttrl_polyak(float* dst, const float* src, int64_t n, float tau, ttrl_stream_t stream) {
   return polyak(dst, src, n, tau, TTRL_STREAM(stream));
+}
+
+int ttrl_blend_multi(const ttrl_blend_pair* pairs, int count, int mode, float tau,
+                     ttrl_stream_t stream) {
+  return blend_multi(pairs, count, mode, tau, TTRL_STREAM(stream));
 }
 
 int ttrl_gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row,

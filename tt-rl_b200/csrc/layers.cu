@@ -84,6 +84,14 @@ static int check_conv(const ttrl_conv_geom* g) {
 
 // ---------------------------------------------------------------- Linear
 
+// Workspace bytes linear_fwd needs: the same orientation rule as below
+// (output features as tile rows when the batch is narrower).
+size_t linear_fwd_ws(int m, int k, int n, int precision) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return gemm_workspace_bytes(m < 128 && n > m ? make_desc(n, m, k, precision)
+                                               : make_desc(m, n, k, precision));
+}
+
 int linear_fwd(const float* x, const float* w, const float* b, float* y, int m, int k, int n,
                int relu, int precision, float* ws, size_t wsb, int* status, cudaStream_t st) {
   if (m <= 0 || n <= 0 || k <= 0) return set_error(TTRL_EINVAL, "linear_fwd: bad extents");

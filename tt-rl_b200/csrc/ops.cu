@@ -278,11 +278,107 @@ int polyak(float* dst, const float* src, int64_t n, float tau, cudaStream_t st) 
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("polyak launch", e);
 }
 
+// ------------------------------------------------- multi-tensor blend/copy
+
+// One launch over a list of (dst, src, n) pairs: the DQN hard target copy
+// (dst = src, bit for bit) or the Polyak blend (dst = (1-tau) dst + tau src)
+// of every parameter of a network. The pairs are cut into tiles of
+// kBlendTile elements; a block takes tiles in a grid-stride loop and finds
+// each tile's pair among the <= kBlendMax prefix sums.
+constexpr int kBlendMax = 48;
+constexpr int kBlendTile = 4096;
+
+struct BlendArgs {
+  int count;
+  int mode;
+  float keep, take;
+  float* dst[kBlendMax];
+  const float* src[kBlendMax];
+  int64_t n[kBlendMax];
+  int64_t first_tile[kBlendMax + 1];
+};
+
+__global__ void __launch_bounds__(256) blend_kernel(const __grid_constant__ BlendArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t tiles = a.first_tile[a.count];
+  int t = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    while (a.first_tile[t + 1] <= tile) ++t;
+    const int64_t base = (tile - a.first_tile[t]) * kBlendTile;
+    const int64_t left = a.n[t] - base;
+    const int64_t len = left < kBlendTile ? left : kBlendTile;
+    float* __restrict__ d = a.dst[t] + base;
+    const float* __restrict__ s = a.src[t] + base;
+    const bool vec = ((reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(s)) & 15) == 0;
+    const int64_t nvec = vec ? len / 4 : 0;
+    for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x) {
+      const float4 x = reinterpret_cast<const float4*>(s)[i];
+      float4 y;
+      if (a.mode == TTRL_BLEND_COPY) {
+        y = x;
+      } else {
+        // Order of ttrl/algos/sac/targets.py:55-61: add(mul(dst, 1-tau),
+        // mul(src, tau)), each rounded on its own (no fused multiply-add).
+        const float4 o = reinterpret_cast<const float4*>(d)[i];
+        y.x = __fadd_rn(__fmul_rn(o.x, a.keep), __fmul_rn(x.x, a.take));
+        y.y = __fadd_rn(__fmul_rn(o.y, a.keep), __fmul_rn(x.y, a.take));
+        y.z = __fadd_rn(__fmul_rn(o.z, a.keep), __fmul_rn(x.z, a.take));
+        y.w = __fadd_rn(__fmul_rn(o.w, a.keep), __fmul_rn(x.w, a.take));
+      }
+      reinterpret_cast<float4*>(d)[i] = y;
+    }
+    for (int64_t i = nvec * 4 + threadIdx.x; i < len; i += blockDim.x) {
+      if (a.mode == TTRL_BLEND_COPY) {
+        d[i] = s[i];
+      } else {
+        d[i] = __fadd_rn(__fmul_rn(d[i], a.keep), __fmul_rn(s[i], a.take));
+      }
+    }
+  }
+}
+
+int blend_multi(const ttrl_blend_pair* pairs, int count, int mode, float tau, cudaStream_t st) {
+  if (count < 0 || (count > 0 && pairs == nullptr))
+    return set_error(TTRL_EINVAL, "blend_multi: bad pair list");
+  if (mode != TTRL_BLEND_COPY && mode != TTRL_BLEND_POLYAK)
+    return set_error(TTRL_EINVAL, "blend_multi: unknown mode %d", mode);
+  for (int start = 0; start < count; start += kBlendMax) {
+    BlendArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.mode = mode;
+    a.keep = 1.0f - tau;
+    a.take = tau;
+    int64_t tiles = 0;
+    for (int i = start; i < count && a.count < kBlendMax; ++i) {
+      const ttrl_blend_pair& p = pairs[i];
+      if (p.n < 0 || (p.n > 0 && (p.dst == nullptr || p.src == nullptr)))
+        return set_error(TTRL_EINVAL, "blend_multi: pair %d has a null pointer or n < 0", i);
+      if (p.n == 0) continue;
+      a.dst[a.count] = p.dst;
+      a.src[a.count] = p.src;
+      a.n[a.count] = p.n;
+      a.first_tile[a.count] = tiles;
+      tiles += (p.n + kBlendTile - 1) / kBlendTile;
+      ++a.count;
+    }
+    if (a.count == 0) continue;
+    a.first_tile[a.count] = tiles;
+    int blocks = static_cast<int>(tiles < 148 * 4 ? tiles : 148 * 4);
+    const cudaError_t le = launch_pdl(blend_kernel, dim3(blocks), dim3(256), 0, st, a);
+    note_launch();
+    const cudaError_t e = le != cudaSuccess ? le : cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("blend_multi launch", e);
+  }
+  return TTRL_OK;
+}
+
 // ------------------------------------------------------- bounded-wait check
 
 // Self-check of the library's bounded waits: one thread waits on an
-// mbarrier that nothing arrives on, gives up after the wait bound (about a
-// second), records kErrWaitTimeout in *status and returns, leaving the
+// mbarrier that nothing arrives on, gives up after the wait bound
+// (kWaitTimeoutNs, two seconds of global time), records kErrWaitTimeout in
+// *status and returns, leaving the
 // context usable. Nothing traps or faults.
 __global__ void wait_probe_kernel(int* status) {
   __shared__ __align__(8) uint64_t bar;

@@ -24,36 +24,35 @@ from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import dqn_td_huber
 
-__all__ = ["step_inputs", "update_loss", "obs_to_rows"]
+__all__ = ["DQNLearner", "step_inputs", "update_loss", "obs_to_rows"]
 
 
 def step_inputs(obs_shape, device, *, batch: int, num_actions: int, mask_n: int = 0,
                 prioritized: bool = False, uint8_frames: bool = True) -> dict:
-    """The fixed device buffers one update reads (ttrl/algos/dqn/losses.py:44-74)."""
-    dev = as_device(device)
-
-    def zeros(*shape, dtype=torch.float32):
-        return Tensor(torch.zeros(shape, dtype=dtype, device=dev))
-
-    inputs = {
-        "rewards": zeros(batch, 1),
-        "dones": zeros(batch, 1),
-        "discounts": zeros(batch, 1),
-        "actions_onehot": zeros(batch, num_actions),
-    }
+    """The fixed device buffers one update reads (ttrl/algos/dqn/losses.py:44-74),
+    laid out in one allocation so that a whole batch uploads in one copy."""
+    from ttrl_b200.engine.step import input_arena
+    f32 = torch.float32
+    specs = {"obs": None, "next_obs": None}
     shape = tuple(int(v) for v in obs_shape)
     for which in ("obs", "next_obs"):
         if len(shape) == 3 and uint8_frames:
-            inputs[which] = zeros(batch, *shape, dtype=torch.uint8)
+            specs[which] = ((batch, *shape), torch.uint8)
         elif len(shape) == 3:
             c, h, w = shape
-            inputs[which] = zeros(1, 1, batch * h * w, c)
+            specs[which] = ((1, 1, batch * h * w, c), f32)
         else:
-            inputs[which] = zeros(batch, shape[0])
+            specs[which] = ((batch, shape[0]), f32)
+    specs.update(rewards=((batch, 1), f32), dones=((batch, 1), f32),
+                 discounts=((batch, 1), f32), actions_onehot=((batch, num_actions), f32))
     if mask_n:
-        inputs["next_mask"] = Tensor(torch.ones((batch, mask_n), device=dev))
+        specs["next_mask"] = ((batch, mask_n), f32)
     if prioritized:
-        inputs["is_weights"] = Tensor(torch.ones((batch, 1), device=dev))
+        specs["is_weights"] = ((batch, 1), f32)
+    inputs = input_arena(device, specs)
+    for name in ("next_mask", "is_weights"):
+        if name in inputs:
+            inputs[name].data.fill_(1.0)
     return inputs
 
 
@@ -118,3 +117,67 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
     if grad_sq is not None:
         metrics["grad_sq"] = Tensor(grad_sq.reshape(1, 1), requires_grad=False)
     return metrics
+
+
+class DQNLearner:
+    """The learner half of the reference's DQN agent: online and target
+    Q-networks, Adam, and the update as one graph replay, with the agent's
+    target schedule -- after every `target_sync_interval`-th update the
+    target network becomes a bit-for-bit copy of the online one, in place
+    and in one launch (ttrl/algos/dqn/agent.py:180-208, which calls
+    ttrl/engine/nn/module.py:164-189). Each network's parameters sit in one
+    flat arena, so that copy is a single contiguous pair."""
+
+    def __init__(self, online, target, obs_shape, num_actions: int, device=None, *,
+                 batch: int = 32, lr: float = 1e-4, eps: float = 1e-8, double: bool = True,
+                 huber_delta: float = 1.0, target_sync_interval: int = 8_000,
+                 mask_n: int = 0, prioritized: bool = False):
+        from ttrl_b200.engine.nn import parameter_arena
+        from ttrl_b200.engine.optim import Adam
+        from ttrl_b200.engine.step import TrainStep
+        if target_sync_interval < 1:
+            raise ValueError(f"DQNLearner: target_sync_interval must be at least 1, got "
+                             f"{target_sync_interval}")
+        self.online, self.target = online, target
+        self.device = as_device(device)
+        self.online_arena = parameter_arena([online])
+        self.target_arena = parameter_arena([target])
+        self.target.copy_from(self.online)
+        self.target_sync_interval = int(target_sync_interval)
+        self.update_count = 0
+        self.optimizer = Adam(list(online.parameters()), lr=lr, eps=eps)
+        self.inputs = step_inputs(obs_shape, self.device, batch=batch, num_actions=num_actions,
+                                  mask_n=mask_n, prioritized=prioritized)
+        self.step = TrainStep(
+            lambda i: update_loss(online, target, i, num_actions=num_actions, double=double,
+                                  huber_delta=huber_delta, mask_n=mask_n,
+                                  prioritized=prioritized),
+            self.inputs, self.device, optimizer=self.optimizer, mode="traced_fwd_bwd")
+
+    def load(self, **arrays) -> None:
+        """Bind one batch of host arrays (obs, next_obs, actions_onehot,
+        rewards, dones, discounts, ...) into the update's input buffers."""
+        for name, value in arrays.items():
+            self.step.load_input(name, value)
+
+    def update(self, **arrays) -> dict:
+        """One update on the given batch (bound first when arrays are given),
+        then the target schedule; returns the update's metrics."""
+        if arrays:
+            self.load(**arrays)
+        metrics = self.step.run()
+        self._after_update()
+        return metrics
+
+    def launch(self) -> None:
+        """One update on the bound batch without reading metrics back."""
+        self.step.launch()
+        self._after_update()
+
+    def _after_update(self) -> None:
+        self.update_count += 1
+        if self.update_count % self.target_sync_interval == 0:
+            self.target.copy_from(self.online)
+
+    def close(self) -> None:
+        self.step.close()

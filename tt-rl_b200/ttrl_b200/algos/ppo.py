@@ -23,6 +23,7 @@ import torch
 
 from ttrl_b200.algos.grads import clip_grad_norm_device
 from ttrl_b200.device import context
+from ttrl_b200.engine.nn import parameter_arena
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import ppo_objective
@@ -177,6 +178,9 @@ class PPOLearner(ReplayedUpdate):
         if self.minibatches == 0 or self.minibatches * mb > self.rollout_size:
             raise ValueError(f"rollout of {rollout_size} holds no minibatch of {mb}")
         self.steps_per_update = cfg.epochs * self.minibatches
+        # One flat arena for the parameters: a replica average is one
+        # in-place collective over it (ttrl_b200.engine.mesh.ParamSync).
+        self.param_arena = parameter_arena([net])
         self.params = list(net.parameters())
         self.optimizer = Adam(self.params, lr=cfg.lr, eps=cfg.eps)
         self.rng = np.random.default_rng(seed)
@@ -228,11 +232,17 @@ class PPOLearner(ReplayedUpdate):
 
     _STAGED = ("obs", "actions", "old_logp", "values", "returns", "advantages")
 
-    def stage_rollout(self, obs_u8, actions, old_logp, values, returns, advantages) -> None:
+    def stage_rollout(self, obs_u8, actions, old_logp, values, returns,
+                      advantages) -> torch.cuda.Event:
         """Start uploading the NEXT rollout (pinned host tensors, already
         normalised advantages) into device staging buffers on a copy stream,
         beside whatever update is running; `commit_staged()` makes it the
-        rollout the next replay reads."""
+        rollout the next replay reads.
+
+        The copies read the host tensors asynchronously. The returned event
+        completes once they have; until then the host tensors must not be
+        changed (wait on it with `event.synchronize()` before refilling a
+        pinned buffer for the next rollout)."""
         if getattr(self, "_staging", None) is None:
             self._staging = {k: torch.empty_like(getattr(self, k)) for k in self._STAGED}
             self._copy_stream = torch.cuda.Stream(self.device)
@@ -247,6 +257,7 @@ class PPOLearner(ReplayedUpdate):
                 self._staging[k].copy_(t.reshape(self._staging[k].shape), non_blocking=True)
             self._staged = torch.cuda.Event()
             self._staged.record(self._copy_stream)
+        return self._staged
 
     def commit_staged(self) -> None:
         """Order the current stream after the staged upload and copy it into

@@ -32,6 +32,7 @@ import torch
 from ttrl_b200.algos.grads import clip_grad_norm_device
 from ttrl_b200.algos.ppo import PPOConfig, ReplayedUpdate
 from ttrl_b200.device import context
+from ttrl_b200.engine.nn import parameter_arena
 from ttrl_b200.engine.autograd import Tensor, as_device
 from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import ppo_objective
@@ -146,6 +147,9 @@ class RecurrentPPOLearner(ReplayedUpdate):
             raise ValueError("RecurrentPPOLearner: one shared memory is supported (a single-leaf "
                              f"observation), got memories {sorted(hidden)}")
         self.hidden_size = int(hidden[ACTOR])
+        # One flat arena for the parameters: a replica average is one
+        # in-place collective over it (ttrl_b200.engine.mesh.ParamSync).
+        self.param_arena = parameter_arena([net])
         self.params = list(net.parameters())
         self.optimizer = Adam(self.params, lr=cfg.lr, eps=cfg.eps)
         self.rng = np.random.default_rng(seed)

@@ -285,11 +285,9 @@ class SACLearner:
     # -- one update --------------------------------------------------------
 
     def _polyak(self) -> None:
-        """t <- (1 - tau) t + tau c for every target/critic pair
-        (ttrl/algos/sac/targets.py:45-96)."""
-        ctx = context(self.device)
-        for t, c in self._pairs:
-            ctx.polyak(t.data, c.data, self.cfg.tau)
+        """t <- (1 - tau) t + tau c for every target/critic pair, all pairs in
+        one launch (ttrl/algos/sac/targets.py:45-96)."""
+        context(self.device).blend([(t.data, c.data) for t, c in self._pairs], self.cfg.tau)
 
     def _update(self) -> dict:
         opts = (self.critic_opt, self.policy_opt, self.alpha_opt)

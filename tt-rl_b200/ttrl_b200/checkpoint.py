@@ -243,7 +243,12 @@ def _optimizer_state(opt, like) -> dict:
         stored_m = np.asarray(like["m"][i])
         if layout is None or stored_m.shape == tuple(layout.oihw):
             continue
-        prepared = solve_cp(stored_m.shape, layout.oihw, v=np.asarray(like["v"][i]))
+        prepared = getattr(layout, "stored_layout", None)
+        if prepared is None or prepared.shape != stored_m.shape:
+            # Not loaded from this file: recover the channel stride from the
+            # file's own second moment, refusing to guess when it cannot tell.
+            prepared = solve_cp(stored_m.shape, layout.oihw, v=np.asarray(like["v"][i]),
+                                strict=True)
         state["m"][i] = prepared.pack(state["m"][i])
         state["v"][i] = prepared.pack(state["v"][i])
     return state

@@ -474,6 +474,21 @@ class DeviceContext:
         check(lib().ttrl_copy_strided(dst.data_ptr(), ds, src.data_ptr(), ss, sh, nd,
                                       int(accumulate), self.stream), "ttrl_copy_strided")
 
+    def blend(self, pairs, tau: float | None = None) -> None:
+        """One launch over `pairs` of same-size (dst, src) fp32 tensors:
+        dst = src bit for bit (tau None: the hard target copy), else the
+        Polyak blend dst = (1 - tau) * dst + tau * src."""
+        arr = (_lib.BlendPair * max(len(pairs), 1))()
+        for i, (d, s_) in enumerate(pairs):
+            if d.numel() != s_.numel():
+                raise ValueError(f"blend: pair {i} has {d.numel()} and {s_.numel()} elements")
+            if not d.is_contiguous() or not s_.is_contiguous():
+                raise ValueError(f"blend: pair {i} is not contiguous")
+            arr[i] = _lib.BlendPair(_ptr(_f32(d, "dst")), _ptr(_f32(s_, "src")), d.numel())
+        mode = _lib.BLEND_COPY if tau is None else _lib.BLEND_POLYAK
+        check(lib().ttrl_blend_multi(arr, len(pairs), mode, float(tau or 0.0), self.stream),
+              "ttrl_blend_multi")
+
     def polyak(self, dst, src, tau: float) -> None:
         check(lib().ttrl_polyak(_ptr(_f32(dst, "dst")), _ptr(_f32(src, "src")), dst.numel(),
                                 float(tau), self.stream), "ttrl_polyak")

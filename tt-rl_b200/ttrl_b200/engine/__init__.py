@@ -30,6 +30,8 @@ _LAZY = {
     "adam_fused_scalars": "optim",
     "TrainStep": "step",
     "read_metrics": "step",
+    "InputBinder": "step",
+    "ActingCarry": "carry",
     "CapturedTrace": "trace",
     "TraceCaptureError": "trace",
     "capture": "trace",

@@ -2,8 +2,11 @@
 
 Same contract as the reference tape (ttrl/engine/autograd.py:56-235):
 `Tensor(data, requires_grad, _parents, _op)`, fp32 gradient accumulation,
-post-order DFS over an explicit stack, a scalar seed of 1.0, no
-retain_graph (the tape is torn down in a `finally`), and `no_grad`.
+every node's backward run after all of its consumers', a scalar seed of 1.0,
+no retain_graph (the tape is released whether backward finishes or raises),
+and `no_grad`. The traversal here counts, for every node reachable from the
+root, how many of its consumers are still pending, and runs a node once that
+count reaches zero (a ready stack, first parent first).
 
 Two additions serve the fused kernels:
 
@@ -30,7 +33,8 @@ __all__ = ["Tensor", "backward", "no_grad", "is_grad_enabled", "DEFAULT_DTYPE"]
 DEFAULT_DTYPE = torch.float32
 GRAD_ACCUM_DTYPE = torch.float32
 
-_GRAD_ENABLED = True
+#: Open `no_grad` blocks; recording is on only at depth zero.
+_NO_GRAD_DEPTH = 0
 
 #: The tensor whose backward() is running. A fused loss node that is the root
 #: receives the unit seed and can skip scaling its precomputed gradient.
@@ -42,21 +46,22 @@ def backward_root():
 
 
 def is_grad_enabled() -> bool:
-    return _GRAD_ENABLED
+    return _NO_GRAD_DEPTH == 0
 
 
 class no_grad:
-    """Ops built inside record no tape (ttrl/engine/autograd.py:30-44)."""
+    """Inside this block no op records a tape node (the forward-only target
+    and acting passes), as ttrl/engine/autograd.py:30-44 specifies. Blocks
+    nest; leaving the outermost one turns recording back on."""
 
     def __enter__(self):
-        global _GRAD_ENABLED
-        self._prev = _GRAD_ENABLED
-        _GRAD_ENABLED = False
+        global _NO_GRAD_DEPTH
+        _NO_GRAD_DEPTH += 1
         return self
 
     def __exit__(self, *exc):
-        global _GRAD_ENABLED
-        _GRAD_ENABLED = self._prev
+        global _NO_GRAD_DEPTH
+        _NO_GRAD_DEPTH -= 1
         return False
 
 
@@ -70,7 +75,13 @@ _UNIT_SEEDS: dict = {}
 def _unit_seed(like):
     """d(loss)/d(loss) = 1, shaped like the scalar root: one constant per
     device and shape, made outside any capture (no fill launch per
-    backward); inside a first capture, filled by a kernel instead."""
+    backward); inside a first capture, filled by a kernel instead.
+
+    The constant is shared by every backward on the device and is bound as
+    the root's `.grad` afterwards, so the root's gradient is read-only: an
+    in-place change to it would change the seed of every later backward.
+    Its fill is waited for once, on the host, before first use, so a
+    backward issued on any stream reads the finished constant."""
     key = (like.device, tuple(like.shape))
     seed = _UNIT_SEEDS.get(key)
     if seed is None:
@@ -79,6 +90,7 @@ def _unit_seed(like):
             context(like.device).ew("fill", None, None, seed, 1.0)
             return seed
         seed = torch.ones(like.shape, dtype=GRAD_ACCUM_DTYPE, device=like.device)
+        torch.cuda.current_stream(like.device).synchronize()
         _UNIT_SEEDS[key] = seed
     return seed
 
@@ -231,70 +243,80 @@ class Tensor:
         return Tensor(self.data, requires_grad=False)
 
     def backward(self):
+        """Run the tape from this scalar back to the leaves, once.
+
+        Afterwards `.grad` of this tensor is the shared unit seed: read it,
+        never write it in place."""
         if not self.requires_grad:
             raise RuntimeError(
-                "backward() called on a Tensor that requires no gradient; it "
-                "carries no tape (a leaf, a detached node, or built inside "
-                "no_grad()), so this call would silently produce no parameter "
-                "gradients at all."
-            )
+                "backward(): this tensor has requires_grad=False -- it was never "
+                "recorded (a leaf without gradient, a detach(), or a result built "
+                "under no_grad()), so there is no tape to run and no parameter "
+                "would receive a gradient.")
         if self._backward_done:
             raise RuntimeError(
-                "backward() called a second time on the same graph; this tape "
-                "does not keep saved activations alive for a second pass "
-                "(no retain_graph). Build a fresh forward pass instead."
-            )
-        topo: list[Tensor] = []
-        seen: set[int] = set()
-        stack: list[tuple[Tensor, bool]] = [(self, False)]
-        while stack:
-            node, expanded = stack.pop()
-            if expanded:
-                topo.append(node)
-                continue
-            if id(node) in seen:
-                continue
-            seen.add(id(node))
-            stack.append((node, True))
-            for parent in node._parents:
-                if id(parent) not in seen:
-                    stack.append((parent, False))
-
-        numel = 1
-        for dim in self.shape:
-            numel *= dim
-        if numel != 1:
+                "backward(): this graph's tape has already been run and released; "
+                "saved activations are not kept for a second pass. Run the "
+                "forward again to build a new graph.")
+        size = 1
+        for extent in self.shape:
+            size *= extent
+        if size != 1:
             raise RuntimeError(
-                f"backward() called on a non-scalar Tensor with shape {self.shape} "
-                f"(numel={numel}); there is no `gradient=` kwarg to seed a "
-                "non-scalar backward pass, so reduce to a scalar first."
-            )
+                f"backward(): the root must hold one value, got shape {self.shape} "
+                f"({size} values). Reduce it to a scalar (mean or sum) first; a "
+                "non-scalar seed is not supported.")
+
+        # Every node reachable from the root, and for each the number of
+        # its consumers in this graph that have yet to run.
+        pending: dict[int, int] = {id(self): 0}
+        nodes: list[Tensor] = [self]
+        frontier = [self]
+        while frontier:
+            node = frontier.pop()
+            for parent in node._parents:
+                key = id(parent)
+                if key in pending:
+                    pending[key] += 1
+                else:
+                    pending[key] = 1
+                    nodes.append(parent)
+                    frontier.append(parent)
+
         self.grad = _unit_seed(self.data)
         # Not owned: an op that accumulates into the root's gradient copies
         # it first, so the shared constant is never written.
         self._grad_owned = False
         global _BACKWARD_ROOT
-        prev_root, _BACKWARD_ROOT = _BACKWARD_ROOT, self
+        outer_root, _BACKWARD_ROOT = _BACKWARD_ROOT, self
         try:
-            for node in reversed(topo):
-                grad = node.grad
-                if grad is not None:
+            ready = [self]
+            while ready:
+                node = ready.pop()
+                if node.grad is not None:
                     if node._backward_done and node is not self:
                         raise RuntimeError(
-                            "backward() reached a node whose tape was already "
-                            "consumed by a previous backward() call on a graph "
-                            "sharing this subgraph; reusing a consumed subgraph "
-                            "is not supported (no retain_graph)."
-                        )
-                    node._backward(grad)
+                            "backward(): part of this graph was already consumed by an "
+                            "earlier backward() (a subgraph shared by two losses); its "
+                            "saved activations are gone. Build each loss from its own "
+                            "forward pass.")
+                    node._backward(node.grad)
+                # Parents whose last consumer this was become ready; pushed
+                # last-to-first so the first parent is taken next.
+                for parent in reversed(node._parents):
+                    key = id(parent)
+                    pending[key] -= 1
+                    if pending[key] == 0:
+                        ready.append(parent)
         finally:
-            _BACKWARD_ROOT = prev_root
+            _BACKWARD_ROOT = outer_root
             # Weight gradients issued on side lanes are complete before
             # anything after backward() runs on the current stream.
             context(self.data.device).join()
-            for node in topo:
-                if node._op:
-                    node._backward_done = True
+            # Release the tape. Leaves stay usable by the next step's graph,
+            # so only recorded nodes are marked as consumed.
+            for node in nodes:
+                node._backward_done = node._backward_done or bool(node._op)
                 node._backward = _no_backward
                 node._parents = ()
 
@@ -342,7 +364,7 @@ def _is_scalar(x) -> bool:
 
 
 def _needs(*tensors) -> bool:
-    return _GRAD_ENABLED and any(t.requires_grad for t in tensors)
+    return _NO_GRAD_DEPTH == 0 and any(t.requires_grad for t in tensors)
 
 
 def _detached(data) -> Tensor:

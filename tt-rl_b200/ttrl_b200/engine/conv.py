@@ -30,7 +30,7 @@ import torch
 
 from ttrl_b200.device import context, conv_geom
 from ttrl_b200.engine.autograd import Tensor, as_device
-from ttrl_b200.engine.nn import Module
+from ttrl_b200.engine.nn import Module, check_state_layout
 from ttrl_b200.engine.ops import conv2d_nhwc
 from ttrl_b200.engine.packing import default_layout, solve_cp
 from ttrl_b200.engine.tensor import restore_in_place
@@ -247,21 +247,11 @@ class Conv2d(Module):
         return state
 
     def load_state_dict(self, state: dict, device=None) -> None:
-        reference = self.state_dict()
-        got, expected = set(state.keys()), set(reference)
-        if got != expected:
-            raise ValueError(
-                "load_state_dict: checkpoint keys do not match module "
-                f"parameters (missing={sorted(expected - got)}, "
-                f"extra={sorted(got - expected)})"
-            )
-        for name, want in reference.items():
-            shape = tuple(int(d) for d in np.asarray(state[name]).shape)
-            if shape != want.shape:
-                raise ValueError(
-                    f"load_state_dict: shape mismatch for {name!r}: "
-                    f"checkpoint has {shape}, parameter expects {want.shape}"
-                )
+        """OIHW weight (and (1,1,1,C) bias) into the device buffers, in place."""
+        layout = {"weight": self._oihw_shape}
+        if self.bias is not None:
+            layout["bias"] = tuple(self.bias.data.shape)
+        check_state_layout(state, layout, "Conv2d")
         self.load_weight_numpy(state["weight"])
         if self.bias is not None:
             restore_in_place(self.bias.data, state["bias"])
@@ -322,6 +312,8 @@ class ConvWeightLayout:
         self.oihw = tuple(int(d) for d in conv._oihw_shape)
         self._to_device = conv._to_device_layout
         self._from_device = conv._from_device_layout
+        # The prepared layout a checkpoint's moments were read in, if any.
+        self.stored_layout = None
 
     def to_portable(self, device_array) -> np.ndarray:
         return self._from_device(np.asarray(device_array, np.float32))
@@ -334,6 +326,10 @@ class ConvWeightLayout:
         if a.shape == self.oihw:
             return self._to_device(a)
         layout = solve_cp(a.shape, self.oihw, v=v)
+        # Kept so that writing the moments back packs them into the rows
+        # they were read from, even after training has made v ambiguous or
+        # for a v that was zero at load.
+        self.stored_layout = layout
         return self._to_device(layout.unpack(a))
 
     def to_stored(self, device_array, like=None, *, v_like=None) -> np.ndarray:
@@ -342,7 +338,10 @@ class ConvWeightLayout:
         w = self.to_portable(device_array)
         if like is None or np.shape(like) == self.oihw:
             return w
-        return solve_cp(np.shape(like), self.oihw, v=v_like).pack(w)
+        layout = self.stored_layout
+        if layout is None or layout.shape != tuple(np.shape(like)):
+            layout = solve_cp(np.shape(like), self.oihw, v=v_like, strict=True)
+        return layout.pack(w)
 
     def prepared(self, device_array) -> np.ndarray:
         """The moment in the reference device library's default prepared layout."""

@@ -32,10 +32,8 @@ class Linear(Module):
 
     def __init__(self, in_features: int, out_features: int, device=None, *, bias: bool = True):
         if in_features <= 0 or out_features <= 0:
-            raise ValueError(
-                "Linear: in_features and out_features must be > 0, got "
-                f"in_features={in_features}, out_features={out_features}"
-            )
+            raise ValueError(f"Linear({in_features}, {out_features}): both widths have to be "
+                             "positive")
         self.in_features = int(in_features)
         self.out_features = int(out_features)
         bound = 1.0 / math.sqrt(in_features)
@@ -61,9 +59,11 @@ class LayerNorm(Module):
 
     def __init__(self, normalized_shape: int, device=None, *, eps: float = 1e-5):
         if normalized_shape <= 0:
-            raise ValueError(f"LayerNorm: normalized_shape must be > 0, got {normalized_shape}")
+            raise ValueError(f"LayerNorm({normalized_shape}): the normalised width has to be "
+                             "positive")
         if eps <= 0.0:
-            raise ValueError(f"LayerNorm: eps must be > 0, got {eps}")
+            raise ValueError(f"LayerNorm(eps={eps}): eps has to be positive, since a row of "
+                             "equal values has zero variance")
         self.normalized_shape = int(normalized_shape)
         self.eps = float(eps)
         dev = as_device(device)
@@ -74,10 +74,9 @@ class LayerNorm(Module):
 
     def forward(self, x: Tensor) -> Tensor:
         if int(x.shape[-1]) != self.normalized_shape:
-            raise ValueError(
-                f"LayerNorm({self.normalized_shape}): expected a last axis of "
-                f"{self.normalized_shape} features, got shape {tuple(x.shape)}."
-            )
+            raise ValueError(f"LayerNorm({self.normalized_shape}) was given an input of shape "
+                             f"{tuple(x.shape)}, whose last axis is not {self.normalized_shape} "
+                             "wide")
         centred = sub(x, mean_dim(x, dim=-1))
         variance = mean_dim(square(centred), dim=-1)
         return add(mul(div(centred, sqrt(add(variance, self.eps))), self.weight), self.bias)
@@ -130,7 +129,7 @@ class Flatten(Module):
 
     def __init__(self, h: int, w: int, channels: int):
         if h <= 0 or w <= 0 or channels <= 0:
-            raise ValueError(f"Flatten: h, w and channels must be > 0, got {h}, {w}, {channels}")
+            raise ValueError(f"Flatten({h}, {w}, {channels}): every extent has to be positive")
         self.h = int(h)
         self.w = int(w)
         self.channels = int(channels)
@@ -144,9 +143,6 @@ class Flatten(Module):
         rows = self.h * self.w
         if (len(shape) != 4 or shape[0] != 1 or shape[1] != 1 or shape[3] != self.channels
                 or shape[2] % rows != 0):
-            raise ValueError(
-                f"Flatten({self.h}, {self.w}, {self.channels}): expected "
-                f"flattened-NHWC input of shape [1, 1, N*{self.h}*{self.w}, "
-                f"{self.channels}], got {shape}"
-            )
+            raise ValueError(f"Flatten({self.h}, {self.w}, {self.channels}) reads NHWC rows "
+                             f"[1, 1, images * {rows}, {self.channels}]; this input is {shape}")
         return reshape(x, (shape[2] // rows, self.out_features))

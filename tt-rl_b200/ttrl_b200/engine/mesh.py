@@ -1,33 +1,37 @@
-"""`ParamSync`: periodic exact parameter averaging across N replicas
-(ttrl/engine/mesh/sync.py:102-249).
+"""`ParamSync`: exact parameter averaging across N replicas every
+`sync_every` updates (ttrl/engine/mesh/sync.py:102-249).
 
-Two backends behind the reference's interface:
+The contract kept from the reference: only the online parameters move (each
+replica's Adam moments stay its own), replicas must share one parameter
+schema (names and shapes, checked at construction and again before every
+average), targets given to `average` are refreshed from the averaged weights
+only when the average succeeded, and a failure raises `ParamSyncError`
+saying which parameters were written.
 
-* **One process per GPU (the B200 design).** Construct with the local
-  module(s) and a `torch.distributed` process group (NCCL over NVLink /
-  NVSwitch). `average()` packs the online parameters into one flat fp32
-  buffer with copy kernels, runs ONE all-reduce with `ReduceOp.AVG` (NCCL's
-  average: the sum and the 1/N scale in one collective), and unpacks in
-  place. Adam moments stay local, as in the reference.
+Two backends:
+
+* **One process per GPU (the B200 design).** Built with the local module(s)
+  and a `torch.distributed` process group. The parameters live in one flat
+  fp32 arena (`parameter_arena`), so an average is ONE in-place all-reduce
+  of that buffer -- NCCL's `ReduceOp.AVG` over NVLink / NVSwitch, the sum and
+  the 1/N in one collective -- with no packing copies around it. A gloo group
+  (host replicas, CPU tests) sums and then divides, since gloo has no AVG.
 * **In-process replicas (the reference's shape).** With no group, the N
-  modules are averaged by `reduce_fn` (default `host_all_reduce_sum`, the
-  reference's exact fp32 host sum in replica order) then divided by N and
-  written back in place.
-
-Both keep the reference's contract: online parameters only, validated
-schemas (names and shapes), targets refreshed from the averaged weights
-when given, and a partial-failure message that says what was averaged.
+  modules are read to the host, each replica's parameters as one flat
+  vector, and `reduce_fn` (default `host_all_reduce_sum`: the exact fp32 sum
+  in replica order) combines them in ONE call; the result divided by N is
+  written back in place. A reduction that raises or comes back short
+  leaves every replica as it was.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+import datetime
 from typing import Callable, Sequence
 
 import numpy as np
-import torch
 
-from ttrl_b200.device import context
+from ttrl_b200.engine.nn import parameter_arena
 from ttrl_b200.engine.tensor import restore_in_place
 
 __all__ = ["ParamSync", "ParamSyncError", "host_all_reduce_sum", "param_schema",
@@ -39,194 +43,208 @@ class ParamSyncError(RuntimeError):
 
 
 def host_all_reduce_sum(arrays: list) -> list:
-    """Exact fp32 elementwise sum in replica order, identical on every entry
-    (ttrl/engine/mesh/sync.py:60-70)."""
-    summed = np.asarray(arrays[0], dtype=np.float32).copy()
+    """The elementwise fp32 sum of `arrays`, added in replica order, handed
+    back once per replica (ttrl/engine/mesh/sync.py:60-70). The caller
+    divides by the replica count."""
+    total = np.array(arrays[0], dtype=np.float32, copy=True)
     for a in arrays[1:]:
-        summed = summed + np.asarray(a, dtype=np.float32)
-    return [summed for _ in arrays]
+        np.add(total, np.asarray(a, dtype=np.float32), out=total)
+    return [total] * len(arrays)
 
 
 def param_schema(module) -> tuple:
-    params = list(module.parameters())
-    names = [n for n, _ in module.named_parameters()]
-    if len(names) != len(params):
+    """((name, shape), ...) of a replica's parameters in order: what every
+    replica must agree on before averaging by position makes sense."""
+    named = list(module.named_parameters())
+    count = sum(1 for _ in module.parameters())
+    if count != len(named):
         raise ParamSyncError(
-            f"{type(module).__name__}: {len(names)} parameter names for "
-            f"{len(params)} parameters; named_parameters() and parameters() disagree."
-        )
-    return tuple((str(n), tuple(p.shape)) for n, p in zip(names, params))
+            f"{type(module).__name__} has {count} parameters but names {len(named)}; "
+            "a schema cannot be formed from inconsistent listings.")
+    return tuple((str(name), tuple(int(d) for d in p.shape)) for name, p in named)
 
 
 def replica_schema(modules: Sequence) -> tuple:
-    schemas = [param_schema(m) for m in modules]
-    if len(set(schemas)) != 1:
-        raise ParamSyncError(
-            "replica parameter schemas differ by name or shape, so a positional "
-            f"average would mix unrelated tensors: {schemas}. Every replica must build "
-            "the identical model in the identical order."
-        )
-    return schemas[0]
+    """The schema all `modules` share; raises ParamSyncError if any differs."""
+    first = param_schema(modules[0])
+    for index, module in enumerate(modules[1:], start=1):
+        other = param_schema(module)
+        if other != first:
+            raise ParamSyncError(
+                f"replica parameter schemas differ: replica 0 has {first} and replica "
+                f"{index} has {other}. Averaging by position would combine unrelated "
+                "tensors; build the same model, in the same order, on every replica.")
+    return first
 
 
-@dataclass
 class ParamSync:
-    modules: list
-    sync_every: int = 1
-    reduce_fn: Callable = field(default=host_all_reduce_sum, repr=False)
-    group: object = field(default=None, repr=False)
-    _updates_since_sync: int = field(default=0, init=False, repr=False)
+    """Average the online parameters of N replicas every `sync_every` calls
+    of `maybe_average()`.
 
-    def __post_init__(self) -> None:
-        if self.sync_every < 1:
-            raise ValueError(f"sync_every must be >= 1, got {self.sync_every}")
+    `modules`: one module per replica in replica order (in-process), or this
+    process's own module(s) when `group` is a process group. With a group,
+    the parameters are placed in one flat arena at construction -- build
+    the ParamSync before capturing any graph that reads them. `timeout_s`
+    bounds the wait for a gloo all-reduce; an NCCL group is bounded by the
+    timeout it was created with (its watchdog aborts a stuck collective and
+    the next call raises), and either failure surfaces as ParamSyncError."""
+
+    def __init__(self, modules, sync_every: int = 1,
+                 reduce_fn: Callable = host_all_reduce_sum, group=None,
+                 timeout_s: float | None = None):
+        if sync_every < 1:
+            raise ValueError(f"ParamSync: sync_every must be at least 1, got {sync_every}")
+        self.modules = list(modules)
+        if not self.modules:
+            raise ValueError("ParamSync: no replica modules were given")
         self.n = len(self.modules)
-        if self.n < 1:
-            raise ValueError("ParamSync needs at least one replica, got none")
+        self.sync_every = int(sync_every)
+        self.reduce_fn = reduce_fn
+        self.group = group
+        self.timeout_s = timeout_s
+        self._since = 0
         self._schema = replica_schema(self.modules)
-        self._nparams = len(self._schema)
-        self._flat = None
         self._world = 1
         self._nccl = False
-        if self.group is not None:
+        self._arena = None
+        if group is not None:
             import torch.distributed as dist
-            self._world = dist.get_world_size(self.group)
-            self._nccl = str(dist.get_backend(self.group)).lower() == "nccl"
+            self._world = dist.get_world_size(group)
+            self._nccl = str(dist.get_backend(group)).lower() == "nccl"
+            self._arena = parameter_arena(self.modules)
 
     # -- schedule --------------------------------------------------------
 
     def maybe_average(self, targets: Sequence | None = None) -> bool:
-        self._updates_since_sync += 1
-        if self._updates_since_sync >= self.sync_every:
-            self._updates_since_sync = 0
-            self.average(targets=targets)
-            return True
-        return False
+        """Count one learner update; average on every `sync_every`-th call.
+        Returns whether this call averaged."""
+        self._since += 1
+        if self._since < self.sync_every:
+            return False
+        self._since = 0
+        self.average(targets=targets)
+        return True
 
     def average(self, targets: Sequence | None = None) -> None:
-        if targets is not None and len(targets) != self.n:
-            raise ValueError(f"expected {self.n} target modules, got {len(targets)}")
-        self._require_schema("average")
+        """Replace every replica's online parameters by their mean over
+        replicas, in place; then, if `targets` are given (one per local
+        module), hard-copy each from its averaged online module."""
+        self._check_targets(targets)
+        self._check_schema("average")
         if self.group is not None:
-            self._average_distributed()
+            self._collective_average()
         else:
-            self._average_in_process()
+            self._host_average()
         self._refresh_targets(targets)
 
-    # -- NCCL path -------------------------------------------------------
+    @property
+    def arena(self):
+        """The flat buffer the collective reduces (process-group mode)."""
+        return self._arena
 
-    def _flat_buffer(self, params):
-        total = sum(p.data.numel() for p in params)
-        if self._flat is None or self._flat.numel() != total:
-            self._flat = torch.empty(total, dtype=torch.float32, device=params[0].data.device)
-        return self._flat
+    # -- process group ----------------------------------------------------
 
-    def _average_distributed(self) -> None:
+    def _wait(self, work) -> None:
+        if self.timeout_s is not None and not self._nccl:
+            work.wait(datetime.timedelta(seconds=float(self.timeout_s)))
+        else:
+            work.wait()
+
+    def _collective_average(self) -> None:
         import torch.distributed as dist
-        for module in self.modules:
-            params = list(module.parameters())
-            flat = self._flat_buffer(params)
-            # On a GPU the packing runs as this library's copy kernels; host
-            # replicas (gloo process groups) pack with plain tensor copies.
-            if flat.is_cuda:
-                copy = context(flat.device).copy_strided
+        flat = self._arena
+        try:
+            if self._nccl:
+                self._wait(dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=self.group,
+                                           async_op=True))
             else:
-                def copy(dst, src):
-                    dst.copy_(src)
-            off = 0
-            for p in params:
-                n = p.data.numel()
-                copy(flat[off:off + n], p.data.reshape(-1))
-                off += n
-            try:
-                if self._nccl:
-                    # NCCL's average: the sum and the 1/N in one collective.
-                    dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=self.group)
-                else:
-                    # gloo has no AVG: sum, then the 1/N (host replicas only).
-                    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
-                    flat.div_(self._world)
-            except Exception as e:
-                raise ParamSyncError(
-                    f"ParamSync.average(): the all-reduce failed: {e}. No parameter was "
-                    "written back, so this replica holds its own pre-call values; the "
-                    "other ranks may not. Re-sync (broadcast) before resuming."
-                ) from e
-            off = 0
-            for p in params:
-                n = p.data.numel()
-                copy(p.data.reshape(-1), flat[off:off + n])
-                off += n
+                self._wait(dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group,
+                                           async_op=True))
+                flat.div_(self._world)
+        except Exception as exc:
+            raise ParamSyncError(
+                f"ParamSync.average(): the all-reduce over {self._world} ranks did not "
+                f"complete ({exc}). This rank's parameters were not replaced by an "
+                "average; other ranks may differ. Broadcast from one rank before "
+                "training on.") from exc
 
-    # -- in-process path (reference semantics) ---------------------------
+    # -- in-process replicas ----------------------------------------------
 
-    def _average_in_process(self) -> None:
-        per_replica = [list(m.parameters()) for m in self.modules]
-        for j in range(self._nparams):
-            shards = [per_replica[i][j] for i in range(self.n)]
-            try:
-                self._all_reduce_param(shards)
-            except Exception as e:
-                raise ParamSyncError(
-                    f"ParamSync.average(): the reduction failed on parameter "
-                    f"{j}/{self._nparams}: {e}. Parameters 0..{j - 1} may already be "
-                    f"fully averaged across replicas; parameter {j} may be PARTIALLY "
-                    f"propagated; parameters {j + 1}..{self._nparams - 1} are untouched. "
-                    "Re-sync (for example broadcast() from a known-good replica) before "
-                    "resuming or checkpointing."
-                ) from e
-
-    def _all_reduce_param(self, shards) -> None:
+    def _host_average(self) -> None:
         if self.n == 1:
             return
-        arrays = [np.asarray(s.numpy(), dtype=np.float32) for s in shards]
-        shape = arrays[0].shape
-        for a in arrays[1:]:
-            if a.shape != shape:
-                raise ParamSyncError(
-                    f"parameter shape mismatch across replicas: {shape} vs {a.shape}"
-                )
-        summed = self.reduce_fn(arrays)
-        if len(summed) != len(shards):
+        per_replica = [list(m.parameters()) for m in self.modules]
+        shapes = [tuple(p.shape) for p in per_replica[0]]
+        sizes = [int(np.prod(s, dtype=np.int64)) for s in shapes]
+        vectors = [np.concatenate([np.asarray(p.numpy(), np.float32).reshape(-1)
+                                   for p in params]) for params in per_replica]
+        count = len(shapes)
+        try:
+            summed = self.reduce_fn(vectors)
+        except Exception as exc:
             raise ParamSyncError(
-                f"reduce_fn returned {len(summed)} results for {len(shards)} replica "
-                "shards; a short result would silently leave some replicas unaveraged."
-            )
-        n = np.float32(self.n)
-        for shard, total in zip(shards, summed):
-            restore_in_place(shard.data, np.asarray(total, dtype=np.float32) / n)
+                f"ParamSync.average(): the reduction failed on parameter 0 of {count} "
+                f"(all {count} parameters reduce together as one vector): {exc}. Nothing "
+                "was written; every replica keeps its pre-call parameters.") from exc
+        if len(summed) != self.n:
+            raise ParamSyncError(
+                f"ParamSync.average(): reduce_fn returned {len(summed)} results for "
+                f"{self.n} replica vectors; writing them would leave replicas "
+                "unaveraged, so nothing was written.")
+        for total in summed:
+            if np.shape(total) != vectors[0].shape:
+                raise ParamSyncError(
+                    f"ParamSync.average(): reduce_fn returned a vector of shape "
+                    f"{np.shape(total)} for replica vectors of {vectors[0].shape}; nothing "
+                    "was written.")
+        scale = np.float32(self.n)
+        for params, total in zip(per_replica, summed):
+            mean = np.asarray(total, np.float32) / scale
+            offset = 0
+            for p, shape, size in zip(params, shapes, sizes):
+                restore_in_place(p.data, mean[offset:offset + size].reshape(shape))
+                offset += size
 
-    # -- broadcast / targets --------------------------------------------
+    # -- broadcast / targets ------------------------------------------------
 
     def broadcast(self, src: int = 0, targets: Sequence | None = None) -> None:
-        if targets is not None and len(targets) != self.n:
-            raise ValueError(f"expected {self.n} target modules, got {len(targets)}")
-        self._require_schema("broadcast")
+        """Give every replica replica `src`'s online parameters (the start of
+        a run: N replicas of one model, not the mean of N initialisations)."""
+        self._check_targets(targets)
+        self._check_schema("broadcast")
         if self.group is not None:
             import torch.distributed as dist
-            for p in self.modules[0].parameters():
-                dist.broadcast(p.data, src=src, group=self.group)
+            try:
+                self._wait(dist.broadcast(self._arena, src=src, group=self.group,
+                                          async_op=True))
+            except Exception as exc:
+                raise ParamSyncError(f"ParamSync.broadcast(): the broadcast from rank {src} "
+                                     f"did not complete ({exc}).") from exc
         else:
             if not 0 <= src < self.n:
-                raise ValueError(f"src replica {src} out of range for {self.n} replicas")
-            per_replica = [list(m.parameters()) for m in self.modules]
-            for j in range(self._nparams):
-                source = np.asarray(per_replica[src][j].numpy(), dtype=np.float32)
-                for i in range(self.n):
-                    if i != src:
-                        restore_in_place(per_replica[i][j].data, source)
+                raise ValueError(f"ParamSync.broadcast: src {src} is not one of the "
+                                 f"{self.n} replicas")
+            source = [np.asarray(p.numpy(), np.float32)
+                      for p in self.modules[src].parameters()]
+            for i, module in enumerate(self.modules):
+                if i != src:
+                    for p, value in zip(module.parameters(), source):
+                        restore_in_place(p.data, value)
         self._refresh_targets(targets)
 
-    def _require_schema(self, what: str) -> None:
-        current = replica_schema(self.modules)
-        if current != self._schema:
+    def _check_targets(self, targets) -> None:
+        if targets is not None and len(targets) != self.n:
+            raise ValueError(f"ParamSync: {len(targets)} target modules for {self.n} "
+                             "replicas")
+
+    def _check_schema(self, what: str) -> None:
+        now = replica_schema(self.modules)
+        if now != self._schema:
             raise ParamSyncError(
-                "the replica parameter schema changed since ParamSync was built: "
-                f"{self._schema} -> {current}. Refusing to {what}."
-            )
+                f"the parameter schema changed since ParamSync was built (was "
+                f"{self._schema}, now {now}); will not {what}.")
 
     def _refresh_targets(self, targets) -> None:
-        if targets is None:
-            return
-        for online, target in zip(self.modules, targets):
-            target.copy_from(online)
+        if targets is not None:
+            for online, target in zip(self.modules, targets):
+                target.copy_from(online)

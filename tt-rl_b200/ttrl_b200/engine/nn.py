@@ -8,11 +8,12 @@ from __future__ import annotations
 from typing import Iterator
 
 import numpy as np
+import torch
 
 from ttrl_b200.engine.autograd import Tensor
-from ttrl_b200.engine.tensor import copy_tensor_in_place, restore_in_place
+from ttrl_b200.engine.tensor import restore_in_place
 
-__all__ = ["Module", "ModuleList", "ModuleDict"]
+__all__ = ["Module", "ModuleList", "ModuleDict", "check_state_layout", "parameter_arena"]
 
 
 def _is_container(value) -> bool:
@@ -130,53 +131,112 @@ class Module:
         return out
 
     def load_state_dict(self, state: dict, device=None) -> None:
-        """Restore parameters in place, after validating every key and shape."""
+        """Write `state` into this module's existing buffers.
+
+        The whole state is checked against the names and shapes this module's
+        own `state_dict()` produces before anything is written, so a state
+        that does not fit changes nothing. Writes go into the buffers that
+        exist (captured graphs keep reading the live weights). `device` is
+        accepted for the reference's signature; the buffers carry their own."""
         slots = self._state_slots()
-        reference = self.state_dict()
-        got, expected = set(state.keys()), set(reference)
-        if got != expected:
-            raise ValueError(
-                "load_state_dict: checkpoint keys do not match module "
-                f"parameters (missing={sorted(expected - got)}, "
-                f"extra={sorted(got - expected)})"
-            )
-        for name, want in reference.items():
-            shape = tuple(int(d) for d in np.asarray(state[name]).shape)
-            if shape != want.shape:
-                raise ValueError(
-                    f"load_state_dict: shape mismatch for {name!r}: "
-                    f"checkpoint has {shape}, parameter expects {want.shape}"
-                )
+        layout = {}
+        for name, target in slots:
+            if isinstance(target, Tensor):
+                layout[name] = tuple(target.data.shape)
+            else:
+                for key, array in target.state_dict().items():
+                    layout[f"{name}.{key}"] = tuple(np.shape(array))
+        check_state_layout(state, layout, type(self).__name__)
         for name, target in slots:
             if isinstance(target, Tensor):
                 restore_in_place(target.data, state[name])
-                continue
-            prefix = f"{name}."
-            target.load_state_dict(
-                {k[len(prefix):]: v for k, v in state.items() if k.startswith(prefix)}
-            )
+            else:
+                cut = len(name) + 1
+                target.load_state_dict({key[cut:]: value for key, value in state.items()
+                                        if key.startswith(name + ".")})
 
     def copy_from(self, other: "Module") -> None:
-        """Hard-copy another module's parameters, in place (target-network sync)."""
-        dst_named = list(self.named_parameters())
-        src_named = list(other.named_parameters())
-        if len(dst_named) != len(src_named):
+        """Make every parameter of this module equal to `other`'s, in place and
+        bit for bit, in one launch (the hard target-network sync). The two
+        modules must list the same parameter names with the same shapes."""
+        mine = dict(self.named_parameters())
+        theirs = dict(other.named_parameters())
+        if list(mine) != list(theirs):
             raise ValueError(
-                f"copy_from: parameter count mismatch ({len(dst_named)} vs "
-                f"{len(src_named)}); target and source modules do not match"
-            )
-        for (dst_name, dst), (src_name, src) in zip(dst_named, src_named, strict=True):
-            if dst_name != src_name:
-                raise ValueError(
-                    f"copy_from: parameter name mismatch ({dst_name!r} vs "
-                    f"{src_name!r}); the two modules have different structure"
-                )
-            if tuple(dst.shape) != tuple(src.shape):
-                raise ValueError(
-                    f"copy_from: shape mismatch for {dst_name!r}: target "
-                    f"{tuple(dst.shape)}, source {tuple(src.shape)}"
-                )
-            copy_tensor_in_place(dst, src)
+                f"copy_from: the modules are not the same network; parameters only here: "
+                f"{sorted(set(mine) - set(theirs))}, only in the source: "
+                f"{sorted(set(theirs) - set(mine))}, or the same names in another order")
+        for name, dst in mine.items():
+            if tuple(dst.shape) != tuple(theirs[name].shape):
+                raise ValueError(f"copy_from: {name!r} is {tuple(dst.shape)} here and "
+                                 f"{tuple(theirs[name].shape)} in the source")
+        pairs = [(dst.data, theirs[name].data) for name, dst in mine.items()
+                 if dst.data.data_ptr() != theirs[name].data.data_ptr()]
+        if not pairs:
+            return
+        if not pairs[0][0].is_cuda:
+            # Host replicas (gloo process groups on the CPU) hold host tensors.
+            for dst, src in pairs:
+                dst.copy_(src)
+            return
+        from ttrl_b200.device import context
+        context(pairs[0][0].device).blend(pairs)
+
+
+def check_state_layout(state: dict, layout: dict, owner: str) -> None:
+    """Raise ValueError unless `state` has exactly the keys of `layout`
+    (name -> shape) with those shapes."""
+    missing = sorted(set(layout) - set(state))
+    unknown = sorted(set(state) - set(layout))
+    if missing or unknown:
+        raise ValueError(f"{owner}.load_state_dict: the state does not fit this module: "
+                         f"missing {missing}, not parameters of it {unknown}")
+    for name, shape in layout.items():
+        got = tuple(int(d) for d in np.shape(state[name]))
+        if got != tuple(shape):
+            raise ValueError(f"{owner}.load_state_dict: {name!r} is {got} in the state but "
+                             f"{tuple(shape)} in the module")
+
+
+def parameter_arena(modules, *, align: int = 64) -> torch.Tensor:
+    """Place the parameters of `modules` (in order) in one flat fp32 buffer,
+    each starting on an `align`-float (256-byte) boundary, and rebind every
+    parameter's `.data` to its view of it; returns the buffer. Parameters
+    already laid out that way are left where they are.
+
+    Graphs captured before this call keep the old addresses, so call it
+    before capturing anything that reads the parameters."""
+    params = []
+    seen = set()
+    for module in modules:
+        for p in module.parameters():
+            if id(p) not in seen:
+                seen.add(id(p))
+                params.append(p)
+    if not params:
+        raise ValueError("parameter_arena: no parameters")
+    offsets, total = [], 0
+    for p in params:
+        offsets.append(total)
+        total += (p.data.numel() + align - 1) // align * align
+    first = params[0].data
+    storage = first.untyped_storage()
+    start = first.storage_offset()
+    placed = (first.dtype == torch.float32 and storage.nbytes() >= 4 * (start + total)
+              and all(p.data.is_contiguous() and p.data.dtype == torch.float32
+                      and p.data.untyped_storage().data_ptr() == storage.data_ptr()
+                      and p.data.storage_offset() == start + off
+                      for p, off in zip(params, offsets)))
+    if placed:
+        flat = torch.empty(0, dtype=torch.float32, device=first.device)
+        return flat.set_(storage, start, (total,), (1,))
+    flat = torch.zeros(total, dtype=torch.float32, device=first.device)
+    for p, off in zip(params, offsets):
+        n = p.data.numel()
+        view = flat[off:off + n].view(p.data.shape)
+        view.copy_(p.data)
+        p.data = view
+    return flat
 
 
 class ModuleList(Module):

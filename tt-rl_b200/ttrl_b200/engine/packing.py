@@ -28,7 +28,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-__all__ = ["PreparedLayout", "default_layout", "candidate_layouts", "solve_cp"]
+__all__ = ["AmbiguousLayout", "PreparedLayout", "default_layout", "candidate_layouts",
+           "solve_cp"]
 
 
 def _round_up(x: int, m: int) -> int:
@@ -118,11 +119,19 @@ def candidate_layouts(rows: int, cols: int, out_channels: int, in_channels: int,
     return out
 
 
-def solve_cp(shape, oihw, *, v=None) -> PreparedLayout:
+class AmbiguousLayout(ValueError):
+    """The stored moments fit several prepared layouts and cannot tell them
+    apart (a second moment that is zero everywhere, for a weight that never
+    had a gradient, in a matrix whose shape is not the default layout's)."""
+
+
+def solve_cp(shape, oihw, *, v=None, strict: bool = False) -> PreparedLayout:
     """The layout of a stored `[1, 1, rows, cols]` moment for an OIHW weight:
     among the candidates, the ones whose padding holds zeros in `v`; of those
     the default layout if it is one, else the one whose live region `v`
-    fills most (v > 0 on every trained weight)."""
+    fills most (v > 0 on every trained weight). With `strict` there is no
+    preference for the default: several candidates that `v` fills equally
+    (an all-zero `v`) raise `AmbiguousLayout` instead of picking one."""
     if len(shape) != 4 or shape[0] != 1 or shape[1] != 1:
         raise ValueError(f"a prepared conv moment is [1, 1, rows, cols], got {tuple(shape)}")
     o, c, kh, kw = (int(d) for d in oihw)
@@ -132,8 +141,18 @@ def solve_cp(shape, oihw, *, v=None) -> PreparedLayout:
     if v is not None:
         cands = [lay for lay in cands if lay.padding_is_zero(v)] or cands
     default = default_layout(o, c, kh, kw)
-    if default in cands:
-        return default
+    if len(cands) == 1 or (default in cands and not strict):
+        return default if default in cands else cands[0]
     if v is None:
+        if strict and len(cands) > 1:
+            raise AmbiguousLayout(f"{len(cands)} prepared layouts of shape {tuple(shape)} hold an "
+                                  f"{tuple(oihw)} weight and no second moment tells them apart")
         return cands[0]
-    return max(cands, key=lambda lay: int(np.count_nonzero(lay.unpack(v))))
+    filled = [int(np.count_nonzero(lay.unpack(v))) for lay in cands]
+    best = max(filled)
+    if strict and filled.count(best) > 1:
+        raise AmbiguousLayout(
+            f"{filled.count(best)} prepared layouts of shape {tuple(shape)} hold an "
+            f"{tuple(oihw)} weight equally well (the stored second moment has "
+            f"{best} non-zero live entries), so the channel stride cannot be recovered")
+    return cands[filled.index(best)]
