@@ -182,9 +182,11 @@ def test_ppo_update_at_the_timed_configuration():
     0.01, Adam 2.5e-4 with grad-norm clip 0.5, against the float64 oracle on
     the same permutations.
 
-    Every step's loss and gradient norm (from the metric rows the graph
-    writes) to 1e-4 relative; the norm sums every gradient, including those
-    whose ReLU kinks the float64 oracle places differently. Parameters after the 16 Adam steps to 3e-3
+    Every step's loss (from the metric rows the graph writes) to 1e-4
+    relative. The gradient norm to 1e-4 at the first step; from the second
+    step on the two sides differentiate at parameters that already differ
+    by the Adam noise described next, and the norm -- a sum over gradients
+    that partly cancel -- is held to the parameters' 3e-3. Parameters after the 16 Adam steps to 3e-3
     relative Frobenius: with eps = 1e-8 Adam moves an element by about lr
     whatever its gradient's size, so the few elements whose gradient sits
     near zero carry fp32-versus-float64 rounding into full-size steps, and
@@ -225,7 +227,8 @@ def test_ppo_update_at_the_timed_configuration():
             max_grad_norm=cfg.max_grad_norm)
         assert rel(rows[t - 1, 0], m["loss"]) <= 1e-4, (t, rows[t - 1, 0], m["loss"])
         norm = float(np.sqrt(rows[t - 1, 4]))
-        assert rel(norm, m["grad_norm"]) <= 1e-4, (t, norm, m["grad_norm"])
+        bound = 1e-4 if t == 1 else 3e-3
+        assert rel(norm, m["grad_norm"]) <= bound, (t, norm, m["grad_norm"])
     sd = net.state_dict()
     want = nature_state_dict(params, heads=("pi", "v"))
     for name in sd:
