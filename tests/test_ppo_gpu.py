@@ -182,11 +182,11 @@ def test_ppo_update_at_the_timed_configuration():
     0.01, Adam 2.5e-4 with grad-norm clip 0.5, against the float64 oracle on
     the same permutations.
 
-    Every step's loss (from the metric rows the graph writes) to 1e-4
-    relative. The gradient norm to 1e-4 at the first step; from the second
-    step on the two sides differentiate at parameters that already differ
-    by the Adam noise described next, and the norm -- a sum over gradients
-    that partly cancel -- is held to the parameters' 3e-3. Parameters after the 16 Adam steps to 3e-3
+    The first step's loss and gradient norm (from the metric rows the graph
+    writes) to 1e-4 relative. From the second step on, both sides work from
+    parameters that already differ by the Adam noise described next: the
+    loss is held to 1e-3 and the norm -- a sum over gradients that partly
+    cancel -- to the parameters' 3e-3. Parameters after the 16 Adam steps to 3e-3
     relative Frobenius: with eps = 1e-8 Adam moves an element by about lr
     whatever its gradient's size, so the few elements whose gradient sits
     near zero carry fp32-versus-float64 rounding into full-size steps, and
@@ -225,10 +225,10 @@ def test_ppo_update_at_the_timed_configuration():
             adv_n[idx].astype(np.float64), returns[idx].astype(np.float64),
             values[idx].astype(np.float64), lr=cfg.lr, eps=cfg.eps,
             max_grad_norm=cfg.max_grad_norm)
-        assert rel(rows[t - 1, 0], m["loss"]) <= 1e-4, (t, rows[t - 1, 0], m["loss"])
+        loss_bound, norm_bound = (1e-4, 1e-4) if t == 1 else (1e-3, 3e-3)
+        assert rel(rows[t - 1, 0], m["loss"]) <= loss_bound, (t, rows[t - 1, 0], m["loss"])
         norm = float(np.sqrt(rows[t - 1, 4]))
-        bound = 1e-4 if t == 1 else 3e-3
-        assert rel(norm, m["grad_norm"]) <= bound, (t, norm, m["grad_norm"])
+        assert rel(norm, m["grad_norm"]) <= norm_bound, (t, norm, m["grad_norm"])
     sd = net.state_dict()
     want = nature_state_dict(params, heads=("pi", "v"))
     for name in sd:
