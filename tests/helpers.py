@@ -36,6 +36,27 @@ def nature_state_dict(p, heads=("q",)):
     return sd
 
 
+def oracle_params_from_state(sd, heads=("q",)):
+    """The inverse of nature_state_dict: a Nature-CNN state_dict (portable
+    layout) -> the oracle's parameter dict, float64."""
+    names = nature_state_dict({k: np.zeros(1) for k in _ORACLE_KEYS[heads]}, heads)
+    return {key: np.asarray(sd[name], np.float64).reshape(_oracle_shape(key, sd[name]))
+            for key, name in zip(_ORACLE_KEYS[heads], names)}
+
+
+_ORACLE_KEYS = {
+    ("q",): ["conv0.w", "conv0.b", "conv1.w", "conv1.b", "conv2.w", "conv2.b", "fc.w", "fc.b",
+             "q.w", "q.b"],
+    ("pi", "v"): ["conv0.w", "conv0.b", "conv1.w", "conv1.b", "conv2.w", "conv2.b", "fc.w",
+                  "fc.b", "pi.w", "pi.b", "v.w", "v.b"],
+}
+
+
+def _oracle_shape(key, value):
+    a = np.asarray(value)
+    return (a.size,) if key.endswith(".b") else a.shape
+
+
 def oracle_grads_to_named(g, heads=("q",)):
     """Oracle gradient dict -> {state_dict name: OIHW/(in,out) array}."""
     return nature_state_dict(g, heads)

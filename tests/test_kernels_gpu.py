@@ -467,3 +467,68 @@ def test_conv_backward_matches_the_reference_composition(name, stride):
     ctx.conv_dgrad(dev(dy.reshape(-1, cout)), dev(ol.oihw_to_krsc(wt * np.float32(scale))),
                    None, dx, geom, accumulate=False)
     assert rel(host(dx).reshape(x.shape), d[name + ".dx"]) <= TOL_X3
+
+
+# The stream-K weight gradient (csrc/wgrad_sk.cu) serves layers whose input
+# is exact in tf32 (raw frames): conv1 in its space-to-depth form and any
+# exact-input layer with C a multiple of 32, Cout 32 or 64, kh*kw*C <= 256.
+SK_CASES = [
+    # n, h, w, c, cout, k, stride: batch sizes that leave a partial last
+    # 32-pixel block (n=1: 400 pixels), a few k-blocks per CTA (n=32) and the
+    # PPO minibatch (n=256); a 128-row, 64-channel case
+    (1, 21, 21, 64, 32, 2, 1),
+    (3, 21, 21, 64, 32, 2, 1),
+    (32, 21, 21, 64, 32, 2, 1),
+    (256, 21, 21, 64, 32, 2, 1),
+    (8, 9, 9, 32, 64, 2, 1),
+]
+
+
+@pytest.mark.parametrize("case", SK_CASES)
+def test_stream_k_conv_wgrad(case):
+    """dW (scaled by alpha) and db against the float64 oracle at 1e-4; then,
+    on the same buffers, the accumulate flags add a second call's result; and
+    two identical calls agree bit for bit (partials summed in a fixed order)."""
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    n, h, w, c, cout, k, s = case
+    geom = conv_geom(n, h, w, c, cout, k, k, s, 0).with_exact_input(True)
+    rng = np.random.default_rng(n * 31 + c)
+    x = rng.integers(0, 256, (n, h, w, c)).astype(np.float32)  # exact in tf32
+    dy = rng.standard_normal((n, geom.oh, geom.ow, cout)).astype(np.float32)
+    alpha = 1.0 / 255.0
+    ref_w = ol.conv2d_wgrad(x.astype(np.float64), dy.astype(np.float64), k, stride=s,
+                            input_scale=alpha)
+    ref_b = dy.astype(np.float64).reshape(-1, cout).sum(0)
+    xd, dyd = dev(x.reshape(-1, c)), dev(dy.reshape(-1, cout))
+    dw = torch.empty((cout, k, k, c), device="cuda")
+    db = torch.empty((cout,), device="cuda")
+    ctx.conv_wgrad(xd, dyd, dw, db, geom, alpha, accumulate=False, accumulate_db=False)
+    first_w, first_b = host(dw).copy(), host(db).copy()
+    assert rel(ol.krsc_to_oihw(first_w), ref_w) <= TOL_X3
+    assert rel(first_b, ref_b) <= TOL_X3
+    ctx.conv_wgrad(xd, dyd, dw, db, geom, alpha, accumulate=False, accumulate_db=False)
+    assert np.array_equal(host(dw), first_w) and np.array_equal(host(db), first_b)
+    ctx.conv_wgrad(xd, dyd, dw, db, geom, alpha, accumulate=True, accumulate_db=True)
+    assert rel(ol.krsc_to_oihw(host(dw)), 2 * ref_w) <= TOL_X3
+    assert rel(host(db), 2 * ref_b) <= TOL_X3
+    ctx.check_status()
+
+
+def test_stream_k_conv_wgrad_single_pass_tf32():
+    """One TF32 pass over dY rounded to nearest (the windows are exact): the
+    accuracy class of the reference's HiFi4 matmuls, 1e-3."""
+    from ttrl_b200._lib import PREC_TF32
+    from ttrl_b200.device import conv_geom
+    ctx = _ctx()
+    geom = conv_geom(32, 21, 21, 64, 32, 2, 2, 1, 0).with_exact_input(True)
+    rng = np.random.default_rng(9)
+    x = rng.integers(0, 256, (32, 21, 21, 64)).astype(np.float32)
+    dy = rng.standard_normal((32, 20, 20, 32)).astype(np.float32)
+    ref_w = ol.conv2d_wgrad(x.astype(np.float64), dy.astype(np.float64), 2, stride=1)
+    dw = torch.empty((32, 2, 2, 64), device="cuda")
+    db = torch.empty((32,), device="cuda")
+    ctx.conv_wgrad(dev(x.reshape(-1, 64)), dev(dy.reshape(-1, 32)), dw, db, geom, 1.0,
+                   accumulate=False, accumulate_db=False, precision=PREC_TF32)
+    assert rel(ol.krsc_to_oihw(host(dw)), ref_w) <= 1e-3
+    assert rel(host(db), dy.astype(np.float64).reshape(-1, 32).sum(0)) <= 1e-5

@@ -1212,6 +1212,16 @@ static int resolve_operand(const ttrl_operand& in, int ones_row, DevOperand& out
   return set_error(TTRL_EINVAL, "gemm operand kind %d is unknown", in.kind);
 }
 
+// The operand resolution and TMA map encoders, for the other kernels of
+// this library that load the same operands.
+int gemm_resolve_operand(const ttrl_operand& in, int ones_row, DevOperand& out) {
+  return resolve_operand(in, ones_row, out);
+}
+bool gemm_im2col_map(const DevOperand& o, CUtensorMap* map) { return encode_im2col_map(o, map); }
+bool gemm_tile_map(const DevOperand& o, int rows, CUtensorMap* map) {
+  return encode_operand_map(o, rows, map);
+}
+
 static int pick_bn(int n) {
   if (n <= 32) return 32;
   if (n <= 64) return 64;

@@ -113,6 +113,19 @@ int set_cuda_error(const char* what, cudaError_t e);
 int gemm_init_device();
 int gru_init_device();
 size_t gemm_workspace_bytes(const ttrl_gemm_desc& d);
+int gemm_resolve_operand(const ttrl_operand& in, int ones_row, DevOperand& out);
+bool gemm_im2col_map(const DevOperand& o, CUtensorMap* map);
+bool gemm_tile_map(const DevOperand& o, int rows, CUtensorMap* map);
+
+// Stream-K convolution weight gradient (wgrad_sk.cu): one CTA per SM over a
+// slice of the pixels for the whole of dW, for layers whose input is exact
+// in tf32 (raw frames), C a multiple of 32, Cout 32 or 64, kh*kw*C <= 256.
+bool wgrad_sk_geometry(const ttrl_conv_geom* g);
+bool wgrad_sk_applies(const ttrl_conv_geom* g, const float* x, const float* dy);
+size_t wgrad_sk_ws(const ttrl_conv_geom* g);
+int wgrad_sk_run(const float* x, const float* dy, float* dw, float* db, const ttrl_conv_geom* g,
+                 float alpha, int accumulate, int accumulate_db, int precision, float* ws,
+                 size_t wsb, int* status, cudaStream_t st);
 // Launch one GEMM. `counters` (kCounterBytes, zeroed) and `partials` back
 // a split-K schedule; both may be null when K is not split.
 int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* counters,

@@ -553,11 +553,26 @@ int conv_dgrad(const float* dy, const float* w, const float* mask, float* dx,
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("col2im launch", e);
 }
 
+// The stream-K weight gradient is on unless TTRL_WGRAD_SK=0 (which keeps
+// the general GEMM, for comparisons).
+static bool wgrad_sk_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TTRL_WGRAD_SK");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return on;
+}
+
 size_t conv_wgrad_ws(const ttrl_conv_geom* g) {
   const int m = g->n * g->oh * g->ow;
   const int kk = g->kh * g->kw * g->c;
   ttrl_gemm_desc d = make_desc(kk + 1, g->cout, m, TTRL_PREC_TF32X3);
-  return gemm_workspace_bytes(d);
+  const size_t generic = gemm_workspace_bytes(d);
+  if (wgrad_sk_geometry(g) && wgrad_sk_enabled()) {
+    const size_t sk = wgrad_sk_ws(g);
+    return sk > generic ? sk : generic;
+  }
+  return generic;
 }
 
 int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl_conv_geom* g,
@@ -565,6 +580,9 @@ int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl
                size_t wsb, int* status, cudaStream_t st) {
   int rc = check_conv(g);
   if (rc) return rc;
+  if (wgrad_sk_enabled() && wgrad_sk_applies(g, x, dy))
+    return wgrad_sk_run(x, dy, dw, db, g, alpha, accumulate, accumulate_db, precision, ws, wsb,
+                        status, st);
   const int m = g->n * g->oh * g->ow;
   const int kk = g->kh * g->kw * g->c;
   ttrl_gemm_desc d = make_desc(kk + (db ? 1 : 0), g->cout, m, precision);
