@@ -686,9 +686,11 @@ def bench_recurrent(device, args):
 # ncu summaries under profiles/ name the exact command they came from.
 
 #: (input extent, in channels, out channels, kernel, stride). conv1s2d is
-#: conv1 in the space-to-depth form the nets run it in (fold 4).
+#: conv1 in the space-to-depth form the nets run it in (fold 4), reading raw
+#: 0..255 pixels (exact in tf32) as the first layer does.
 PROFILE_CONV = {"conv1": (84, 4, 32, 8, 4), "conv1s2d": (21, 64, 32, 2, 1),
                 "conv2": (20, 32, 64, 4, 2), "conv3": (9, 64, 64, 3, 1)}
+PROFILE_EXACT = ("conv1", "conv1s2d")
 
 #: The Nature-DQN parameter shapes as the device holds them (conv weights
 #: KRSC, conv1 folded): 1,687,206 floats.
@@ -701,10 +703,13 @@ def _profile_conv(layer: str, kind: str):
         import torch
         from ttrl_b200.device import context, conv_geom
         hw, c, co, k, st = PROFILE_CONV[layer]
-        g = conv_geom(args.batch, hw, hw, c, co, k, k, st, 0)
+        exact = layer in PROFILE_EXACT
+        g = conv_geom(args.batch, hw, hw, c, co, k, k, st, 0).with_exact_input(exact)
         rng = np.random.default_rng(0)
         dev = torch.device("cuda", 0)
-        x = torch.from_numpy(rng.standard_normal((args.batch * hw * hw, c)).astype(np.float32)).to(dev)
+        x = (rng.integers(0, 256, (args.batch * hw * hw, c)) if exact
+             else rng.standard_normal((args.batch * hw * hw, c)))
+        x = torch.from_numpy(x.astype(np.float32)).to(dev)
         w = torch.from_numpy(rng.standard_normal((co, k, k, c)).astype(np.float32)).to(dev)
         b = torch.zeros(co, device=dev)
         y = torch.empty((args.batch * g.oh * g.ow, co), device=dev)

@@ -19,7 +19,10 @@ namespace ttrl {
 // the hardware may cut short), so waiting warps sleep instead of spinning on
 // the issue slots the working warps need; the global timer, read every 64
 // polls, ends the wait after kWaitTimeoutNs.
-constexpr uint32_t kWaitPollNs = 100000;
+#ifndef TTRL_WAIT_POLL_NS
+#define TTRL_WAIT_POLL_NS 100000
+#endif
+constexpr uint32_t kWaitPollNs = TTRL_WAIT_POLL_NS;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
 __device__ __forceinline__ uint64_t global_ns() {

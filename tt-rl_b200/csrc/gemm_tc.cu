@@ -59,6 +59,15 @@ constexpr int kThreads = 256;                       // loader threads
 constexpr int kBlockThreads = kThreads + 64;        // + the MMA warp + the TMA producer warp
 constexpr int kMmaWarp = kLoadWarps;
 constexpr int kProducerWarp = kLoadWarps + 1;
+// When both operands arrive by TMA, the loader warps form this many groups
+// that take alternate k-blocks, each covering a whole stage, so that several
+// stages' split or rounding passes are in flight at once. A pass is bound by
+// shared-memory load latency (the loads queue behind the tensor core's own
+// operand reads), not by its bytes, so one stage at a time would serialise
+// that latency into every k-block.
+constexpr int kLoaderGroups = 2;
+constexpr int kGroupWarps = kLoadWarps / kLoaderGroups;
+constexpr int kGroupThreads = kGroupWarps * 32;
 
 // Largest cluster (in split CTAs) the split-K reduction may use on each
 // device: 16 where the hardware can co-schedule it, else the portable 8.
@@ -71,6 +80,23 @@ static int g_max_cluster[64];
 __device__ __align__(16) float kOnes4[4] = {1.f, 1.f, 1.f, 1.f};
 __device__ __align__(16) float kOneZeros[4] = {1.f, 0.f, 0.f, 0.f};
 
+
+// 16-byte shared-memory load and store on a 32-bit shared-window address.
+// The loader warps address stages this way: a generic pointer into shared
+// memory costs an address-space resolution on every access.
+__device__ __forceinline__ float4 lds4(uint32_t saddr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(saddr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void sts4(uint32_t saddr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
 
 // General element address (used by the scalar fallback modes only).
 __device__ __forceinline__ const float* opnd_addr(const DevOperand& o, int r, int k, bool& ok) {
@@ -252,20 +278,24 @@ struct Loader {
   // Single-pass precision: round the chunks this thread owns (the ones
   // `split` would read) to tf32 in place.
   __device__ __forceinline__ void round_in_place(const DevOperand& o, uint8_t* raw_gen,
-                                                 int tid) const {
+                                                 uint32_t raw_s, int tid) const {
     if (o.mode == kModeKVec || o.mode == kModeMNVec) {
+      uint32_t off[P];
+      float4 x[P];
 #pragma unroll
       for (int i = 0; i < P; ++i) {
-        const uint32_t off = o.mode == kModeKVec
-                                 ? kmajor_off((tid >> 3) + i * 32, (tid & 7) * 4)
-                                 : mnmajor_off((tid % RC) * 4, tid / RC + i * (kThreads / RC));
-        float4* p = reinterpret_cast<float4*>(raw_gen + off);
-        float4 x = *p;
-        x.x = tf32_round(x.x);
-        x.y = tf32_round(x.y);
-        x.z = tf32_round(x.z);
-        x.w = tf32_round(x.w);
-        *p = x;
+        off[i] = raw_s + (o.mode == kModeKVec
+                              ? kmajor_off((tid >> 3) + i * 32, (tid & 7) * 4)
+                              : mnmajor_off((tid % RC) * 4, tid / RC + i * (kThreads / RC)));
+        x[i] = lds4(off[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        x[i].x = tf32_round(x[i].x);
+        x[i].y = tf32_round(x[i].y);
+        x[i].z = tf32_round(x[i].z);
+        x[i].w = tf32_round(x[i].w);
+        sts4(off[i], x[i]);
       }
     } else {
       const bool rows_fast = o.mode == kModeScalarR;
@@ -284,7 +314,8 @@ struct Loader {
   // only the remainder lo = x - trunc(x) is written, to the low tile at the
   // same offset.
   __device__ __forceinline__ void split(const DevOperand& o, const uint8_t* raw_gen,
-                                        uint8_t* lo_gen, int tid) const {
+                                        uint8_t* lo_gen, uint32_t raw_s, uint32_t lo_s,
+                                        int tid) const {
     if (o.mode == kModeKVec || o.mode == kModeMNVec) {
       uint32_t off[P];
       float4 x[P];
@@ -293,7 +324,7 @@ struct Loader {
         off[i] = o.mode == kModeKVec
                      ? kmajor_off((tid >> 3) + i * 32, (tid & 7) * 4)
                      : mnmajor_off((tid % RC) * 4, tid / RC + i * (kThreads / RC));
-        x[i] = *reinterpret_cast<const float4*>(raw_gen + off[i]);
+        x[i] = lds4(raw_s + off[i]);
       }
 #pragma unroll
       for (int i = 0; i < P; ++i) {
@@ -302,7 +333,7 @@ struct Loader {
         lo.y = tf32_low(x[i].y);
         lo.z = tf32_low(x[i].z);
         lo.w = tf32_low(x[i].w);
-        *reinterpret_cast<float4*>(lo_gen + off[i]) = lo;
+        sts4(lo_s + off[i], lo);
       }
     } else {
       const bool rows_fast = o.mode == kModeScalarR;
@@ -690,10 +721,12 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
     if (args.a_tma) prefetch_tensormap(&args.tma_a);
     if (args.b_tma) prefetch_tensormap(&args.tma_b);
   }
+  // Both operands by TMA: the loader warps work in groups (see kLoaderGroups).
+  const bool grouped = args.a_tma != 0 && args.b_tma != 0;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(empty0 + s * 8, 1);
-      mbar_init(full0 + s * 8, kLoadWarps);
+      mbar_init(full0 + s * 8, grouped ? kGroupWarps : kLoadWarps);
       mbar_init(tfull0 + s * 8, 1);
     }
     for (int l = 0; l < L; ++l) mbar_init(loempty0 + l * 8, 1);
@@ -748,6 +781,44 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
       if (!a_tma) la.issue(oa, raw_a(st), row0, k0, tid);
       if (!b_tma) lb.issue(ob, raw_b(st), col0, k0, tid);
     };
+    if (grouped) {
+      // Group g takes k-blocks g, g + kLoaderGroups, ...; each thread covers
+      // kLoaderGroups thread slots of the 256-thread stage layout.
+      const int grp = warp / kGroupWarps;
+      const int gt = tid % kGroupThreads;
+#pragma unroll 1
+      for (int i = grp; i < nk; i += kLoaderGroups) {
+        const int s = i % S;
+        if (!mbar_wait(tfull0 + s * 8, (i / S) & 1)) timed_out = true;
+#pragma unroll
+        for (int v = 0; v < kLoaderGroups; ++v) {
+          const int vt = gt + v * kGroupThreads;
+          if (a_ones_by_loader)
+            la.fill_ones_row(oa, sgen + s * Cfg::kTile, row0, (kb0 + i) * 32, vt);
+          if (round_a) la.round_in_place(oa, sgen + s * Cfg::kTile, raw_a(s), vt);
+          if (round_b)
+            lb.round_in_place(ob, sgen + s * Cfg::kTile + Cfg::kABytes, raw_b(s), vt);
+        }
+        if (split_a || split_b) {
+          const int l = i % LL;
+          if (i >= L && !mbar_wait(loempty0 + l * 8, ((i - L) / LL) & 1)) timed_out = true;
+          const uint8_t* hi = sgen + s * Cfg::kTile;
+          uint8_t* lo = sgen + (lo_base - sbase) + l * Cfg::kTile;
+          const uint32_t lo_s = lo_base + l * Cfg::kTile;
+#pragma unroll
+          for (int v = 0; v < kLoaderGroups; ++v) {
+            const int vt = gt + v * kGroupThreads;
+            if (split_a) la.split(oa, hi, lo, raw_a(s), lo_s, vt);
+            if (split_b)
+              lb.split(ob, hi + Cfg::kABytes, lo + Cfg::kABytes, raw_b(s), lo_s + Cfg::kABytes,
+                       vt);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full0 + s * 8);
+      }
+    }
     if (any_gather) {
 #pragma unroll 1
       for (int s = 0; s < AHEAD; ++s) {
@@ -756,7 +827,7 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
       }
     }
 #pragma unroll 1
-    for (int i = 0; i < nk; ++i) {
+    for (int i = 0; i < (grouped ? 0 : nk); ++i) {
       if (any_gather) {
         const int j = i + AHEAD;
         if (j < nk) {
@@ -773,8 +844,9 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
       const int s = i % S;
       if (any_tma && !mbar_wait(tfull0 + s * 8, (i / S) & 1)) timed_out = true;
       if (a_ones_by_loader) la.fill_ones_row(oa, sgen + s * Cfg::kTile, row0, (kb0 + i) * 32, tid);
-      if (round_a) la.round_in_place(oa, sgen + s * Cfg::kTile, tid);
-      if (round_b) lb.round_in_place(ob, sgen + s * Cfg::kTile + Cfg::kABytes, tid);
+      if (round_a) la.round_in_place(oa, sgen + s * Cfg::kTile, raw_a(s), tid);
+      if (round_b)
+        lb.round_in_place(ob, sgen + s * Cfg::kTile + Cfg::kABytes, raw_b(s), tid);
       if (split_a || split_b) {
         const int l = i % LL;
         if (i >= L) {
@@ -783,8 +855,10 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
         }
         const uint8_t* hi = sgen + s * Cfg::kTile;
         uint8_t* lo = sgen + (lo_base - sbase) + l * Cfg::kTile;
-        if (split_a) la.split(oa, hi, lo, tid);
-        if (split_b) lb.split(ob, hi + Cfg::kABytes, lo + Cfg::kABytes, tid);
+        const uint32_t lo_s = lo_base + l * Cfg::kTile;
+        if (split_a) la.split(oa, hi, lo, raw_a(s), lo_s, tid);
+        if (split_b)
+          lb.split(ob, hi + Cfg::kABytes, lo + Cfg::kABytes, raw_b(s), lo_s + Cfg::kABytes, tid);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -1478,8 +1552,12 @@ int gemm_run(const ttrl_gemm_desc& d, int a_ones_row, const EpiExtra& ex, int* c
   // Several waves of CTAs, or a short walk along K (where a deep ring buys
   // little): the half-size variant runs two CTAs per SM, which also lets
   // GEMMs on concurrent launch lanes share SMs.
+#ifdef TTRL_GEMM_FULL_ONLY
+  const bool small = false;
+#else
   const bool small = !s.cluster && (static_cast<long long>(s.tiles) * s.splits > 148 ||
                                     s.kb_per_split <= kSmallMaxKBlocks);
+#endif
   cudaError_t e;
 #define TTRL_LAUNCH(BNV)                                                              \
   (split3 ? (small ? launch_bn<BNV, true, true>(args, grid, cz, stream)                \

@@ -580,9 +580,13 @@ int conv_wgrad(const float* x, const float* dy, float* dw, float* db, const ttrl
                size_t wsb, int* status, cudaStream_t st) {
   int rc = check_conv(g);
   if (rc) return rc;
-  if (wgrad_sk_enabled() && wgrad_sk_applies(g, x, dy))
-    return wgrad_sk_run(x, dy, dw, db, g, alpha, accumulate, accumulate_db, precision, ws, wsb,
-                        status, st);
+  if (wgrad_sk_enabled() && wgrad_sk_applies(g, x, dy)) {
+    // EUNSUPPORTED (no TMA map for these operands) is refused before any
+    // launch; the general GEMM then takes the call.
+    rc = wgrad_sk_run(x, dy, dw, db, g, alpha, accumulate, accumulate_db, precision, ws, wsb,
+                      status, st);
+    if (rc != TTRL_EUNSUPPORTED) return rc;
+  }
   const int m = g->n * g->oh * g->ow;
   const int kk = g->kh * g->kw * g->c;
   ttrl_gemm_desc d = make_desc(kk + (db ? 1 : 0), g->cout, m, precision);
