@@ -409,6 +409,60 @@ int ttrl_ppo_loss(const float* logits, const float* value, const int32_t* action
                   float value_clip_eps, float value_coef, float entropy_coef,
                   ttrl_stream_t stream);
 
+/* SAC's heads, fused (each call is one launch; results equal the reference's
+ * composed tape ops, rounding for rounding where the order of a sum allows).
+ *
+ * ttrl_sac_sample: the tanh-squashed Gaussian of ttrl/algos/sac/policy.py:
+ * 30-40 with the log-density of ttrl/algos/gaussian.py:55-90 and the action
+ * box of gaussian.py:150-165. log_std = clamp(log_std_raw, min, max) by the
+ * relu identities of ttrl/engine/ops/select.py:54-63; u = mean +
+ * exp(log_std) * noise; logp[b] = normal_logp(u) - sum(log(1 - tanh(u)^2))
+ * - log_det; the env action tanh(u) * scale + centre lands in columns
+ * [obs_dim, obs_dim + action_dim) of `joint` ([batch][obs_dim +
+ * action_dim]), whose first obs_dim columns receive `obs` -- the critic's
+ * concat(obs, action) input (ttrl/nets/fusion.py) built in the same launch.
+ * With pack_joint != NULL the launch also writes [pack_obs | pack_act] rows
+ * into pack_joint (the replayed batch's critic input). */
+#define TTRL_SAC_MAX_CRITICS 8
+int ttrl_sac_sample(const float* mean, const float* log_std_raw, const float* noise,
+                    const float* scale, const float* centre, const float* obs, float* joint,
+                    float* logp, int batch, int action_dim, int obs_dim, float log_std_min,
+                    float log_std_max, float log_det, const float* pack_obs,
+                    const float* pack_act, float* pack_joint, ttrl_stream_t stream);
+
+/* Backward of ttrl_sac_sample: d_mean and d_log_std_raw (each written, or
+ * added to when its accumulate flag is set) from d_action (element (b, d)
+ * at d_action[b * d_action_ld + d]; NULL: zero) and d_logp ([batch]; NULL:
+ * zero). The forward is recomputed from the same inputs. */
+int ttrl_sac_sample_backward(const float* mean, const float* log_std_raw, const float* noise,
+                             const float* scale, const float* d_action, int64_t d_action_ld,
+                             const float* d_logp, float* d_mean, float* d_log_std_raw,
+                             int accumulate_mean, int accumulate_log_std, int batch,
+                             int action_dim, float log_std_min, float log_std_max,
+                             ttrl_stream_t stream);
+
+/* The twin-critic loss of ttrl/algos/sac/losses.py:46-76: alpha =
+ * exp(*log_alpha); y = r + (1 - done) * discount * (min_i q_target[i] -
+ * alpha * next_logp) (min by the relu identity); loss = 0.5 * sum_i
+ * mean(w * (q[i] - y)^2) (w = is_weights, or 1 when NULL); dq[i] = d loss /
+ * d q[i]; target = y; td_abs (NULL: skipped) = mean_i |q[i] - y|
+ * (losses.py:30-43). All vectors [batch]; q, q_target, dq are host arrays of
+ * n_critics device pointers. batch * n_critics * 4 bytes must fit 200 KB. */
+int ttrl_sac_critic_loss(const float* const* q, const float* const* q_target, int n_critics,
+                         const float* next_logp, const float* log_alpha, const float* rewards,
+                         const float* dones, const float* discounts, const float* is_weights,
+                         float* loss, float* alpha, float* target, float* const* dq,
+                         float* td_abs, int batch, ttrl_stream_t stream);
+
+/* The actor loss mean(alpha * logp - min_i q[i]) of ttrl/algos/sac/losses.py:
+ * 79-84 with dq[i] and d_logp, and (alpha_loss != NULL) the temperature loss
+ * -mean(log_alpha * (logp + target_entropy)) of losses.py:87-95 with its
+ * gradient d_log_alpha. batch * 12 bytes must fit 200 KB. */
+int ttrl_sac_actor_loss(const float* const* q, int n_critics, const float* logp,
+                        const float* log_alpha, float target_entropy, float* loss,
+                        float* const* dq, float* d_logp, float* alpha_loss,
+                        float* d_log_alpha, int batch, ttrl_stream_t stream);
+
 /* ------------------------------------------------------------------ acting */
 
 /* The DQN acting choice over q[batch][n_actions]: greedy = the first maximum

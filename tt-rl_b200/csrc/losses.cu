@@ -28,19 +28,6 @@ __device__ float block_sum(float v, float* red) {
   return s;
 }
 
-__device__ __forceinline__ float relu_f(float x) { return x > 0.f ? x : 0.f; }
-
-// clamp(x, lo, hi) as ttrl/engine/ops/select.py:54-63 composes it:
-// lifted = relu(x - lo) + lo ; out = hi - relu(hi - lifted). `pass` is the
-// derivative (1 strictly inside the band, 0 at or beyond a bound).
-__device__ __forceinline__ float clamp_ref(float x, float lo, float hi, float& pass) {
-  const float a = __fsub_rn(x, lo);
-  const float lifted = __fadd_rn(relu_f(a), lo);
-  const float b = __fsub_rn(hi, lifted);
-  pass = (a > 0.f && b > 0.f) ? 1.f : 0.f;
-  return __fsub_rn(hi, relu_f(b));
-}
-
 // ---------------------------------------------------------------- DQN
 
 

@@ -150,6 +150,14 @@ _SIGNATURES = {
     "ttrl_dqn_loss": (_c_int, [_vp] * 13 + [_c_int, _c_int, _c_float, _c_int, _vp]),
     "ttrl_ppo_loss": (_c_int, [_vp] * 12 + [_c_int, _c_int, _c_float, _c_float, _c_float,
                                              _c_float, _vp]),
+    "ttrl_sac_sample": (_c_int, [_vp] * 8 + [_c_int, _c_int, _c_int, _c_float, _c_float,
+                                             _c_float, _vp, _vp, _vp, _vp]),
+    "ttrl_sac_sample_backward": (_c_int, [_vp] * 5 + [ctypes.c_int64] + [_vp] * 3
+                                 + [_c_int] * 4 + [_c_float, _c_float, _vp]),
+    "ttrl_sac_critic_loss": (_c_int, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), _c_int]
+                             + [_vp] * 9 + [ctypes.POINTER(_vp), _vp, _c_int, _vp]),
+    "ttrl_sac_actor_loss": (_c_int, [ctypes.POINTER(_vp), _c_int, _vp, _vp, _c_float, _vp,
+                                     ctypes.POINTER(_vp), _vp, _vp, _vp, _c_int, _vp]),
     "ttrl_gru_gates_fwd": (_c_int, [_vp] * 7 + [_c_int, _c_int, _vp]),
     "ttrl_gru_gates_bwd": (_c_int, [_vp, _vp, _vp, _c_int] + [_vp] * 5 + [_c_int, _c_int, _vp]),
     "ttrl_gru_mask": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),

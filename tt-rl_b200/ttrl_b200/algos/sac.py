@@ -18,6 +18,14 @@ parameters do not request gradients. The reference's actor backward computes
 critic weight gradients and then discards them (the region steps only the
 policy); skipping those two weight-gradient GEMMs leaves d loss / d action,
 and so every policy gradient, as it was.
+
+For nets of `build_sac_nets`'s shape (a Gaussian-head policy, critics that
+read concat(obs, action) directly), the learner runs the regions on the fused
+heads of engine.ops (`sac_sample`, `sac_critic_loss`, `sac_actor_loss`): the
+sample with its log-density and its backward, each loss with its gradient,
+one launch each, in place of the reference's elementwise chains; both online
+critics read one concat(obs, action) buffer. The composed functions below
+stay the reference's op-for-op form (`fused=False` runs the learner on them).
 """
 
 from __future__ import annotations
@@ -33,13 +41,15 @@ from ttrl_b200.algos.grads import grad_sq_device
 from ttrl_b200.device import context
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.ops import (abs_, add, apply_done_mask, div, exp, log, mean_all,
-                                  minimum, mul, neg, relu, square, sub, sum_dim, tanh)
+                                  minimum, mul, neg, relu, sac_actor_loss, sac_critic_loss,
+                                  sac_sample, square, sub, sum_dim, tanh)
 from ttrl_b200.engine.optim import Adam
 from ttrl_b200.engine.trace import capture
 
 __all__ = ["LOG_2PI", "softplus", "normal_logp", "log_one_minus_tanh_sq", "squashed_logp",
            "ActionScale", "SquashedGaussian", "min_q", "critic_loss", "actor_loss",
-           "alpha_loss", "priority_errors", "critic_region", "actor_region", "SACConfig",
+           "alpha_loss", "priority_errors", "critic_region", "actor_region",
+           "critic_region_fused", "actor_region_fused", "fused_heads_apply", "SACConfig",
            "SACLearner"]
 
 LOG_2PI = math.log(2.0 * math.pi)
@@ -212,6 +222,96 @@ def actor_region(nets, dist, batch, log_alpha: Tensor, target_entropy: float, *,
     return metrics
 
 
+# ------------------------------------------------------------ fused regions
+
+def fused_heads_apply(nets) -> bool:
+    """True for nets the fused heads serve: a policy that is an encoder and a
+    Gaussian head, and critics (and targets) reading concat(obs, action)
+    through an encoder without layers."""
+    from ttrl_b200.nets.heads import GaussianHead
+    from ttrl_b200.nets.models import ConcatEncoder, ContinuousCritic, EncoderHead
+    policy = getattr(nets, "policy", None)
+    if not isinstance(policy, EncoderHead) or not isinstance(policy.head, GaussianHead):
+        return False
+    critics, targets = list(nets.critics), list(nets.targets)
+    if not critics or len(critics) != len(targets) or len(critics) > 8:
+        return False
+    for net in critics + targets:
+        if not isinstance(net, ContinuousCritic) or not isinstance(net.encoder, ConcatEncoder):
+            return False
+        if getattr(net.encoder.encoder, "has_parameters", True):
+            return False
+    return True
+
+
+def _policy_raw(policy, obs):
+    """(mean, log-std before the clamp) of a Gaussian-head policy."""
+    features = policy.encoder(obs)
+    heads = policy.head.heads
+    return heads["mean"](features), heads["log_std"](features)
+
+
+def _sample(dist, policy, mean, raw, noise, obs, pack=None):
+    head = policy.head
+    scale = dist.scale
+    return sac_sample(mean, raw, noise, scale._scale.data.reshape(-1),
+                      scale._centre.data.reshape(-1), scale.log_det,
+                      log_std_min=head.log_std_min, log_std_max=head.log_std_max, obs=obs,
+                      pack=pack)
+
+
+def critic_region_fused(nets, dist, batch, log_alpha: Tensor, *, prioritized: bool) -> dict:
+    """critic_region on the fused heads: the next-state sample also packs the
+    replayed concat(obs, action) that both online critics read."""
+    with no_grad():
+        mean, raw = _policy_raw(nets.policy, batch.next_obs)
+        joint_next, next_logp, joint = _sample(dist, nets.policy, mean, raw,
+                                               batch["next_noise"], batch.next_obs,
+                                               pack=(batch.obs, batch["actions"]))
+        q_next = [net.head(joint_next) for net in nets.targets]
+    qs = [critic.head(joint) for critic in nets.critics]
+    loss, alpha, target, td_abs = sac_critic_loss(
+        qs, q_next, next_logp, log_alpha, batch["rewards"], batch["dones"],
+        batch["discounts"], weights=batch["is_weights"] if prioritized else None,
+        want_td_abs=prioritized)
+    loss.backward()
+    metrics = {"critic_loss": loss, "alpha": alpha, "q_target": target}
+    total = grad_sq_device(nets.critic_parameters())
+    if total is not None:
+        metrics["critic_grad_sq"] = total
+    if prioritized:
+        metrics["td_abs"] = td_abs
+    return metrics
+
+
+def actor_region_fused(nets, dist, batch, log_alpha: Tensor, target_entropy: float, *,
+                       learn_alpha: bool) -> dict:
+    """actor_region on the fused heads (critic parameters request no
+    gradient, as in actor_region)."""
+    critic_params = nets.critic_parameters()
+    flags = [p.requires_grad for p in critic_params]
+    for p in critic_params:
+        p.requires_grad = False
+    try:
+        mean, raw = _policy_raw(nets.policy, batch.obs)
+        joint, logp, _ = _sample(dist, nets.policy, mean, raw, batch["noise"], batch.obs)
+        qs = [critic.head(joint) for critic in nets.critics]
+        loss, dual = sac_actor_loss(qs, logp, log_alpha, target_entropy,
+                                    learn_alpha=learn_alpha)
+        loss.backward()
+    finally:
+        for p, f in zip(critic_params, flags):
+            p.requires_grad = f
+    metrics = {"actor_loss": loss, "logp": logp.detach()}
+    total = grad_sq_device(nets.policy_parameters())
+    if total is not None:
+        metrics["actor_grad_sq"] = total
+    if learn_alpha:
+        dual.backward()
+        metrics["alpha_loss"] = dual
+    return metrics
+
+
 # ----------------------------------------------------------------- learner
 
 class _Batch(dict):
@@ -234,8 +334,16 @@ class SACLearner:
     """Graph-replayed SAC update over bound device batch buffers."""
 
     def __init__(self, nets, low, high, batch_size: int, obs_dim: int, device=None, *,
-                 cfg: SACConfig = SACConfig(), prioritized: bool = False):
+                 cfg: SACConfig = SACConfig(), prioritized: bool = False,
+                 fused: bool | None = None):
         self.nets = nets
+        # The fused heads where the nets allow them (fused=None), or as asked.
+        if fused is None:
+            fused = fused_heads_apply(nets)
+        elif fused and not fused_heads_apply(nets):
+            raise ValueError("SACLearner(fused=True): the nets are not a Gaussian-head policy "
+                             "with critics on concat(obs, action)")
+        self.fused = bool(fused)
         self.cfg = cfg
         self.device = as_device(device)
         self.dist = SquashedGaussian(low, high, self.device)
@@ -293,13 +401,15 @@ class SACLearner:
         opts = (self.critic_opt, self.policy_opt, self.alpha_opt)
         for opt in opts:
             opt.zero_grad()
-        critic = critic_region(self.nets, self.dist, self.batch, self.log_alpha,
-                               prioritized=self.prioritized)
+        critic_fn, actor_fn = ((critic_region_fused, actor_region_fused) if self.fused
+                               else (critic_region, actor_region))
+        critic = critic_fn(self.nets, self.dist, self.batch, self.log_alpha,
+                           prioritized=self.prioritized)
         self.critic_opt.step()
         for opt in opts:
             opt.zero_grad()
-        actor = actor_region(self.nets, self.dist, self.batch, self.log_alpha,
-                             self.target_entropy, learn_alpha=self.cfg.learn_alpha)
+        actor = actor_fn(self.nets, self.dist, self.batch, self.log_alpha,
+                         self.target_entropy, learn_alpha=self.cfg.learn_alpha)
         self.policy_opt.step()
         if self.cfg.learn_alpha:
             self.alpha_opt.step()

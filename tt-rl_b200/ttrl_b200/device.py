@@ -59,8 +59,8 @@ _NO_PROFILE = _NoProfile()
 class _Profile:
     """CUDA events around one library call on the launching stream."""
 
-    def __init__(self, ctx, name, flops):
-        self.ctx, self.name, self.flops = ctx, name, flops
+    def __init__(self, ctx, name, flops, call=None):
+        self.ctx, self.name, self.flops, self.call = ctx, name, flops, call
 
     def __enter__(self):
         self.start = torch.cuda.Event(enable_timing=True)
@@ -70,7 +70,7 @@ class _Profile:
 
     def __exit__(self, *exc):
         self.end.record(torch.cuda.current_stream(self.ctx.device))
-        self.ctx.profile.append((self.name, self.flops, self.start, self.end))
+        self.ctx.profile.append((self.name, self.flops, self.start, self.end, self.call))
         return False
 
 
@@ -155,15 +155,22 @@ class DeviceContext:
         # Contraction precision of every GEMM this context launches (a call
         # may override it); set_precision changes it.
         self.precision = PRECISION
-        # When a list, every GEMM-family call appends (name, flops, start, end).
+        # When a list, every GEMM-family call appends (name, flops, start, end,
+        # call), `call` a closure that issues the same launch again.
         self.profile = None
         for lane in range(WEIGHT_LANES + 1):  # the preparation lane needs none up front
             self.reserve(64 << 20, lane=lane)
 
-    def _timed(self, name: str, flops: int = 0):
+    def _timed(self, name: str, flops: int = 0, call=None):
         if self.profile is None or torch.cuda.is_current_stream_capturing():
             return _NO_PROFILE
-        return _Profile(self, name, flops)
+        return _Profile(self, name, flops, call)
+
+    def _call(self, name: str, flops: int, call) -> None:
+        """Run one library call; when profiling, bracket it with events and
+        keep `call` so that it can be issued again for a device timing."""
+        with self._timed(name, flops, call):
+            call()
 
     # -- workspace -------------------------------------------------------
 
@@ -281,11 +288,11 @@ class DeviceContext:
         m, k = x.shape[-2], x.shape[-1]
         n = w.shape[1]
         ws, wsb = self.workspace()
-        with self._timed(f"linear_fwd[{m}x{k}x{n}]", 2 * m * k * n):
-            check(lib().ttrl_linear_fwd(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")),
-                                        _ptr(_f32(b, "b")), _ptr(_f32(y, "y")), m, k, n,
-                                        int(relu), prec, ws, wsb, self.status_ptr(),
-                                        self.stream), "ttrl_linear_fwd")
+        self._call(f"linear_fwd[{m}x{k}x{n}]", 2 * m * k * n,
+                   lambda: check(lib().ttrl_linear_fwd(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")),
+                                            _ptr(_f32(b, "b")), _ptr(_f32(y, "y")), m, k, n,
+                                            int(relu), prec, ws, wsb, self.status_ptr(),
+                                            self.stream), "ttrl_linear_fwd"))
 
     def linear_dgrad(self, g, w, mask, dx, accumulate: bool,
                      precision: int | None = None) -> None:
@@ -293,11 +300,11 @@ class DeviceContext:
         m, n = g.shape[-2], g.shape[-1]
         k = w.shape[0]
         ws, wsb = self.workspace()
-        with self._timed(f"linear_dgrad[{m}x{k}x{n}]", 2 * m * k * n):
-            check(lib().ttrl_linear_dgrad(_ptr(_f32(g, "g")), _ptr(_f32(w, "w")),
-                                          _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")), m, k, n,
-                                          int(accumulate), prec, ws, wsb, self.status_ptr(),
-                                          self.stream), "ttrl_linear_dgrad")
+        self._call(f"linear_dgrad[{m}x{k}x{n}]", 2 * m * k * n,
+                   lambda: check(lib().ttrl_linear_dgrad(_ptr(_f32(g, "g")), _ptr(_f32(w, "w")),
+                                              _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")), m, k, n,
+                                              int(accumulate), prec, ws, wsb, self.status_ptr(),
+                                              self.stream), "ttrl_linear_dgrad"))
 
     def linear_wgrad(self, x, g, dw, db, accumulate: bool, accumulate_db: bool,
                      precision: int | None = None) -> None:
@@ -306,11 +313,11 @@ class DeviceContext:
         n = g.shape[-1]
         need = lib().ttrl_linear_wgrad_workspace_bytes(m, k, n)
         ws, wsb = self.workspace(need)
-        with self._timed(f"linear_wgrad[{m}x{k}x{n}]", 2 * m * k * n):
-            check(lib().ttrl_linear_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(g, "g")),
-                                          _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), m, k, n,
-                                          int(accumulate), int(accumulate_db), prec, ws, wsb,
-                                          self.status_ptr(), self.stream), "ttrl_linear_wgrad")
+        self._call(f"linear_wgrad[{m}x{k}x{n}]", 2 * m * k * n,
+                   lambda: check(lib().ttrl_linear_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(g, "g")),
+                                              _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), m, k, n,
+                                              int(accumulate), int(accumulate_db), prec, ws, wsb,
+                                              self.status_ptr(), self.stream), "ttrl_linear_wgrad"))
 
     # -- conv ------------------------------------------------------------
 
@@ -319,12 +326,12 @@ class DeviceContext:
         prec = self._prec(precision)
         g = geom.c_struct()
         ws, wsb = self.workspace()
-        with self._timed(f"conv_fprop[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
-                         _conv_flops(geom)):
-            check(lib().ttrl_conv_fprop(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")), _ptr(_f32(b, "b")),
-                                        _ptr(_f32(y, "y")), ctypes.byref(g), float(alpha),
-                                        int(relu), prec, ws, wsb, self.status_ptr(),
-                                        self.stream), "ttrl_conv_fprop")
+        self._call(f"conv_fprop[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom),
+                   lambda: check(lib().ttrl_conv_fprop(_ptr(_f32(x, "x")), _ptr(_f32(w, "w")), _ptr(_f32(b, "b")),
+                                            _ptr(_f32(y, "y")), ctypes.byref(g), float(alpha),
+                                            int(relu), prec, ws, wsb, self.status_ptr(),
+                                            self.stream), "ttrl_conv_fprop"))
 
     def conv_dgrad(self, dy, w, mask, dx, geom: Geom, accumulate: bool,
                    precision: int | None = None) -> None:
@@ -332,12 +339,12 @@ class DeviceContext:
         g = geom.c_struct()
         need = lib().ttrl_conv_dgrad_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
-        with self._timed(f"conv_dgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
-                         _conv_flops(geom)):
-            check(lib().ttrl_conv_dgrad(_ptr(_f32(dy, "dy")), _ptr(_f32(w, "w")),
-                                        _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
-                                        ctypes.byref(g), int(accumulate), prec, ws, wsb,
-                                        self.status_ptr(), self.stream), "ttrl_conv_dgrad")
+        self._call(f"conv_dgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom),
+                   lambda: check(lib().ttrl_conv_dgrad(_ptr(_f32(dy, "dy")), _ptr(_f32(w, "w")),
+                                            _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
+                                            ctypes.byref(g), int(accumulate), prec, ws, wsb,
+                                            self.status_ptr(), self.stream), "ttrl_conv_dgrad"))
 
     def conv_dgrad_weights_bytes(self, geom: Geom) -> int:
         """Bytes of the stacked sub-kernels of the two-step data gradient, or
@@ -357,13 +364,13 @@ class DeviceContext:
         g = geom.c_struct()
         need = lib().ttrl_conv_dgrad_prepared_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
-        with self._timed(f"conv_dgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
-                         _conv_flops(geom)):
-            check(lib().ttrl_conv_dgrad_prepared(_ptr(_f32(dy, "dy")), _ptr(_f32(wt, "wt")),
-                                                 _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
-                                                 ctypes.byref(g), int(accumulate), prec, ws, wsb,
-                                                 self.status_ptr(), self.stream),
-                  "ttrl_conv_dgrad_prepared")
+        self._call(f"conv_dgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom),
+                   lambda: check(lib().ttrl_conv_dgrad_prepared(_ptr(_f32(dy, "dy")), _ptr(_f32(wt, "wt")),
+                                                     _ptr(_f32(mask, "mask")), _ptr(_f32(dx, "dx")),
+                                                     ctypes.byref(g), int(accumulate), prec, ws, wsb,
+                                                     self.status_ptr(), self.stream),
+                      "ttrl_conv_dgrad_prepared"))
 
     def conv_wgrad(self, x, dy, dw, db, geom: Geom, alpha: float, accumulate: bool,
                    accumulate_db: bool, precision: int | None = None) -> None:
@@ -371,13 +378,13 @@ class DeviceContext:
         g = geom.c_struct()
         need = lib().ttrl_conv_wgrad_workspace_bytes(ctypes.byref(g))
         ws, wsb = self.workspace(need)
-        with self._timed(f"conv_wgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
-                         _conv_flops(geom)):
-            check(lib().ttrl_conv_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(dy, "dy")),
-                                        _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), ctypes.byref(g),
-                                        float(alpha), int(accumulate), int(accumulate_db),
-                                        prec, ws, wsb, self.status_ptr(), self.stream),
-                  "ttrl_conv_wgrad")
+        self._call(f"conv_wgrad[{geom.kh}x{geom.kw}/{geom.stride} {geom.c}->{geom.cout}]",
+                         _conv_flops(geom),
+                   lambda: check(lib().ttrl_conv_wgrad(_ptr(_f32(x, "x")), _ptr(_f32(dy, "dy")),
+                                            _ptr(_f32(dw, "dw")), _ptr(_f32(db, "db")), ctypes.byref(g),
+                                            float(alpha), int(accumulate), int(accumulate_db),
+                                            prec, ws, wsb, self.status_ptr(), self.stream),
+                      "ttrl_conv_wgrad"))
 
     def u8_to_f32(self, frames, index, out, scale: float = 1.0, fold: int = 1) -> None:
         """uint8 NCHW frames (optionally gathered by `index`) to fp32 NHWC rows,
@@ -591,6 +598,47 @@ class DeviceContext:
                                   _ptr(metrics), _ptr(new_logp), _ptr(dlogits), _ptr(dvalue), b,
                                   a, float(clip), float(vclip), float(vcoef), float(entcoef),
                                   self.stream), "ttrl_ppo_loss")
+
+    # -- SAC heads ---------------------------------------------------------
+
+    def sac_sample(self, mean, raw, noise, scale, centre, obs, joint, logp, lo: float,
+                   hi: float, log_det: float, pack=None) -> None:
+        b, d = mean.shape[0], mean.shape[1]
+        o = 0 if obs is None else obs.shape[1]
+        po, pa, pj = (None, None, None) if pack is None else pack
+        check(lib().ttrl_sac_sample(_ptr(mean), _ptr(raw), _ptr(noise), _ptr(scale),
+                                    _ptr(centre), _ptr(obs), _ptr(joint), _ptr(logp), b, d, o,
+                                    float(lo), float(hi), float(log_det), _ptr(po), _ptr(pa),
+                                    _ptr(pj), self.stream), "ttrl_sac_sample")
+
+    def sac_sample_backward(self, mean, raw, noise, scale, d_action, ld: int, d_logp, d_mean,
+                            d_raw, acc_mean: bool, acc_raw: bool, lo: float, hi: float) -> None:
+        b, d = mean.shape[0], mean.shape[1]
+        check(lib().ttrl_sac_sample_backward(_ptr(mean), _ptr(raw), _ptr(noise), _ptr(scale),
+                                             _ptr(d_action), int(ld), _ptr(d_logp),
+                                             _ptr(d_mean), _ptr(d_raw), int(acc_mean),
+                                             int(acc_raw), b, d, float(lo), float(hi),
+                                             self.stream), "ttrl_sac_sample_backward")
+
+    def sac_critic_loss(self, qs, q_targets, next_logp, log_alpha, rewards, dones, discounts,
+                        is_weights, loss, alpha, target, dqs, td_abs) -> None:
+        n = len(qs)
+        arr = lambda ts: (ctypes.c_void_p * n)(*[_ptr(t) for t in ts])
+        check(lib().ttrl_sac_critic_loss(arr(qs), arr(q_targets), n, _ptr(next_logp),
+                                         _ptr(log_alpha), _ptr(rewards), _ptr(dones),
+                                         _ptr(discounts), _ptr(is_weights), _ptr(loss),
+                                         _ptr(alpha), _ptr(target), arr(dqs), _ptr(td_abs),
+                                         int(qs[0].shape[0]), self.stream),
+              "ttrl_sac_critic_loss")
+
+    def sac_actor_loss(self, qs, logp, log_alpha, target_entropy: float, loss, dqs, d_logp,
+                       alpha_loss, d_log_alpha) -> None:
+        n = len(qs)
+        arr = lambda ts: (ctypes.c_void_p * n)(*[_ptr(t) for t in ts])
+        check(lib().ttrl_sac_actor_loss(arr(qs), n, _ptr(logp), _ptr(log_alpha),
+                                        float(target_entropy), _ptr(loss), arr(dqs),
+                                        _ptr(d_logp), _ptr(alpha_loss), _ptr(d_log_alpha),
+                                        int(qs[0].shape[0]), self.stream), "ttrl_sac_actor_loss")
 
 
 def context(device=None) -> DeviceContext:

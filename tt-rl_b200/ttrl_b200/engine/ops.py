@@ -33,6 +33,7 @@ __all__ = [
     "masks", "non_finite_check", "one_hot_device", "one_hot_gather",
     "one_hot_host", "purge_lane_caches", "purge_matmul_caches",
     "linear", "conv2d_nhwc", "dqn_td_huber", "ppo_objective",
+    "sac_sample", "sac_critic_loss", "sac_actor_loss",
 ]
 
 
@@ -866,3 +867,158 @@ def ppo_objective(logits: Tensor, value: Tensor, actions, old_logp, advantages, 
 
     out._backward = _backward
     return out, parts, nl
+
+
+# --------------------------------------------------------------------------
+# SAC heads
+# --------------------------------------------------------------------------
+
+def _raw_data(t):
+    if t is None:
+        return None
+    d = t.data if isinstance(t, Tensor) else t
+    return d if d.is_contiguous() else d.contiguous()
+
+
+def sac_sample(mean: Tensor, log_std_raw: Tensor, noise, scale, centre, log_det: float, *,
+               log_std_min: float, log_std_max: float, obs=None, pack=None):
+    """The squashed-Gaussian sample of ttrl/algos/sac/policy.py:30-40 as one
+    kernel, from the policy's raw outputs: the log-std clamp of the Gaussian
+    head, u = mean + exp(log_std) * noise, the log-density of
+    ttrl/algos/gaussian.py:55-90 and the env action tanh(u) * scale + centre.
+
+    The action is written after `obs`'s columns, as the critic input
+    concat(obs, action); `pack` = (obs', action') also writes concat(obs',
+    action') in the same launch. -> (joint (B, obs + D), logp (B, 1), packed
+    joint or None). joint and logp are differentiable in mean and
+    log_std_raw; their backward is one kernel, run once both gradients are
+    in."""
+    b, d = int(mean.shape[0]), int(mean.shape[1])
+    o = 0 if obs is None else int(obs.shape[1])
+    dev = mean.data
+    ctx = _ctx(dev)
+    joint = _new((b, o + d), dev)
+    logp = _new((b, 1), dev)
+    packed = _new((b, o + d), dev) if pack is not None else None
+    md, rd, nd = _raw_data(mean), _raw_data(log_std_raw), _raw_data(noise)
+    lo, hi = float(log_std_min), float(log_std_max)
+    ctx.sac_sample(md, rd, nd, scale, centre, _raw_data(obs), joint, logp, lo, hi, log_det,
+                   pack=None if pack is None else (_raw_data(pack[0]), _raw_data(pack[1]), packed))
+    packed_t = None if packed is None else Tensor(packed, requires_grad=False)
+    if not _needs(mean, log_std_raw):
+        return _detached(joint), _detached(logp), packed_t
+    out = Tensor(joint, True, (mean, log_std_raw), "sac_sample")
+    # logp is a consumer of the joint node, so the joint node's backward runs
+    # after logp's: by then both gradients are known.
+    lp = Tensor(logp, True, (out,), "sac_logp")
+    pending = {}
+
+    def _logp_backward(grad):
+        pending["logp"] = grad if grad.is_contiguous() else grad.contiguous()
+        if out.grad is None:
+            # No action gradient has arrived yet: start the action's gradient
+            # at zero for any later consumer to accumulate into, so that the
+            # joint node still runs.
+            zero = _new(joint.shape, joint)
+            ctx.ew("fill", None, None, zero, 0.0)
+            out._set_grad(zero)
+
+    def _backward(grad):
+        if grad.stride(-1) != 1:
+            grad = grad.contiguous()
+        if mean.requires_grad:
+            mbuf, macc = mean._grad_slot()
+        else:
+            mbuf, macc = _new(mean.shape, dev), False
+        if log_std_raw.requires_grad:
+            rbuf, racc = log_std_raw._grad_slot()
+        else:
+            rbuf, racc = _new(log_std_raw.shape, dev), False
+        ctx.sac_sample_backward(md, rd, nd, scale, grad.narrow(1, o, d), grad.stride(0),
+                                pending.get("logp"), mbuf, rbuf, macc, racc, lo, hi)
+        if mean.requires_grad:
+            mean._set_grad(mbuf)
+        if log_std_raw.requires_grad:
+            log_std_raw._set_grad(rbuf)
+
+    lp._backward = _logp_backward
+    out._backward = _backward
+    return out, lp, packed_t
+
+
+def sac_critic_loss(qs, q_targets, next_logp, log_alpha, rewards, dones, discounts, *,
+                    weights=None, want_td_abs: bool = False):
+    """The twin-critic loss of ttrl/algos/sac/losses.py:46-76 as one kernel,
+    from the online critics' Q(s, a) and the targets' Q(s', a') with the
+    next log-density (the no_grad target side). alpha = exp(log_alpha) is
+    read on the device. -> (loss (1,1), alpha (1,1), target (B,1), |TD| mean
+    over critics (B,1) or None); loss is differentiable in every q."""
+    qs, q_targets = list(qs), list(q_targets)
+    if len(qs) != len(q_targets):
+        raise ValueError(f"sac_critic_loss: {len(qs)} critics but {len(q_targets)} targets")
+    b = int(qs[0].shape[0])
+    dev = qs[0].data
+    loss, alpha = _new((1, 1), dev), _new((1, 1), dev)
+    target = _new((b, 1), dev)
+    td_abs = _new((b, 1), dev) if want_td_abs else None
+    dqs = [_new((b, 1), dev) for _ in qs]
+    _ctx(dev).sac_critic_loss([_flat(q) for q in qs], [_flat(t) for t in q_targets],
+                              _flat(next_logp), _flat(log_alpha), _flat(rewards), _flat(dones),
+                              _flat(discounts), _flat(weights), loss, alpha, target, dqs, td_abs)
+    alpha_t = Tensor(alpha, requires_grad=False)
+    target_t = Tensor(target, requires_grad=False)
+    td_t = None if td_abs is None else Tensor(td_abs, requires_grad=False)
+    if not _needs(*qs):
+        return _detached(loss), alpha_t, target_t, td_t
+    out = Tensor(loss, True, tuple(qs), "sac_critic_loss")
+
+    def _backward(grad):
+        for q, dq in zip(qs, dqs):
+            if q.requires_grad:
+                _scaled_into_grad(out, grad, dq.reshape(q.shape), q)
+
+    out._backward = _backward
+    return out, alpha_t, target_t, td_t
+
+
+def sac_actor_loss(qs, logp: Tensor, log_alpha: Tensor, target_entropy: float, *,
+                   learn_alpha: bool = True):
+    """The actor loss mean(alpha * logp - min_i Q_i(s, a~pi)) of
+    ttrl/algos/sac/losses.py:79-84 and the temperature loss of :87-95, one
+    kernel. -> (actor loss (1,1) differentiable in every q and in logp,
+    temperature loss (1,1) differentiable in log_alpha, or None)."""
+    qs = list(qs)
+    b = int(qs[0].shape[0])
+    dev = qs[0].data
+    loss = _new((1, 1), dev)
+    dqs = [_new((b, 1), dev) for _ in qs]
+    d_logp = _new((b, 1), dev)
+    dual = _new((1, 1), dev) if learn_alpha else None
+    d_log_alpha = _new(tuple(log_alpha.shape), dev) if learn_alpha else None
+    _ctx(dev).sac_actor_loss([_flat(q) for q in qs], _flat(logp), _flat(log_alpha),
+                             float(target_entropy), loss, dqs, d_logp, dual, d_log_alpha)
+    dual_t = None
+    if learn_alpha:
+        if _needs(log_alpha):
+            dual_t = Tensor(dual, True, (log_alpha,), "sac_alpha_loss")
+
+            def _dual_backward(grad):
+                _scaled_into_grad(dual_t, grad, d_log_alpha, log_alpha)
+
+            dual_t._backward = _dual_backward
+        else:
+            dual_t = _detached(dual)
+    parents = (*qs, logp)
+    if not _needs(*parents):
+        return _detached(loss), dual_t
+    out = Tensor(loss, True, parents, "sac_actor_loss")
+
+    def _backward(grad):
+        for q, dq in zip(qs, dqs):
+            if q.requires_grad:
+                _scaled_into_grad(out, grad, dq.reshape(q.shape), q)
+        if logp.requires_grad:
+            _scaled_into_grad(out, grad, d_logp, logp)
+
+    out._backward = _backward
+    return out, dual_t
