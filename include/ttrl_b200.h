@@ -271,7 +271,7 @@ typedef struct {
   float* v;    /* V = v / (1 - b2), the reference's stored second moment */
   int64_t numel;
   int32_t step_index; /* index into the device step-counter array */
-  int32_t pad0;
+  int32_t lr_index;   /* index into lr_device (0 when one rate serves all) */
 } ttrl_adam_tensor;
 
 /* Multi-tensor fused Adam step in the reference's S/V form
@@ -287,10 +287,13 @@ typedef struct {
  * kernel leaves it zero). `grad_scale` (device float, may be NULL)
  * multiplies every gradient first (the clip factor of
  * ttrl/algos/grads.py:29-43); weight_decay adds wd*p to g next
- * (adam.py:110-113). `lr_device` (device double, may be NULL) overrides
- * `lr` at execution time, so a replayed graph follows a learning-rate
- * schedule (ttrl/algos/ppo/learn.py:54-56). Up to TTRL_ADAM_MAX_TENSORS
- * tensors per call. */
+ * (adam.py:110-113). `lr_device` (device doubles, may be NULL) overrides
+ * `lr` at execution time, tensor i reading lr_device[tensors[i].lr_index],
+ * so a replayed graph follows a learning-rate schedule
+ * (ttrl/algos/ppo/learn.py:54-56) and one launch can step the parameters of
+ * several optimizers (SAC's policy and temperature, ttrl/algos/sac/
+ * agent.py:218-238) that share betas, eps and weight decay but keep their
+ * own rates and counters. Up to TTRL_ADAM_MAX_TENSORS tensors per call. */
 #define TTRL_ADAM_MAX_TENSORS 64
 int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
                    const float* grad_scale, const double* lr_device, double lr, double b1,

@@ -317,6 +317,49 @@ def test_adam_matches_reference_sv_form():
     assert int(host(ticket)[0]) == 0
 
 
+def test_adam_shared_launch_equals_separate_steps():
+    """Two Adams joined by share_launch (different learning rates and
+    parameter counts, as SAC's policy and temperature) stepped by
+    step_together in one launch: bit for bit the two separate steps, with
+    each optimizer's counters and rate its own; a later lr change of one of
+    them is seen by the joint launch."""
+    from ttrl_b200.engine.autograd import Tensor
+    from ttrl_b200.engine.optim import Adam, share_launch, step_together
+    rng = np.random.default_rng(15)
+    shapes_a, shapes_b = [(256, 17), (256,), (3, 256)], [(1, 1)]
+
+    def make():
+        pa = [Tensor(dev(rng0.standard_normal(s).astype(np.float32)), True) for s in shapes_a]
+        pb = [Tensor(dev(rng0.standard_normal(s).astype(np.float32)), True) for s in shapes_b]
+        return pa, pb, Adam(pa, lr=3e-4), Adam(pb, lr=1e-3)
+
+    rng0 = np.random.default_rng(1)
+    pa1, pb1, oa1, ob1 = make()
+    rng0 = np.random.default_rng(1)
+    pa2, pb2, oa2, ob2 = make()
+    share_launch([oa2, ob2])
+    from ttrl_b200._lib import lib
+    for t in range(3):
+        if t == 2:
+            ob1.lr = ob2.lr = 5e-4
+        grads = [rng.standard_normal(p.shape).astype(np.float32) for p in pa1 + pb1]
+        for params in ((pa1 + pb1), (pa2 + pb2)):
+            for p, g in zip(params, grads):
+                p.grad = dev(g)
+        oa1.step()
+        ob1.step()
+        before = lib().ttrl_launch_count()
+        step_together([oa2, ob2])
+        assert lib().ttrl_launch_count() - before == 1
+    for p1, p2 in zip(pa1 + pb1, pa2 + pb2):
+        assert np.array_equal(host(p1.data), host(p2.data))
+    for o1, o2 in ((oa1, oa2), (ob1, ob2)):
+        assert o1.steps == o2.steps and o1.t == o2.t
+        assert host(o2._dev_steps).tolist() == o2.steps
+        for m1, m2 in zip(o1.m + o1.v, o2.m + o2.v):
+            assert np.array_equal(host(m1), host(m2))
+
+
 def test_grad_sqnorm_and_clip_factor():
     ctx = _ctx()
     rng = np.random.default_rng(14)

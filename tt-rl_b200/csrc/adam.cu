@@ -114,9 +114,9 @@ __global__ void __launch_bounds__(kAdamThreads, kAdamBlocksPerSM)
   // per tensor computes them (double precision) while the first loads are
   // in flight.
   __shared__ AdamScalars ks[TTRL_ADAM_MAX_TENSORS];
-  const double lr = a.lr_device ? *a.lr_device : a.lr;
   const float gs = a.grad_scale != nullptr ? *a.grad_scale : 1.f;
   for (int q = threadIdx.x; q < a.count; q += blockDim.x) {
+    const double lr = a.lr_device ? a.lr_device[a.t[q].lr_index] : a.lr;
     const int step = a.steps[a.t[q].step_index] + 1;
     const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
     const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));

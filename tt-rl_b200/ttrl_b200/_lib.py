@@ -84,7 +84,7 @@ CONV_INPUT_EXACT = 1
 class AdamTensor(ctypes.Structure):
     _fields_ = [
         ("param", _vp), ("grad", _vp), ("s", _vp), ("v", _vp),
-        ("numel", ctypes.c_int64), ("step_index", ctypes.c_int32), ("pad0", ctypes.c_int32),
+        ("numel", ctypes.c_int64), ("step_index", ctypes.c_int32), ("lr_index", ctypes.c_int32),
     ]
 
 

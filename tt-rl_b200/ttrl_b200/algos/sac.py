@@ -43,7 +43,7 @@ from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.ops import (abs_, add, apply_done_mask, div, exp, log, mean_all,
                                   minimum, mul, neg, relu, sac_actor_loss, sac_critic_loss,
                                   sac_sample, square, sub, sum_dim, tanh)
-from ttrl_b200.engine.optim import Adam
+from ttrl_b200.engine.optim import Adam, share_launch, step_together
 from ttrl_b200.engine.trace import capture
 
 __all__ = ["LOG_2PI", "softplus", "normal_logp", "log_one_minus_tanh_sq", "squashed_logp",
@@ -356,6 +356,8 @@ class SACLearner:
         self.critic_opt = Adam(nets.critic_parameters(), lr=cfg.lr)
         self.policy_opt = Adam(nets.policy_parameters(), lr=cfg.lr)
         self.alpha_opt = Adam([self.log_alpha], lr=cfg.lr)
+        # The policy and temperature steps run back to back: one launch.
+        share_launch([self.policy_opt, self.alpha_opt])
         B, D = int(batch_size), self.dim
         dev = self.device
 
@@ -410,9 +412,8 @@ class SACLearner:
             opt.zero_grad()
         actor = actor_fn(self.nets, self.dist, self.batch, self.log_alpha,
                          self.target_entropy, learn_alpha=self.cfg.learn_alpha)
-        self.policy_opt.step()
-        if self.cfg.learn_alpha:
-            self.alpha_opt.step()
+        step_together([self.policy_opt, self.alpha_opt] if self.cfg.learn_alpha
+                      else [self.policy_opt])
         self._polyak()
         return {**critic, **actor}
 

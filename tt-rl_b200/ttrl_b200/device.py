@@ -410,14 +410,14 @@ class DeviceContext:
 
     def adam_step(self, tensors, steps, ticket, grad_scale, lr, b1, b2, eps, wd,
                   lr_device=None) -> None:
-        """`tensors`: list of (param, grad, S, V, step_index)."""
+        """`tensors`: list of (param, grad, S, V, step_index[, lr_index])."""
         for start in range(0, len(tensors), 64):
             chunk = tensors[start:start + 64]
             arr = (_lib.AdamTensor * len(chunk))()
-            for i, (p, g, s, v, idx) in enumerate(chunk):
+            for i, (p, g, s, v, idx, *rest) in enumerate(chunk):
                 arr[i] = _lib.AdamTensor(_ptr(_f32(p, "param")), _ptr(_f32(g, "grad")),
                                          _ptr(_f32(s, "S")), _ptr(_f32(v, "V")), p.numel(),
-                                         int(idx), 0)
+                                         int(idx), int(rest[0]) if rest else 0)
             check(lib().ttrl_adam_step(arr, len(chunk), _ptr(steps), _ptr(ticket),
                                        _ptr(grad_scale), _ptr(lr_device), float(lr), float(b1),
                                        float(b2), float(eps), float(wd), self.stream),

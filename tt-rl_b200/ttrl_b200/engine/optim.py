@@ -19,7 +19,7 @@ import torch
 from ttrl_b200.device import context
 from ttrl_b200.engine.tensor import MASTER_DTYPE, restore_in_place, to_host
 
-__all__ = ["Optimizer", "Adam", "adam_fused_scalars"]
+__all__ = ["Optimizer", "Adam", "adam_fused_scalars", "share_launch", "step_together"]
 
 
 def adam_fused_scalars(lr: float, b1: float, b2: float, eps: float, t: int) -> tuple[float, float]:
@@ -82,6 +82,8 @@ class Adam(Optimizer):
         self.grad_scale = None
         # Indices stepped by the launch recorded inside a graph capture.
         self.captured_indices: list[int] | None = None
+        # (group, counter base, rate slot) once share_launch joined it.
+        self._shared = None
 
     # The learning rate lives on the device too, so a replayed graph reads
     # the current value (PPO's annealing, ttrl/algos/ppo/learn.py:54-56).
@@ -102,26 +104,35 @@ class Adam(Optimizer):
     def _v_scale(self) -> float:
         return 1 - self.b2
 
-    def step(self) -> None:
-        """One update of every parameter that holds a gradient."""
+    def _pending(self, step_base: int = 0, lr_index: int = 0):
+        """(tensors, stepped indices) of the parameters that hold a gradient."""
         tensors = []
         stepped = []
         for i, p in enumerate(self.params):
             if p.grad is None:
                 continue
             g = p.grad if p.grad.is_contiguous() else p.grad.contiguous()
-            tensors.append((p.data, g.reshape(p.data.shape), self.m[i], self.v[i], i))
+            tensors.append((p.data, g.reshape(p.data.shape), self.m[i], self.v[i],
+                            step_base + i, lr_index))
             stepped.append(i)
-        if tensors:
-            context(self._device).adam_step(
-                tensors, self._dev_steps, self._ticket, self.grad_scale, self._lr, self.b1,
-                self.b2, self.eps, self.weight_decay, lr_device=self._lr_dev)
+        return tensors, stepped
+
+    def _finish(self, stepped) -> None:
         self.grad_scale = None
         if torch.cuda.is_current_stream_capturing():
             # Recorded, not run: TrainStep advances the host mirror per replay.
             self.captured_indices = stepped
             return
         self.advance(stepped)
+
+    def step(self) -> None:
+        """One update of every parameter that holds a gradient."""
+        tensors, stepped = self._pending()
+        if tensors:
+            context(self._device).adam_step(
+                tensors, self._dev_steps, self._ticket, self.grad_scale, self._lr, self.b1,
+                self.b2, self.eps, self.weight_decay, lr_device=self._lr_dev)
+        self._finish(stepped)
 
     def advance(self, stepped) -> None:
         """Advance the host mirror of the device step counters."""
@@ -210,3 +221,76 @@ class Adam(Optimizer):
         for i, arr in enumerate(device_form["v"]):
             restore_in_place(self.v[i], np.asarray(arr) / vs)
         self._dev_steps.copy_(torch.tensor(steps, dtype=torch.int32))
+
+
+class _SharedLaunch:
+    """Device state that several Adams keep side by side so that one kernel
+    launch can step them all: their step counters in one int32 array, their
+    learning rates in one float64 array, one ticket."""
+
+    def __init__(self, opts):
+        dev = opts[0]._device
+        counts = [len(o.params) for o in opts]
+        self.steps = torch.zeros(sum(counts), dtype=torch.int32, device=dev)
+        self.lrs = torch.zeros(len(opts), dtype=torch.float64, device=dev)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.opts = list(opts)
+        self.bases = []
+        base = 0
+        for slot, (o, n) in enumerate(zip(opts, counts)):
+            self.steps[base:base + n].copy_(o._dev_steps)
+            self.lrs[slot:slot + 1].copy_(o._lr_dev)
+            # Views: every in-place write of the optimizer (load_state_dict,
+            # the lr setter, a restore) lands in the shared arrays.
+            o._dev_steps = self.steps[base:base + n]
+            o._lr_dev = self.lrs[slot:slot + 1]
+            o._shared = (self, base, slot)
+            self.bases.append(base)
+            base += n
+
+
+def share_launch(opts) -> None:
+    """Let `step_together(opts)` step these Adams in one kernel launch. Each
+    keeps its own parameters, moments, step counters, learning rate and
+    state_dict; only where the device copies of the counters and the rate
+    live changes. All must be on one device."""
+    opts = list(opts)
+    if len(opts) < 2:
+        return
+    if any(not isinstance(o, Adam) for o in opts):
+        raise TypeError("share_launch: Adam optimizers only")
+    if len({o._device for o in opts}) != 1:
+        raise ValueError("share_launch: the optimizers live on different devices")
+    if sum(len(o.params) for o in opts) > 64:
+        raise ValueError("share_launch: more than 64 parameters in all")
+    _SharedLaunch(opts)
+
+
+def step_together(opts) -> None:
+    """step() every optimizer of `opts`: one launch when they were joined by
+    share_launch and agree on betas, eps and weight decay with no gradient
+    scale pending (the math per parameter is unchanged: each reads its own
+    counter and rate); otherwise one step() each, in order."""
+    opts = list(opts)
+    shared = [getattr(o, "_shared", None) for o in opts]
+    group = shared[0][0] if shared and shared[0] is not None else None
+    joint = (group is not None and all(s is not None and s[0] is group for s in shared)
+             and all(o.grad_scale is None for o in opts)
+             and len({(o.b1, o.b2, o.eps, o.weight_decay) for o in opts}) == 1)
+    if not joint:
+        for o in opts:
+            o.step()
+        return
+    tensors, stepped = [], []
+    for o, (_, base, slot) in zip(opts, shared):
+        t, s = o._pending(base, slot)
+        tensors += t
+        stepped.append(s)
+    if tensors:
+        head = opts[0]
+        context(head._device).adam_step(tensors, group.steps, group.ticket, None, head._lr,
+                                        head.b1, head.b2, head.eps, head.weight_decay,
+                                        lr_device=group.lrs)
+    for o, s in zip(opts, stepped):
+        o._finish(s)
+
