@@ -23,7 +23,14 @@ class InputBinder:
     few host-to-device copies as there are contiguous runs of them (one, when
     every input is loaded). With `deferred`, `load` only stages and
     `flush()` (TrainStep calls it before every replay) issues the copies;
-    otherwise every `load` uploads at once."""
+    otherwise every `load` uploads at once.
+
+    A deferred binder over an input arena overlaps the upload with the work
+    already queued: the host-to-device copy goes on a copy stream into one
+    of two device staging arenas, and the current stream, once that copy is
+    in, moves the staged bytes into the bound buffers with one device copy
+    per run. The upload of update k+1 thus runs while update k still reads
+    the bound buffers; the bound addresses never change."""
 
     STAGES = 3
 
@@ -56,6 +63,13 @@ class InputBinder:
         self._mirror = None
         self._from_mirror: set = set()
         self.last_upload = None
+        # Overlapped uploads (deferred, arena): copy stream, two device
+        # staging arenas and, per arena, the event after which it is free.
+        self._overlap = deferred and self._arena is not None
+        self._copy_stream = None
+        self._dev_stage: list = [None, None]
+        self._stage_free: list = [None, None]
+        self._dslot = 0
 
     def _stage(self):
         """The pinned buffer of the current ring slot, free for writing."""
@@ -121,10 +135,14 @@ class InputBinder:
         names = sorted(self._dirty, key=lambda k: self._offset[k])
         mirrored = [k for k in names if k in self._from_mirror]
         staged = [k for k in names if k not in self._from_mirror]
-        self._upload(self._mirror_buf if mirrored else None, mirrored)
-        self._upload(buf, staged)
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(self.device))
+        cur = torch.cuda.current_stream(self.device)
+        if self._overlap and not torch.cuda.is_current_stream_capturing():
+            ev = self._flush_overlapped(cur, buf, mirrored, staged)
+        else:
+            self._upload(self._mirror_buf if mirrored else None, mirrored)
+            self._upload(buf, staged)
+            ev = torch.cuda.Event()
+            ev.record(cur)
         self.last_upload = ev
         if staged:
             self._events[self._slot] = ev
@@ -132,24 +150,62 @@ class InputBinder:
         self._dirty.clear()
         self._from_mirror.clear()
 
+    def _runs(self, names):
+        """Byte ranges covering `names` (sorted by offset): an input starting
+        where the previous one ends (up to its 256-byte alignment) joins its
+        run."""
+        runs = []
+        start = end = None
+        for k in names:
+            off, n = self._offset[k], self._nbytes[k]
+            if start is not None and off <= (end + 255) // 256 * 256:
+                end = max(end, off + n)
+                continue
+            if start is not None:
+                runs.append((start, end))
+            start, end = off, off + n
+        if start is not None:
+            runs.append((start, end))
+        return runs
+
+    def _flush_overlapped(self, cur, buf, mirrored, staged):
+        """Upload on the copy stream into a device staging arena, then move it
+        into the bound buffers on `cur` once the upload is in. -> the event
+        after which the host sources may be rewritten."""
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+        slot = self._dslot
+        stage = self._dev_stage[slot]
+        if stage is None:
+            stage = self._dev_stage[slot] = torch.empty(self._span, dtype=torch.uint8,
+                                                        device=self.device)
+        cs = self._copy_stream
+        if self._stage_free[slot] is not None:
+            cs.wait_event(self._stage_free[slot])
+        with torch.cuda.stream(cs):
+            for src, names in ((self._mirror_buf if mirrored else None, mirrored),
+                               (buf, staged)):
+                for a, b in self._runs(names):
+                    stage[a:b].copy_(src[a:b], non_blocking=True)
+        up = torch.cuda.Event()
+        up.record(cs)
+        cur.wait_event(up)
+        for a, b in self._runs(sorted(mirrored + staged, key=lambda k: self._offset[k])):
+            self._arena[a:b].copy_(stage[a:b], non_blocking=True)
+        free = torch.cuda.Event()
+        free.record(cur)
+        self._stage_free[slot] = free
+        self._dslot = 1 - slot
+        return up
+
     def _upload(self, buf, names) -> None:
         """Host-to-device copies of `names` (sorted by offset) out of `buf`,
         which holds each at its input offset."""
         if not names:
             return
         if self._arena is not None:
-            # Contiguous runs: an input starting where the previous one ends
-            # (up to its 256-byte alignment) joins its run.
-            start = end = None
-            for k in names:
-                off, n = self._offset[k], self._nbytes[k]
-                if start is not None and off <= (end + 255) // 256 * 256:
-                    end = max(end, off + n)
-                    continue
-                if start is not None:
-                    self._arena[start:end].copy_(buf[start:end], non_blocking=True)
-                start, end = off, off + n
-            self._arena[start:end].copy_(buf[start:end], non_blocking=True)
+            for a, b in self._runs(names):
+                self._arena[a:b].copy_(buf[a:b], non_blocking=True)
         else:
             for k in names:
                 dst, off = self._tensors[k], self._offset[k]
@@ -157,9 +213,11 @@ class InputBinder:
                 dst.copy_(src, non_blocking=True)
 
     def close(self) -> None:
-        for ev in self._events + [self.last_upload]:
+        for ev in self._events + self._stage_free + [self.last_upload]:
             if ev is not None:
                 ev.synchronize()
+        self._dev_stage = [None, None]
+        self._stage_free = [None, None]
         self._mirror = None
         self._mirror_buf = None
         self._slots = [None] * self.STAGES
