@@ -234,6 +234,30 @@ def cpu_ppo_steps(n_steps: int, seed: int = 0):
     return times
 
 
+def cpu_dqn_updates(n_updates: int, seed: int = 0):
+    """The reference's arithmetic on the host (numpy fp32, all BLAS threads):
+    Nature-DQN batch-32 double-DQN updates with Adam. Seconds per update."""
+    from oracle import learner as ref
+    rng = np.random.default_rng(seed)
+    online = ref.nature_params(rng, heads=(("q", 6),))
+    target = ref.nature_params(rng, heads=(("q", 6),))
+    obs = rng.integers(0, 256, (32, 84, 84, 4)).astype(np.float32)
+    nxt = rng.integers(0, 256, (32, 84, 84, 4)).astype(np.float32)
+    acts = rng.integers(0, 6, 32)
+    rew = rng.choice([-1.0, 0.0, 1.0], 32).astype(np.float32)
+    dones = np.zeros(32, np.float32)
+    disc = np.full(32, 0.99, np.float32)
+    state = None
+    times = []
+    for t in range(1, n_updates + 1):
+        t0 = time.perf_counter()
+        out = ref.dqn_update(online, target, obs, nxt, acts, rew, dones, disc,
+                             adam_state=state, t=t)
+        online, state = out[2], out[3]
+        times.append(time.perf_counter() - t0)
+    return times
+
+
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
@@ -615,6 +639,14 @@ def bench_dqn(device, args):
     e2e_ms = (time.perf_counter() - t0) * 1000 / E
     h2d = sum(v.nbytes for v in arrays.values())
     learner.close()
+    cpu = {}
+    if not args.no_cpu_baseline:
+        cpu_dqn_updates(2)  # warm-up (BLAS threads, allocations)
+        t = statistics.median(cpu_dqn_updates(20, seed=1))
+        cpu = {"cpu_baseline": {"value": 1.0 / t, "unit": "updates/s", "cores": os.cpu_count(),
+                                "kind": "port",
+                                "sample": "median of 20 double-DQN batch-32 updates with Adam "
+                                          "(oracle.learner.dqn_update, numpy fp32)"}}
     return {"metric": "Nature-DQN batch-32 learner updates/sec (fwd x3 + bwd + Adam, one graph "
                       "replay per update)",
             "value": 1000.0 / ms, "unit": "updates/s", "ms_per_update": ms,
@@ -622,7 +654,7 @@ def bench_dqn(device, args):
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 3 * 4},
             "gpu_launches_per_update": launches,
             "achieved_tflops": DQN_FLOP_PER_UPDATE / (ms * 1e-3) / 1e12,
-            "target": ">= 5000 updates/s"}
+            "target": ">= 5000 updates/s", **cpu}
 
 
 def bench_sac(device, args):
@@ -765,19 +797,28 @@ def _profile_conv(layer: str, kind: str):
     return run
 
 
-def _profile_fc1(args):
-    import torch
-    from ttrl_b200.device import context
-    dev = torch.device("cuda", 0)
-    rng = np.random.default_rng(0)
-    x = torch.from_numpy(rng.standard_normal((args.batch, 3136)).astype(np.float32)).to(dev)
-    w = torch.from_numpy(rng.standard_normal((3136, 512)).astype(np.float32)).to(dev)
-    b = torch.zeros(512, device=dev)
-    y = torch.empty((args.batch, 512), device=dev)
-    ctx = context(dev)
-    for _ in range(args.reps):
-        ctx.linear_fwd(x, w, b, y, True)
-    torch.cuda.synchronize()
+def _profile_fc1(kind: str):
+    """The Nature-CNN hidden layer (3136 -> 512) at --batch rows: forward,
+    data gradient (ReLU mask fused) or weight gradient (with the bias)."""
+    def run(args):
+        import torch
+        from ttrl_b200.device import context
+        dev = torch.device("cuda", 0)
+        rng = np.random.default_rng(0)
+        x = torch.from_numpy(rng.standard_normal((args.batch, 3136)).astype(np.float32)).to(dev)
+        w = torch.from_numpy(rng.standard_normal((3136, 512)).astype(np.float32)).to(dev)
+        b = torch.zeros(512, device=dev)
+        y = torch.empty((args.batch, 512), device=dev)
+        ctx = context(dev)
+        for _ in range(args.reps):
+            if kind == "fwd":
+                ctx.linear_fwd(x, w, b, y, True)
+            elif kind == "dgrad":
+                ctx.linear_dgrad(y, w, x, torch.empty_like(x), False)
+            else:
+                ctx.linear_wgrad(x, y, torch.empty_like(w), b, False, False)
+        torch.cuda.synchronize()
+    return run
 
 
 def _dqn_param_tensors(sets: int):
@@ -919,7 +960,8 @@ def _profile_sac(args):
 PROFILE_CASES = {f"{layer}_{kind}": _profile_conv(layer, kind)
                  for layer in PROFILE_CONV for kind in ("fprop", "dgrad", "wgrad")}
 PROFILE_CASES.update({
-    "fc1_fwd": _profile_fc1, "adam_dqn": _profile_adam(1), "adam_dqn_x4": _profile_adam(4),
+    "fc1_fwd": _profile_fc1("fwd"), "fc1_dgrad": _profile_fc1("dgrad"),
+    "fc1_wgrad": _profile_fc1("wgrad"), "adam_dqn": _profile_adam(1), "adam_dqn_x4": _profile_adam(4),
     "sqnorm_dqn": _profile_sqnorm(1), "sqnorm_dqn_x4": _profile_sqnorm(4),
     "u8_s2d": _profile_u8_s2d, "dqn_update": _profile_dqn, "ppo_update": _profile_ppo,
     "rppo_update": _profile_rppo, "sac_update": _profile_sac,

@@ -293,11 +293,17 @@ typedef struct {
  * (ttrl/algos/ppo/learn.py:54-56) and one launch can step the parameters of
  * several optimizers (SAC's policy and temperature, ttrl/algos/sac/
  * agent.py:218-238) that share betas, eps and weight decay but keep their
- * own rates and counters. Up to TTRL_ADAM_MAX_TENSORS tensors per call. */
+ * own rates and counters. `bias_table` (device doubles, may be NULL) holds
+ * the bias terms of steps t = 1..bias_steps as pairs (1 - b1^t, c_t), the
+ * host's own pow() results; a step beyond the table reads its last pair,
+ * which must be the converged one (1, 1), so the table is finite. NULL: the
+ * kernel evaluates pow() itself. Up to TTRL_ADAM_MAX_TENSORS tensors per
+ * call. */
 #define TTRL_ADAM_MAX_TENSORS 64
 int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
                    const float* grad_scale, const double* lr_device, double lr, double b1,
-                   double b2, double eps, double weight_decay, ttrl_stream_t stream);
+                   double b2, double eps, double weight_decay, const double* bias_table,
+                   int64_t bias_steps, ttrl_stream_t stream);
 
 /* out[0] = sum over tensors of sum(g^2), accumulated in double and reduced
  * in a fixed order (ttrl/algos/grads.py:13-26 grad_norm's float64 sum,

@@ -15,12 +15,15 @@ namespace ttrl {
 
 // A block walks chunks of kAdamChunk elements in a grid-stride loop over a
 // grid of at most kAdamBlocksPerSM blocks per SM (one wave). Each thread owns
-// kAdamQuads float4 quads of a chunk and issues every load of them before
-// its first store: one memory round trip per thread per chunk.
+// kAdamQuads float4 quads of a chunk. The operands of the NEXT chunk are
+// copied into shared memory asynchronously (cp.async) while the current
+// one is computed, so a block keeps its loads in flight through its
+// arithmetic instead of alternating between the two; each thread copies and
+// later reads only its own shared-memory slots.
 constexpr int kAdamThreads = 256;
-constexpr int kAdamQuads = 2;
+constexpr int kAdamQuads = 1;
 constexpr int kAdamChunk = kAdamThreads * kAdamQuads * 4;  // elements per chunk
-constexpr int kAdamBlocksPerSM = 3;
+constexpr int kAdamBlocksPerSM = 4;
 
 struct AdamArgs {
   ttrl_adam_tensor t[TTRL_ADAM_MAX_TENSORS];
@@ -32,6 +35,8 @@ struct AdamArgs {
   int32_t* ticket;
   const float* grad_scale;
   const double* lr_device;
+  const double* bias;     // [bias_steps][2]: (1 - b1^t, c_t) for t = 1.., or null
+  long long bias_steps;
   double lr, b1, b2, eps, wd;
 };
 
@@ -77,38 +82,69 @@ __device__ __forceinline__ void adam_elem(const AdamScalars& k, float g, float& 
   p = __fsub_rn(p, d);
 }
 
-__device__ __forceinline__ int adam_tensor_of(const AdamArgs& a, long long chunk) {
-  int ti = 0;  // count <= 64: a linear scan is cheap
-  while (ti + 1 < a.count && a.chunk_start[ti + 1] <= chunk) ++ti;
-  return ti;
+
+struct AdamSpan {
+  int ti;
+  bool vec;
+  long long begin, end;
+};
+
+// The span of chunk c; `from` is a tensor index at or before c's (a block's
+// chunks only move forward, so the scan resumes where the last one ended).
+__device__ __forceinline__ AdamSpan adam_span(const AdamArgs& a, long long c, int from) {
+  AdamSpan s;
+  s.ti = from;
+  while (s.ti + 1 < a.count && a.chunk_start[s.ti + 1] <= c) ++s.ti;
+  const ttrl_adam_tensor& T = a.t[s.ti];
+  s.begin = (c - a.chunk_start[s.ti]) * kAdamChunk;
+  s.end = s.begin + kAdamChunk < T.numel ? s.begin + kAdamChunk : T.numel;
+  s.vec = (a.vec_mask >> s.ti) & 1ull;
+  return s;
+}
+
+// Operand order in a stage: gradient, parameter, S, V.
+using AdamStage = float4[4][kAdamQuads][kAdamThreads];
+
+// One commit group: this thread's quads of the chunk `s` into `stage`
+// (zero-filled past the tensor's end).
+__device__ __forceinline__ void adam_prefetch(const AdamArgs& a, const AdamSpan& s,
+                                              AdamStage& stage) {
+  const ttrl_adam_tensor& T = a.t[s.ti];
+  const float* src[4] = {T.grad, T.param, T.s, T.v};
+#pragma unroll
+  for (int u = 0; u < kAdamQuads; ++u) {
+    const long long i = s.begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+    const long long left = s.end - i;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t dst = smem_u32(&stage[k][u][threadIdx.x]);
+      if (s.vec) {
+        const uint32_t bytes = left >= 4 ? 16u : (left > 0 ? static_cast<uint32_t>(left) * 4u : 0u);
+        cp_async16(dst, bytes ? src[k] + i : src[k], bytes);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool in = j < left;
+          cp_async4(dst + 4u * j, in ? src[k] + i + j : src[k], in ? 4u : 0u);
+        }
+      }
+    }
+  }
+  cp_async_commit();
 }
 
 __global__ void __launch_bounds__(kAdamThreads, kAdamBlocksPerSM)
     adam_kernel(const __grid_constant__ AdamArgs a) {
   pdl_trigger();
   pdl_wait();
+  __shared__ __align__(16) AdamStage stage[2];
   const long long total = a.chunk_start[a.count];
   long long chunk = blockIdx.x;
-  float4 g[kAdamQuads], p[kAdamQuads], S[kAdamQuads], V[kAdamQuads];
-  int ti = 0;
-  long long begin = 0, end = 0;
-  bool vec = false;
-  auto load = [&](long long c) {
-    ti = adam_tensor_of(a, c);
-    const ttrl_adam_tensor& T = a.t[ti];
-    begin = (c - a.chunk_start[ti]) * kAdamChunk;
-    end = begin + kAdamChunk < T.numel ? begin + kAdamChunk : T.numel;
-    vec = (a.vec_mask >> ti) & 1ull;
-#pragma unroll
-    for (int u = 0; u < kAdamQuads; ++u) {
-      const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
-      g[u] = load4(T.grad, i, end, vec);
-      p[u] = load4(T.param, i, end, vec);
-      S[u] = load4(T.s, i, end, vec);
-      V[u] = load4(T.v, i, end, vec);
-    }
-  };
-  if (chunk < total) load(chunk);
+  AdamSpan cur{};
+  if (chunk < total) {
+    cur = adam_span(a, chunk, 0);
+    adam_prefetch(a, cur, stage[0]);
+  }
 
   // The bias-correction scalars depend only on a tensor's step: one thread
   // per tensor computes them (double precision) while the first loads are
@@ -118,9 +154,17 @@ __global__ void __launch_bounds__(kAdamThreads, kAdamBlocksPerSM)
   for (int q = threadIdx.x; q < a.count; q += blockDim.x) {
     const double lr = a.lr_device ? a.lr_device[a.t[q].lr_index] : a.lr;
     const int step = a.steps[a.t[q].step_index] + 1;
-    const double bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
-    const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
-    const double c = sqrt((1.0 - a.b2) / bc2);
+    double bc1, c;
+    if (a.bias != nullptr) {
+      // Host-computed bias terms: one load instead of two double pow()s.
+      const long long t = step < a.bias_steps ? step : a.bias_steps;
+      bc1 = a.bias[2 * (t - 1)];
+      c = a.bias[2 * (t - 1) + 1];
+    } else {
+      bc1 = 1.0 - pow(a.b1, static_cast<double>(step));
+      const double bc2 = 1.0 - pow(a.b2, static_cast<double>(step));
+      c = sqrt((1.0 - a.b2) / bc2);
+    }
     AdamScalars k;
     k.alpha_t = static_cast<float>(lr * (1.0 - a.b1) / bc1 / c);
     k.eps_t = static_cast<float>(a.eps / c);
@@ -133,24 +177,40 @@ __global__ void __launch_bounds__(kAdamThreads, kAdamBlocksPerSM)
   }
   __syncthreads();
 
+  int st = 0;
   while (chunk < total) {
-    const AdamScalars k = ks[ti];
-    const ttrl_adam_tensor& T = a.t[ti];
+    const long long next = chunk + gridDim.x;
+    AdamSpan nxt{};
+    if (next < total) {
+      nxt = adam_span(a, next, cur.ti);
+      adam_prefetch(a, nxt, stage[st ^ 1]);
+    } else {
+      cp_async_commit();  // an empty group: the wait below still means "current chunk in"
+    }
+    cp_async_wait<1>();
+    const AdamScalars k = ks[cur.ti];
+    const ttrl_adam_tensor& T = a.t[cur.ti];
 #pragma unroll
     for (int u = 0; u < kAdamQuads; ++u) {
-      const long long i = begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
-      if (i >= end) continue;
-      adam_elem(k, g[u].x, p[u].x, S[u].x, V[u].x);
-      adam_elem(k, g[u].y, p[u].y, S[u].y, V[u].y);
-      adam_elem(k, g[u].z, p[u].z, S[u].z, V[u].z);
-      adam_elem(k, g[u].w, p[u].w, S[u].w, V[u].w);
-      store4(T.v, i, end, vec, V[u]);
-      store4(T.s, i, end, vec, S[u]);
-      store4(T.param, i, end, vec, p[u]);
+      const long long i = cur.begin + (static_cast<long long>(u) * kAdamThreads + threadIdx.x) * 4;
+      if (i >= cur.end) continue;
+      const float4 g = stage[st][0][u][threadIdx.x];
+      float4 p = stage[st][1][u][threadIdx.x];
+      float4 S = stage[st][2][u][threadIdx.x];
+      float4 V = stage[st][3][u][threadIdx.x];
+      adam_elem(k, g.x, p.x, S.x, V.x);
+      adam_elem(k, g.y, p.y, S.y, V.y);
+      adam_elem(k, g.z, p.z, S.z, V.z);
+      adam_elem(k, g.w, p.w, S.w, V.w);
+      store4(T.v, i, cur.end, cur.vec, V);
+      store4(T.s, i, cur.end, cur.vec, S);
+      store4(T.param, i, cur.end, cur.vec, p);
     }
-    chunk += gridDim.x;
-    if (chunk < total) load(chunk);
+    chunk = next;
+    cur = nxt;
+    st ^= 1;
   }
+  cp_async_wait<0>();
 
   // The last block to finish advances every step counter of this launch,
   // after all blocks have read them.
@@ -175,7 +235,9 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) 
 
 int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
               const float* grad_scale, const double* lr_device, double lr, double b1, double b2,
-              double eps, double wd, cudaStream_t st) {
+              double eps, double wd, const double* bias, long long bias_steps, cudaStream_t st) {
+  if (bias != nullptr && bias_steps < 1)
+    return set_error(TTRL_EINVAL, "adam: a bias table needs at least one step");
   if (count <= 0) return TTRL_OK;
   if (count > TTRL_ADAM_MAX_TENSORS)
     return set_error(TTRL_EINVAL, "adam: %d tensors exceeds the per-call limit %d", count,
@@ -200,6 +262,8 @@ int adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_
   a.ticket = ticket;
   a.grad_scale = grad_scale;
   a.lr_device = lr_device;
+  a.bias = bias;
+  a.bias_steps = bias_steps;
   a.lr = lr;
   a.b1 = b1;
   a.b2 = b2;

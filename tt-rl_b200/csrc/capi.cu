@@ -50,7 +50,7 @@ int u8_to_f32(const uint8_t*, const int32_t*, float*, int, int, int, int, float,
 int u8_to_f32_s2d(const uint8_t*, const int32_t*, float*, int, int, int, int, int, float,
                   cudaStream_t);
 int adam_step(const ttrl_adam_tensor*, int, int32_t*, int32_t*, const float*, const double*,
-              double, double, double, double, double, cudaStream_t);
+              double, double, double, double, double, const double*, long long, cudaStream_t);
 int grad_sqnorm(const float* const*, const int64_t*, int, float*, float, void*, size_t,
                 cudaStream_t);
 size_t sqnorm_ws_bytes(const int64_t*, int);
@@ -187,9 +187,10 @@ int ttrl_u8_nchw_to_f32_s2d(const uint8_t* in, const int32_t* index, float* out,
 
 int ttrl_adam_step(const ttrl_adam_tensor* tensors, int count, int32_t* steps, int32_t* ticket,
                    const float* grad_scale, const double* lr_device, double lr, double b1,
-                   double b2, double eps, double weight_decay, ttrl_stream_t stream) {
+                   double b2, double eps, double weight_decay, const double* bias_table,
+                   int64_t bias_steps, ttrl_stream_t stream) {
   return adam_step(tensors, count, steps, ticket, grad_scale, lr_device, lr, b1, b2, eps,
-                   weight_decay, TTRL_STREAM(stream));
+                   weight_decay, bias_table, bias_steps, TTRL_STREAM(stream));
 }
 
 int ttrl_grad_sqnorm(const float* const* grads, const int64_t* numels, int count, float* out,

@@ -131,7 +131,8 @@ _SIGNATURES = {
     "ttrl_u8_nchw_to_f32_s2d": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                          _c_float, _vp]),
     "ttrl_adam_step": (_c_int, [ctypes.POINTER(AdamTensor), _c_int, _vp, _vp, _vp, _vp,
-                                _c_double, _c_double, _c_double, _c_double, _c_double, _vp]),
+                                _c_double, _c_double, _c_double, _c_double, _c_double, _vp,
+                                ctypes.c_int64, _vp]),
     "ttrl_grad_sqnorm": (_c_int, [ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_int64), _c_int,
                                   _vp, _c_float, _vp, _c_size, _vp]),
     "ttrl_grad_sqnorm_workspace_bytes": (_c_size, [ctypes.POINTER(ctypes.c_int64), _c_int]),

@@ -409,7 +409,7 @@ class DeviceContext:
     # -- optimizer -------------------------------------------------------
 
     def adam_step(self, tensors, steps, ticket, grad_scale, lr, b1, b2, eps, wd,
-                  lr_device=None) -> None:
+                  lr_device=None, bias=None) -> None:
         """`tensors`: list of (param, grad, S, V, step_index[, lr_index])."""
         for start in range(0, len(tensors), 64):
             chunk = tensors[start:start + 64]
@@ -420,7 +420,8 @@ class DeviceContext:
                                          int(idx), int(rest[0]) if rest else 0)
             check(lib().ttrl_adam_step(arr, len(chunk), _ptr(steps), _ptr(ticket),
                                        _ptr(grad_scale), _ptr(lr_device), float(lr), float(b1),
-                                       float(b2), float(eps), float(wd), self.stream),
+                                       float(b2), float(eps), float(wd), _ptr(bias),
+                                       0 if bias is None else bias.shape[0], self.stream),
                   "ttrl_adam_step")
 
     def grad_sqnorm(self, grads, out, max_norm: float, workspace) -> None:

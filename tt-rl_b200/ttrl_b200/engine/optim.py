@@ -19,7 +19,8 @@ import torch
 from ttrl_b200.device import context
 from ttrl_b200.engine.tensor import MASTER_DTYPE, restore_in_place, to_host
 
-__all__ = ["Optimizer", "Adam", "adam_fused_scalars", "share_launch", "step_together"]
+__all__ = ["Optimizer", "Adam", "adam_bias_table", "adam_fused_scalars", "share_launch",
+           "step_together"]
 
 
 def adam_fused_scalars(lr: float, b1: float, b2: float, eps: float, t: int) -> tuple[float, float]:
@@ -30,6 +31,42 @@ def adam_fused_scalars(lr: float, b1: float, b2: float, eps: float, t: int) -> t
     bc2 = 1 - b2 ** t
     c = math.sqrt((1 - b2) / bc2)
     return lr * (1 - b1) / bc1 / c, eps / c
+
+
+#: Longest bias-term table built (steps); betas that converge later fall
+#: back to the kernel's own pow().
+BIAS_TABLE_MAX_STEPS = 1 << 20
+
+_BIAS_TABLES: dict = {}
+
+
+def adam_bias_table(b1: float, b2: float, device):
+    """(T, 2) float64 device table of (1 - b1^t, sqrt((1 - b2)/(1 - b2^t)))
+    for t = 1..T, the terms of adam_fused_scalars from the host's pow(); T
+    is the first step at which both have converged to 1 (in double), so the
+    kernel reads the last row for every later step. None when that takes
+    more than BIAS_TABLE_MAX_STEPS steps. One table per (betas, device)."""
+    key = (float(b1), float(b2), str(device))
+    if key in _BIAS_TABLES:
+        return _BIAS_TABLES[key]
+    tiny = math.ldexp(1.0, -54)  # 1 - x == 1 in double once x < 2^-54
+    need = 1
+    for b in (b1, b2):
+        if b > 0.0:
+            need = max(need, int(math.ceil(math.log(tiny) / math.log(b))) + 2)
+    table = None
+    if need <= BIAS_TABLE_MAX_STEPS:
+        # Python's own pow (the reference's `b ** t`), not a vectorised one
+        # that may round differently.
+        rows = []
+        for t in range(1, need + 1):
+            bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
+            rows.append((bc1, math.sqrt((1 - b2) / bc2)))
+            if bc1 == 1.0 and bc2 == 1.0:
+                table = torch.tensor(rows, dtype=torch.float64).to(device)
+                break
+    _BIAS_TABLES[key] = table
+    return table
 
 
 class Optimizer:
@@ -84,6 +121,7 @@ class Adam(Optimizer):
         self.captured_indices: list[int] | None = None
         # (group, counter base, rate slot) once share_launch joined it.
         self._shared = None
+        self._bias = adam_bias_table(b1, b2, dev)
 
     # The learning rate lives on the device too, so a replayed graph reads
     # the current value (PPO's annealing, ttrl/algos/ppo/learn.py:54-56).
@@ -131,7 +169,7 @@ class Adam(Optimizer):
         if tensors:
             context(self._device).adam_step(
                 tensors, self._dev_steps, self._ticket, self.grad_scale, self._lr, self.b1,
-                self.b2, self.eps, self.weight_decay, lr_device=self._lr_dev)
+                self.b2, self.eps, self.weight_decay, lr_device=self._lr_dev, bias=self._bias)
         self._finish(stepped)
 
     def advance(self, stepped) -> None:
@@ -215,6 +253,7 @@ class Adam(Optimizer):
         self.b1, self.b2 = b1, b2
         self.eps = eps
         self.weight_decay = weight_decay
+        self._bias = adam_bias_table(self.b1, self.b2, self._device)
         ms, vs = self._m_scale, self._v_scale
         for i, arr in enumerate(device_form["m"]):
             restore_in_place(self.m[i], np.asarray(arr) / ms)
@@ -276,7 +315,8 @@ def step_together(opts) -> None:
     group = shared[0][0] if shared and shared[0] is not None else None
     joint = (group is not None and all(s is not None and s[0] is group for s in shared)
              and all(o.grad_scale is None for o in opts)
-             and len({(o.b1, o.b2, o.eps, o.weight_decay) for o in opts}) == 1)
+             and len({(o.b1, o.b2, o.eps, o.weight_decay) for o in opts}) == 1
+             and len({id(o._bias) for o in opts}) == 1)
     if not joint:
         for o in opts:
             o.step()
@@ -290,7 +330,7 @@ def step_together(opts) -> None:
         head = opts[0]
         context(head._device).adam_step(tensors, group.steps, group.ticket, None, head._lr,
                                         head.b1, head.b2, head.eps, head.weight_decay,
-                                        lr_device=group.lrs)
+                                        lr_device=group.lrs, bias=head._bias)
     for o, s in zip(opts, stepped):
         o._finish(s)
 
