@@ -354,6 +354,19 @@ struct Loader {
 // one element per iteration would serialise a round trip per element.
 // Rows equal to `ex.row2` are the synthetic ones row: column sums of B,
 // stored unscaled into `ex.out2`.
+
+// One output value: alpha * acc (+ bias in the same rounding), zeroed where
+// the mask is not positive, ReLU, plus the previous output.
+__device__ __forceinline__ float epi_value(const ttrl_epilogue& ep, float acc, float add, float mk,
+                                           float old) {
+  float v = ep.bias_mode != TTRL_BIAS_NONE ? __fmaf_rn(ep.alpha, acc, add)
+                                           : __fmul_rn(ep.alpha, acc);
+  if (!(mk > 0.f)) v = 0.f;
+  if (ep.relu) v = v > 0.f ? v : 0.f;
+  if (ep.accumulate) v = __fadd_rn(v, old);
+  return v;
+}
+
 template <int U>
 __device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const EpiExtra& ex,
                                                 const int (&r)[U], const int (&c)[U],
@@ -409,12 +422,7 @@ __device__ __forceinline__ void epi_store_batch(const ttrl_epilogue& ep, const E
       ex.out2[static_cast<long long>(c[u]) * ex.cs2] = v;
       continue;
     }
-    float v = ep.alpha * acc[u];
-    if (ep.bias_mode != TTRL_BIAS_NONE) v += add[u];
-    if (!(mk[u] > 0.f)) v = 0.f;
-    if (ep.relu) v = v > 0.f ? v : 0.f;
-    if (ep.accumulate) v += old[u];
-    ep.out[oo[u]] = v;
+    ep.out[oo[u]] = epi_value(ep, acc[u], add[u], mk[u], old[u]);
   }
 }
 
@@ -462,49 +470,155 @@ __device__ __forceinline__ float4 ld_dsmem4(uint32_t saddr, int rank) {
   return v;
 }
 
+__device__ __forceinline__ bool aligned16_dev(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Whether groups of 4 consecutive elements along the staged tile's
+// contiguous dimension are 4 consecutive, 16-byte aligned floats of the
+// output (and of the mask): then the epilogue moves them as float4.
+__device__ __forceinline__ bool epi_vec_ok(const ttrl_epilogue& ep, const EpiExtra& ex,
+                                           bool colmajor) {
+  if (!aligned16_dev(ep.out)) return false;
+  if (!colmajor) {
+    if (ep.ocs != 1 || (ep.ors & 3)) return false;
+    if (ex.scatter_s && (ex.scatter_c & 3)) return false;
+    if (ep.mask && (ep.mcs != 1 || (ep.mrs & 3) || !aligned16_dev(ep.mask))) return false;
+  } else {
+    if (ex.scatter_s || ep.ors != 1 || (ep.ocs & 3)) return false;
+    if (ep.mask && (ep.mrs != 1 || (ep.mcs & 3) || !aligned16_dev(ep.mask))) return false;
+  }
+  return true;
+}
+
+// Up to P groups of 4 output elements, each a float4 at out + oo[p] with
+// its mask at mask + mo[p] and its bias values b[p]: every mask and
+// accumulate load is issued before the first store.
+template <int P>
+__device__ __forceinline__ void epi_store_vec(const ttrl_epilogue& ep, const long long (&oo)[P],
+                                              const long long (&mo)[P], const float4 (&b)[P],
+                                              const float4 (&acc)[P], const bool (&ok)[P]) {
+  float4 mk[P], old[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    mk[p] = make_float4(1.f, 1.f, 1.f, 1.f);
+    old[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ok[p]) {
+      if (ep.mask != nullptr) mk[p] = *reinterpret_cast<const float4*>(ep.mask + mo[p]);
+      if (ep.accumulate) old[p] = *reinterpret_cast<const float4*>(ep.out + oo[p]);
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    if (!ok[p]) continue;
+    float4 v;
+    v.x = epi_value(ep, acc[p].x, b[p].x, mk[p].x, old[p].x);
+    v.y = epi_value(ep, acc[p].y, b[p].y, mk[p].y, old[p].y);
+    v.z = epi_value(ep, acc[p].z, b[p].z, mk[p].z, old[p].z);
+    v.w = epi_value(ep, acc[p].w, b[p].w, mk[p].w, old[p].w);
+    *reinterpret_cast<float4*>(ep.out + oo[p]) = v;
+  }
+}
+
+// Staged float4 at shared byte address `off`: this CTA's, or with nsrc > 1
+// the sum in cluster-rank order of the nsrc cluster CTAs' values there.
+__device__ __forceinline__ float4 staged4(uint32_t off, int nsrc) {
+  if (nsrc == 1) return ld_smem4(off);
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int q = 0; q < nsrc; ++q) {
+    const float4 p = ld_dsmem4(off, q);
+    v.x += p.x;
+    v.y += p.y;
+    v.z += p.z;
+    v.w += p.w;
+  }
+  return v;
+}
+
 // Stores rows [r_lo, r_hi) x [0, cols) of a staged tile through the
 // epilogue. With nsrc > 1 each value is the sum, in cluster-rank order, of
 // the same element of the nsrc cluster CTAs' staged tiles. Every thread
-// owns 4-element groups along the staged tile's contiguous dimension.
-template <int BN>
+// owns 4-element groups along the staged tile's contiguous dimension. Where
+// the output layout allows (epi_vec_ok) a group moves as one float4 and P
+// groups are processed together, their loads issued before any store;
+// other groups (a ragged edge, the column-sum row) take the per-element
+// path.
+template <int BN, int P>
 __device__ __forceinline__ void store_tile(const ttrl_epilogue& ep, const EpiExtra& ex,
                                            uint32_t tile_s, bool colmajor, int row0, int col0,
                                            int r_lo, int r_hi, int cols, int nsrc, int tid) {
   using St = Stage<BN>;
+  const bool vec = epi_vec_ok(ep, ex, colmajor);
   int rr[4], cc[4];
   float acc[4];
+  float4 vacc[P], vb[P];
+  long long oo[P], mo[P];
   if (!colmajor) {
     constexpr int G = BN / 4;             // column groups per row
     constexpr int RSTEP = kThreads / G;   // rows per pass
     const int c0 = (tid % G) * 4;
     if (c0 >= cols) return;
-    for (int r = r_lo + tid / G; r < r_hi; r += RSTEP) {
-      const uint32_t off = tile_s + (r * St::kLdRow + c0) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (nsrc == 1) {
-        v = ld_smem4(off);
-      } else {
-#pragma unroll 4
-        for (int q = 0; q < nsrc; ++q) {
-          const float4 p = ld_dsmem4(off, q);
-          v.x += p.x;
-          v.y += p.y;
-          v.z += p.z;
-          v.w += p.w;
-        }
-      }
-      acc[0] = v.x;
-      acc[1] = v.y;
-      acc[2] = v.z;
-      acc[3] = v.w;
-      int nv = 0;
+    const bool full = vec && c0 + 4 <= cols;
+    const int col = col0 + c0;
+    // Per-thread constants of the group's columns: their bias values and,
+    // for a sub-pixel scatter, their parity class and first channel.
+    float4 bcol = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (full && ep.bias_mode == TTRL_BIAS_COL)
+      bcol = make_float4(ep.bias[col], ep.bias[col + 1], ep.bias[col + 2], ep.bias[col + 3]);
+    int ch = col, py = 0, px = 0;
+    if (full && ex.scatter_s) {
+      const int q = fdiv(ex.f_sc, col);
+      ch = col - q * ex.scatter_c;
+      py = fdiv(ex.f_s, q);
+      px = q - py * ex.scatter_s;
+    }
+    for (int rb = r_lo + tid / G; rb < r_hi; rb += RSTEP * P) {
+      bool ok[P];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        rr[u] = row0 + r;
-        cc[u] = col0 + c0 + u;
-        if (c0 + u < cols) nv = u + 1;
+      for (int p = 0; p < P; ++p) {
+        ok[p] = false;
+        oo[p] = mo[p] = 0;
+        const int r = rb + p * RSTEP;
+        if (r >= r_hi) continue;
+        const float4 v = staged4(tile_s + (r * St::kLdRow + c0) * 4, nsrc);
+        const int row = row0 + r;
+        if (!full || row == ex.row2) {
+          acc[0] = v.x;
+          acc[1] = v.y;
+          acc[2] = v.z;
+          acc[3] = v.w;
+          int nv = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            rr[u] = row;
+            cc[u] = col + u;
+            if (c0 + u < cols) nv = u + 1;
+          }
+          epi_store_batch<4>(ep, ex, rr, cc, acc, nv);
+          continue;
+        }
+        long long pix = row;
+        if (ex.scatter_s) {
+          const int img = fdiv(ex.f_ghw, row);
+          const int rem = row - img * ex.scatter_gh * ex.scatter_gw;
+          const int i = fdiv(ex.f_gw, rem);
+          const int j = rem - i * ex.scatter_gw;
+          pix = (static_cast<long long>(img) * ex.scatter_h + ex.scatter_s * i + py) *
+                    ex.scatter_w + ex.scatter_s * j + px;
+        }
+        oo[p] = pix * ep.ors + ch;
+        mo[p] = pix * ep.mrs + ch;
+        vacc[p] = v;
+        if (ep.bias_mode == TTRL_BIAS_ROW) {
+          const float br = ep.bias[row];
+          vb[p] = make_float4(br, br, br, br);
+        } else {
+          vb[p] = bcol;
+        }
+        ok[p] = true;
       }
-      epi_store_batch<4>(ep, ex, rr, cc, acc, nv);
+      epi_store_vec<P>(ep, oo, mo, vb, vacc, ok);
     }
   } else {
     const int r_span = r_hi - r_lo;
@@ -512,33 +626,48 @@ __device__ __forceinline__ void store_tile(const ttrl_epilogue& ep, const EpiExt
     const int rg = tid & 31;
     if (rg >= G) return;
     const int r = r_lo + rg * 4;
-    for (int c = tid >> 5; c < cols; c += kThreads / 32) {
-      const uint32_t off = tile_s + (c * St::kLdCol + r) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (nsrc == 1) {
-        v = ld_smem4(off);
-      } else {
-#pragma unroll 4
-        for (int q = 0; q < nsrc; ++q) {
-          const float4 p = ld_dsmem4(off, q);
-          v.x += p.x;
-          v.y += p.y;
-          v.z += p.z;
-          v.w += p.w;
-        }
-      }
-      acc[0] = v.x;
-      acc[1] = v.y;
-      acc[2] = v.z;
-      acc[3] = v.w;
-      int nv = 0;
+    const int row = row0 + r;
+    const bool full = vec && r + 4 <= r_hi && !(ex.row2 >= row && ex.row2 < row + 4);
+    float4 brow = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (full && ep.bias_mode == TTRL_BIAS_ROW)
+      brow = make_float4(ep.bias[row], ep.bias[row + 1], ep.bias[row + 2], ep.bias[row + 3]);
+    for (int cb = tid >> 5; cb < cols; cb += (kThreads / 32) * P) {
+      bool ok[P];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        rr[u] = row0 + r + u;
-        cc[u] = col0 + c;
-        if (r + u < r_hi) nv = u + 1;
+      for (int p = 0; p < P; ++p) {
+        ok[p] = false;
+        oo[p] = mo[p] = 0;
+        const int c = cb + p * (kThreads / 32);
+        if (c >= cols) continue;
+        const float4 v = staged4(tile_s + (c * St::kLdCol + r) * 4, nsrc);
+        if (!full) {
+          acc[0] = v.x;
+          acc[1] = v.y;
+          acc[2] = v.z;
+          acc[3] = v.w;
+          int nv = 0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            rr[u] = row + u;
+            cc[u] = col0 + c;
+            if (r + u < r_hi) nv = u + 1;
+          }
+          epi_store_batch<4>(ep, ex, rr, cc, acc, nv);
+          continue;
+        }
+        const long long colv = col0 + c;
+        oo[p] = row + colv * ep.ocs;
+        mo[p] = row + colv * ep.mcs;
+        vacc[p] = v;
+        if (ep.bias_mode == TTRL_BIAS_COL) {
+          const float bc = ep.bias[colv];
+          vb[p] = make_float4(bc, bc, bc, bc);
+        } else {
+          vb[p] = brow;
+        }
+        ok[p] = true;
       }
-      epi_store_batch<4>(ep, ex, rr, cc, acc, nv);
+      epi_store_vec<P>(ep, oo, mo, vb, vacc, ok);
     }
   }
 }
@@ -976,12 +1105,12 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
     const int r_lo = min(rows, rank * per);
     const int r_hi = min(rows, r_lo + per);
     if (warp < kLoadWarps)
-      store_tile<BN>(ep, ex, smem_u32(tile), colmajor, row0, col0, r_lo, r_hi, cols, csplits,
+      store_tile<BN, SMALL ? 1 : 4>(ep, ex, smem_u32(tile), colmajor, row0, col0, r_lo, r_hi, cols, csplits,
                      tid);
     cluster_sync_all();  // peers have finished reading this CTA's tile
   } else if (warp < kLoadWarps) {
     if (args.ws == nullptr) {
-      store_tile<BN>(ep, ex, smem_u32(tile), colmajor, row0, col0, 0, rows, cols, 1, tid);
+      store_tile<BN, SMALL ? 1 : 4>(ep, ex, smem_u32(tile), colmajor, row0, col0, 0, rows, cols, 1, tid);
     } else {
       // Long-K split through global memory: this split's partial tile.
       float* wz = args.ws + static_cast<long long>(blockIdx.z) * args.m * args.n;
