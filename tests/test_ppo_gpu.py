@@ -188,7 +188,9 @@ def test_ppo_update_at_the_timed_configuration():
     the fc1 weight after 16 steps, with or without any one kernel); each of
     the 16 steps is instead held to the single-step bounds:
       - the loss, at the parameters the device holds before the step, 1e-5;
-      - every gradient, with the device's ReLU gates, 1e-4;
+      - every gradient, with the device's ReLU gates, 1e-4 relative (a head's
+        bias gradient, a cancelling sum over the minibatch, relative to the
+        sum of its summands' magnitudes);
       - the clipped Adam update the device applied, against the oracle's
         Adam step from the same parameters, moments and gradient, 1e-6.
     The graph-replayed rollout update then reproduces these 16 eager steps
@@ -245,8 +247,21 @@ def test_ppo_update_at_the_timed_configuration():
         row = eager.metric_buf[t - 1].cpu().numpy()
         assert rel(row[0], loss) <= 1e-5, (t, row[0], loss)
         got = grads_in_state_layout(eager.net)
+        # A head's bias gradient is the sum over the minibatch of that head's
+        # output gradient, residuals of both signs that largely cancel: its
+        # error is that of its summands, so it is judged against the norm of
+        # the summands' magnitudes (sum_b |d out_b|); every other tensor
+        # against its own norm.
+        summands = {"heads.value": np.sum(np.abs(dv), axis=0),
+                    "heads.policy": np.sum(np.abs(dl), axis=0)}
         for name, g in got.items():
-            assert rel(g.reshape(grads[name].shape), grads[name]) <= TOL_GRAD, (t, name)
+            want = np.asarray(grads[name], np.float64)
+            err = float(np.linalg.norm(g.reshape(want.shape) - want))
+            scale = float(np.linalg.norm(want))
+            for head, mags in summands.items():
+                if name.startswith(head) and name.endswith("bias"):
+                    scale = max(scale, float(np.linalg.norm(mags)))
+            assert err <= TOL_GRAD * scale, (t, name, err, scale)
         # The Adam step the device applied, from its own state.
         dev_grads = [q.grad.detach().cpu().numpy().astype(np.float64) for q in eager.params]
         norm = float(np.sqrt(sum(float(np.sum(g * g)) for g in dev_grads)))

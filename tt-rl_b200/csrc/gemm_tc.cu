@@ -1452,6 +1452,13 @@ constexpr int kSmallMaxKBlocks = TTRL_SMALL_MAX_KBLOCKS;
 static Schedule make_schedule(const ttrl_gemm_desc& d) {
   Schedule s;
   s.bn = pick_bn(d.n);
+  // A quarter wave of 128-wide tiles or less (the SAC MLP's and the batch-32
+  // DQN's layers): 64-wide tiles give twice the CTAs, and their smaller
+  // stages leave room for a second low-part slot, so the split pass of one
+  // k-block overlaps the MMAs of the previous one. Larger grids keep the
+  // 128-wide tile: with several GEMMs in flight on the launch lanes, the
+  // extra CTAs cost more than they gain.
+  if (s.bn == 128 && ((d.m + 127) / 128) * ((d.n + 127) / 128) <= 148 / 4) s.bn = 64;
   s.kblocks = (d.k + 31) / 32;
   s.tiles = ((d.m + 127) / 128) * ((d.n + s.bn - 1) / s.bn);
   const int cmax = max_cluster_for_current_device();
