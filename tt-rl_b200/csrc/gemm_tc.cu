@@ -496,7 +496,8 @@ __device__ __forceinline__ bool epi_vec_ok(const ttrl_epilogue& ep, const EpiExt
 // accumulate load is issued before the first store.
 template <int P>
 __device__ __forceinline__ void epi_store_vec(const ttrl_epilogue& ep, const long long (&oo)[P],
-                                              const long long (&mo)[P], const float4 (&b)[P],
+                                              const long long (&mo)[P], float4 bconst,
+                                              const float (&bslot)[P], bool per_slot,
                                               const float4 (&acc)[P], const bool (&ok)[P]) {
   float4 mk[P], old[P];
 #pragma unroll
@@ -511,11 +512,12 @@ __device__ __forceinline__ void epi_store_vec(const ttrl_epilogue& ep, const lon
 #pragma unroll
   for (int p = 0; p < P; ++p) {
     if (!ok[p]) continue;
+    const float4 b = per_slot ? make_float4(bslot[p], bslot[p], bslot[p], bslot[p]) : bconst;
     float4 v;
-    v.x = epi_value(ep, acc[p].x, b[p].x, mk[p].x, old[p].x);
-    v.y = epi_value(ep, acc[p].y, b[p].y, mk[p].y, old[p].y);
-    v.z = epi_value(ep, acc[p].z, b[p].z, mk[p].z, old[p].z);
-    v.w = epi_value(ep, acc[p].w, b[p].w, mk[p].w, old[p].w);
+    v.x = epi_value(ep, acc[p].x, b.x, mk[p].x, old[p].x);
+    v.y = epi_value(ep, acc[p].y, b.y, mk[p].y, old[p].y);
+    v.z = epi_value(ep, acc[p].z, b.z, mk[p].z, old[p].z);
+    v.w = epi_value(ep, acc[p].w, b.w, mk[p].w, old[p].w);
     *reinterpret_cast<float4*>(ep.out + oo[p]) = v;
   }
 }
@@ -552,7 +554,8 @@ __device__ __forceinline__ void store_tile(const ttrl_epilogue& ep, const EpiExt
   const bool vec = epi_vec_ok(ep, ex, colmajor);
   int rr[4], cc[4];
   float acc[4];
-  float4 vacc[P], vb[P];
+  float4 vacc[P];
+  float bslot[P];
   long long oo[P], mo[P];
   if (!colmajor) {
     constexpr int G = BN / 4;             // column groups per row
@@ -610,15 +613,10 @@ __device__ __forceinline__ void store_tile(const ttrl_epilogue& ep, const EpiExt
         oo[p] = pix * ep.ors + ch;
         mo[p] = pix * ep.mrs + ch;
         vacc[p] = v;
-        if (ep.bias_mode == TTRL_BIAS_ROW) {
-          const float br = ep.bias[row];
-          vb[p] = make_float4(br, br, br, br);
-        } else {
-          vb[p] = bcol;
-        }
+        bslot[p] = ep.bias_mode == TTRL_BIAS_ROW ? ep.bias[row] : 0.f;
         ok[p] = true;
       }
-      epi_store_vec<P>(ep, oo, mo, vb, vacc, ok);
+      epi_store_vec<P>(ep, oo, mo, bcol, bslot, ep.bias_mode == TTRL_BIAS_ROW, vacc, ok);
     }
   } else {
     const int r_span = r_hi - r_lo;
@@ -659,15 +657,10 @@ __device__ __forceinline__ void store_tile(const ttrl_epilogue& ep, const EpiExt
         oo[p] = row + colv * ep.ocs;
         mo[p] = row + colv * ep.mcs;
         vacc[p] = v;
-        if (ep.bias_mode == TTRL_BIAS_COL) {
-          const float bc = ep.bias[colv];
-          vb[p] = make_float4(bc, bc, bc, bc);
-        } else {
-          vb[p] = brow;
-        }
+        bslot[p] = ep.bias_mode == TTRL_BIAS_COL ? ep.bias[colv] : 0.f;
         ok[p] = true;
       }
-      epi_store_vec<P>(ep, oo, mo, vb, vacc, ok);
+      epi_store_vec<P>(ep, oo, mo, brow, bslot, ep.bias_mode == TTRL_BIAS_COL, vacc, ok);
     }
   }
 }
