@@ -389,6 +389,19 @@ int ttrl_blend_multi(const ttrl_blend_pair* pairs, int count, int mode, float ta
 int ttrl_gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row,
                      ttrl_stream_t stream);
 
+/* The same gather for up to TTRL_GATHER_MAX_JOBS arrays that share one
+ * index list (a minibatch's actions, old log-probs, values, returns and
+ * advantages), in one launch. */
+#define TTRL_GATHER_MAX_JOBS 8
+typedef struct {
+  const void* src;
+  void* dst;
+  int32_t row;  /* 4-byte words per row */
+  int32_t pad0;
+} ttrl_gather_job;
+int ttrl_gather_rows_multi(const ttrl_gather_job* jobs, int count, const int32_t* idx, int n,
+                           ttrl_stream_t stream);
+
 /* ------------------------------------------------------------------ losses */
 
 /* One DQN update's loss head, fused: the online Q(s,a) gather, the

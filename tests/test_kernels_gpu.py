@@ -575,3 +575,30 @@ def test_stream_k_conv_wgrad_single_pass_tf32():
                    accumulate=False, accumulate_db=False, precision=PREC_TF32)
     assert rel(ol.krsc_to_oihw(host(dw)), ref_w) <= 1e-3
     assert rel(host(db), dy.astype(np.float64).reshape(-1, 32).sum(0)) <= 1e-5
+
+
+def test_gather_rows_multi_equals_one_gather_per_array():
+    """The minibatch gather of ttrl/buffers/rollout.py:271-282 for several
+    arrays sharing one index list (int32 actions, fp32 fields, rows of
+    several words) in one launch: bit for bit one gather per array, with
+    repeated and out-of-order indices."""
+    ctx = _ctx()
+    rng = np.random.default_rng(21)
+    n_src, n = 300, 97
+    idx = torch.from_numpy(rng.integers(0, n_src, n).astype(np.int32)).cuda()
+    srcs = [torch.from_numpy(rng.integers(0, 6, n_src).astype(np.int32)).cuda(),
+            dev(rng.standard_normal(n_src).astype(np.float32)),
+            dev(rng.standard_normal((n_src, 7)).astype(np.float32)),
+            dev(rng.standard_normal((n_src, 3, 4)).astype(np.float32))]
+    one = [torch.empty((n,) + tuple(s.shape[1:]), dtype=s.dtype, device="cuda") for s in srcs]
+    multi = [torch.empty_like(o) for o in one]
+    for s, o in zip(srcs, one):
+        ctx.gather_rows(s, idx, o)
+    from ttrl_b200._lib import lib
+    before = lib().ttrl_launch_count()
+    ctx.gather_rows_multi(list(zip(srcs, multi)), idx)
+    assert lib().ttrl_launch_count() - before == 1
+    for s, o, m in zip(srcs, one, multi):
+        want = s.cpu().numpy()[idx.cpu().numpy()]
+        assert np.array_equal(host(o), want)
+        assert np.array_equal(host(m), want)

@@ -63,6 +63,7 @@ int polyak(float*, const float*, int64_t, float, cudaStream_t);
 int blend_multi(const ttrl_blend_pair*, int, int, float, cudaStream_t);
 int wait_probe(int*, cudaStream_t);
 int gather_rows(const void*, const int32_t*, void*, int, int, cudaStream_t);
+int gather_rows_multi(const ttrl_gather_job*, int, const int32_t*, int, cudaStream_t);
 
 
 
@@ -238,6 +239,11 @@ int ttrl_blend_multi(const ttrl_blend_pair* pairs, int count, int mode, float ta
 int ttrl_gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row,
                      ttrl_stream_t stream) {
   return gather_rows(src, idx, dst, n, row, TTRL_STREAM(stream));
+}
+
+int ttrl_gather_rows_multi(const ttrl_gather_job* jobs, int count, const int32_t* idx, int n,
+                           ttrl_stream_t stream) {
+  return gather_rows_multi(jobs, count, idx, n, TTRL_STREAM(stream));
 }
 
 int ttrl_dqn_loss(const float* q, const float* q_sel, const float* q_tgt, const float* onehot,

@@ -255,4 +255,55 @@ int gather_rows(const void* src, const int32_t* idx, void* dst, int n, int row, 
   return e == cudaSuccess ? TTRL_OK : set_cuda_error("gather_rows launch", e);
 }
 
+// Up to TTRL_GATHER_MAX_JOBS arrays gathered by one index list: blockIdx.y
+// picks the array.
+struct GatherMultiArgs {
+  ttrl_gather_job job[TTRL_GATHER_MAX_JOBS];
+  const int32_t* idx;
+  int n;
+};
+
+__global__ void gather_rows_multi_kernel(const __grid_constant__ GatherMultiArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const ttrl_gather_job& j = a.job[blockIdx.y];
+  const uint32_t* __restrict__ src = static_cast<const uint32_t*>(j.src);
+  uint32_t* __restrict__ dst = static_cast<uint32_t*>(j.dst);
+  const int row = j.row;
+  const long long total = static_cast<long long>(a.n) * row;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / row, c = i - r * row;
+    dst[i] = src[static_cast<long long>(a.idx[r]) * row + c];
+  }
+}
+
+int gather_rows_multi(const ttrl_gather_job* jobs, int count, const int32_t* idx, int n,
+                      cudaStream_t st) {
+  if (count <= 0 || n <= 0) return TTRL_OK;
+  if (count > TTRL_GATHER_MAX_JOBS)
+    return set_error(TTRL_EINVAL, "gather_rows_multi: %d arrays (at most %d)", count,
+                     TTRL_GATHER_MAX_JOBS);
+  if (!jobs || !idx) return set_error(TTRL_EINVAL, "gather_rows_multi: null pointer");
+  GatherMultiArgs a;
+  std::memset(&a, 0, sizeof(a));
+  long long most = 0;
+  for (int i = 0; i < count; ++i) {
+    if (!jobs[i].src || !jobs[i].dst || jobs[i].row <= 0)
+      return set_error(TTRL_EINVAL, "gather_rows_multi: array %d is null or has no columns", i);
+    a.job[i] = jobs[i];
+    if (jobs[i].row > most) most = jobs[i].row;
+  }
+  a.idx = idx;
+  a.n = n;
+  const long long total = most * n;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  const cudaError_t le_ = launch_pdl(gather_rows_multi_kernel, dim3(blocks, count), dim3(256), 0,
+                                     st, a);
+  note_launch();
+  cudaError_t e = le_ != cudaSuccess ? le_ : cudaGetLastError();
+  return e == cudaSuccess ? TTRL_OK : set_cuda_error("gather_rows_multi launch", e);
+}
+
 }  // namespace ttrl

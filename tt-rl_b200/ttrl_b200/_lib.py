@@ -14,7 +14,7 @@ import os
 
 __all__ = [
     "LIB_PATH", "TtrlError", "lib", "Operand", "Epilogue", "GemmDesc", "ConvGeom",
-    "AdamTensor", "BlendPair", "BLEND_COPY", "BLEND_POLYAK", "PREC_TF32X3", "PREC_TF32", "OPND_DENSE", "OPND_CONV_FPROP",
+    "AdamTensor", "BlendPair", "GatherJob", "BLEND_COPY", "BLEND_POLYAK", "PREC_TF32X3", "PREC_TF32", "OPND_DENSE", "OPND_CONV_FPROP",
     "OPND_CONV_WGRAD", "BIAS_NONE", "BIAS_ROW", "BIAS_COL", "EXPORTED_SYMBOLS",
 ]
 
@@ -88,6 +88,11 @@ class AdamTensor(ctypes.Structure):
     ]
 
 
+class GatherJob(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("row", ctypes.c_int32),
+                ("pad0", ctypes.c_int32)]
+
+
 class BlendPair(ctypes.Structure):
     _fields_ = [("dst", _vp), ("src", _vp), ("n", ctypes.c_int64)]
 
@@ -148,6 +153,7 @@ _SIGNATURES = {
     "ttrl_polyak": (_c_int, [_vp, _vp, ctypes.c_int64, _c_float, _vp]),
     "ttrl_blend_multi": (_c_int, [ctypes.POINTER(BlendPair), _c_int, _c_int, _c_float, _vp]),
     "ttrl_gather_rows": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),
+    "ttrl_gather_rows_multi": (_c_int, [ctypes.POINTER(GatherJob), _c_int, _vp, _c_int, _vp]),
     "ttrl_dqn_loss": (_c_int, [_vp] * 13 + [_c_int, _c_int, _c_float, _c_int, _vp]),
     "ttrl_ppo_loss": (_c_int, [_vp] * 12 + [_c_int, _c_int, _c_float, _c_float, _c_float,
                                              _c_float, _vp]),

@@ -151,12 +151,10 @@ class ReplayedUpdate:
 
     def _record_metrics(self, k: int, loss, parts, norm) -> None:
         """Step k's metric row: loss, the three parts and the squared grad norm."""
-        ctx = self.ctx
         row = self.metric_buf[k]
-        ctx.copy_strided(row[0:1], loss.data.reshape(1))
-        for j, key in enumerate(("policy_loss", "value_loss", "entropy")):
-            ctx.copy_strided(row[j + 1:j + 2], parts[key].data.reshape(1))
-        ctx.copy_strided(row[4:5], norm[0:1])
+        sources = [loss.data.reshape(1)] + [parts[key].data.reshape(1) for key in
+                                            ("policy_loss", "value_loss", "entropy")] + [norm[0:1]]
+        self.ctx.blend([(row[j:j + 1], src) for j, src in enumerate(sources)])  # one copy launch
 
 
 class PPOLearner(ReplayedUpdate):
@@ -338,10 +336,11 @@ class PPOLearner(ReplayedUpdate):
         c = self.obs_shape[0]
         f2 = self.fold * self.fold
         ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c * f2), 1.0, fold=self.fold)
-        ctx.gather_rows(self.actions, idx, self.mb_actions)
-        for name, src in (("old_logp", self.old_logp), ("values", self.values),
-                          ("returns", self.returns), ("advantages", self.advantages)):
-            ctx.gather_rows(src, idx, self.mb_fields[name])
+        ctx.gather_rows_multi(
+            [(self.actions, self.mb_actions)]
+            + [(src, self.mb_fields[name]) for name, src in (
+                ("old_logp", self.old_logp), ("values", self.values),
+                ("returns", self.returns), ("advantages", self.advantages))], idx)
         self.optimizer.zero_grad()
         rows = Tensor(self.mb_rows)
         rows._exact = True  # raw 0..255 frame values

@@ -265,11 +265,10 @@ class RecurrentPPOLearner(ReplayedUpdate):
             c = self.obs_shape[0]
             f2 = self.fold * self.fold
             ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c * f2), 1.0, fold=self.fold)
-        else:
-            ctx.gather_rows(self.obs, idx, self.mb_rows)
-        ctx.gather_rows(self.actions, idx, self.mb_actions)
-        for name, src in self.fields.items():
-            ctx.gather_rows(src, idx, self.mb_fields[name])
+        pairs = [] if self.image else [(self.obs, self.mb_rows)]
+        pairs += [(self.actions, self.mb_actions)]
+        pairs += [(src, self.mb_fields[name]) for name, src in self.fields.items()]
+        ctx.gather_rows_multi(pairs, idx)
         ctx.gather_rows(self.hidden, self.seq_idx[k], self.mb_h0)
         self.optimizer.zero_grad()
         rows = Tensor(self.mb_rows)

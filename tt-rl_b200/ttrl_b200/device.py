@@ -511,6 +511,22 @@ class DeviceContext:
         check(lib().ttrl_gather_rows(src.data_ptr(), idx.data_ptr(), dst.data_ptr(),
                                      int(idx.numel()), row, self.stream), "ttrl_gather_rows")
 
+    def gather_rows_multi(self, pairs, idx) -> None:
+        """dst[i] = src[idx[i]] for every (src, dst) of `pairs` (4-byte
+        elements, at most 8 pairs), in one launch."""
+        if idx.dtype != torch.int32:
+            raise ValueError("gather_rows_multi: int32 index")
+        jobs = (_lib.GatherJob * len(pairs))()
+        for i, (src, dst) in enumerate(pairs):
+            if src.element_size() != 4 or dst.element_size() != 4:
+                raise ValueError("gather_rows_multi moves 4-byte rows")
+            row = 1
+            for d in src.shape[1:]:
+                row *= int(d)
+            jobs[i] = _lib.GatherJob(src.data_ptr(), dst.data_ptr(), row, 0)
+        check(lib().ttrl_gather_rows_multi(jobs, len(pairs), idx.data_ptr(), int(idx.numel()),
+                                           self.stream), "ttrl_gather_rows_multi")
+
     def gru_gates_fwd(self, gi, gh, hm, start_next, out, gates, hm_next) -> None:
         """One GRU step's gates after its recurrent GEMM (rows [B][3H])."""
         b, hidden = hm.shape[0], hm.shape[1]
