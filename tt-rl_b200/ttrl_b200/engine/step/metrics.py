@@ -21,8 +21,8 @@ def _numel(t) -> int:
 
 
 class MetricPack:
-    """Packs the scalar metrics of one step into one device buffer with copy
-    kernels, so reading them back is a single device-to-host transfer."""
+    """Packs the scalar metrics of one step into one device buffer with one
+    copy launch, so reading them back is a single device-to-host transfer."""
 
     def __init__(self, metrics: dict):
         self.scalar_keys = []
@@ -48,11 +48,13 @@ class MetricPack:
             with lane:
                 self.buffer = torch.empty(len(self.scalar_keys), dtype=torch.float32,
                                           device=dev)
+                pairs = []
                 for i, k in enumerate(self.scalar_keys):
                     src = self.sources[k].data.reshape(1)
                     if src.dtype != torch.float32:
                         src = src.float()
-                    ctx.copy_strided(self.buffer[i:i + 1], src)
+                    pairs.append((self.buffer[i:i + 1], src.contiguous()))
+                ctx.blend(pairs)  # every scalar in one copy launch
 
     def read(self) -> dict:
         out = dict(self.passthrough)
