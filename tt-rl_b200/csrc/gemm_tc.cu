@@ -1459,9 +1459,10 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
   bool global_split = false;
   if (splits <= 0) {
     // Aim for about one wave of 148 SMs with at least 4 k-blocks per CTA.
-    // Up to `cmax` splits reduce inside a cluster; beyond that (long K,
-    // where each CTA would still walk >= 16 k-blocks) up to 64 splits
-    // reduce through global memory.
+    // Up to `cmax` splits reduce inside a cluster; beyond that (where each
+    // CTA of a cmax-way cluster would still walk >= 4 k-blocks: DQN's conv2
+    // and conv3 weight gradients, 81 and 50 k-blocks over 5 tiles) up to 64
+    // splits reduce through global memory, more CTAs with shorter walks.
     splits = 1;
     if (s.tiles < 120 && s.kblocks >= 8) {
       // Whole waves only: tiles x splits stays within the 148 SMs (one CTA
@@ -1470,7 +1471,7 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
       const int most = s.kblocks / 4;
       splits = want < most ? want : most;
       if (splits > cmax) {
-        if (s.kblocks / cmax >= 16) {
+        if (s.kblocks / cmax >= 4) {
           global_split = true;
           if (splits > 64) splits = 64;
         } else {
