@@ -1461,8 +1461,8 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
     // Aim for about one wave of 148 SMs with at least 4 k-blocks per CTA.
     // Up to `cmax` splits reduce inside a cluster; beyond that (where each
     // CTA of a cmax-way cluster would still walk >= 4 k-blocks: DQN's conv2
-    // and conv3 weight gradients, 81 and 50 k-blocks over 5 tiles) up to 64
-    // splits reduce through global memory, more CTAs with shorter walks.
+    // weight gradient, 81 k-blocks over 5 tiles) up to 64 splits reduce
+    // through global memory, more CTAs with shorter walks.
     splits = 1;
     if (s.tiles < 120 && s.kblocks >= 8) {
       // Whole waves only: tiles x splits stays within the 148 SMs (one CTA
