@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from ttrl_b200.algos.grads import clip_grad_norm_device
-from ttrl_b200.device import context
+from ttrl_b200.device import PREP_LANE, context
 from ttrl_b200.engine.nn import parameter_arena
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.conv import input_fold
@@ -200,11 +200,15 @@ class PPOLearner(ReplayedUpdate):
         # when it folds), gathered and converted from the uint8 rollout.
         self.fold = input_fold(net)
         f2 = self.fold * self.fold
-        self.mb_rows = torch.empty((1, 1, mb * h * w // f2, c * f2), dtype=torch.float32,
-                                   device=dev)
-        self.mb_actions = torch.empty(mb, dtype=torch.int32, device=dev)
-        self.mb_fields = {k: torch.empty(mb, dtype=torch.float32, device=dev)
-                          for k in ("old_logp", "values", "returns", "advantages")}
+        # Two sets: step k's inputs are gathered on the preparation lane
+        # while step k - 1 runs (see _minibatch_step).
+        self._mb_sets = [
+            (torch.empty((1, 1, mb * h * w // f2, c * f2), dtype=torch.float32, device=dev),
+             torch.empty(mb, dtype=torch.int32, device=dev),
+             {k: torch.empty(mb, dtype=torch.float32, device=dev)
+              for k in ("old_logp", "values", "returns", "advantages")})
+            for _ in range(2)]
+        self._prepared = None  # the step whose inputs are already being gathered
         self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
                                       dtype=torch.float32, device=dev)
         self.keep = None  # valid slot indices when the rollout has padding slots
@@ -329,26 +333,50 @@ class PPOLearner(ReplayedUpdate):
 
     # -- one gradient step ---------------------------------------------------
 
-    def _minibatch_step(self, k: int) -> None:
-        cfg = self.cfg
-        ctx = self.ctx
+    def _prepare_inputs(self, k: int) -> None:
+        """Gather step k's minibatch into input set k % 2 (on the current
+        stream): its frames converted to the first layer's rows, and its
+        actions and per-sample fields."""
+        mb_rows, mb_actions, mb_fields = self._mb_sets[k % 2]
         idx = self.perm[k]
         c = self.obs_shape[0]
         f2 = self.fold * self.fold
-        ctx.u8_to_f32(self.obs, idx, self.mb_rows.reshape(-1, c * f2), 1.0, fold=self.fold)
-        ctx.gather_rows_multi(
-            [(self.actions, self.mb_actions)]
-            + [(src, self.mb_fields[name]) for name, src in (
+        self.ctx.u8_to_f32(self.obs, idx, mb_rows.reshape(-1, c * f2), 1.0, fold=self.fold)
+        self.ctx.gather_rows_multi(
+            [(self.actions, mb_actions)]
+            + [(src, mb_fields[name]) for name, src in (
                 ("old_logp", self.old_logp), ("values", self.values),
                 ("returns", self.returns), ("advantages", self.advantages))], idx)
+
+    def _update_body(self) -> None:
+        self._prepared = None
+        super()._update_body()
+
+    def _minibatch_step(self, k: int) -> None:
+        cfg = self.cfg
+        ctx = self.ctx
+        if self._prepared != k:
+            self._prepare_inputs(k)
+        # The next step's inputs are gathered on the preparation lane beside
+        # this step's forward and backward; the backward's closing join
+        # orders this step's optimizer step, and so the next step, after it.
+        # The set it fills was last read by step k - 1, which has finished
+        # on every lane by now.
+        if k + 1 < self.steps_per_update:
+            with ctx.side(PREP_LANE):
+                self._prepare_inputs(k + 1)
+            self._prepared = k + 1
+        else:
+            self._prepared = None
+        mb_rows, mb_actions, mb_fields = self._mb_sets[k % 2]
         self.optimizer.zero_grad()
-        rows = Tensor(self.mb_rows)
+        rows = Tensor(mb_rows)
         rows._exact = True  # raw 0..255 frame values
         rows._fold = self.fold
         logits, value = self.net(rows)
         loss, parts, _ = ppo_objective(
-            logits, value, self.mb_actions, self.mb_fields["old_logp"],
-            self.mb_fields["advantages"], self.mb_fields["returns"], self.mb_fields["values"],
+            logits, value, mb_actions, mb_fields["old_logp"],
+            mb_fields["advantages"], mb_fields["returns"], mb_fields["values"],
             clip_eps=cfg.clip_eps, value_clip_eps=cfg.value_clip_eps,
             value_coef=cfg.value_coef, entropy_coef=cfg.entropy_coef)
         loss.backward()
