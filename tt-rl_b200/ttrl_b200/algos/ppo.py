@@ -106,7 +106,9 @@ class ReplayedUpdate:
         self.optimizer.t, self.optimizer.steps = host_steps[0], host_steps[1]
         from ttrl_b200._lib import lib
         before = lib().ttrl_launch_count()
-        self._graph, _ = capture(self.device, self._update_body)
+        # The side lanes carry only weight gradients and the next step's
+        # inputs: the main chain runs at the higher stream priority.
+        self._graph, _ = capture(self.device, self._update_body, critical_main=True)
         self.launches_per_replay = int(lib().ttrl_launch_count() - before)
 
     def replay(self) -> None:
