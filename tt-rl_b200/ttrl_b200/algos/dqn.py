@@ -19,7 +19,7 @@ import numpy as np
 import torch
 
 from ttrl_b200.algos.grads import grad_sq_device
-from ttrl_b200.device import context
+from ttrl_b200.device import FORWARD_LANES, context
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.conv import input_fold
 from ttrl_b200.engine.ops import dqn_td_huber
@@ -88,11 +88,11 @@ def update_loss(online, target, inputs: dict, *, num_actions: int, double: bool 
     main = torch.cuda.current_stream(ctx.device)
     lane = ctx.side if ctx.concurrent else (lambda _k: contextlib.nullcontext())
     with no_grad():
-        with lane(1):
+        with lane(FORWARD_LANES[0]):
             next_target_q = target(next_obs)
             next_target_q.data.record_stream(main)
         if double:
-            with lane(2):
+            with lane(FORWARD_LANES[1]):
                 selector = online(next_obs)
                 selector.data.record_stream(main)
         else:
@@ -152,7 +152,8 @@ class DQNLearner:
             lambda i: update_loss(online, target, i, num_actions=num_actions, double=double,
                                   huber_delta=huber_delta, mask_n=mask_n,
                                   prioritized=prioritized),
-            self.inputs, self.device, optimizer=self.optimizer, mode="traced_fwd_bwd")
+            self.inputs, self.device, optimizer=self.optimizer, mode="traced_fwd_bwd",
+            critical_main=True)
 
     def load(self, **arrays) -> None:
         """Bind one batch of host arrays (obs, next_obs, actions_onehot,

@@ -26,14 +26,19 @@ from ttrl_b200 import _lib
 from ttrl_b200._lib import check, lib
 
 __all__ = ["DeviceContext", "context", "conv_geom", "PRECISION", "SIDE_LANES", "WEIGHT_LANES",
-           "PREP_LANE"]
+           "PREP_LANE", "FORWARD_LANES"]
 
 #: Side streams a context keeps (lanes 1..SIDE_LANES). Weight gradients are
 #: dealt over lanes 1..WEIGHT_LANES; the last lane (PREP_LANE) carries the
 #: short weight-only preparations a forward issues for its backward.
-SIDE_LANES = 3
+SIDE_LANES = 5
 WEIGHT_LANES = 2
 PREP_LANE = 3
+#: Lanes for independent forward branches whose results the main chain waits
+#: for (DQN's two no-grad forwards): created at the device's highest stream
+#: priority, like a `critical_main` capture stream, so the weight-gradient
+#: lanes (default priority) yield SMs to them.
+FORWARD_LANES = (4, 5)
 
 #: Precision of every tensor-core contraction. Split-TF32 (the default)
 #: reproduces fp32 products to ~1e-6 relative, well inside the 1e-3 budget
@@ -158,8 +163,8 @@ class DeviceContext:
         # When a list, every GEMM-family call appends (name, flops, start, end,
         # call), `call` a closure that issues the same launch again.
         self.profile = None
-        for lane in range(WEIGHT_LANES + 1):  # the preparation lane needs none up front
-            self.reserve(64 << 20, lane=lane)
+        for lane in list(range(WEIGHT_LANES + 1)) + list(FORWARD_LANES):
+            self.reserve(64 << 20, lane=lane)  # the preparation lane needs none up front
 
     def _timed(self, name: str, flops: int = 0, call=None):
         if self.profile is None or torch.cuda.is_current_stream_capturing():
@@ -209,7 +214,12 @@ class DeviceContext:
             raise ValueError(f"side lane must be in [1, {SIDE_LANES}], got {lane}")
         s = self._streams.get(lane)
         if s is None:
-            s = self._streams[lane] = torch.cuda.Stream(self.device)
+            if lane in FORWARD_LANES:
+                _, highest = torch.cuda.Stream.priority_range()
+                s = torch.cuda.Stream(self.device, priority=highest)
+            else:
+                s = torch.cuda.Stream(self.device)
+            self._streams[lane] = s
         return s
 
     @contextlib.contextmanager

@@ -37,7 +37,12 @@ class TrainStep:
     """One training step behind one call API, eager or graph-replayed."""
 
     def __init__(self, step_fn: StepFn, inputs: dict, device, *, optimizer=None,
-                 mode: str = "eager", cfg: EngineConfig = DEFAULT):
+                 mode: str = "eager", cfg: EngineConfig = DEFAULT,
+                 critical_main: bool = False):
+        """`critical_main`: capture at the highest stream priority (see
+        `engine.trace.capture`); for steps whose side lanes carry only work
+        off the critical path, or whose critical side work runs on the
+        equally prioritised forward lanes."""
         if mode not in MODES:
             raise ValueError(f"TrainStep mode must be one of {list(MODES)}, got {mode!r}")
         self.step_fn = step_fn
@@ -51,6 +56,7 @@ class TrainStep:
         self._pack: MetricPack | None = None
         self._captured_grads: list = []
         self.launches_per_replay = 0
+        self.critical_main = bool(critical_main)
 
     def load_input(self, name: str, array) -> None:
         self._binder.load(name, array)
@@ -122,7 +128,8 @@ class TrainStep:
             self.optimizer.zero_grad()
         from ttrl_b200._lib import lib
         before = lib().ttrl_launch_count()
-        self._trace, self._pack = capture(self.device, self._record)
+        self._trace, self._pack = capture(self.device, self._record,
+                                          critical_main=self.critical_main)
         self.launches_per_replay = int(lib().ttrl_launch_count() - before)
         if self.optimizer is not None:
             self._captured_grads = [(p, p.grad) for p in self.optimizer.params]

@@ -98,6 +98,10 @@ def capture(device, record: Callable[[], R], *, pool=None,
     result = None
     try:
         with torch.cuda.device(dev):
+            # Side lanes still pending from eager work are joined here, before
+            # the capture: a join inside it would wait on a lane the capture
+            # never forked (uncaptured work).
+            context(dev).join()
             torch.cuda.synchronize(dev)
             with torch.cuda.graph(graph, pool=pool,
                                   stream=_capture_stream(dev) if critical_main else None,
