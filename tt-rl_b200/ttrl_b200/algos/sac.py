@@ -38,7 +38,7 @@ import numpy as np
 import torch
 
 from ttrl_b200.algos.grads import grad_sq_device
-from ttrl_b200.device import context
+from ttrl_b200.device import FORWARD_LANES, context
 from ttrl_b200.engine.autograd import Tensor, as_device, no_grad
 from ttrl_b200.engine.ops import (abs_, add, apply_done_mask, div, exp, log, mean_all,
                                   minimum, mul, neg, relu, sac_actor_loss, sac_critic_loss,
@@ -263,13 +263,27 @@ def _sample(dist, policy, mean, raw, noise, obs, pack=None):
 def critic_region_fused(nets, dist, batch, log_alpha: Tensor, *, prioritized: bool) -> dict:
     """critic_region on the fused heads: the next-state sample also packs the
     replayed concat(obs, action) that both online critics read."""
+    ctx = context(batch.next_obs.data.device)
+    main = torch.cuda.current_stream(ctx.device)
     with no_grad():
         mean, raw = _policy_raw(nets.policy, batch.next_obs)
         joint_next, next_logp, joint = _sample(dist, nets.policy, mean, raw,
                                                batch["next_noise"], batch.next_obs,
                                                pack=(batch.obs, batch["actions"]))
-        q_next = [net.head(joint_next) for net in nets.targets]
+        # The target critics are independent of each other and of the online
+        # critics' forward: on the forward lanes, beside it (parallel branches
+        # of the captured graph); the loss waits for all of them.
+        q_next = []
+        for i, net in enumerate(nets.targets):
+            if ctx.concurrent and len(nets.targets) <= len(FORWARD_LANES):
+                with ctx.side(FORWARD_LANES[i]):
+                    q = net.head(joint_next)
+                    q.data.record_stream(main)
+            else:
+                q = net.head(joint_next)
+            q_next.append(q)
     qs = [critic.head(joint) for critic in nets.critics]
+    ctx.join()
     loss, alpha, target, td_abs = sac_critic_loss(
         qs, q_next, next_logp, log_alpha, batch["rewards"], batch["dones"],
         batch["discounts"], weights=batch["is_weights"] if prioritized else None,
@@ -445,7 +459,7 @@ class SACLearner:
             o.t, o.steps = t, steps
         from ttrl_b200._lib import lib
         before = lib().ttrl_launch_count()
-        self._graph, self._metrics = capture(self.device, self._update)
+        self._graph, self._metrics = capture(self.device, self._update, critical_main=True)
         self.launches_per_replay = int(lib().ttrl_launch_count() - before)
 
     def replay(self) -> None:
