@@ -260,6 +260,24 @@ def _sample(dist, policy, mean, raw, noise, obs, pack=None):
                       pack=pack)
 
 
+def _critics_side_by_side(ctx, critics, joint):
+    """Q(s, a) of every critic on `joint`: the first on the current stream,
+    the others on the forward lanes beside it (their forwards are
+    independent; the tape's backward later runs on the current stream). The
+    caller joins the lanes before using the values."""
+    critics = list(critics)
+    if not ctx.concurrent or len(critics) - 1 > len(FORWARD_LANES):
+        return [critic.head(joint) for critic in critics]
+    main = torch.cuda.current_stream(ctx.device)
+    qs = [None] * len(critics)
+    for i, critic in enumerate(critics[1:]):
+        with ctx.side(FORWARD_LANES[i]):
+            qs[i + 1] = critic.head(joint)
+            qs[i + 1].data.record_stream(main)
+    qs[0] = critics[0].head(joint)
+    return qs
+
+
 def critic_region_fused(nets, dist, batch, log_alpha: Tensor, *, prioritized: bool) -> dict:
     """critic_region on the fused heads: the next-state sample also packs the
     replayed concat(obs, action) that both online critics read."""
@@ -282,7 +300,7 @@ def critic_region_fused(nets, dist, batch, log_alpha: Tensor, *, prioritized: bo
             else:
                 q = net.head(joint_next)
             q_next.append(q)
-    qs = [critic.head(joint) for critic in nets.critics]
+    qs = _critics_side_by_side(ctx, nets.critics, joint)
     ctx.join()
     loss, alpha, target, td_abs = sac_critic_loss(
         qs, q_next, next_logp, log_alpha, batch["rewards"], batch["dones"],
@@ -309,7 +327,9 @@ def actor_region_fused(nets, dist, batch, log_alpha: Tensor, target_entropy: flo
     try:
         mean, raw = _policy_raw(nets.policy, batch.obs)
         joint, logp, _ = _sample(dist, nets.policy, mean, raw, batch["noise"], batch.obs)
-        qs = [critic.head(joint) for critic in nets.critics]
+        ctx = context(batch.obs.data.device)
+        qs = _critics_side_by_side(ctx, nets.critics, joint)
+        ctx.join()
         loss, dual = sac_actor_loss(qs, logp, log_alpha, target_entropy,
                                     learn_alpha=learn_alpha)
         loss.backward()
