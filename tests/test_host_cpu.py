@@ -279,3 +279,33 @@ def test_param_sync_gloo_rank_that_fails_mid_run():
     assert outcome.startswith("ParamSyncError"), outcome
     assert "all-reduce over 2 ranks did not complete" in outcome
     assert values == repr([1.0] * 12)
+
+
+@pytest.mark.parametrize("b1,b2", [(0.9, 0.999), (0.9, 0.99), (0.5, 0.9)])
+def test_adam_bias_table_is_the_reference_arithmetic(b1, b2):
+    """Adam's bias-term table holds, for every step t, exactly the terms of
+    ttrl/engine/optim/scalars.py:13-27 as the host evaluates them (Python's
+    own `**`, `math.sqrt`), up to the first step where both have reached 1
+    in double; the kernel reads the last row for every later step, so that
+    row must equal the terms at any later t."""
+    import math
+    from ttrl_b200.engine.optim import adam_bias_table, adam_fused_scalars
+    table = adam_bias_table(b1, b2, "cpu")
+    assert table is not None and table.dtype == torch.float64
+    rows = table.numpy()
+    T = rows.shape[0]
+    for t in list(range(1, 200)) + list(range(max(1, T - 50), T + 1)):
+        bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
+        assert rows[t - 1, 0] == bc1
+        assert rows[t - 1, 1] == math.sqrt((1 - b2) / bc2)
+    for t in (T, T + 1, 10 * T):
+        bc1, bc2 = 1 - b1 ** t, 1 - b2 ** t
+        assert (bc1, bc2) == (1.0, 1.0)
+        assert rows[-1, 1] == math.sqrt((1 - b2) / bc2)
+    # The kernel's alpha_t = lr * (1 - b1) / bc1 / c and eps_t = eps / c from
+    # the row equal the host's fused scalars.
+    for t in (1, 7, T, 3 * T):
+        r = rows[min(t, T) - 1]
+        alpha, eps_t = adam_fused_scalars(2.5e-4, b1, b2, 1e-8, t)
+        assert 2.5e-4 * (1 - b1) / r[0] / r[1] == alpha
+        assert 1e-8 / r[1] == eps_t
