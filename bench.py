@@ -464,10 +464,10 @@ def run_ours(args):
     t0 = time.perf_counter()
     # Each step's rollout crosses host -> device and its metric rows device ->
     # host inside the timed region. The upload of step k+1 runs on a copy
-    # stream beside the replay of step k, and step k+1 is enqueued before the
-    # host waits for step k's metrics.
+    # stream beside the replay of step k, and the host waits for a step's
+    # metrics two steps later.
     learner.stage_rollout(*staged)
-    pending = None
+    pending = []
     e2e_sync = sync_points(E) if group is not None else set()
     for k in range(E):
         learner.commit_staged()
@@ -475,13 +475,16 @@ def run_ours(args):
         learner.replay()
         if k in e2e_sync:
             sync.average()
-        handle = learner.fetch_metrics()
+        pending.append(learner.fetch_metrics())
         if k + 1 < E:
             learner.stage_rollout(*staged)
-        if pending is not None:
-            learner.metrics_of(pending)
-        pending = handle
-    learner.metrics_of(pending)
+        # The host stays up to two updates ahead of the device: it reads
+        # the metrics of update k-2 while k-1 and k are queued, so a host
+        # hiccup of a few milliseconds leaves no gap on the device.
+        if len(pending) > 2:
+            learner.metrics_of(pending.pop(0))
+    for handle in pending:
+        learner.metrics_of(handle)
     e2e_s = time.perf_counter() - t0
     if group is not None:
         t = torch.tensor([e2e_s], device=device)

@@ -195,8 +195,12 @@ class PPOLearner(ReplayedUpdate):
         self.returns = torch.zeros(R, dtype=torch.float32, device=dev)
         self.advantages = torch.zeros(R, dtype=torch.float32, device=dev)
         self.perm = torch.zeros((self.steps_per_update, mb), dtype=torch.int32, device=dev)
-        self.perm_host = torch.zeros((self.steps_per_update, mb), dtype=torch.int32,
-                                     pin_memory=True)
+        # Three pinned buffers for the host's permutations, so the host may
+        # draw the next update's while the last two uploads are in flight.
+        self._perm_ring = [torch.zeros((self.steps_per_update, mb), dtype=torch.int32,
+                                       pin_memory=True) for _ in range(3)]
+        self._perm_events = [None] * len(self._perm_ring)
+        self._perm_slot = 0
         # Minibatch staging (gathered per step on the device).
         # Frame rows in the order the first convolution reads (space-to-depth
         # when it folds), gathered and converted from the uint8 rollout.
@@ -214,7 +218,6 @@ class PPOLearner(ReplayedUpdate):
         self.metric_buf = torch.zeros((self.steps_per_update, len(self.METRICS)),
                                       dtype=torch.float32, device=dev)
         self.keep = None  # valid slot indices when the rollout has padding slots
-        self._upload_done = None
         self._graph = None
         self.launches_per_replay = 0
 
@@ -249,7 +252,7 @@ class PPOLearner(ReplayedUpdate):
         pinned buffer for the next rollout)."""
         if getattr(self, "_staging", None) is None:
             self._staging = {k: torch.empty_like(getattr(self, k)) for k in self._STAGED}
-            self._copy_stream = torch.cuda.Stream(self.device)
+            self._copy_stream = self._upload_stream()
             self._staged = None
             self._committed = None
         src = dict(zip(self._STAGED, (obs_u8, actions, old_logp, values, returns, advantages)))
@@ -263,6 +266,12 @@ class PPOLearner(ReplayedUpdate):
             self._staged.record(self._copy_stream)
         return self._staged
 
+    def _upload_stream(self) -> torch.cuda.Stream:
+        """The stream host-to-device uploads run on, beside the updates."""
+        if getattr(self, "_uploads", None) is None:
+            self._uploads = torch.cuda.Stream(self.device)
+        return self._uploads
+
     def commit_staged(self) -> None:
         """Order the current stream after the staged upload and copy it into
         the buffers the captured update reads (device to device)."""
@@ -270,8 +279,12 @@ class PPOLearner(ReplayedUpdate):
             raise RuntimeError("commit_staged: no rollout was staged")
         main = torch.cuda.current_stream(self.device)
         main.wait_event(self._staged)
-        for k in self._STAGED:
-            getattr(self, k).copy_(self._staging[k], non_blocking=True)
+        # One copy kernel over every staged array (moved as 4-byte words, bit
+        # for bit): a device-to-device memcpy runs on a copy engine at a
+        # fraction of the SMs' bandwidth (0.3 ms for the 28.9 MB of frames).
+        self.ctx.blend([(getattr(self, k).reshape(-1).view(torch.float32),
+                         self._staging[k].reshape(-1).view(torch.float32))
+                        for k in self._STAGED])
         self.keep = None
         self._committed = torch.cuda.Event()
         self._committed.record(main)
@@ -314,12 +327,20 @@ class PPOLearner(ReplayedUpdate):
                 f"{total // self.cfg.minibatch_size} minibatches of {self.cfg.minibatch_size}, "
                 f"and this learner's captured graph holds {self.minibatches} per epoch")
 
+    @property
+    def perm_host(self) -> torch.Tensor:
+        """The pinned host copy of the last drawn permutations."""
+        return self._perm_ring[self._perm_slot]
+
     def draw_permutations(self) -> None:
         """One permutation of the (valid) rollout slots per epoch, cut into
         minibatches (ttrl/buffers/rollout.py:241-283)."""
         mb = self.cfg.minibatch_size
-        if self._upload_done is not None:
-            self._upload_done.synchronize()  # the previous upload has read perm_host
+        slot = (self._perm_slot + 1) % len(self._perm_ring)
+        if self._perm_events[slot] is not None:
+            # The upload out of this buffer, three draws ago, has read it.
+            self._perm_events[slot].synchronize()
+        buf = self._perm_ring[slot]
         keep = self.keep
         total = self.rollout_size if keep is None else len(keep)
         rows = []
@@ -328,10 +349,30 @@ class PPOLearner(ReplayedUpdate):
             for start in range(0, self.minibatches * mb, mb):
                 idx = perm[start:start + mb]
                 rows.append(idx if keep is None else keep[idx])
-        self.perm_host.numpy()[:] = np.stack(rows).astype(np.int32)
-        self.perm.copy_(self.perm_host, non_blocking=True)
-        self._upload_done = torch.cuda.Event()
-        self._upload_done.record()
+        buf.numpy()[:] = np.stack(rows).astype(np.int32)
+        # The host-to-device copy runs on the copy stream into a device
+        # staging buffer, queued ahead of any rollout upload issued later; the
+        # current stream then moves it into place with one copy kernel. A
+        # host-to-device copy on the current stream would wait on the copy
+        # engine behind a rollout upload in flight (0.3-1.2 ms per update).
+        main = torch.cuda.current_stream(self.device)
+        cs = self._upload_stream()
+        if getattr(self, "_perm_stage", None) is None:
+            self._perm_stage = torch.empty_like(self.perm)
+            self._perm_consumed = None
+        with torch.cuda.stream(cs):
+            if self._perm_consumed is not None:
+                cs.wait_event(self._perm_consumed)  # the last move has read the stage
+            self._perm_stage.copy_(buf, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(cs)
+        main.wait_event(done)
+        self.ctx.blend([(self.perm.view(-1).view(torch.float32),
+                         self._perm_stage.view(-1).view(torch.float32))])
+        self._perm_consumed = torch.cuda.Event()
+        self._perm_consumed.record(main)
+        self._perm_events[slot] = done
+        self._perm_slot = slot
 
     # -- one gradient step ---------------------------------------------------
 
