@@ -629,21 +629,24 @@ def bench_dqn(device, args):
     pinned = step.pinned_inputs()
     for k, v in arrays.items():
         pinned[k].copy_(torch.from_numpy(np.ascontiguousarray(v)).reshape(pinned[k].shape))
-    E = 50
+    # 200 updates (about 40 ms): a 50-update sample moved by 25% with one
+    # host hiccup.
+    E = 200
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     # Every update's inputs go host -> device and its metrics device -> host
-    # inside the timed region; update k+1 is enqueued (its upload ordered
-    # after replay k on the same stream) before the host waits for update k.
-    pending = None
+    # inside the timed region; the upload of update k+1 runs on a copy stream
+    # beside replay k, and the host reads an update's metrics two updates
+    # later.
+    pending = []
     for _ in range(E):
         learner.load(**pinned)
         learner.launch()
-        handle = step.fetch_metrics()
-        if pending is not None:
-            step.metrics_of(pending)
-        pending = handle
-    step.metrics_of(pending)
+        pending.append(step.fetch_metrics())
+        if len(pending) > 2:  # the host reads update k-2's metrics
+            step.metrics_of(pending.pop(0))
+    for handle in pending:
+        step.metrics_of(handle)
     e2e_ms = (time.perf_counter() - t0) * 1000 / E
     h2d = sum(v.nbytes for v in arrays.values())
     learner.close()
