@@ -81,7 +81,10 @@ def test_linear_dgrad_masked(m, k, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(32, 3136, 512), (32, 512, 6), (256, 14, 256), (5, 13, 7),
-                                   (256, 3136, 512)])
+                                   (256, 3136, 512),
+                                   # ones row inside a partly filled 32-row box, a
+                                   # reduction that ends inside a k-block
+                                   (64, 200, 128), (40, 1000, 256)])
 def test_linear_wgrad_with_bias_grad(m, k, n):
     ctx = _ctx()
     rng = np.random.default_rng(3 * m + k)

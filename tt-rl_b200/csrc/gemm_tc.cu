@@ -897,7 +897,10 @@ __global__ void __launch_bounds__(kBlockThreads, SMALL ? 2 : 1)
     const bool a_tma = args.a_tma != 0, b_tma = args.b_tma != 0;
     const bool any_tma = a_tma || b_tma;
     const bool any_gather = !(a_tma && b_tma);
-    const bool a_ones_by_loader = (args.im2col & 1) && a_mn && oa.ones_row;
+    // An MN-major A loaded by TMA (dense, or a weight gradient's windows)
+    // whose appended ones row is not in memory: the TMA fills it with zeros
+    // and the loader warps write the ones into each stage after it lands.
+    const bool a_ones_by_loader = a_tma && a_mn && oa.ones_row;
     auto issue_gathers = [&](int st, int kb) {
       const int k0 = kb * 32;
       if (!a_tma) la.issue(oa, raw_a(st), row0, k0, tid);
@@ -1319,9 +1322,12 @@ static bool encode_im2col_map(const DevOperand& o, CUtensorMap* map) {
 
 // The TMA map of a dense operand whose tiles are R rows x 32 k, or false
 // when the operand is gathered instead (conv windows, odd strides or
-// alignment, or an appended ones row that is not in memory).
+// alignment, or an appended ones row of a K-major operand).
 static bool encode_operand_map(const DevOperand& o, int R, CUtensorMap* map) {
-  if (o.kind != TTRL_OPND_DENSE || o.ones_row) return false;
+  if (o.kind != TTRL_OPND_DENSE) return false;
+  // An appended ones row (the bias gradient's) lies past the map's extent in
+  // MN-major tiles, where the TMA writes zeros and the loader warps the ones.
+  if (o.ones_row && o.mode != kModeMNVec) return false;
   if (o.mode != kModeKVec && o.mode != kModeMNVec) return false;
   if (o.rows <= 0 || o.kdim <= 0) return false;
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
