@@ -459,6 +459,44 @@ def test_gemm_many_waves_half_footprint(n, k, prec, transposed):
     assert rel(got, ref) <= (TOL_X3 if prec == 0 else TOL_TF32)
 
 
+@pytest.mark.parametrize("n,relu", [(32, 0), (128, 1)])
+def test_gemm_half_footprint_epilogue_mask_row_bias_accumulate(n, relu):
+    """The half-footprint GEMM's row-major epilogue with every global input
+    it reads per group (the ReLU-backward mask, the old output when
+    accumulating, a per-row bias), over a ragged many-wave grid:
+    out = old + relu?((alpha * acc + bias[row]) * [mask > 0])."""
+    import ctypes
+    from ttrl_b200 import _lib
+    ctx = _ctx()
+    m, k, alpha = 128 * 170 + 37, 64, 0.5
+    rng = np.random.default_rng(n + relu)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    bias = rng.standard_normal(m).astype(np.float32)
+    mask = rng.standard_normal((m, n)).astype(np.float32)
+    old = rng.standard_normal((m, n)).astype(np.float32)
+    da, db, dbias, dmask = dev(a), dev(b), dev(bias), dev(mask)
+    y = dev(old)
+    d = _lib.GemmDesc()
+    d.m, d.n, d.k, d.precision, d.splits = m, n, k, _lib.PREC_TF32X3, 1
+    d.a.ptr, d.a.kind, d.a.rows, d.a.kdim, d.a.rs, d.a.ks = da.data_ptr(), 0, m, k, k, 1
+    d.b.ptr, d.b.kind, d.b.rows, d.b.kdim, d.b.rs, d.b.ks = db.data_ptr(), 0, n, k, k, 1
+    d.ep.out, d.ep.ors, d.ep.ocs, d.ep.alpha = y.data_ptr(), n, 1, alpha
+    d.ep.bias, d.ep.bias_mode = dbias.data_ptr(), _lib.BIAS_ROW
+    d.ep.mask, d.ep.mrs, d.ep.mcs = dmask.data_ptr(), n, 1
+    d.ep.relu, d.ep.accumulate = relu, 1
+    ws, wsb = ctx.workspace(_lib.lib().ttrl_gemm_workspace_bytes(ctypes.byref(d)))
+    _lib.check(_lib.lib().ttrl_gemm(ctypes.byref(d), ws, wsb, ctx.status_ptr(), ctx.stream),
+               "ttrl_gemm")
+    got = host(y)
+    ctx.check_status()
+    v = alpha * (a.astype(np.float64) @ b.astype(np.float64).T) + bias[:, None]
+    v = np.where(mask > 0, v, 0.0)
+    if relu:
+        v = np.maximum(v, 0.0)
+    assert rel(got, old + v) <= TOL_X3
+
+
 def test_bounded_wait_gives_up_and_the_context_stays_usable():
     """A wait on a barrier that nothing completes (ttrl_wait_probe) gives up
     after the library's bound, records status 1001, and the next launches on
