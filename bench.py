@@ -54,11 +54,12 @@ RPPO_FLOP_PER_STEP = 2 * 26_526_976 * 512  # 3F_r - conv1 dX per row, 512 rows
 # DRAM bytes (read + write) per launch of the kernels that have been the
 # dominant one, from one ncu capture each of `python bench.py --profile-case
 # <case> --batch 256` (conv1s2d_wgrad, conv1s2d_fprop, conv2_dgrad,
-# fc1_wgrad).
+# conv3_dgrad, fc1_wgrad).
 NCU_TRAFFIC_BYTES = {
     "conv_wgrad[2x2/1 64->32]": 42.106624e6 + 512,
     "conv_fprop[2x2/1 64->32]": 29.039872e6,
     "conv_dgrad[4x4/2 32->64]": 18.6368e6,
+    "conv_dgrad[3x3/1 64->64]": 8.75648e6,
     "linear_wgrad[256x3136x512]": 3.847168e6,
 }
 
