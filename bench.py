@@ -377,13 +377,22 @@ def run_ours(args):
         import torch.distributed as dist
         # NCCL's communicator log (ranks, transports, NVLS) goes to stderr:
         # NCCL writes it to file descriptor 1, which now points at stderr,
-        # and the one JSON line leaves through a copy of the real stdout.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # and the one JSON line leaves through a copy of the real stdout. A
+        # level that prints no communicator lines (unset, WARN, VERSION) is
+        # raised to INFO for the INIT subsystem.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "WARN", "VERSION", "NONE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         _route_stdout_to_stderr()
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
         group = dist.group.WORLD
+    # Which physical GPU each rank ran on (outside the timed region).
+    gpu_ids = [str(torch.cuda.get_device_properties(device).uuid)]
+    if group is not None:
+        gpu_ids = [None] * world
+        dist.all_gather_object(gpu_ids, str(torch.cuda.get_device_properties(device).uuid),
+                               group=group)
     from ttrl_b200.device import context
     from ttrl_b200.engine.mesh import ParamSync
 
@@ -520,6 +529,9 @@ def run_ours(args):
                        "epochs": EPOCHS, "grad_steps_per_step": STEPS_PER_UPDATE,
                        "parallelism": f"dp{world}", "sync_every_updates": SYNC_EVERY,
                        "syncs_in_timed_region": syncs,
+                       "ranks": world,
+                       "rank_gpus": gpu_ids,
+                       "distinct_gpus": len(set(gpu_ids)),
                        "sync_rule": "after every 50th update and after the last one "
                                     "(ceil(steps / 50) averages)" if world > 1 else "none (N=1)",
                        "allreduce_ms_total": round(sync_ms, 4),
