@@ -74,6 +74,12 @@ constexpr int kGroupThreads = kGroupWarps * 32;
 // Written by gemm_init_device.
 static int g_max_cluster[64];
 
+// How many clusters of each size (2..16 split CTAs) of the full-footprint
+// variant can be resident at once on each device, per tile width (32, 64,
+// 128) and precision (single pass, split-TF32); 0 where not queried.
+// Written by gemm_init_device.
+static int g_active_clusters[64][3][2][17];
+
 // Constant sources for the synthetic "ones" row an operand may append: a
 // GEMM whose A operand carries a row of ones produces the column sums of B
 // (the bias gradient) in that row of D.
@@ -1207,6 +1213,33 @@ static int set_smem_attr(int* cluster_cap) {
   return TTRL_OK;
 }
 
+// Records g_active_clusters for one variant (cudaOccupancyMaxActiveClusters
+// over cluster sizes 2..cap: clusters pack into GPCs, so fewer of a size
+// that does not divide a GPC's SMs fit than the SM count suggests).
+template <int BN, bool SPLIT>
+static void record_active_clusters(int dev, int cap) {
+  using Cfg = TileCfg<BN, SPLIT, false>;
+  const int bi = BN == 32 ? 0 : BN == 64 ? 1 : 2;
+  for (int cz = 2; cz <= cap && cz <= 16; ++cz) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, cz);
+    cfg.blockDim = dim3(kBlockThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = cz;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<BN, SPLIT, false>, &cfg) ==
+        cudaSuccess)
+      g_active_clusters[dev][bi][SPLIT ? 1 : 0][cz] = clusters;
+  }
+  cudaGetLastError();  // a refused query leaves no sticky error
+}
+
 int gemm_init_device() {
   int rc = TTRL_OK;
   int cap = 16;
@@ -1217,7 +1250,15 @@ int gemm_init_device() {
   if ((rc = set_smem_attr<64, false>(&cap))) return rc;
   if ((rc = set_smem_attr<128, false>(&cap))) return rc;
   int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) g_max_cluster[dev] = cap;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+    g_max_cluster[dev] = cap;
+    record_active_clusters<32, true>(dev, cap);
+    record_active_clusters<64, true>(dev, cap);
+    record_active_clusters<128, true>(dev, cap);
+    record_active_clusters<32, false>(dev, cap);
+    record_active_clusters<64, false>(dev, cap);
+    record_active_clusters<128, false>(dev, cap);
+  }
   return TTRL_OK;
 }
 
@@ -1441,6 +1482,15 @@ static int max_cluster_for_current_device() {
   return g_max_cluster[dev] > 0 ? g_max_cluster[dev] : 8;
 }
 
+// Resident clusters of `cz` CTAs for this tile width and precision on the
+// current device, or 0 when unknown.
+static int active_clusters(int bn, bool split3, int cz) {
+  int dev = 0;
+  if (cz < 2 || cz > 16 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  const int bi = bn == 32 ? 0 : bn == 64 ? 1 : 2;
+  return g_active_clusters[dev][bi][split3 ? 1 : 0][cz];
+}
+
 // Non-cluster GEMMs whose CTAs each walk at most this many k-blocks use the
 // half-footprint variant.
 #ifndef TTRL_SMALL_MAX_KBLOCKS
@@ -1482,6 +1532,18 @@ static Schedule make_schedule(const ttrl_gemm_desc& d) {
           if (splits > 64) splits = 64;
         } else {
           splits = cmax;
+        }
+      }
+      // Every cluster resident at once: clusters pack into GPCs, and a
+      // size that leaves some unplaced runs a second wave (PPO's fc1
+      // forward, 16 tiles: 9-way clusters 26.3 us, 6-way 17.6 us). Fall
+      // back to the largest size that fits in one wave.
+      if (!global_split) {
+        const bool split3 = d.precision == TTRL_PREC_TF32X3;
+        while (splits > 1) {
+          const int fit = active_clusters(s.bn, split3, splits);
+          if (fit == 0 || fit >= s.tiles) break;
+          --splits;
         }
       }
       if (splits < 1) splits = 1;
