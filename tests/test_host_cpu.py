@@ -309,3 +309,40 @@ def test_adam_bias_table_is_the_reference_arithmetic(b1, b2):
         alpha, eps_t = adam_fused_scalars(2.5e-4, b1, b2, 1e-8, t)
         assert 2.5e-4 * (1 - b1) / r[0] / r[1] == alpha
         assert 1e-8 / r[1] == eps_t
+
+
+def _bench_reference_arm(env_extra):
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ)
+    env.update(env_extra)
+    return subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference",
+                           "--steps", "1", "--warmup", "0"], cwd=root, env=env,
+                          capture_output=True, text=True, timeout=600)
+
+
+def test_bench_reference_arm_line_contract():
+    """`bench.py --impl reference` (the CPU port of the reference's path, no
+    GPU needed) prints one JSON line with the CUDA arm's metric and workload,
+    its own cpu_baseline, and an end-to-end figure with no host-device bytes."""
+    import json
+    import bench
+    r = _bench_reference_arm({"WORLD_SIZE": "1", "RANK": "0", "LOCAL_RANK": "0"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    assert d["metric"] == bench.METRIC and d["unit"] == "samples/s"
+    assert d["higher_is_better"] is True and d["value"] > 0
+    assert d["config"]["workload"] == "ppo_nature_cnn_rollout8x128_mb256_epochs4"
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": "samples/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+
+
+def test_bench_reference_arm_other_ranks_exit_without_work():
+    """Under torchrun only rank 0 runs the reference arm and prints its line;
+    the other ranks exit 0 and print nothing."""
+    r = _bench_reference_arm({"WORLD_SIZE": "2", "RANK": "1", "LOCAL_RANK": "1"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
