@@ -803,6 +803,16 @@ struct TileCfg {
   static constexpr int kSmem =
       (kStages + kLoSlots) * kTile + 1024 /*align slack*/ + 512 /*barriers*/;
   static_assert(kStages >= 2, "at least two pipeline stages");
+  // With both operands by TMA, the two loader groups take alternate k-blocks
+  // and the first kStages of them land without any MMA having run, so a
+  // loader can reach k-block i when only the MMAs of k-block i - kStages
+  // are known to be done. Its wait for low-part slot i % kLoSlots is a
+  // parity wait on the MMAs of k-block i - kLoSlots; it is only sound when
+  // the slot's previous phase (k-block i - 2 kLoSlots) is already complete,
+  // or a wait one phase early passes at once and the loader overwrites low
+  // parts the MMAs still read.
+  static_assert(!SPLIT || kStages <= 2 * kLoSlots,
+                "a loader may run at most one low-part-slot phase ahead of the MMAs");
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static_assert((kStages + kLoSlots) * kTile >= Stage<BN>::kBytes,
                 "epilogue staging fits in the rings");
