@@ -13,8 +13,11 @@ rollout updates (the reference's sync_every unit).
 
 Also reported: the Nature-DQN batch-32 update (configs[0] shapes; forward x3,
 double-DQN Huber loss, backward, Adam) as updates/sec from one graph replay
-each, end-to-end numbers through host buffers, the live per-kernel roofline,
-the CPU baseline, and the clocks seen during the timed region.
+each, the SAC and recurrent PPO updates, end-to-end numbers through host
+buffers (the PPO one the median of three runs), the live per-kernel roofline
+(the longest contraction and its next two contenders), the CPU baseline, and
+the clocks seen during the timed region. At N>1 the line also names the GPU
+each rank ran on.
 
 `--impl reference` times the reference's arithmetic on the host CPU (the
 numpy oracle restating it; the reference itself needs ttnn and a
